@@ -1,0 +1,536 @@
+// Sparse neighbour aggregation and feature gather (sm_100a).
+//
+// CSR SpMM, row-split: every row becomes ceil(nnz / kChunk) warp tasks (at
+// least one). A task accumulates its nnz range in fp32 registers: the warp
+// broadcasts (col, val) pairs by shuffle and each lane loads 16-byte slices
+// of the gathered X rows (a 256-wide fp32 row is 1 KB: two fully coalesced
+// 512-byte warp loads). Rows with one task write Y directly; longer rows
+// write fp32 partials that a fixup kernel sums in task order, so results are
+// deterministic. This is the HBM-bound gather form of the aggregation
+// (sum_j val_j * X[col_j]), which has ~0.5 flop per byte and stays off the
+// tensor cores.
+//
+// References: mean pooling as jax.ops.segment_sum / max(count, 1)
+// (dgf/src/learning/jax/layers/hetero_gnn.py:283-295); SparseMatrix @ dense
+// (dgf/src/learning/jax/layers/homo_gnn_sparse_deferred.py:138-161, matrix
+// built in dgf/src/learning/jax/message_passing.py:24-38); feature gather
+// full_feature_value[node_idxs] (dgf/src/sampling/in_memory_sampler.py:
+// 338-346).
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "primitives.cuh"
+
+namespace dgfx {
+namespace {
+
+constexpr int kChunk = 256;        // nnz per SpMM task
+constexpr int kWarpsPerBlock = 8;  // 256-thread blocks
+
+__device__ __forceinline__ void load_vec(const float* p, float* o) {
+  const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+  o[0] = v.x;
+  o[1] = v.y;
+  o[2] = v.z;
+  o[3] = v.w;
+}
+__device__ __forceinline__ void load_vec(const __nv_bfloat16* p, float* o) {
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    o[2 * i] = f.x;
+    o[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store_vec(float* p, const float* o) {
+  *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
+}
+__device__ __forceinline__ void store_vec(__nv_bfloat16* p, const float* o) {
+  uint4 v;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+template <class T> struct Vec;
+template <> struct Vec<float> { static constexpr int n = 4; };
+template <> struct Vec<__nv_bfloat16> { static constexpr int n = 8; };
+
+// ---- task planning --------------------------------------------------------
+__global__ void spmm_count_kernel(const int64_t* __restrict__ rowptr, int64_t rows, int32_t* __restrict__ cnt,
+                                  int32_t* __restrict__ split_cnt) {
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < rows;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t nnz = rowptr[r + 1] - rowptr[r];
+    const int64_t c = nnz <= kChunk ? 1 : (nnz + kChunk - 1) / kChunk;
+    cnt[r] = static_cast<int32_t>(c);
+    split_cnt[r] = c > 1 ? static_cast<int32_t>(c) : 0;
+  }
+}
+
+__global__ void spmm_fill_kernel(const int64_t* __restrict__ task_off, int64_t rows, int32_t* __restrict__ task_row) {
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < rows;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    for (int64_t t = task_off[r]; t < task_off[r + 1]; ++t) task_row[t] = static_cast<int32_t>(r);
+  }
+}
+
+// ---- main kernel ----------------------------------------------------------
+// CPL = 16-byte chunks per lane (feature slice per warp = 32 * CPL * VEC).
+template <class XT, class YT, int CPL>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+spmm_kernel(const int64_t* __restrict__ rowptr, const int32_t* __restrict__ col, const float* __restrict__ val,
+            const XT* __restrict__ X, YT* __restrict__ Y, int64_t feat, int64_t f0, int64_t fw,
+            const int64_t* __restrict__ task_off, const int32_t* __restrict__ task_row,
+            const int64_t* __restrict__ split_off, float* __restrict__ partial, int64_t rows, int normalize,
+            int64_t num_cols) {
+  constexpr int V = Vec<XT>::n;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
+  const int64_t ntasks = task_off[rows];
+  const int nchunks = static_cast<int>(fw / V);
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(kWarpsPerBlock) + (threadIdx.x >> 5); t < ntasks; t += warps) {
+    const int64_t r = task_row[t];
+    const int64_t j = t - task_off[r];
+    const int64_t rb = rowptr[r], re = rowptr[r + 1];
+    const int64_t b = rb + j * kChunk;
+    const int64_t e = min(re, b + kChunk);
+    float acc[CPL][V];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c)
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[c][i] = 0.f;
+    for (int64_t base = b; base < e; base += 32) {
+      const int m = static_cast<int>(e - base < 32 ? e - base : 32);
+      const int64_t idx = base + lane;
+      int32_t my_col = lane < m ? (col != nullptr ? col[idx] : static_cast<int32_t>(idx)) : 0;
+      float my_val = lane < m ? (val != nullptr ? val[idx] : 1.f) : 0.f;
+      if (my_col < 0 || my_col >= num_cols) {  // out-of-range column: no contribution
+        my_col = 0;
+        my_val = 0.f;
+      }
+      int i = 0;
+      for (; i + 4 <= m; i += 4) {
+        float x[4][CPL][V];
+        float wv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t cc = __shfl_sync(0xffffffffu, my_col, i + u);
+          wv[u] = __shfl_sync(0xffffffffu, my_val, i + u);
+          const XT* row = X + cc * feat + f0;
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) {
+            const int ch = lane + 32 * c;
+            if (ch < nchunks) load_vec(row + ch * V, x[u][c]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int c = 0; c < CPL; ++c)
+#pragma unroll
+            for (int q = 0; q < V; ++q) acc[c][q] = fmaf(wv[u], x[u][c][q], acc[c][q]);
+      }
+      for (; i < m; ++i) {
+        const int64_t cc = __shfl_sync(0xffffffffu, my_col, i);
+        const float wv = __shfl_sync(0xffffffffu, my_val, i);
+        const XT* row = X + cc * feat + f0;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const int ch = lane + 32 * c;
+          if (ch < nchunks) {
+            float x[V];
+            load_vec(row + ch * V, x);
+#pragma unroll
+            for (int q = 0; q < V; ++q) acc[c][q] = fmaf(wv, x[q], acc[c][q]);
+          }
+        }
+      }
+    }
+    const int64_t ntask_r = task_off[r + 1] - task_off[r];
+    if (ntask_r == 1) {
+      float scale = 1.f;
+      if (normalize) scale = 1.f / static_cast<float>((re - rb > 1 ? re - rb : 1));
+      YT* out = Y + r * feat + f0;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int ch = lane + 32 * c;
+        if (ch < nchunks) {
+          float o[V];
+#pragma unroll
+          for (int q = 0; q < V; ++q) o[q] = acc[c][q] * scale;
+          store_vec(out + ch * V, o);
+        }
+      }
+    } else {
+      float* out = partial + (split_off[r] + j) * fw;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int ch = lane + 32 * c;
+        if (ch < nchunks) {
+#pragma unroll
+          for (int q = 0; q < V; q += 4) store_vec(out + ch * V + q, &acc[c][q]);
+        }
+      }
+    }
+  }
+}
+
+// Sums the partials of split rows in task order: one warp per row.
+template <class YT>
+__global__ void spmm_fixup_kernel(const int64_t* __restrict__ rowptr, const int64_t* __restrict__ split_off,
+                                  const float* __restrict__ partial, YT* __restrict__ Y, int64_t rows, int64_t feat,
+                                  int64_t f0, int64_t fw, int normalize) {
+  constexpr int V = Vec<YT>::n;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; r < rows; r += warps) {
+    const int64_t s0 = split_off[r], s1 = split_off[r + 1];
+    if (s1 - s0 == 0) continue;
+    float scale = 1.f;
+    if (normalize) scale = 1.f / static_cast<float>((rowptr[r + 1] - rowptr[r] > 1 ? rowptr[r + 1] - rowptr[r] : 1));
+    for (int64_t ch = lane; ch < fw / V; ch += 32) {
+      float acc[V];
+#pragma unroll
+      for (int q = 0; q < V; ++q) acc[q] = 0.f;
+      for (int64_t s = s0; s < s1; ++s) {
+        const float* src = partial + s * fw + ch * V;
+#pragma unroll
+        for (int q = 0; q < V; q += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(src + q);
+          acc[q] += v.x;
+          acc[q + 1] += v.y;
+          acc[q + 2] += v.z;
+          acc[q + 3] += v.w;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < V; ++q) acc[q] *= scale;
+      store_vec(Y + r * feat + f0 + ch * V, acc);
+    }
+  }
+}
+
+// ---- segment_sum helpers --------------------------------------------------
+// rowptr[s] = first item with id >= s (ids sorted ascending), s in [0, nseg].
+__global__ void sorted_bounds_kernel(const int64_t* __restrict__ ids, int64_t n, int64_t nseg,
+                                     int64_t* __restrict__ rowptr) {
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s <= nseg;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t lo = 0, hi = n;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (ids[mid] < s) lo = mid + 1;
+      else hi = mid;
+    }
+    rowptr[s] = lo;
+  }
+}
+
+template <class XT>
+__global__ void segment_atomic_kernel(const XT* __restrict__ data, const int64_t* __restrict__ ids, int64_t n,
+                                      int64_t feat, int64_t nseg, float* __restrict__ acc, int32_t* __restrict__ cnt) {
+  constexpr int V = Vec<XT>::n;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t i = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; i < n; i += warps) {
+    const int64_t s = ids[i];
+    if (s < 0 || s >= nseg) continue;
+    if (lane == 0 && cnt != nullptr) atomicAdd(&cnt[s], 1);
+    for (int64_t ch = lane; ch < feat / V; ch += 32) {
+      float x[V];
+      load_vec(data + i * feat + ch * V, x);
+#pragma unroll
+      for (int q = 0; q < V; q += 4) {
+        atomicAdd(reinterpret_cast<float4*>(acc + s * feat + ch * V + q), make_float4(x[q], x[q + 1], x[q + 2], x[q + 3]));
+      }
+    }
+  }
+}
+
+template <class YT>
+__global__ void segment_finish_kernel(const float* __restrict__ acc, const int32_t* __restrict__ cnt, int64_t nseg,
+                                      int64_t feat, YT* __restrict__ out) {
+  constexpr int V = Vec<YT>::n;
+  const int64_t nvec = nseg * (feat / V);
+  for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < nvec;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t s = v / (feat / V);
+    float scale = 1.f;
+    if (cnt != nullptr) scale = 1.f / static_cast<float>(max(cnt[s], 1));
+    float o[V];
+#pragma unroll
+    for (int q = 0; q < V; ++q) o[q] = acc[v * V + q] * scale;
+    store_vec(out + v * V, o);
+  }
+}
+
+// ---- gather ---------------------------------------------------------------
+__global__ void gather_rows_kernel(const uint4* __restrict__ table, int64_t num_table_rows, int64_t vec_per_row,
+                                   const int64_t* __restrict__ ids, int64_t n, uint4* __restrict__ out) {
+  const int64_t total = n * vec_per_row;
+  for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = v / vec_per_row, c = v - i * vec_per_row;
+    const int64_t r = ids[i];
+    uint4 x = make_uint4(0, 0, 0, 0);
+    if (r >= 0 && r < num_table_rows) x = __ldg(table + r * vec_per_row + c);
+    out[v] = x;
+  }
+}
+
+// Rows [range[0], range[1]) of ids (bounds read on the device, at most
+// max_rows): out[i] = table[ids[range[0] + i]].
+__global__ void gather_rows_ranged_kernel(const uint4* __restrict__ table, int64_t num_table_rows, int64_t vec_per_row,
+                                          const int64_t* __restrict__ ids, const int64_t* __restrict__ range,
+                                          int64_t max_rows, uint4* __restrict__ out) {
+  const int64_t lo = range[0];
+  int64_t n = range[1] - lo;
+  n = n < max_rows ? n : max_rows;
+  const int64_t total = n * vec_per_row;
+  for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = v / vec_per_row, c = v - i * vec_per_row;
+    const int64_t r = ids[lo + i];
+    uint4 x = make_uint4(0, 0, 0, 0);
+    if (r >= 0 && r < num_table_rows) x = __ldg(table + r * vec_per_row + c);
+    out[v] = x;
+  }
+}
+
+int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+unsigned grid_for(int64_t work, int threads) {
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  const int64_t b = ceil_div(std::max<int64_t>(work, 1), threads);
+  return static_cast<unsigned>(std::min(b, cap));
+}
+
+struct SpmmBufs {
+  int32_t* cnt;
+  int32_t* split_cnt;
+  int64_t* task_off;
+  int64_t* split_off;
+  int32_t* task_row;
+  float* partial;
+};
+
+int64_t max_tasks(int64_t rows, int64_t nnz) { return rows + nnz / kChunk + 1; }
+int64_t max_split_tasks(int64_t nnz) { return 2 * (nnz / kChunk) + 2; }
+// Feature columns handled per launch (fp32 partial slice width).
+int64_t feat_block(int64_t feat, int dtype) {
+  const int64_t cap = dtype == DGFX_BF16 ? 1024 : 512;
+  return std::min(feat, cap);
+}
+
+void carve_spmm(Arena& a, int64_t rows, int64_t nnz, int64_t feat, SpmmBufs* b) {
+  b->cnt = a.take<int32_t>(static_cast<size_t>(rows));
+  b->split_cnt = a.take<int32_t>(static_cast<size_t>(rows));
+  b->task_off = a.take<int64_t>(static_cast<size_t>(rows + 1));
+  b->split_off = a.take<int64_t>(static_cast<size_t>(rows + 1));
+  b->task_row = a.take<int32_t>(static_cast<size_t>(max_tasks(rows, nnz)));
+  b->partial = a.take<float>(static_cast<size_t>(max_split_tasks(nnz) * std::min<int64_t>(feat, 1024)));
+}
+
+size_t spmm_ws(int64_t rows, int64_t nnz, int64_t feat) {
+  Arena a(nullptr, 0);
+  SpmmBufs b;
+  carve_spmm(a, rows, nnz, feat, &b);
+  return a.used + scan_workspace_bytes(rows + 1) + 1024;
+}
+
+template <class XT, class YT>
+int launch_spmm(const int64_t* rowptr, const int32_t* col, const float* val, int64_t rows, int64_t num_cols,
+                const void* x, void* y, int64_t feat, int normalize, const SpmmBufs& b, cudaStream_t stream, int xdtype) {
+  constexpr int V = Vec<XT>::n;
+  const int64_t fb = feat_block(feat, xdtype);
+  const unsigned grid = static_cast<unsigned>(sm_count() * 8);
+  for (int64_t f0 = 0; f0 < feat; f0 += fb) {
+    const int64_t fw = std::min(fb, feat - f0);
+    const int64_t chunks = fw / V;
+    const XT* X = static_cast<const XT*>(x);
+    YT* Y = static_cast<YT*>(y);
+    if (chunks <= 32) {
+      spmm_kernel<XT, YT, 1><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
+                                                                        b.task_off, b.task_row, b.split_off,
+                                                                        b.partial, rows, normalize, num_cols);
+    } else if (chunks <= 64) {
+      spmm_kernel<XT, YT, 2><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
+                                                                        b.task_off, b.task_row, b.split_off,
+                                                                        b.partial, rows, normalize, num_cols);
+    } else {
+      spmm_kernel<XT, YT, 4><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
+                                                                        b.task_off, b.task_row, b.split_off,
+                                                                        b.partial, rows, normalize, num_cols);
+    }
+    DGFX_CUDA_TRY(cudaGetLastError());
+    spmm_fixup_kernel<YT><<<grid_for(rows * 32, 256), 256, 0, stream>>>(rowptr, b.split_off, b.partial, Y, rows,
+                                                                         feat, f0, fw, normalize);
+    DGFX_CUDA_TRY(cudaGetLastError());
+  }
+  return DGFX_OK;
+}
+
+int check_dtype(int t) { return t == DGFX_F32 || t == DGFX_BF16; }
+
+}  // namespace
+}  // namespace dgfx
+
+using namespace dgfx;
+
+extern "C" int dgfx_gather_rows(const void* d_table, int64_t num_table_rows, int64_t row_bytes,
+                                const int64_t* d_row_ids, int64_t num_rows, void* d_out, dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (row_bytes <= 0 || row_bytes % 16 != 0 || num_rows < 0 || num_table_rows < 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_gather_rows: row_bytes must be a positive multiple of 16");
+  }
+  if (num_rows == 0) return DGFX_OK;
+  if (reinterpret_cast<uintptr_t>(d_table) % 16 != 0 || reinterpret_cast<uintptr_t>(d_out) % 16 != 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_gather_rows: table and out must be 16-byte aligned");
+  }
+  const int64_t vpr = row_bytes / 16;
+  gather_rows_kernel<<<grid_for(num_rows * vpr, 256), 256, 0, stream>>>(
+      static_cast<const uint4*>(d_table), num_table_rows, vpr, d_row_ids, num_rows, static_cast<uint4*>(d_out));
+  DGFX_CUDA_TRY(cudaGetLastError());
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_gather_rows_ranged(const void* d_table, int64_t num_table_rows, int64_t row_bytes,
+                                       const int64_t* d_row_ids, const int64_t* d_range, int64_t max_rows,
+                                       void* d_out, dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (row_bytes <= 0 || row_bytes % 16 != 0 || max_rows < 0 || num_table_rows < 0 || d_range == nullptr) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_gather_rows_ranged: bad arguments");
+  }
+  if (max_rows == 0) return DGFX_OK;
+  if (reinterpret_cast<uintptr_t>(d_table) % 16 != 0 || reinterpret_cast<uintptr_t>(d_out) % 16 != 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_gather_rows_ranged: table and out must be 16-byte aligned");
+  }
+  const int64_t vpr = row_bytes / 16;
+  gather_rows_ranged_kernel<<<grid_for(max_rows * vpr, 256), 256, 0, stream>>>(
+      static_cast<const uint4*>(d_table), num_table_rows, vpr, d_row_ids, d_range, max_rows,
+      static_cast<uint4*>(d_out));
+  DGFX_CUDA_TRY(cudaGetLastError());
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_spmm_workspace_size(int64_t num_rows, int64_t nnz, int64_t feat, size_t* bytes) {
+  if (bytes == nullptr || num_rows < 0 || nnz < 0 || feat <= 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_spmm_workspace_size: bad arguments");
+  }
+  *bytes = spmm_ws(num_rows, nnz, feat);
+  return DGFX_OK;
+}
+
+namespace {
+int spmm_impl(const int64_t* rowptr, const int32_t* col, const float* val, int64_t rows, int64_t nnz,
+              int64_t num_cols, const void* x, int xt, void* y, int yt, int64_t feat, int normalize, void* ws,
+              size_t ws_bytes, cudaStream_t stream) {
+  Arena arena(ws, ws_bytes);
+  if (ws == nullptr || ws_bytes < spmm_ws(rows, nnz, feat)) return fail(DGFX_ERR_WORKSPACE, "spmm: workspace too small");
+  SpmmBufs b;
+  carve_spmm(arena, rows, nnz, feat, &b);
+  spmm_count_kernel<<<grid_for(rows, 256), 256, 0, stream>>>(rowptr, rows, b.cnt, b.split_cnt);
+  DGFX_CUDA_TRY(cudaGetLastError());
+  const size_t mark = arena.used;
+  DGFX_TRY(exclusive_scan<int32_t>(b.cnt, b.task_off, rows, true, arena, stream));
+  arena.used = mark;
+  DGFX_TRY(exclusive_scan<int32_t>(b.split_cnt, b.split_off, rows, true, arena, stream));
+  spmm_fill_kernel<<<grid_for(rows, 256), 256, 0, stream>>>(b.task_off, rows, b.task_row);
+  DGFX_CUDA_TRY(cudaGetLastError());
+  if (xt == DGFX_F32 && yt == DGFX_F32) return launch_spmm<float, float>(rowptr, col, val, rows, num_cols, x, y, feat, normalize, b, stream, xt);
+  if (xt == DGFX_F32 && yt == DGFX_BF16) return launch_spmm<float, __nv_bfloat16>(rowptr, col, val, rows, num_cols, x, y, feat, normalize, b, stream, xt);
+  if (xt == DGFX_BF16 && yt == DGFX_F32) return launch_spmm<__nv_bfloat16, float>(rowptr, col, val, rows, num_cols, x, y, feat, normalize, b, stream, xt);
+  return launch_spmm<__nv_bfloat16, __nv_bfloat16>(rowptr, col, val, rows, num_cols, x, y, feat, normalize, b, stream, xt);
+}
+}  // namespace
+
+extern "C" int dgfx_spmm_csr(const int64_t* d_rowptr, const int32_t* d_col, const float* d_val, int64_t num_rows,
+                             int64_t num_cols, int64_t nnz, const void* d_x, int x_dtype, void* d_y, int y_dtype,
+                             int64_t feat, int32_t normalize, void* d_workspace, size_t workspace_bytes,
+                             dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!check_dtype(x_dtype) || !check_dtype(y_dtype)) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_spmm_csr: dtype");
+  if (num_rows < 0 || num_cols < 0 || nnz < 0 || feat <= 0 || d_rowptr == nullptr || d_y == nullptr) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_spmm_csr: bad arguments");
+  }
+  if (feat % 8 != 0) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_spmm_csr: feat must be a multiple of 8");
+  if (num_cols >= (int64_t(1) << 31)) return fail(DGFX_ERR_UNSUPPORTED, "dgfx_spmm_csr: more than 2^31 - 1 columns");
+  if (reinterpret_cast<uintptr_t>(d_x) % 16 != 0 || reinterpret_cast<uintptr_t>(d_y) % 16 != 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_spmm_csr: X and Y must be 16-byte aligned");
+  }
+  if (num_rows == 0) return DGFX_OK;
+  if (nnz > 0 && d_col == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_spmm_csr: null col");
+  return spmm_impl(d_rowptr, d_col, d_val, num_rows, nnz, num_cols, d_x, x_dtype, d_y, y_dtype, feat, normalize,
+                   d_workspace, workspace_bytes, stream);
+}
+
+extern "C" int dgfx_segment_sum_workspace_size(int64_t num_items, int64_t feat, int64_t num_segments, size_t* bytes) {
+  if (bytes == nullptr || num_items < 0 || feat <= 0 || num_segments < 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_segment_sum_workspace_size: bad arguments");
+  }
+  const size_t sorted = align_up(sizeof(int64_t) * (num_segments + 1), 256) + spmm_ws(num_segments, num_items, feat);
+  const size_t atomic = align_up(sizeof(float) * num_segments * feat, 256) + align_up(sizeof(int32_t) * num_segments, 256);
+  *bytes = std::max(sorted, atomic) + 1024;
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_segment_sum(const void* d_data, int data_dtype, const int64_t* d_ids, int64_t n, int64_t feat,
+                                int64_t nseg, int32_t mean, int32_t sorted, void* d_out, int out_dtype,
+                                void* d_workspace, size_t workspace_bytes, dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!check_dtype(data_dtype) || !check_dtype(out_dtype)) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_segment_sum: dtype");
+  if (n < 0 || feat <= 0 || nseg < 0 || feat % 8 != 0) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_segment_sum: bad arguments");
+  if (n >= (int64_t(1) << 31)) return fail(DGFX_ERR_UNSUPPORTED, "dgfx_segment_sum: more than 2^31 - 1 items");
+  if (nseg == 0) return DGFX_OK;
+  size_t need = 0;
+  DGFX_TRY(dgfx_segment_sum_workspace_size(n, feat, nseg, &need));
+  if (d_workspace == nullptr || workspace_bytes < need) return fail(DGFX_ERR_WORKSPACE, "dgfx_segment_sum: workspace too small");
+  Arena arena(d_workspace, workspace_bytes);
+  if (sorted) {
+    int64_t* rowptr = arena.take<int64_t>(static_cast<size_t>(nseg + 1));
+    sorted_bounds_kernel<<<grid_for(nseg + 1, 256), 256, 0, stream>>>(d_ids, n, nseg, rowptr);
+    DGFX_CUDA_TRY(cudaGetLastError());
+    // Items are gathered in place: X row j = data row j (identity columns).
+    return spmm_impl(rowptr, nullptr, nullptr, nseg, n, n, d_data, data_dtype, d_out, out_dtype, feat, mean,
+                     arena.base + arena.used, workspace_bytes - arena.used, stream);
+  }
+  float* acc = arena.take<float>(static_cast<size_t>(nseg * feat));
+  int32_t* cnt = mean ? arena.take<int32_t>(static_cast<size_t>(nseg)) : nullptr;
+  DGFX_CUDA_TRY(cudaMemsetAsync(acc, 0, sizeof(float) * nseg * feat, stream));
+  if (cnt != nullptr) DGFX_CUDA_TRY(cudaMemsetAsync(cnt, 0, sizeof(int32_t) * nseg, stream));
+  if (n > 0) {
+    if (data_dtype == DGFX_F32) {
+      segment_atomic_kernel<float><<<grid_for(n * 32, 256), 256, 0, stream>>>(
+          static_cast<const float*>(d_data), d_ids, n, feat, nseg, acc, cnt);
+    } else {
+      segment_atomic_kernel<__nv_bfloat16><<<grid_for(n * 32, 256), 256, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(d_data), d_ids, n, feat, nseg, acc, cnt);
+    }
+    DGFX_CUDA_TRY(cudaGetLastError());
+  }
+  if (out_dtype == DGFX_F32) {
+    segment_finish_kernel<float><<<grid_for(nseg * feat / 4, 256), 256, 0, stream>>>(acc, cnt, nseg, feat,
+                                                                                     static_cast<float*>(d_out));
+  } else {
+    segment_finish_kernel<__nv_bfloat16><<<grid_for(nseg * feat / 8, 256), 256, 0, stream>>>(
+        acc, cnt, nseg, feat, static_cast<__nv_bfloat16*>(d_out));
+  }
+  DGFX_CUDA_TRY(cudaGetLastError());
+  return DGFX_OK;
+}

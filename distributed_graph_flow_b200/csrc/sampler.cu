@@ -1,0 +1,782 @@
+// Per-seed k-hop sampler (sm_100a).
+//
+// Semantics follow DGF's SampleBuilder::RecursiveGrow / Grow and
+// Sampler::Sample (dgf/src/sampling/in_memory_sampler_ext.cc:231-370,
+// 418-533) with the per-node samplers of dgf/src/sampling/
+// in_memory_sampler.cc:22-364.
+//
+// Design. The sampling plan is unrolled on the host into a padded expansion
+// tree: every plan node instance gets a fixed "position" in depth-first
+// pre-order, with hop_width slots reserved per plan edge, so a plan node's
+// padded subtree has Z(p) = 1 + sum_c hop_width(c) * Z(child(c)) positions and
+// one seed's tree has T = Z(root). The reference's depth-first traversal
+// visits instances in exactly this position order (plan edges in order, the
+// picked neighbours of one edge in pick order), so:
+//   * "first discovery" of a node = its smallest position,
+//   * the reference's local id = number of first discoveries of the same
+//     nodeset at smaller positions (a scan),
+// and no recursion or ordered map is needed. One CTA samples one seed:
+//   1. level-synchronous expansion: a task per (position, plan edge) reads the
+//      row, applies the timestamp cutoff (upper_bound on the time-sorted row)
+//      and the masked edge, and writes the picked neighbours into the child
+//      slots (-1 marks an empty slot);
+//   2. relabel: hash table keyed by (nodeset, node) keeps the minimum position
+//      (atomicMin), then a block scan numbers first discoveries per nodeset
+//      (with_replacement: every occupied position is a new node);
+//   3. edges: one 64-bit key (edgeset, src_local, dst_local) per occupied
+//      non-root position, bitonic-sorted in the block, then deduplicated; this
+//      equals the reference's btree_set iteration order;
+//   4. per-seed results go to a scratch slice; two scans and a compaction
+//      kernel produce the merged batch.
+// Arrays live in shared memory when the tree is small enough (T <= 4096),
+// otherwise in a per-CTA slice of the workspace.
+//
+// Random mode draws from Philox4x32-10 keyed by the sampler seed with counter
+// (tree position, plan edge | draw block, seed slot, call index) and picks k
+// of n with Floyd's algorithm (Bentley & Floyd, "Programming pearls: a sample
+// of brilliance", CACM 1987), output in adjacency order. This is a different
+// generator from the reference's std::mt19937_64, so random-mode results
+// match the reference in distribution (uniform k-subsets of the valid row),
+// not bit for bit; FIRST and MOST_RECENT modes and fanout >= degree are exact.
+#include <algorithm>
+#include <cstring>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "primitives.cuh"
+
+namespace dgfx {
+namespace {
+
+constexpr uint64_t kEmptyKey = ~0ull;
+constexpr int kMaxNodesets = 64;
+constexpr int kMaxEdgesets = 256;
+constexpr int kMaxSmemPositions = 4096;
+constexpr int64_t kMaxPositions = int64_t(1) << 24;
+
+struct EdgeDev {
+  const int64_t* rowptr;
+  const int32_t* col;
+  const int64_t* ts;
+  const int64_t* edge_pos;
+  int64_t num_edges;
+  int32_t k;        // hop width
+  int32_t stride;   // Z(child)
+  int32_t edgeset;
+  int32_t reversed;
+};
+
+struct Params {
+  const EdgeDev* edges;
+  const int4* tasks;       // (parent position, plan edge, first child slot, 0)
+  const int32_t* level;    // tasks of depth d: [level[d], level[d+1])
+  int32_t depth;           // number of expansion levels
+  const int2* pos_info;    // (parent position, plan edge << 8 | nodeset)
+  int32_t T, N2, H, log2H;
+  int32_t num_nodesets, num_edgesets;
+  int32_t root_has_children;
+  int64_t root_num_src;
+  int32_t with_replacement, mode, mask_edgeset;
+  const int64_t* seeds;
+  const int64_t* seed_ts;
+  const int64_t* masks;
+  int64_t B;
+  uint32_t key0, key1, call_lo, call_hi;
+  int32_t* scratch_nodes;    // [B][T]
+  uint64_t* scratch_edges;   // [B][T]
+  int32_t* node_cnt;         // [NS][B]
+  int32_t* edge_cnt;         // [ES][B]
+  char* global_work;         // per-CTA arrays when not in shared memory
+  size_t work_stride;
+  unsigned long long* status;  // [0] first bad seed slot, [1] ts missing, [2] table overflow
+};
+
+// Per-CTA working arrays (shared or global memory).
+struct Work {
+  int32_t* node;    // [T]
+  int32_t* local;   // [T]
+  uint64_t* hkey;   // [H]   (reused as the edge-key array, N2 <= H)
+  int32_t* hval;    // [H]
+};
+
+__host__ __device__ inline size_t work_bytes(int T, int H) {
+  return static_cast<size_t>(T) * 8 + static_cast<size_t>(H) * 12 + 64;
+}
+
+__device__ inline Work carve_work(char* base, int T, int H) {
+  Work w;
+  w.hkey = reinterpret_cast<uint64_t*>(base);
+  w.hval = reinterpret_cast<int32_t*>(base + static_cast<size_t>(H) * 8);
+  w.node = reinterpret_cast<int32_t*>(base + static_cast<size_t>(H) * 12);
+  w.local = w.node + T;
+  return w;
+}
+
+__device__ __forceinline__ uint64_t draw64(const Params& p, int32_t q, int32_t e, uint32_t m, uint32_t slot) {
+  U4 c{static_cast<uint32_t>(q), static_cast<uint32_t>(e) | ((m >> 1) << 16), slot, p.call_lo};
+  const U4 r = philox4x32_10(c, p.key0 ^ p.call_hi, p.key1);
+  return (m & 1u) ? (static_cast<uint64_t>(r.w) << 32 | r.z) : (static_cast<uint64_t>(r.y) << 32 | r.x);
+}
+
+// One expansion task: pick up to k neighbours of node v over plan edge e and
+// write them to the child slots base + j * stride (j < k).
+__device__ void expand_task(const Params& p, const Work& w, int32_t q, int32_t e, int32_t base, int64_t v,
+                            bool has_ts, int64_t seed_ts, int64_t mask, uint32_t slot) {
+  const EdgeDev E = p.edges[e];
+  const int32_t k = E.k, stride = E.stride;
+  int32_t cnt = 0;
+  if (v >= 0) {
+    const int64_t rb = E.rowptr[v];
+    const int64_t re = E.rowptr[v + 1];
+    int64_t n = re - rb;
+    const bool temporal = has_ts && E.ts != nullptr;
+    if (!has_ts && E.ts != nullptr) {
+      // SampleRandomUniform / SampleFirst on a temporal index fail
+      // (in_memory_sampler.cc:26-30, 168-172).
+      atomicOr(&p.status[1], 1ull);
+      n = 0;
+    }
+    if (temporal && n > 0) {
+      // upper_bound(ts[rb..re), seed_ts): first position with ts > seed_ts.
+      int64_t lo = 0, hi = n;
+      while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (E.ts[rb + mid] <= seed_ts) lo = mid + 1;
+        else hi = mid;
+      }
+      n = lo;
+    }
+    int64_t moff = -1;
+    if (!temporal && mask >= 0 && E.edgeset == p.mask_edgeset && E.edge_pos != nullptr && mask < E.num_edges) {
+      const int64_t pos = E.edge_pos[mask];
+      if (pos >= rb && pos < rb + n) moff = pos - rb;
+    }
+    const int64_t nv = n - (moff >= 0 ? 1 : 0);
+    cnt = static_cast<int32_t>(nv < k ? nv : k);
+    const int mode = (p.mode == DGFX_MODE_MOST_RECENT && !temporal) ? DGFX_MODE_RANDOM : p.mode;
+    if (cnt > 0) {
+      if (mode == DGFX_MODE_RANDOM && cnt < nv) {
+        // Floyd: for j = nv-cnt .. nv-1 pick t in [0, j]; take t unless
+        // already taken, else take j. Chosen offsets go to the child slots.
+        int32_t taken = 0;
+        for (int64_t j = nv - cnt; j < nv; ++j) {
+          const uint64_t r = draw64(p, q, e, static_cast<uint32_t>(taken), slot);
+          int64_t t = static_cast<int64_t>(bounded64(r, static_cast<uint64_t>(j + 1)));
+          for (int32_t i = 0; i < taken; ++i) {
+            if (w.node[base + i * stride] == t) {
+              t = j;
+              break;
+            }
+          }
+          w.node[base + taken * stride] = static_cast<int32_t>(t);
+          ++taken;
+        }
+        // Adjacency order (insertion sort over the slots).
+        for (int32_t i = 1; i < cnt; ++i) {
+          const int32_t x = w.node[base + i * stride];
+          int32_t j = i - 1;
+          while (j >= 0 && w.node[base + j * stride] > x) {
+            w.node[base + (j + 1) * stride] = w.node[base + j * stride];
+            --j;
+          }
+          w.node[base + (j + 1) * stride] = x;
+        }
+        for (int32_t i = 0; i < cnt; ++i) {
+          int64_t off = w.node[base + i * stride];
+          if (moff >= 0 && off >= moff) ++off;
+          w.node[base + i * stride] = E.col[rb + off];
+        }
+      } else {
+        const int64_t first = (mode == DGFX_MODE_MOST_RECENT) ? nv - cnt : 0;
+        for (int32_t i = 0; i < cnt; ++i) {
+          int64_t off = first + i;
+          if (moff >= 0 && off >= moff) ++off;
+          w.node[base + i * stride] = E.col[rb + off];
+        }
+      }
+    }
+  }
+  for (int32_t i = cnt; i < k; ++i) w.node[base + i * stride] = -1;
+}
+
+// Exclusive scan over items [0, n) of a block: value(i) is read twice (must
+// not depend on what sink writes), sink(i, prefix) receives each prefix.
+template <class V, class S>
+__device__ uint64_t block_scan_items(int n, V value, S sink, uint64_t* smem33) {
+  const int per = (n + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
+  const int lo = min(n, static_cast<int>(threadIdx.x) * per);
+  const int hi = min(n, lo + per);
+  uint64_t s = 0;
+  for (int i = lo; i < hi; ++i) s += value(i);
+  uint64_t total = 0;
+  uint64_t pre = block_exclusive_scan<uint64_t>(s, smem33, &total);
+  for (int i = lo; i < hi; ++i) {
+    const uint64_t v = value(i);
+    sink(i, pre);
+    pre += v;
+  }
+  __syncthreads();
+  return total;
+}
+
+__global__ void __launch_bounds__(256) sample_kernel(Params p) {
+  extern __shared__ __align__(16) char smem_dyn[];
+  __shared__ uint64_t scan_tmp[33];
+  __shared__ int32_t ns_count[kMaxNodesets];
+  __shared__ int32_t ns_base[kMaxNodesets];
+  __shared__ int32_t es_count[kMaxEdgesets];
+
+  const int64_t sample = blockIdx.x;
+  const int T = p.T;
+  char* base = p.global_work != nullptr ? p.global_work + static_cast<size_t>(sample) * p.work_stride : smem_dyn;
+  const Work w = carve_work(base, T, p.H);
+  const uint32_t slot = static_cast<uint32_t>(sample);
+
+  const int64_t seed = p.seeds[sample];
+  const bool has_ts = p.seed_ts != nullptr;
+  const int64_t sts = has_ts ? p.seed_ts[sample] : 0;
+  const int64_t mask = p.masks != nullptr ? p.masks[sample] : -1;
+
+  for (int i = threadIdx.x; i < p.num_nodesets; i += blockDim.x) ns_count[i] = 0;
+  for (int i = threadIdx.x; i < p.num_edgesets; i += blockDim.x) es_count[i] = 0;
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    if (p.root_has_children && (seed < 0 || seed >= p.root_num_src)) {
+      atomicMin(&p.status[0], static_cast<unsigned long long>(sample));
+      ok = false;
+    }
+    w.node[0] = ok ? static_cast<int32_t>(seed) : -1;
+  }
+  __syncthreads();
+
+  // 1. Level-synchronous expansion.
+  for (int d = 0; d < p.depth; ++d) {
+    const int t0 = p.level[d], t1 = p.level[d + 1];
+    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
+      const int4 task = p.tasks[t];
+      expand_task(p, w, task.x, task.y, task.z, w.node[task.x], has_ts, sts, mask, slot);
+    }
+    __syncthreads();
+  }
+
+  // 2. Relabel.
+  if (p.with_replacement) {
+    for (int q = threadIdx.x; q < T; q += blockDim.x) w.local[q] = -1;
+    __syncthreads();
+  } else {
+    for (int i = threadIdx.x; i < p.H; i += blockDim.x) {
+      w.hkey[i] = kEmptyKey;
+      w.hval[i] = 0x7fffffff;
+    }
+    __syncthreads();
+    const uint32_t hmask = static_cast<uint32_t>(p.H - 1);
+    for (int q = threadIdx.x; q < T; q += blockDim.x) {
+      const int32_t v = w.node[q];
+      int32_t slot_q = -1;
+      if (v >= 0) {
+        const int ns = p.pos_info[q].y & 0xFF;
+        const uint64_t key = (static_cast<uint64_t>(ns) << 32) | static_cast<uint32_t>(v);
+        uint32_t h = static_cast<uint32_t>((key * 0x9E3779B97F4A7C15ull) >> (64 - p.log2H)) & hmask;
+        for (int probe = 0; probe < p.H; ++probe) {
+          const unsigned long long prev = atomicCAS(reinterpret_cast<unsigned long long*>(&w.hkey[h]), kEmptyKey, key);
+          if (prev == kEmptyKey || prev == key) {
+            atomicMin(&w.hval[h], q);
+            slot_q = static_cast<int32_t>(h);
+            break;
+          }
+          h = (h + 1) & hmask;
+        }
+        if (slot_q < 0) atomicOr(&p.status[2], 1ull);
+      }
+      w.local[q] = slot_q;
+    }
+    __syncthreads();
+  }
+  // Number first discoveries per nodeset, up to 4 nodesets per pass (16-bit
+  // fields; T <= 65535 here) or 2 per pass (32-bit fields).
+  const int per_pass = T < 65536 ? 4 : 2;
+  const int fbits = 64 / per_pass;
+  const uint64_t fmask = (fbits == 64) ? ~0ull : ((1ull << fbits) - 1);
+  for (int g = 0; g < p.num_nodesets; g += per_pass) {
+    auto first = [&](int q) -> bool {
+      if (p.with_replacement) return w.node[q] >= 0;
+      const int32_t s = w.local[q];
+      return s >= 0 && w.hval[s] == q;
+    };
+    auto value = [&](int q) -> uint64_t {
+      const int ns = p.pos_info[q].y & 0xFF;
+      if (ns < g || ns >= g + per_pass || !first(q)) return 0;
+      return 1ull << ((ns - g) * fbits);
+    };
+    auto sink = [&](int q, uint64_t pre) {
+      const int ns = p.pos_info[q].y & 0xFF;
+      if (ns < g || ns >= g + per_pass || !first(q)) return;
+      const int32_t rank = static_cast<int32_t>((pre >> ((ns - g) * fbits)) & fmask);
+      if (p.with_replacement) w.local[q] = rank;
+      else w.hval[w.local[q]] = -(rank + 1);
+    };
+    const uint64_t tot = block_scan_items(T, value, sink, scan_tmp);
+    if (threadIdx.x == 0) {
+      for (int s = g; s < g + per_pass && s < p.num_nodesets; ++s) {
+        ns_count[s] = static_cast<int32_t>((tot >> ((s - g) * fbits)) & fmask);
+      }
+    }
+  }
+  __syncthreads();
+  if (!p.with_replacement) {
+    for (int q = threadIdx.x; q < T; q += blockDim.x) {
+      const int32_t s = w.local[q];
+      w.local[q] = s >= 0 ? -w.hval[s] - 1 : -1;
+    }
+  }
+  if (threadIdx.x == 0) {
+    int32_t acc = 0;
+    for (int s = 0; s < p.num_nodesets; ++s) {
+      ns_base[s] = acc;
+      acc += ns_count[s];
+    }
+  }
+  __syncthreads();
+
+  // Nodes of this seed, per nodeset in local-id order. Every occurrence of a
+  // node writes the same value to its local slot.
+  int32_t* out_nodes = p.scratch_nodes + sample * static_cast<int64_t>(T);
+  for (int q = threadIdx.x; q < T; q += blockDim.x) {
+    const int32_t v = w.node[q];
+    if (v < 0) continue;
+    const int ns = p.pos_info[q].y & 0xFF;
+    const int32_t l = w.local[q];
+    if (l >= 0) out_nodes[ns_base[ns] + l] = v;
+  }
+
+  // 3. Edge keys (edgeset, src_local, dst_local), sorted and deduplicated.
+  uint64_t* ek = w.hkey;
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.N2; i += blockDim.x) {
+    uint64_t key = kEmptyKey;
+    const int q = i + 1;
+    if (q < T && w.node[q] >= 0 && w.local[q] >= 0) {
+      const int2 info = p.pos_info[q];
+      const int e = info.y >> 8;
+      const EdgeDev& E = p.edges[e];
+      const uint64_t a = static_cast<uint32_t>(w.local[info.x]);
+      const uint64_t b = static_cast<uint32_t>(w.local[q]);
+      const uint64_t src = E.reversed ? b : a, dst = E.reversed ? a : b;
+      key = (static_cast<uint64_t>(E.edgeset) << 48) | (src << 24) | dst;
+    }
+    ek[i] = key;
+  }
+  __syncthreads();
+  for (int kk = 2; kk <= p.N2; kk <<= 1) {
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < p.N2; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint64_t a = ek[i], b = ek[ixj];
+          const bool up = (i & kk) == 0;
+          if ((a > b) == up) {
+            ek[i] = b;
+            ek[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  uint64_t* out_edges = p.scratch_edges + sample * static_cast<int64_t>(T);
+  auto is_new = [&](int i) -> uint64_t {
+    const uint64_t k = ek[i];
+    return (k != kEmptyKey && (i == 0 || ek[i - 1] != k)) ? 1ull : 0ull;
+  };
+  auto put = [&](int i, uint64_t pre) {
+    const uint64_t k = ek[i];
+    if (k != kEmptyKey && (i == 0 || ek[i - 1] != k)) {
+      out_edges[pre] = k;
+      atomicAdd(&es_count[static_cast<int>(k >> 48)], 1);
+    }
+  };
+  block_scan_items(p.N2, is_new, put, scan_tmp);
+
+  for (int s = threadIdx.x; s < p.num_nodesets; s += blockDim.x) p.node_cnt[s * p.B + sample] = ns_count[s];
+  for (int e = threadIdx.x; e < p.num_edgesets; e += blockDim.x) p.edge_cnt[e * p.B + sample] = es_count[e];
+}
+
+// Merged batch from the per-seed scratch: one warp per seed.
+__global__ void compact_kernel(Params p, const int64_t* __restrict__ node_off, const int64_t* __restrict__ edge_off,
+                               int root_ns, int64_t* __restrict__ node_ids, int64_t* __restrict__ edge_src,
+                               int64_t* __restrict__ edge_dst) {
+  const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= p.B) return;
+  const int64_t i = warp;
+  const int32_t* src_nodes = p.scratch_nodes + i * static_cast<int64_t>(p.T);
+  const uint64_t* src_edges = p.scratch_edges + i * static_cast<int64_t>(p.T);
+  int64_t acc = 0;
+  for (int s = 0; s < p.num_nodesets; ++s) {
+    const int64_t o = node_off[s * p.B + i];
+    const int64_t c = node_off[s * p.B + i + 1] - o;
+    for (int64_t j = lane; j < c; j += 32) {
+      int64_t v = src_nodes[acc + j];
+      if (s == root_ns && j == 0) v = p.seeds[i];
+      node_ids[o + j] = v;
+    }
+    acc += c;
+  }
+  acc = 0;
+  for (int e = 0; e < p.num_edgesets; ++e) {
+    const int64_t o = edge_off[e * p.B + i];
+    const int64_t c = edge_off[e * p.B + i + 1] - o;
+    for (int64_t j = lane; j < c; j += 32) {
+      const uint64_t k = src_edges[acc + j];
+      edge_src[o + j] = static_cast<int64_t>((k >> 24) & 0xFFFFFFull);
+      edge_dst[o + j] = static_cast<int64_t>(k & 0xFFFFFFull);
+    }
+    acc += c;
+  }
+}
+
+}  // namespace
+}  // namespace dgfx
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+using namespace dgfx;
+
+struct dgfx_sampler {
+  // Plan, unrolled.
+  int32_t T = 0, N2 = 1, H = 2, log2H = 1, depth = 0;
+  int32_t num_nodesets = 0, num_edgesets = 0, root_ns = 0, root_has_children = 0;
+  int64_t root_num_src = 0;
+  int32_t with_replacement = 0, mode = 0, mask_edgeset = -1;
+  uint64_t seed = 0;
+  bool use_smem = true;
+  int threads = 256;
+  // Device tables (one allocation).
+  void* d_tables = nullptr;
+  EdgeDev* d_edges = nullptr;
+  int4* d_tasks = nullptr;
+  int32_t* d_level = nullptr;
+  int2* d_pos = nullptr;
+  unsigned long long* d_status = nullptr;
+  int64_t last_B = 0;
+  const int64_t* last_seeds = nullptr;
+  std::vector<EdgeDev> h_edges;
+};
+
+namespace {
+
+int pow2_at_least(int64_t x) {
+  int64_t p = 1;
+  while (p < x) p <<= 1;
+  return static_cast<int>(p);
+}
+
+struct SampleBufs {
+  int32_t* scratch_nodes;
+  uint64_t* scratch_edges;
+  int32_t* node_cnt;
+  int32_t* edge_cnt;
+  char* global_work;
+};
+
+void carve_sample(Arena& a, const dgfx_sampler* s, int64_t B, SampleBufs* b) {
+  b->scratch_nodes = a.take<int32_t>(static_cast<size_t>(B * s->T));
+  b->scratch_edges = a.take<uint64_t>(static_cast<size_t>(B * s->T));
+  b->node_cnt = a.take<int32_t>(static_cast<size_t>(B * s->num_nodesets));
+  b->edge_cnt = a.take<int32_t>(static_cast<size_t>(B * s->num_edgesets));
+  b->global_work = s->use_smem ? nullptr : a.take<char>(static_cast<size_t>(B) * work_bytes(s->T, s->H));
+}
+
+size_t sample_ws_bytes(const dgfx_sampler* s, int64_t B) {
+  Arena a(nullptr, 0);
+  SampleBufs b;
+  carve_sample(a, s, B, &b);
+  const int64_t n = std::max<int64_t>(B * s->num_nodesets, B * s->num_edgesets) + 1;
+  return a.used + scan_workspace_bytes(n) + 1024;
+}
+
+}  // namespace
+
+extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_nodeset,
+                                   const int32_t* node_first_edge, const int32_t* node_num_edges,
+                                   int32_t num_plan_edges, const int32_t* edge_edgeset,
+                                   const int32_t* edge_reversed, const int32_t* edge_hop_width,
+                                   const int32_t* edge_child, int32_t with_replacement, int32_t num_nodesets,
+                                   const int64_t* num_nodes, int32_t num_edgesets, const dgfx_csr_view* forward,
+                                   const dgfx_csr_view* backward, int32_t mode, int32_t edgeset_to_mask,
+                                   uint64_t seed, dgfx_sampler** out) {
+  if (out == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_create: out is null");
+  *out = nullptr;
+  if (num_plan_nodes < 1 || num_plan_edges < 0 || num_nodesets < 1 || num_edgesets < 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_create: empty plan or schema");
+  }
+  if (num_nodesets > kMaxNodesets || num_edgesets > kMaxEdgesets) {
+    return fail(DGFX_ERR_UNSUPPORTED, "dgfx_sampler_create: at most 64 nodesets and 256 edgesets");
+  }
+  if (mode < DGFX_MODE_RANDOM || mode > DGFX_MODE_MOST_RECENT) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_create: unknown mode");
+  }
+  for (int32_t i = 0; i < num_plan_nodes; ++i) {
+    if (node_nodeset[i] < 0 || node_nodeset[i] >= num_nodesets || node_num_edges[i] < 0 ||
+        node_first_edge[i] < 0 || node_first_edge[i] + node_num_edges[i] > num_plan_edges) {
+      return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_create: malformed plan node " + std::to_string(i));
+    }
+  }
+  for (int32_t j = 0; j < num_plan_edges; ++j) {
+    if (edge_edgeset[j] < 0 || edge_edgeset[j] >= num_edgesets || edge_child[j] <= 0 ||
+        edge_child[j] >= num_plan_nodes || edge_hop_width[j] < 0) {
+      return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_create: malformed plan edge " + std::to_string(j));
+    }
+    const dgfx_csr_view& v = edge_reversed[j] ? backward[edge_edgeset[j]] : forward[edge_edgeset[j]];
+    if (v.rowptr == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "Check failed edges.has_value()");
+  }
+  auto s = std::make_unique<dgfx_sampler>();
+  s->num_nodesets = num_nodesets;
+  s->num_edgesets = num_edgesets;
+  s->with_replacement = with_replacement != 0;
+  s->mode = mode;
+  s->mask_edgeset = edgeset_to_mask;
+  s->seed = seed;
+  s->root_ns = node_nodeset[0];
+
+  // Padded subtree sizes Z(p): memoised recursion with a cycle guard.
+  std::vector<int64_t> Z(num_plan_nodes, -1);
+  std::vector<int> state(num_plan_nodes, 0);
+  std::function<int64_t(int)> size_of = [&](int pn) -> int64_t {
+    if (Z[pn] >= 0) return Z[pn];
+    if (state[pn] == 1) return -1;
+    state[pn] = 1;
+    int64_t z = 1;
+    for (int c = 0; c < node_num_edges[pn]; ++c) {
+      const int j = node_first_edge[pn] + c;
+      const int64_t zc = size_of(edge_child[j]);
+      if (zc < 0) return -1;
+      z += static_cast<int64_t>(edge_hop_width[j]) * zc;
+      if (z > kMaxPositions) return -1;
+    }
+    state[pn] = 2;
+    return Z[pn] = z;
+  };
+  const int64_t T = size_of(0);
+  if (T < 0) {
+    return fail(DGFX_ERR_UNSUPPORTED, "dgfx_sampler_create: sampling plan expands to more than 2^24 tree positions "
+                                      "per seed (or is cyclic)");
+  }
+  s->T = static_cast<int32_t>(T);
+  s->N2 = pow2_at_least(std::max<int64_t>(T, 2));
+  s->H = pow2_at_least(2 * T);
+  s->log2H = 0;
+  while ((1 << s->log2H) < s->H) ++s->log2H;
+  s->use_smem = T <= kMaxSmemPositions;
+
+  // Pre-order positions and expansion tasks by depth.
+  std::vector<int2> pos(static_cast<size_t>(T));
+  std::vector<std::vector<int4>> tasks_by_depth;
+  std::function<void(int, int64_t, int64_t, int, int)> place = [&](int pn, int64_t q, int64_t parent, int pedge,
+                                                                   int depth) {
+    pos[q] = make_int2(static_cast<int>(parent), (pedge < 0 ? 0 : pedge << 8) | node_nodeset[pn]);
+    int64_t off = q + 1;
+    for (int c = 0; c < node_num_edges[pn]; ++c) {
+      const int j = node_first_edge[pn] + c;
+      const int64_t zc = Z[edge_child[j]];
+      if (static_cast<int>(tasks_by_depth.size()) <= depth) tasks_by_depth.resize(depth + 1);
+      tasks_by_depth[depth].push_back(make_int4(static_cast<int>(q), j, static_cast<int>(off), 0));
+      for (int k = 0; k < edge_hop_width[j]; ++k) place(edge_child[j], off + k * zc, q, j, depth + 1);
+      off += static_cast<int64_t>(edge_hop_width[j]) * zc;
+    }
+  };
+  place(0, 0, -1, -1, 0);
+  if (num_plan_edges >= (1 << 23)) return fail(DGFX_ERR_UNSUPPORTED, "dgfx_sampler_create: too many plan edges");
+  std::vector<int4> tasks;
+  std::vector<int32_t> level{0};
+  for (auto& v : tasks_by_depth) {
+    tasks.insert(tasks.end(), v.begin(), v.end());
+    level.push_back(static_cast<int32_t>(tasks.size()));
+  }
+  s->depth = static_cast<int32_t>(tasks_by_depth.size());
+  s->root_has_children = node_num_edges[0] > 0;
+  if (s->root_has_children) {
+    const int j = node_first_edge[0];
+    const dgfx_csr_view& v = edge_reversed[j] ? backward[edge_edgeset[j]] : forward[edge_edgeset[j]];
+    s->root_num_src = v.num_src;
+  }
+  s->h_edges.resize(num_plan_edges);
+  for (int j = 0; j < num_plan_edges; ++j) {
+    const dgfx_csr_view& v = edge_reversed[j] ? backward[edge_edgeset[j]] : forward[edge_edgeset[j]];
+    EdgeDev& E = s->h_edges[j];
+    E.rowptr = v.rowptr;
+    E.col = v.col;
+    E.ts = v.ts;
+    E.edge_pos = (edge_edgeset[j] == edgeset_to_mask) ? v.edge_pos : nullptr;
+    E.num_edges = v.num_edges;
+    E.k = edge_hop_width[j];
+    E.stride = static_cast<int32_t>(Z[edge_child[j]]);
+    E.edgeset = edge_edgeset[j];
+    E.reversed = edge_reversed[j] != 0;
+  }
+  (void)num_nodes;
+
+  // One device allocation for all tables.
+  const size_t b_edges = align_up(sizeof(EdgeDev) * std::max<size_t>(1, s->h_edges.size()), 256);
+  const size_t b_tasks = align_up(sizeof(int4) * std::max<size_t>(1, tasks.size()), 256);
+  const size_t b_level = align_up(sizeof(int32_t) * level.size(), 256);
+  const size_t b_pos = align_up(sizeof(int2) * pos.size(), 256);
+  const size_t b_status = 256;
+  char* d = nullptr;
+  DGFX_CUDA_TRY(cudaMalloc(&d, b_edges + b_tasks + b_level + b_pos + b_status));
+  s->d_tables = d;
+  s->d_edges = reinterpret_cast<EdgeDev*>(d);
+  s->d_tasks = reinterpret_cast<int4*>(d + b_edges);
+  s->d_level = reinterpret_cast<int32_t*>(d + b_edges + b_tasks);
+  s->d_pos = reinterpret_cast<int2*>(d + b_edges + b_tasks + b_level);
+  s->d_status = reinterpret_cast<unsigned long long*>(d + b_edges + b_tasks + b_level + b_pos);
+  if (!s->h_edges.empty()) {
+    DGFX_CUDA_TRY(cudaMemcpy(s->d_edges, s->h_edges.data(), sizeof(EdgeDev) * s->h_edges.size(), cudaMemcpyHostToDevice));
+  }
+  if (!tasks.empty()) DGFX_CUDA_TRY(cudaMemcpy(s->d_tasks, tasks.data(), sizeof(int4) * tasks.size(), cudaMemcpyHostToDevice));
+  DGFX_CUDA_TRY(cudaMemcpy(s->d_level, level.data(), sizeof(int32_t) * level.size(), cudaMemcpyHostToDevice));
+  DGFX_CUDA_TRY(cudaMemcpy(s->d_pos, pos.data(), sizeof(int2) * pos.size(), cudaMemcpyHostToDevice));
+  const unsigned long long init[3] = {~0ull, 0ull, 0ull};
+  DGFX_CUDA_TRY(cudaMemcpy(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice));
+
+  // Threads per CTA: enough for the bitonic sort's N2/2 pairs, 32..256.
+  s->threads = std::min(256, std::max(32, s->N2 / 2));
+  if (s->use_smem) {
+    const size_t smem = work_bytes(s->T, s->H);
+    if (smem > 48 * 1024) {
+      DGFX_CUDA_TRY(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+    }
+  }
+  *out = s.release();
+  return DGFX_OK;
+}
+
+extern "C" void dgfx_sampler_destroy(dgfx_sampler* s) {
+  if (s == nullptr) return;
+  if (s->d_tables != nullptr) cudaFree(s->d_tables);
+  delete s;
+}
+
+extern "C" int dgfx_sampler_tree_size(const dgfx_sampler* s, int64_t* positions) {
+  if (s == nullptr || positions == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_tree_size: null");
+  *positions = s->T;
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_sampler_workspace_size(const dgfx_sampler* s, int64_t num_seeds, size_t* bytes) {
+  if (s == nullptr || bytes == nullptr || num_seeds < 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_workspace_size: bad arguments");
+  }
+  *bytes = sample_ws_bytes(s, num_seeds);
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_sampler_output_capacity(const dgfx_sampler* s, int64_t num_seeds, int64_t* max_nodes,
+                                            int64_t* max_edges) {
+  if (s == nullptr || max_nodes == nullptr || max_edges == nullptr || num_seeds < 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_output_capacity: bad arguments");
+  }
+  *max_nodes = num_seeds * s->T;
+  *max_edges = num_seeds * std::max(0, s->T - 1);
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_ts,
+                                   const int64_t* d_masked_edges, int64_t B, uint64_t call_index,
+                                   const dgfx_sample_out* out, void* d_workspace, size_t workspace_bytes,
+                                   dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (s == nullptr || out == nullptr || B < 0) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_sample: bad arguments");
+  if (B > 0 && d_seeds == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_sample: null seeds");
+  if (B >= (int64_t(1) << 31)) return fail(DGFX_ERR_UNSUPPORTED, "dgfx_sampler_sample: more than 2^31 - 1 seeds");
+  if (d_masked_edges != nullptr && s->mask_edgeset < 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "masked_edge_idxs provided but no edgeset to mask configured.");
+  }
+  if (d_workspace == nullptr || workspace_bytes < sample_ws_bytes(s, B)) {
+    return fail(DGFX_ERR_WORKSPACE, "dgfx_sampler_sample: workspace too small");
+  }
+  const unsigned long long init[3] = {~0ull, 0ull, 0ull};
+  DGFX_CUDA_TRY(cudaMemcpyAsync(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice, stream));
+  s->last_B = B;
+  s->last_seeds = d_seeds;
+  Arena arena(d_workspace, workspace_bytes);
+  SampleBufs b;
+  carve_sample(arena, s, B, &b);
+  if (B == 0) {
+    DGFX_CUDA_TRY(cudaMemsetAsync(out->node_offsets, 0, sizeof(int64_t), stream));
+    DGFX_CUDA_TRY(cudaMemsetAsync(out->edge_offsets, 0, sizeof(int64_t), stream));
+    return DGFX_OK;
+  }
+  Params p{};
+  p.edges = s->d_edges;
+  p.tasks = s->d_tasks;
+  p.level = s->d_level;
+  p.depth = s->depth;
+  p.pos_info = s->d_pos;
+  p.T = s->T;
+  p.N2 = s->N2;
+  p.H = s->H;
+  p.log2H = s->log2H;
+  p.num_nodesets = s->num_nodesets;
+  p.num_edgesets = s->num_edgesets;
+  p.root_has_children = s->root_has_children;
+  p.root_num_src = s->root_num_src;
+  p.with_replacement = s->with_replacement;
+  p.mode = s->mode;
+  p.mask_edgeset = s->mask_edgeset;
+  p.seeds = d_seeds;
+  p.seed_ts = d_seed_ts;
+  p.masks = d_masked_edges;
+  p.B = B;
+  p.key0 = static_cast<uint32_t>(s->seed);
+  p.key1 = static_cast<uint32_t>(s->seed >> 32);
+  p.call_lo = static_cast<uint32_t>(call_index);
+  p.call_hi = static_cast<uint32_t>(call_index >> 32);
+  p.scratch_nodes = b.scratch_nodes;
+  p.scratch_edges = b.scratch_edges;
+  p.node_cnt = b.node_cnt;
+  p.edge_cnt = b.edge_cnt;
+  p.global_work = b.global_work;
+  p.work_stride = work_bytes(s->T, s->H);
+  p.status = s->d_status;
+  const size_t smem = s->use_smem ? work_bytes(s->T, s->H) : 0;
+  sample_kernel<<<static_cast<unsigned>(B), s->threads, smem, stream>>>(p);
+  DGFX_CUDA_TRY(cudaGetLastError());
+  const size_t mark = arena.used;
+  DGFX_TRY(exclusive_scan<int32_t>(b.node_cnt, out->node_offsets, B * s->num_nodesets, true, arena, stream));
+  arena.used = mark;
+  DGFX_TRY(exclusive_scan<int32_t>(b.edge_cnt, out->edge_offsets, B * s->num_edgesets, true, arena, stream));
+  const int64_t threads = 256;
+  const int64_t blocks = ceil_div(B * 32, threads);
+  compact_kernel<<<static_cast<unsigned>(blocks), static_cast<unsigned>(threads), 0, stream>>>(
+      p, out->node_offsets, out->edge_offsets, s->root_ns, out->node_ids, out->edge_src, out->edge_dst);
+  DGFX_CUDA_TRY(cudaGetLastError());
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_sampler_check(dgfx_sampler* s, dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (s == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_check: null sampler");
+  unsigned long long st[3];
+  DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
+  DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
+  if (st[0] != ~0ull) {
+    int64_t seed = 0;
+    DGFX_CUDA_TRY(cudaMemcpy(&seed, s->last_seeds + st[0], sizeof(seed), cudaMemcpyDeviceToHost));
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "The source node idx " + std::to_string(static_cast<uint64_t>(seed)) +
+                                               " is out of bounds. Should be lower than " +
+                                               std::to_string(s->root_num_src));
+  }
+  if (st[1] != 0) {
+    return fail(DGFX_ERR_FAILED_PRECONDITION,
+                "Cannot use SampleRandomUniform when timestamps are available. Use "
+                "SampleRandomUniformWithTimestamp instead.");
+  }
+  if (st[2] != 0) return fail(DGFX_ERR_INTERNAL, "sampler: dedup table overflow");
+  return DGFX_OK;
+}

@@ -1,0 +1,506 @@
+"""Device implementation of DGF's native sampler module.
+
+Mirrors the surface of the reference's nanobind module
+``_in_memory_sampler_ext`` (dgf/src/sampling/in_memory_sampler_ext.cc:
+1248-1276): ``CreateSampler``, ``Sampler.Sample`` / ``EdgesetNameToEdgesetIdx``
+/ ``__str__`` and ``BuildAdjacencyIndex`` / ``AdjacencyIndex.__str__``, with
+the same argument meaning and error messages. Adjacency indices live in HBM
+(built by ``dgfx_csr_build``) and sampling runs in ``dgfx_sampler_sample``;
+this module only marshals arrays and plans through the C ABI. Nothing here
+computes on the host.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+
+from distributed_graph_flow_b200 import _native
+from distributed_graph_flow_b200.data import in_memory_graph as img
+from distributed_graph_flow_b200.data import schema as schema_lib
+
+
+def _torch():
+    return _native.require_cuda()
+
+
+def _cropped(values) -> str:
+    vals = [int(v) for v in values[:10]]
+    s = ", ".join(str(v) for v in vals)
+    return s + (", ..." if len(values) > 10 else "")
+
+
+class AdjacencyIndex:
+    """CSR of one direction of one edge set, resident in HBM.
+
+    rowptr int64[num_src + 1], col int32[E], optional ts int64[E] and
+    edge_pos int64[E] (CSR position of each original edge; set when the edge
+    set is masked). Same content as the reference's AdjacencyIndex
+    (dgf/src/sampling/in_memory_sampler.h:60-163).
+    """
+
+    def __init__(self, rowptr, col, ts, edge_pos, num_src: int, num_dst: int):
+        self.rowptr = rowptr
+        self.col = col
+        self.ts = ts
+        self.edge_pos = edge_pos
+        self.num_src = int(num_src)
+        self.num_dst = int(num_dst)
+        self.num_edges = int(col.numel())
+
+    def view(self) -> _native.CsrView:
+        return _native.CsrView(
+            _native.ptr(self.rowptr),
+            _native.ptr(self.col),
+            _native.ptr(self.ts),
+            _native.ptr(self.edge_pos),
+            self.num_src,
+            self.num_dst,
+            self.num_edges,
+        )
+
+    def __str__(self) -> str:
+        # AdjacencyIndex::to_string (in_memory_sampler.h:117-132): sizes and
+        # at most the first ten entries.
+        blocks = self.rowptr[:11].cpu().numpy()
+        targets = self.col[:11].cpu().numpy()
+        return (
+            f"AdjacencyIndex(source_blocks=({self.num_src + 1})[{_cropped(blocks)}],"
+            f" target_node_idxs=({self.num_edges})[{_cropped(targets)}])"
+        )
+
+
+def build_adjacency_index_device(
+    src, dst, ts, num_source_nodes: int, num_target_nodes: int, reversed: bool, populate_edge_idxs: bool, stream=None
+) -> AdjacencyIndex:
+    """Builds an index from device int64 edge arrays (no host round trip)."""
+    torch = _torch()
+    lib = _native.lib()
+    n = int(src.numel())
+    num_src, num_dst = (num_target_nodes, num_source_nodes) if reversed else (num_source_nodes, num_target_nodes)
+    dev = src.device
+    rowptr = torch.empty(num_src + 1, dtype=torch.int64, device=dev)
+    col = torch.empty(max(n, 1), dtype=torch.int32, device=dev)[:n]
+    ts_out = torch.empty(max(n, 1), dtype=torch.int64, device=dev)[:n] if ts is not None else None
+    edge_pos = torch.empty(max(n, 1), dtype=torch.int64, device=dev)[:n] if populate_edge_idxs else None
+    need = ctypes.c_size_t()
+    _native.check(lib.dgfx_csr_build_workspace_size(n, num_source_nodes, num_target_nodes, int(ts is not None), ctypes.byref(need)))
+    ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
+    _native.check(
+        lib.dgfx_csr_build(
+            _native.ptr(src), _native.ptr(dst), _native.ptr(ts), n, num_source_nodes, num_target_nodes, int(bool(reversed)),
+            _native.ptr(rowptr), _native.ptr(col), _native.ptr(ts_out), _native.ptr(edge_pos),
+            _native.ptr(ws), need.value, _native.stream_handle(stream),
+        )
+    )
+    return AdjacencyIndex(rowptr, col, ts_out, edge_pos, num_src, num_dst)
+
+
+def BuildAdjacencyIndex(
+    py_adjacency,
+    py_timestamps=None,
+    reversed: bool = False,
+    num_source_nodes: int = 0,
+    num_target_nodes: int = 0,
+    populate_edge_idxs: bool = False,
+) -> AdjacencyIndex:
+    """Same contract as the reference's BuildAdjacencyIndex (ext.cc:1020-1093)."""
+    torch = _torch()
+    adj = np.asarray(py_adjacency)
+    if adj.ndim != 2 or adj.shape[0] != 2:
+        raise ValueError("adjacency must have shape [2, num_edges]")
+    adj = np.ascontiguousarray(adj.astype(np.int64, copy=False))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    src = torch.from_numpy(adj[0].copy()).to(dev, non_blocking=False)
+    dst = torch.from_numpy(adj[1].copy()).to(dev, non_blocking=False)
+    ts = None
+    if py_timestamps is not None:
+        if populate_edge_idxs:
+            raise ValueError("Check failed !populate_edge_idxs")
+        ts = torch.from_numpy(np.ascontiguousarray(np.asarray(py_timestamps, dtype=np.int64))).to(dev)
+    return build_adjacency_index_device(src, dst, ts, int(num_source_nodes), int(num_target_nodes), reversed, populate_edge_idxs)
+
+
+class _PlanArrays:
+    """A SamplingPlan flattened for dgfx_sampler_create (node 0 = root)."""
+
+    def __init__(self, plan, nodeset_index: Dict[str, int], edgeset_index: Dict[str, int]):
+        self.node_nodeset: List[int] = []
+        self.node_first_edge: List[int] = []
+        self.node_num_edges: List[int] = []
+        self.edge_edgeset: List[int] = []
+        self.edge_reversed: List[int] = []
+        self.edge_hop_width: List[int] = []
+        self.edge_child: List[int] = []
+        self.nodes = []  # python PlanNode per flattened node
+        queue = [plan.root]
+        self._add_node(plan.root, nodeset_index)
+        head = 0
+        while head < len(queue):
+            pn = queue[head]
+            i = head
+            head += 1
+            self.node_first_edge[i] = len(self.edge_edgeset)
+            self.node_num_edges[i] = len(pn.children)
+            for child in pn.children:
+                if child.edgeset not in edgeset_index:
+                    raise ValueError(f"Key not found in map: {child.edgeset}")
+                self.edge_edgeset.append(edgeset_index[child.edgeset])
+                self.edge_reversed.append(int(bool(child.reversed)))
+                self.edge_hop_width.append(int(child.hop_width))
+                self.edge_child.append(len(self.nodes))
+                self._add_node(child.node, nodeset_index)
+                queue.append(child.node)
+
+    def _add_node(self, pn, nodeset_index):
+        if pn.nodeset not in nodeset_index:
+            raise ValueError(f"Key not found in map: {pn.nodeset}")
+        self.nodes.append(pn)
+        self.node_nodeset.append(nodeset_index[pn.nodeset])
+        self.node_first_edge.append(0)
+        self.node_num_edges.append(0)
+
+    @staticmethod
+    def arr32(v: List[int]):
+        return (ctypes.c_int32 * max(1, len(v)))(*v)
+
+
+def _plan_to_string(plan, nodeset_index, edgeset_index) -> str:
+    """SamplingPlan::to_string (dgf/src/sampling/in_memory_sampler.h:184-238)."""
+
+    def node_str(pn, indent: int) -> str:
+        prefix = " " * (2 * indent)
+        if not pn.children:
+            kids = "[]"
+        else:
+            kids = "[\n" + ",\n".join(edge_str(c, indent + 1) for c in pn.children) + "\n" + prefix + "]"
+        return f"{prefix}Node(nodeset_idx={nodeset_index[pn.nodeset]}, children={kids})"
+
+    def edge_str(pe, indent: int) -> str:
+        prefix = " " * (2 * indent)
+        return (
+            f"{prefix}Edge(edgeset_idx={edgeset_index[pe.edgeset]}, reversed={int(bool(pe.reversed))},"
+            f" hop_width={pe.hop_width}, node=\n{node_str(pe.node, indent + 1)})"
+        )
+
+    return f"SamplingPlan(root=\n{node_str(plan.root, 0)},\n  with_replacement={int(bool(plan.with_replacement))}\n)"
+
+
+class MergedBatch:
+    """Device-resident sampler output for one call (see dgfx_sample_out).
+
+    node_ids[node_offsets[s*B + i]:node_offsets[s*B + i + 1]] are the
+    ``#idx`` of node set s in sample i; edge_src / edge_dst likewise per edge
+    set e (local ids). Offsets carry one trailing total.
+    """
+
+    def __init__(self, B, nodeset_names, edgeset_names, node_ids, node_offsets, edge_src, edge_dst, edge_offsets):
+        self.B = B
+        self.nodeset_names = nodeset_names
+        self.edgeset_names = edgeset_names
+        self.node_ids = node_ids
+        self.node_offsets = node_offsets
+        self.edge_src = edge_src
+        self.edge_dst = edge_dst
+        self.edge_offsets = edge_offsets
+
+    def nodeset_range(self, s: int, offsets_host: np.ndarray) -> Tuple[int, int]:
+        return int(offsets_host[s * self.B]), int(offsets_host[(s + 1) * self.B])
+
+
+class Sampler:
+    """Device sampler created by CreateSampler."""
+
+    def __init__(self):
+        self._handle = None
+        self._buffers = {}
+        self._calls = 0
+
+    def __del__(self):
+        h = getattr(self, "_handle", None)
+        if h:
+            try:
+                _native.lib().dgfx_sampler_destroy(h)
+            except Exception:  # interpreter shutdown
+                pass
+            self._handle = None
+
+    # -- introspection ---------------------------------------------------
+    def __str__(self) -> str:
+        ns = ", ".join(f"{n}: {i}" for n, i in sorted(self._nodeset_index.items()))
+        es = ", ".join(f"{n}: {i}" for n, i in sorted(self._edgeset_index.items()))
+        nodesets = ", ".join(f"{{idx={i}, num_nodes={n}}}" for i, n in enumerate(self._num_nodes))
+        return (
+            f"Sampler(\n  plan={_plan_to_string(self._plan, self._nodeset_index, self._edgeset_index)},\n"
+            f"  nodeset_index={{{ns}}},\n  edgeset_index={{{es}}},\n  nodesets=[{nodesets}]\n)"
+        )
+
+    def EdgesetNameToEdgesetIdx(self, name: str) -> int:
+        if name not in self._edgeset_index:
+            raise ValueError(f"Key not found in map: {name}")
+        return self._edgeset_index[name]
+
+    @property
+    def tree_size(self) -> int:
+        v = ctypes.c_int64()
+        _native.check(_native.lib().dgfx_sampler_tree_size(self._handle, ctypes.byref(v)))
+        return v.value
+
+    # -- sampling --------------------------------------------------------
+    def _workspace(self, nbytes: int):
+        """Scratch reused across calls (calls on one sampler are serialised
+        on the stream they are issued on)."""
+        torch = _torch()
+        buf = self._buffers.get("ws")
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(1, nbytes), dtype=torch.uint8, device=self._device)
+            self._buffers["ws"] = buf
+        return buf
+
+    def _validate_args(self, B, seed_ts, masks):
+        if seed_ts is not None:
+            if not self._has_temporal:
+                raise ValueError(
+                    "seed_timestamps provided but no temporal edgesets configured. Set "
+                    "the 'edgeset_timestamp_features' field in the sampling plan."
+                )
+            if int(seed_ts.numel()) != B:
+                raise ValueError("seed_node_idxs and seed_timestamps must have the same size")
+        if masks is not None:
+            if self._mask_edgeset < 0:
+                raise ValueError("masked_edge_idxs provided but no edgeset to mask configured.")
+            if int(masks.numel()) != B:
+                raise ValueError("seed_node_idxs and masked_edge_idxs must have the same size")
+
+    def sample_merged(self, seeds, seed_ts=None, masks=None, stream=None, call_index: Optional[int] = None,
+                      check: bool = True) -> MergedBatch:
+        """Samples one subgraph per seed into a device-resident merged batch.
+
+        seeds / seed_ts / masks are int64 device tensors. With check=False the
+        call stays asynchronous (errors are latched; call ``check()``).
+        """
+        torch = _torch()
+        lib = _native.lib()
+        B = int(seeds.numel())
+        self._validate_args(B, seed_ts, masks)
+        max_nodes = ctypes.c_int64()
+        max_edges = ctypes.c_int64()
+        _native.check(lib.dgfx_sampler_output_capacity(self._handle, B, ctypes.byref(max_nodes), ctypes.byref(max_edges)))
+        need = ctypes.c_size_t()
+        _native.check(lib.dgfx_sampler_workspace_size(self._handle, B, ctypes.byref(need)))
+        NS, ES = len(self._nodeset_names), len(self._edgeset_names)
+        dev = self._device
+        node_ids = torch.empty(max(1, max_nodes.value), dtype=torch.int64, device=dev)
+        node_off = torch.empty(NS * B + 1, dtype=torch.int64, device=dev)
+        edge_src = torch.empty(max(1, max_edges.value), dtype=torch.int64, device=dev)
+        edge_dst = torch.empty(max(1, max_edges.value), dtype=torch.int64, device=dev)
+        edge_off = torch.empty(ES * B + 1, dtype=torch.int64, device=dev)
+        ws = self._workspace(need.value)
+        out = _native.SampleOut(
+            _native.ptr(node_ids), _native.ptr(node_off), _native.ptr(edge_src), _native.ptr(edge_dst), _native.ptr(edge_off)
+        )
+        if call_index is None:
+            call_index = self._calls
+            self._calls += 1
+        sh = _native.stream_handle(stream)
+        _native.check(
+            lib.dgfx_sampler_sample(
+                self._handle, _native.ptr(seeds), _native.ptr(seed_ts), _native.ptr(masks), B, int(call_index),
+                ctypes.byref(out), _native.ptr(ws), need.value, sh,
+            )
+        )
+        if check:
+            self.check(stream)
+        return MergedBatch(B, self._nodeset_names, self._edgeset_names, node_ids, node_off, edge_src, edge_dst,
+                           edge_off)
+
+    def check(self, stream=None) -> None:
+        _native.check(_native.lib().dgfx_sampler_check(self._handle, _native.stream_handle(stream)))
+
+    def _to_device(self, arr, name):
+        torch = _torch()
+        if arr is None:
+            return None
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.int64))
+        return torch.from_numpy(a).to(self._device, non_blocking=False)
+
+    def Sample(self, seed_node_idx, seed_timestamps=None, masked_edge_idxs=None) -> list:
+        """Reference-compatible: a list of InMemoryGraph holding only "#idx"."""
+        seeds = self._to_device(seed_node_idx, "seeds")
+        ts = self._to_device(seed_timestamps, "ts")
+        masks = self._to_device(masked_edge_idxs, "masks")
+        batch = self.sample_merged(seeds, ts, masks)
+        return export_graphs(batch)
+
+    def SubGraph(self, seed_node_idx):
+        raise NotImplementedError("SubGraph extraction is not implemented on the B200 sampler yet")
+
+    def MultiSubGraphs(self, seed_node_idx):
+        raise NotImplementedError("MultiSubGraphs extraction is not implemented on the B200 sampler yet")
+
+    def RandomWalkNegativeSampling(self, seed_node_idxs, target_edgeset_idx, num_walks, num_negatives_per_seed):
+        raise NotImplementedError("RandomWalkNegativeSampling is not implemented on the B200 sampler yet")
+
+
+def batch_to_host(batch: MergedBatch):
+    """Copies a merged batch's exact-size arrays to host numpy arrays."""
+    node_off = batch.node_offsets.cpu().numpy()
+    edge_off = batch.edge_offsets.cpu().numpy()
+    n_nodes = int(node_off[-1])
+    n_edges = int(edge_off[-1])
+    node_ids = batch.node_ids[:n_nodes].cpu().numpy()
+    edges = np.empty((2, n_edges), dtype=np.int64)
+    if n_edges:
+        edges[0] = batch.edge_src[:n_edges].cpu().numpy()
+        edges[1] = batch.edge_dst[:n_edges].cpu().numpy()
+    return node_ids, node_off, edges, edge_off
+
+
+def export_graphs(batch: MergedBatch, host=None) -> List[img.InMemoryGraph]:
+    """One InMemoryGraph per seed with "#idx" and [2, E] adjacency
+    (ExportToInMemoryGraph, in_memory_sampler_ext.cc:372-397): every node set
+    and edge set is present, in index (sorted-name) order."""
+    node_ids, node_off, edges, edge_off = host if host is not None else batch_to_host(batch)
+    B = batch.B
+    graphs = []
+    for i in range(B):
+        nodesets = {}
+        for s, name in enumerate(batch.nodeset_names):
+            a, b = int(node_off[s * B + i]), int(node_off[s * B + i + 1])
+            nodesets[name] = img.InMemoryNodeSet(num_nodes=b - a, features={"#idx": node_ids[a:b]})
+        edgesets = {}
+        for e, name in enumerate(batch.edgeset_names):
+            a, b = int(edge_off[e * B + i]), int(edge_off[e * B + i + 1])
+            edgesets[name] = img.InMemoryEdgeSet(adjacency=edges[:, a:b])
+        graphs.append(img.InMemoryGraph(node_sets=nodesets, edge_sets=edgesets))
+    return graphs
+
+
+def CreateSampler(
+    graph: img.InMemoryGraph,
+    plan,
+    debug_sampling: bool,
+    num_threads: int,
+    seed: int,
+    py_schema: schema_lib.GraphSchema,
+    edgeset_to_mask: Optional[str] = None,
+    edgeset_timestamp_features: Optional[Dict[str, str]] = None,
+    sampling_mode: Optional[int] = None,
+    device=None,
+) -> Sampler:
+    """Same contract as the reference's CreateSampler (ext.cc:1216-1246).
+
+    num_threads is accepted for compatibility; the GPU grid replaces the
+    reference's thread pool. sampling_mode (an extension) overrides the mode
+    chosen by debug_sampling, e.g. MODE_MOST_RECENT.
+    """
+    torch = _torch()
+    edgeset_timestamp_features = dict(edgeset_timestamp_features or {})
+    nodeset_index = py_schema.nodeset_index()
+    edgeset_index = py_schema.edgeset_index()
+    nodeset_names = sorted(py_schema.node_sets)
+    edgeset_names = sorted(py_schema.edge_sets)
+    plan_arrays = _PlanArrays(plan, nodeset_index, edgeset_index)
+
+    mask_idx = -1
+    if edgeset_to_mask is not None:
+        if edgeset_to_mask not in edgeset_index:
+            raise ValueError(f"Edgeset '{edgeset_to_mask}' does not exist in schema")
+        mask_idx = edgeset_index[edgeset_to_mask]
+    for name in edgeset_timestamp_features:
+        if name not in edgeset_index:
+            raise ValueError(f"Edgeset '{name}' does not exist in schema")
+
+    num_nodes = []
+    for name in nodeset_names:
+        if name not in graph.node_sets:
+            raise ValueError(f"Key not found in dict: {name}")
+        n = graph.node_sets[name].num_nodes
+        if n is None:
+            raise ValueError(f"num_nodes of nodeset '{name}' is not set")
+        num_nodes.append(int(n))
+
+    # Which directions of which edge sets the plan walks, with endpoint
+    # consistency checks (Sampler::IndexEdgeSets, ext.cc:1124-1163).
+    src_ns = [-1] * len(edgeset_names)
+    dst_ns = [-1] * len(edgeset_names)
+    need_fwd = [False] * len(edgeset_names)
+    need_bwd = [False] * len(edgeset_names)
+    for i, _ in enumerate(plan_arrays.nodes):
+        for c in range(plan_arrays.node_num_edges[i]):
+            j = plan_arrays.node_first_edge[i] + c
+            e = plan_arrays.edge_edgeset[j]
+            here = plan_arrays.node_nodeset[i]
+            there = plan_arrays.node_nodeset[plan_arrays.edge_child[j]]
+            s, t = (there, here) if plan_arrays.edge_reversed[j] else (here, there)
+            if not (src_ns[e] in (-1, s)):
+                raise ValueError("Check failed edgeset.source_nodeset == -1 || edgeset.source_nodeset == node.nodeset_idx")
+            if not (dst_ns[e] in (-1, t)):
+                raise ValueError("Check failed edgeset.target_nodeset == -1 || edgeset.target_nodeset == child.node->nodeset_idx")
+            src_ns[e], dst_ns[e] = s, t
+            if plan_arrays.edge_reversed[j]:
+                need_bwd[e] = True
+            else:
+                need_fwd[e] = True
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    fwd: List[Optional[AdjacencyIndex]] = [None] * len(edgeset_names)
+    bwd: List[Optional[AdjacencyIndex]] = [None] * len(edgeset_names)
+    with torch.cuda.device(dev):
+        for e, name in enumerate(edgeset_names):
+            if not (need_fwd[e] or need_bwd[e]):
+                continue
+            if name not in graph.edge_sets:
+                raise ValueError(f"Key not found in dict: {name}")
+            es = graph.edge_sets[name]
+            ts = None
+            if name in edgeset_timestamp_features:
+                feat = edgeset_timestamp_features[name]
+                if feat not in es.features:
+                    raise ValueError(f"Key not found in dict: {feat}")
+                ts = es.features[feat]
+            ns_src, ns_dst = num_nodes[src_ns[e]], num_nodes[dst_ns[e]]
+            if need_fwd[e]:
+                fwd[e] = BuildAdjacencyIndex(es.adjacency, ts, False, ns_src, ns_dst, e == mask_idx)
+            if need_bwd[e]:
+                bwd[e] = BuildAdjacencyIndex(es.adjacency, ts, True, ns_src, ns_dst, e == mask_idx)
+
+        mode = _native.MODE_FIRST if debug_sampling else _native.MODE_RANDOM
+        if sampling_mode is not None:
+            mode = int(sampling_mode)
+        if seed is None or seed < 0:
+            seed = int.from_bytes(os.urandom(8), "little") >> 1
+        empty = _native.CsrView()
+        fwd_views = (_native.CsrView * max(1, len(edgeset_names)))(*[x.view() if x else empty for x in fwd])
+        bwd_views = (_native.CsrView * max(1, len(edgeset_names)))(*[x.view() if x else empty for x in bwd])
+        pa = plan_arrays
+        handle = ctypes.c_void_p()
+        _native.check(
+            _native.lib().dgfx_sampler_create(
+                len(pa.node_nodeset), pa.arr32(pa.node_nodeset), pa.arr32(pa.node_first_edge), pa.arr32(pa.node_num_edges),
+                len(pa.edge_edgeset), pa.arr32(pa.edge_edgeset), pa.arr32(pa.edge_reversed), pa.arr32(pa.edge_hop_width),
+                pa.arr32(pa.edge_child), int(bool(plan.with_replacement)), len(nodeset_names),
+                (ctypes.c_int64 * len(num_nodes))(*num_nodes), len(edgeset_names), fwd_views, bwd_views, mode, mask_idx,
+                int(seed) & ((1 << 64) - 1), ctypes.byref(handle),
+            )
+        )
+    s = Sampler()
+    s._handle = handle.value
+    s._device = dev
+    s._plan = plan
+    s._nodeset_index = nodeset_index
+    s._edgeset_index = edgeset_index
+    s._nodeset_names = nodeset_names
+    s._edgeset_names = edgeset_names
+    s._num_nodes = num_nodes
+    s._fwd = fwd
+    s._bwd = bwd
+    s._mask_edgeset = mask_idx
+    s._has_temporal = bool(edgeset_timestamp_features)
+    s._mode = mode
+    s._seed = seed
+    s._root_nodeset = plan.root.nodeset
+    return s

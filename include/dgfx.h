@@ -1,0 +1,229 @@
+/*
+ * dgfx.h — C ABI of the B200 (sm_100a) implementation of DGF's in-memory
+ * k-hop temporal neighbour sampler and of the sparse neighbour aggregation
+ * that feeds its GNN layers.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only. Pointers named d_* are device pointers
+ *     on the current CUDA device; everything else is host memory.
+ *   - Every entry point returns a dgfx status (0 = DGFX_OK). On failure,
+ *     dgfx_last_error() returns the message (per host thread). Status codes
+ *     reuse absl's numbering so a binding can map INVALID_ARGUMENT and
+ *     FAILED_PRECONDITION to Python ValueError exactly like the reference's
+ *     status caster (dgf/src/util/status_caster.h:17-21, 83-88).
+ *   - Work is enqueued on the caller's stream. Temporaries live in a
+ *     caller-provided workspace whose size the matching *_workspace_size
+ *     query returns; the library allocates no per-call device memory.
+ *   - No entry point falls back to a CPU implementation.
+ */
+#ifndef DGFX_H_
+#define DGFX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef struct CUstream_st* dgfx_stream; /* == cudaStream_t */
+
+enum {
+  DGFX_OK = 0,
+  DGFX_ERR_INVALID_ARGUMENT = 3,
+  DGFX_ERR_NOT_FOUND = 5,
+  DGFX_ERR_FAILED_PRECONDITION = 9,
+  DGFX_ERR_INTERNAL = 13,
+  DGFX_ERR_CUDA = 100,
+  DGFX_ERR_WORKSPACE = 101,
+  DGFX_ERR_UNSUPPORTED = 102
+};
+
+enum { DGFX_F32 = 0, DGFX_BF16 = 1 };
+
+/* Sampling modes. RANDOM and FIRST are the reference's two modes
+ * (create_sampler(debug_sampling=False/True), in_memory_sampler.py:349-363,
+ * applied in SampleBuilder::RecursiveGrow, in_memory_sampler_ext.cc:250-279).
+ * MOST_RECENT has no reference counterpart: the newest k edges whose
+ * timestamp is <= the seed timestamp; non-temporal edgesets sample as RANDOM. */
+enum { DGFX_MODE_RANDOM = 0, DGFX_MODE_FIRST = 1, DGFX_MODE_MOST_RECENT = 2 };
+
+/* Message of the last failure on this host thread ("" if none). */
+const char* dgfx_last_error(void);
+/* Library ABI version (major * 100 + minor). */
+int dgfx_version(void);
+
+/* ------------------------------------------------------------------------
+ * Adjacency index (CSR of one direction of one edgeset).
+ * Replaces AdjacencyIndex::CreateFromEdgeList (in_memory_sampler.cc:220-257)
+ * behind BuildAdjacencyIndex (in_memory_sampler_ext.cc:1020-1093): ids are
+ * validated (first invalid edge reported with the reference's message), the
+ * edges are sorted by (source, timestamp, target) with duplicates kept, and
+ * the row pointers are filled. Layout: rowptr int64[num_src + 1], col
+ * int32[E], ts int64[E] (temporal only), edge_pos int64[E] where
+ * edge_pos[e] = CSR position of original edge e (only when masking is
+ * configured; the inverse of the reference's parallel edge_idxs array).
+ * num_src / num_dst are the edgeset's source / target node counts *before*
+ * the reversal, as in the reference. Synchronises `stream` once to report
+ * invalid ids.
+ * ------------------------------------------------------------------------ */
+int dgfx_csr_build_workspace_size(int64_t num_edges, int64_t num_src,
+                                  int64_t num_dst, int has_ts, size_t* bytes);
+int dgfx_csr_build(const int64_t* d_src, const int64_t* d_dst,
+                   const int64_t* d_ts, int64_t num_edges, int64_t num_src,
+                   int64_t num_dst, int reversed, int64_t* d_rowptr,
+                   int32_t* d_col, int64_t* d_ts_out, int64_t* d_edge_pos,
+                   void* d_workspace, size_t workspace_bytes,
+                   dgfx_stream stream);
+
+/* Device view of one built index. rowptr == NULL marks "not built". */
+typedef struct dgfx_csr_view {
+  const int64_t* rowptr;
+  const int32_t* col;
+  const int64_t* ts;       /* NULL: non-temporal edgeset */
+  const int64_t* edge_pos; /* NULL: no masking on this edgeset */
+  int64_t num_src;
+  int64_t num_dst;
+  int64_t num_edges;
+} dgfx_csr_view;
+
+/* ------------------------------------------------------------------------
+ * Sampler. Replaces the native Sampler of _in_memory_sampler_ext
+ * (CreateSampler in_memory_sampler_ext.cc:1216-1246; Sampler::Sample
+ * :418-533 with SampleBuilder::Grow/RecursiveGrow :231-370).
+ *
+ * Plan: node i (node 0 = root) has nodeset node_nodeset[i] and plan edges
+ * [node_first_edge[i], node_first_edge[i] + node_num_edges[i]); plan edge j
+ * walks edgeset edge_edgeset[j] (edge_reversed[j]: backward index) taking up
+ * to edge_hop_width[j] neighbours into plan node edge_child[j]. Mirrors
+ * SamplingPlan (in_memory_sampler.h:172-239).
+ * forward[e] / backward[e]: the indices of edgeset e (rowptr NULL if the plan
+ * does not walk that direction). Views are borrowed: they must outlive the
+ * sampler. Output per seed matches the reference: nodes relabelled in
+ * first-discovery depth-first order (all occurrences when with_replacement),
+ * edges deduplicated and sorted by (src_local, dst_local) per edgeset.
+ * ------------------------------------------------------------------------ */
+typedef struct dgfx_sampler dgfx_sampler;
+
+int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_nodeset,
+                        const int32_t* node_first_edge,
+                        const int32_t* node_num_edges, int32_t num_plan_edges,
+                        const int32_t* edge_edgeset,
+                        const int32_t* edge_reversed,
+                        const int32_t* edge_hop_width,
+                        const int32_t* edge_child, int32_t with_replacement,
+                        int32_t num_nodesets, const int64_t* num_nodes,
+                        int32_t num_edgesets, const dgfx_csr_view* forward,
+                        const dgfx_csr_view* backward, int32_t mode,
+                        int32_t edgeset_to_mask, uint64_t seed,
+                        dgfx_sampler** out);
+void dgfx_sampler_destroy(dgfx_sampler* sampler);
+
+/* Positions of the padded per-seed expansion tree (an upper bound on the
+ * nodes of one sample). */
+int dgfx_sampler_tree_size(const dgfx_sampler* sampler, int64_t* positions);
+int dgfx_sampler_workspace_size(const dgfx_sampler* sampler, int64_t num_seeds,
+                                size_t* bytes);
+int dgfx_sampler_output_capacity(const dgfx_sampler* sampler,
+                                 int64_t num_seeds, int64_t* max_nodes,
+                                 int64_t* max_edges);
+
+/* Merged batch written by dgfx_sampler_sample (all device pointers).
+ *   node_ids[node_offsets[s*B + i] .. node_offsets[s*B + i + 1]) are the
+ *     "#idx" of nodeset s in sample i, in local-id order (nodeset-major, then
+ *     sample); node_offsets has num_nodesets*B + 1 entries.
+ *   edge_src / edge_dst[edge_offsets[e*B + i] .. edge_offsets[e*B + i + 1])
+ *     are the local-id adjacency rows of edgeset e in sample i
+ *     (EdgesToNumpyArray layout, in_memory_sampler_nb.h:31-57).
+ * Capacities come from dgfx_sampler_output_capacity. */
+typedef struct dgfx_sample_out {
+  int64_t* node_ids;
+  int64_t* node_offsets;
+  int64_t* edge_src;
+  int64_t* edge_dst;
+  int64_t* edge_offsets;
+} dgfx_sample_out;
+
+/* Samples one subgraph per seed. d_seed_ts (int64[B]) enables the temporal
+ * cutoff (edge ts <= seed ts); d_masked_edges (int64[B], -1 = none) masks one
+ * edge of the masked edgeset per seed. call_index selects the random stream
+ * (Philox4x32-10 keyed by the sampler seed; counter = (call, seed slot, tree
+ * position, plan edge)). Asynchronous: device-side failures (seed out of
+ * range, timestamps missing for a temporal index) are latched and reported
+ * by dgfx_sampler_check. */
+int dgfx_sampler_sample(dgfx_sampler* sampler, const int64_t* d_seeds,
+                        const int64_t* d_seed_ts, const int64_t* d_masked_edges,
+                        int64_t num_seeds, uint64_t call_index,
+                        const dgfx_sample_out* out, void* d_workspace,
+                        size_t workspace_bytes, dgfx_stream stream);
+
+/* Synchronises `stream` and reports the latched status of the last
+ * dgfx_sampler_sample (reference messages, e.g. "The source node idx 7 is out
+ * of bounds. Should be lower than 4"). */
+int dgfx_sampler_check(dgfx_sampler* sampler, dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Feature gather: out[i, :] = table[row_ids[i], :] for row_bytes-wide rows
+ * (row_bytes a multiple of 16). Replaces add_features_to_samples'
+ * full_feature_value[node_idxs] (in_memory_sampler.py:313-346).
+ * Ids outside [0, num_table_rows) produce zero rows.
+ * ------------------------------------------------------------------------ */
+int dgfx_gather_rows(const void* d_table, int64_t num_table_rows,
+                     int64_t row_bytes, const int64_t* d_row_ids,
+                     int64_t num_rows, void* d_out, dgfx_stream stream);
+
+/* Same, for the rows [d_range[0], d_range[1]) of d_row_ids with the bounds
+ * read on the device (at most max_rows rows; out row i <- d_row_ids[
+ * d_range[0] + i]). Lets a node set of a merged batch be gathered without
+ * a host synchronisation. */
+int dgfx_gather_rows_ranged(const void* d_table, int64_t num_table_rows,
+                            int64_t row_bytes, const int64_t* d_row_ids,
+                            const int64_t* d_range, int64_t max_rows,
+                            void* d_out, dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Aggregation.
+ * dgfx_spmm_csr: Y[r, :] = scale_r * sum_j val[j] * X[col[j], :] over row r
+ * of a CSR matrix (rows = message targets, cols = message sources), the
+ * sparse_deferred `SparseMatrix @ dense` form (homo_gnn_sparse_deferred.py:
+ * 138-161, message_passing.py:24-38). val == NULL means 1. normalize = 1
+ * gives the mean pooling of hetero_gnn.py:283-295: scale_r =
+ * 1 / max(deg_r, 1). X and Y are row-major [*, feat]; fp32 accumulation.
+ * Deterministic (fixed summation order).
+ * ------------------------------------------------------------------------ */
+int dgfx_spmm_workspace_size(int64_t num_rows, int64_t nnz, int64_t feat,
+                             size_t* bytes);
+int dgfx_spmm_csr(const int64_t* d_rowptr, const int32_t* d_col,
+                  const float* d_val, int64_t num_rows, int64_t num_cols,
+                  int64_t nnz, const void* d_x, int x_dtype, void* d_y,
+                  int y_dtype, int64_t feat, int32_t normalize,
+                  void* d_workspace, size_t workspace_bytes,
+                  dgfx_stream stream);
+
+/* jax.ops.segment_sum(data, segment_ids, num_segments) as called at
+ * hetero_gnn.py:283-287; mean = 1 adds the division by max(count, 1) of
+ * hetero_gnn.py:288-295. Ids outside [0, num_segments) are dropped (jax
+ * semantics). indices_are_sorted = 1 selects a deterministic segmented
+ * reduction; otherwise fp32 atomic accumulation is used. */
+int dgfx_segment_sum_workspace_size(int64_t num_items, int64_t feat,
+                                    int64_t num_segments, size_t* bytes);
+int dgfx_segment_sum(const void* d_data, int data_dtype,
+                     const int64_t* d_segment_ids, int64_t num_items,
+                     int64_t feat, int64_t num_segments, int32_t mean,
+                     int32_t indices_are_sorted, void* d_out, int out_dtype,
+                     void* d_workspace, size_t workspace_bytes,
+                     dgfx_stream stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DGFX_H_ */

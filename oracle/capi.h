@@ -1,0 +1,218 @@
+// ORACLE — test infrastructure only (see grow.h).
+//
+// extern "C" surface shared by the two oracle builds:
+//   * liboracle.so  — grow.h over the oracle's restated AdjacencyIndex
+//   * _ref/libdgf_ref.so — grow.h over the reference's own AdjacencyIndex,
+//     compiled from dgf/src/sampling/in_memory_sampler.cc
+// Both export the same symbols so one ctypes wrapper (oracle/oracle.py)
+// drives either. Before including this header the translation unit defines
+//   using OracleIndex = ...;                         // index type
+//   dgf_oracle::Status OracleCreate(...);            // CreateFromEdgeList
+//   std::string OracleIndexString(const OracleIndex&);
+#pragma once
+
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "grow.h"
+
+namespace {
+thread_local std::string g_oracle_error;
+
+struct OracleHandle {
+  dgf_oracle::Sampler<OracleIndex> sampler;
+  std::vector<dgf_oracle::Sample> results;
+};
+
+struct IndexHandle {
+  OracleIndex index;
+};
+
+auto CreateFn() {
+  return [](const std::vector<dgf_oracle::InputIdx>& s,
+            const std::vector<dgf_oracle::InputIdx>& t, const std::int64_t* ts,
+            bool populate_edge_idxs, std::size_t num_src, std::size_t num_dst,
+            OracleIndex* out) -> dgf_oracle::Status {
+    return OracleCreate(s, t, ts, populate_edge_idxs, num_src, num_dst, out);
+  };
+}
+}  // namespace
+
+extern "C" {
+
+const char* oracle_last_error() { return g_oracle_error.c_str(); }
+
+// Plan: node i has nodeset node_nodeset[i] and plan edges
+// [node_first_edge[i], node_first_edge[i] + node_num_edges[i]). Graph:
+// edgeset e has num_edges[e] edges (src[e][i], dst[e][i]) and optional ts[e].
+// Returns nullptr on error (message in oracle_last_error()).
+void* oracle_sampler_create(int n_nodesets, const std::int64_t* num_nodes,
+                            int n_edgesets, const std::int64_t* const* src,
+                            const std::int64_t* const* dst,
+                            const std::int64_t* const* ts,
+                            const std::int64_t* num_edges, int n_plan_nodes,
+                            const int* node_nodeset, const int* node_first_edge,
+                            const int* node_num_edges, int n_plan_edges,
+                            const int* edge_edgeset, const int* edge_reversed,
+                            const int* edge_hop_width, const int* edge_child,
+                            int with_replacement, int mode, int num_threads,
+                            std::int64_t seed, int edgeset_to_mask,
+                            int has_temporal) {
+  auto h = std::make_unique<OracleHandle>();
+  auto& s = h->sampler;
+  s.plan.with_replacement = with_replacement != 0;
+  for (int i = 0; i < n_plan_nodes; ++i) {
+    dgf_oracle::PlanNode n;
+    n.nodeset = node_nodeset[i];
+    for (int j = 0; j < node_num_edges[i]; ++j) n.edges.push_back(node_first_edge[i] + j);
+    s.plan.nodes.push_back(n);
+  }
+  for (int i = 0; i < n_plan_edges; ++i) {
+    s.plan.edges.push_back({edge_edgeset[i], edge_reversed[i] != 0, edge_hop_width[i], edge_child[i]});
+  }
+  s.num_nodes.assign(num_nodes, num_nodes + n_nodesets);
+  s.mask_edgeset = edgeset_to_mask;
+  s.mode = mode;
+  s.has_temporal = has_temporal != 0;
+  s.num_threads = num_threads;
+  std::vector<dgf_oracle::EdgeList> lists(n_edgesets);
+  for (int e = 0; e < n_edgesets; ++e) {
+    lists[e].src = src[e];
+    lists[e].dst = dst[e];
+    lists[e].ts = ts != nullptr ? ts[e] : nullptr;
+    lists[e].num_edges = static_cast<std::size_t>(num_edges[e]);
+  }
+  dgf_oracle::Status st = s.Init(lists, seed, CreateFn());
+  if (!st.ok()) {
+    g_oracle_error = st.msg;
+    return nullptr;
+  }
+  return h.release();
+}
+
+void oracle_sampler_free(void* h) { delete static_cast<OracleHandle*>(h); }
+
+// Samples n seeds; keeps the results in the handle. Returns 0 on success,
+// else the status code (message in oracle_last_error()).
+int oracle_sample(void* hv, const std::int64_t* seeds, const std::int64_t* ts,
+                  const std::int64_t* masks, std::int64_t n, int threads) {
+  auto* h = static_cast<OracleHandle*>(hv);
+  dgf_oracle::Status st = h->sampler.SampleBatch(seeds, ts, masks, static_cast<std::size_t>(n), threads, &h->results);
+  if (!st.ok()) {
+    g_oracle_error = st.msg;
+    h->results.clear();
+    return st.code;
+  }
+  return 0;
+}
+
+// node_counts[n * n_nodesets], edge_counts[n * n_edgesets] (sample-major).
+void oracle_result_counts(void* hv, std::int64_t* node_counts, std::int64_t* edge_counts) {
+  auto* h = static_cast<OracleHandle*>(hv);
+  std::size_t a = 0, b = 0;
+  for (const auto& s : h->results) {
+    for (const auto& v : s.nodes) node_counts[a++] = static_cast<std::int64_t>(v.size());
+    for (const auto& v : s.edges) edge_counts[b++] = static_cast<std::int64_t>(v.size());
+  }
+}
+
+// Concatenated in (sample, nodeset) / (sample, edgeset) order.
+void oracle_result_copy(void* hv, std::int64_t* nodes, std::int64_t* esrc, std::int64_t* edst) {
+  auto* h = static_cast<OracleHandle*>(hv);
+  for (const auto& s : h->results) {
+    for (const auto& v : s.nodes) {
+      for (auto x : v) *nodes++ = static_cast<std::int64_t>(x);
+    }
+    for (const auto& v : s.edges) {
+      for (const auto& p : v) {
+        *esrc++ = p.first;
+        *edst++ = p.second;
+      }
+    }
+  }
+}
+
+// ---- single index access (CSR parity and per-node known-answer tests) ----
+
+void* oracle_index_build(const std::int64_t* src, const std::int64_t* dst,
+                         const std::int64_t* ts, std::int64_t num_edges,
+                         std::int64_t num_src, std::int64_t num_dst,
+                         int reversed, int populate_edge_idxs) {
+  auto h = std::make_unique<IndexHandle>();
+  dgf_oracle::EdgeList el{src, dst, ts, static_cast<std::size_t>(num_edges)};
+  dgf_oracle::Status st = dgf_oracle::BuildIndex(el, reversed != 0, static_cast<std::size_t>(num_src),
+                                                 static_cast<std::size_t>(num_dst), populate_edge_idxs != 0,
+                                                 &h->index, CreateFn());
+  if (!st.ok()) {
+    g_oracle_error = st.msg;
+    return nullptr;
+  }
+  return h.release();
+}
+
+void oracle_index_free(void* h) { delete static_cast<IndexHandle*>(h); }
+
+// sizes[0] = len(source_blocks), [1] = len(targets), [2] = len(timestamps),
+// [3] = len(edge_idxs).
+void oracle_index_sizes(void* hv, std::int64_t* sizes) {
+  const auto& x = static_cast<IndexHandle*>(hv)->index;
+  sizes[0] = static_cast<std::int64_t>(x.source_blocks.size());
+  sizes[1] = static_cast<std::int64_t>(x.target_node_idxs.size());
+  sizes[2] = static_cast<std::int64_t>(x.timestamps.size());
+  sizes[3] = static_cast<std::int64_t>(x.edge_idxs.size());
+}
+
+void oracle_index_copy(void* hv, std::int64_t* blocks, std::int64_t* targets,
+                       std::int64_t* timestamps, std::int64_t* edge_idxs) {
+  const auto& x = static_cast<IndexHandle*>(hv)->index;
+  for (std::size_t i = 0; i < x.source_blocks.size(); ++i) blocks[i] = static_cast<std::int64_t>(x.source_blocks[i]);
+  for (std::size_t i = 0; i < x.target_node_idxs.size(); ++i) targets[i] = static_cast<std::int64_t>(x.target_node_idxs[i]);
+  for (std::size_t i = 0; i < x.timestamps.size(); ++i) timestamps[i] = x.timestamps[i];
+  for (std::size_t i = 0; i < x.edge_idxs.size(); ++i) edge_idxs[i] = static_cast<std::int64_t>(x.edge_idxs[i]);
+}
+
+// Writes the index's debug string into buf (truncated to cap); returns its
+// full length.
+std::int64_t oracle_index_string(void* hv, char* buf, std::int64_t cap) {
+  const std::string s = OracleIndexString(static_cast<IndexHandle*>(hv)->index);
+  if (cap > 0) {
+    const std::size_t n = std::min<std::size_t>(s.size(), static_cast<std::size_t>(cap - 1));
+    std::memcpy(buf, s.data(), n);
+    buf[n] = 0;
+  }
+  return static_cast<std::int64_t>(s.size());
+}
+
+// One per-node sampler call. kind: 0 SampleRandomUniform, 1 SampleFirst,
+// 2 SampleRandomUniformWithTimestamp, 3 SampleFirstWithTimestamp.
+// rng_seed seeds a fresh std::mt19937_64. Returns the number of targets
+// written to out (<= cap), or -1 on error.
+std::int64_t oracle_index_sample(void* hv, int kind, std::int64_t source,
+                                 std::int64_t k, std::int64_t seed_ts,
+                                 std::int64_t masked, std::uint64_t rng_seed,
+                                 std::int64_t* out, std::int64_t cap) {
+  const auto& x = static_cast<IndexHandle*>(hv)->index;
+  std::mt19937_64 rng(rng_seed);
+  std::vector<dgf_oracle::InputIdx> res;
+  const auto src = static_cast<dgf_oracle::InputIdx>(source);
+  const auto m = static_cast<dgf_oracle::InputIdx>(masked);
+  dgf_oracle::Status st;
+  switch (kind) {
+    case 0: st = dgf_oracle::ToStatus(x.SampleRandomUniform(src, k, &res, &rng, m)); break;
+    case 1: st = dgf_oracle::ToStatus(x.SampleFirst(src, k, &res, m)); break;
+    case 2: st = dgf_oracle::ToStatus(x.SampleRandomUniformWithTimestamp(src, seed_ts, k, &res, &rng)); break;
+    default: st = dgf_oracle::ToStatus(x.SampleFirstWithTimestamp(src, seed_ts, k, &res)); break;
+  }
+  if (!st.ok()) {
+    g_oracle_error = st.msg;
+    return -1;
+  }
+  const std::int64_t n = std::min<std::int64_t>(cap, static_cast<std::int64_t>(res.size()));
+  for (std::int64_t i = 0; i < n; ++i) out[i] = static_cast<std::int64_t>(res[i]);
+  return static_cast<std::int64_t>(res.size());
+}
+
+}  // extern "C"

@@ -1,0 +1,290 @@
+"""ORACLE — test infrastructure only.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may
+import this module, and only as the checker or as the timed CPU baseline.
+The product (distributed_graph_flow_b200/) never imports it.
+
+Two CPU implementations of DGF's sampling path behind one wrapper:
+  * ``liboracle.so`` — the C++ restatement (grow.h + dgf_oracle.cc), which
+    follows dgf/src/sampling/in_memory_sampler.{h,cc} and
+    in_memory_sampler_ext.cc:231-533, 1020-1246;
+  * ``_ref/libdgf_ref.so`` — the same driver over the reference's own
+    AdjacencyIndex, compiled from its unmodified in_memory_sampler.cc.
+And a float64 numpy restatement of the aggregation math:
+  * segment_sum / mean pooling, dgf/src/learning/jax/layers/hetero_gnn.py:
+    283-295 (jax.ops.segment_sum(data, ids, n) / max(count, 1));
+  * CSR SpMM (sparse_deferred SparseMatrix @ dense,
+    homo_gnn_sparse_deferred.py:138-161) as the same segment sum with
+    row = target, col = source.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Dict, List, Optional
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_ORACLE = HERE / "liboracle.so"
+LIB_REF = HERE / "_ref" / "libdgf_ref.so"
+
+MODE_RANDOM, MODE_FIRST, MODE_MOST_RECENT = 0, 1, 2
+
+_libs: Dict[str, ctypes.CDLL] = {}
+
+_p64 = ctypes.POINTER(ctypes.c_int64)
+_pi = ctypes.POINTER(ctypes.c_int)
+
+
+def build(ref: bool = True) -> None:
+    """Builds liboracle.so (and _ref/ when the reference sources exist)."""
+    import subprocess
+
+    target = "ref" if ref else "all"
+    subprocess.run(["make", "-s", "-C", str(HERE), target], check=True)
+
+
+def available(ref: bool = False) -> bool:
+    return (LIB_REF if ref else LIB_ORACLE).exists()
+
+
+def _lib(ref: bool) -> ctypes.CDLL:
+    key = "ref" if ref else "oracle"
+    if key not in _libs:
+        path = LIB_REF if ref else LIB_ORACLE
+        if not path.exists():
+            raise RuntimeError(f"{path} not built (make -C oracle{' ref' if ref else ''})")
+        lib = ctypes.CDLL(str(path), mode=os.RTLD_NOW | os.RTLD_LOCAL)
+        lib.oracle_last_error.restype = ctypes.c_char_p
+        lib.oracle_sampler_create.restype = ctypes.c_void_p
+        lib.oracle_sampler_create.argtypes = [
+            ctypes.c_int, _p64, ctypes.c_int, ctypes.POINTER(_p64), ctypes.POINTER(_p64), ctypes.POINTER(_p64), _p64,
+            ctypes.c_int, _pi, _pi, _pi, ctypes.c_int, _pi, _pi, _pi, _pi, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+        ]
+        lib.oracle_sampler_free.argtypes = [ctypes.c_void_p]
+        lib.oracle_sample.restype = ctypes.c_int
+        lib.oracle_sample.argtypes = [ctypes.c_void_p, _p64, _p64, _p64, ctypes.c_int64, ctypes.c_int]
+        lib.oracle_result_counts.argtypes = [ctypes.c_void_p, _p64, _p64]
+        lib.oracle_result_copy.argtypes = [ctypes.c_void_p, _p64, _p64, _p64]
+        lib.oracle_index_build.restype = ctypes.c_void_p
+        lib.oracle_index_build.argtypes = [_p64, _p64, _p64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_int, ctypes.c_int]
+        lib.oracle_index_free.argtypes = [ctypes.c_void_p]
+        lib.oracle_index_sizes.argtypes = [ctypes.c_void_p, _p64]
+        lib.oracle_index_copy.argtypes = [ctypes.c_void_p, _p64, _p64, _p64, _p64]
+        lib.oracle_index_string.restype = ctypes.c_int64
+        lib.oracle_index_string.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int64]
+        lib.oracle_index_sample.restype = ctypes.c_int64
+        lib.oracle_index_sample.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_uint64, _p64, ctypes.c_int64]
+        _libs[key] = lib
+    return _libs[key]
+
+
+def _p(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data_as(_p64)
+
+
+def _err(lib) -> str:
+    m = lib.oracle_last_error()
+    return m.decode() if m else ""
+
+
+class OracleError(ValueError):
+    pass
+
+
+class Index:
+    """One adjacency index built by the oracle (or by the reference code)."""
+
+    def __init__(self, adjacency, timestamps=None, reversed=False, num_source_nodes=0, num_target_nodes=0,
+                 populate_edge_idxs=False, ref=False):
+        self.lib = _lib(ref)
+        adj = np.ascontiguousarray(np.asarray(adjacency).astype(np.int64))
+        self._src = np.ascontiguousarray(adj[0])
+        self._dst = np.ascontiguousarray(adj[1])
+        self._ts = None if timestamps is None else np.ascontiguousarray(np.asarray(timestamps, dtype=np.int64))
+        self.h = self.lib.oracle_index_build(_p(self._src), _p(self._dst), _p(self._ts), len(self._src),
+                                             int(num_source_nodes), int(num_target_nodes), int(reversed),
+                                             int(populate_edge_idxs))
+        if not self.h:
+            raise OracleError(_err(self.lib))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib.oracle_index_free(self.h)
+
+    def arrays(self):
+        sizes = np.zeros(4, np.int64)
+        self.lib.oracle_index_sizes(self.h, _p(sizes))
+        out = [np.zeros(int(n), np.int64) for n in sizes]
+        self.lib.oracle_index_copy(self.h, *[_p(a) for a in out])
+        return {"source_blocks": out[0], "target_node_idxs": out[1], "timestamps": out[2], "edge_idxs": out[3]}
+
+    def __str__(self):
+        n = self.lib.oracle_index_string(self.h, None, 0)
+        buf = ctypes.create_string_buffer(int(n) + 1)
+        self.lib.oracle_index_string(self.h, buf, n + 1)
+        return buf.value.decode()
+
+    def sample(self, kind: int, source: int, k: int, seed_ts: int = 0, masked: int = -1, rng_seed: int = 42):
+        cap = 1 << 16
+        out = np.zeros(cap, np.int64)
+        n = self.lib.oracle_index_sample(self.h, kind, source, k, seed_ts, masked, rng_seed, _p(out), cap)
+        if n < 0:
+            raise OracleError(_err(self.lib))
+        return out[: min(n, cap)]
+
+
+def _flatten_plan(plan, nodeset_index, edgeset_index):
+    nodes = [plan.root]
+    node_ns, first, num, e_es, e_rev, e_hw, e_child = [], [], [], [], [], [], []
+    head = 0
+    node_ns.append(nodeset_index[plan.root.nodeset])
+    first.append(0)
+    num.append(0)
+    while head < len(nodes):
+        pn = nodes[head]
+        i = head
+        head += 1
+        first[i] = len(e_es)
+        num[i] = len(pn.children)
+        for c in pn.children:
+            e_es.append(edgeset_index[c.edgeset])
+            e_rev.append(int(bool(c.reversed)))
+            e_hw.append(int(c.hop_width))
+            e_child.append(len(nodes))
+            nodes.append(c.node)
+            node_ns.append(nodeset_index[c.node.nodeset])
+            first.append(0)
+            num.append(0)
+    return node_ns, first, num, e_es, e_rev, e_hw, e_child
+
+
+def _ints(v):
+    return (ctypes.c_int * max(1, len(v)))(*v)
+
+
+class OracleSampler:
+    """CPU sampler with the reference's semantics (see module docstring).
+
+    ``graph`` is any object with ``node_sets[name].num_nodes`` and
+    ``edge_sets[name].adjacency`` / ``.features``; ``plan`` any object with
+    the SamplingPlan fields. Node/edge sets are indexed in sorted-name order.
+    """
+
+    def __init__(self, graph, plan, schema, debug_sampling=False, num_threads=0, seed=0, edgeset_to_mask=None,
+                 edgeset_timestamp_features=None, mode=None, ref=False):
+        self.lib = _lib(ref)
+        ets = dict(edgeset_timestamp_features or {})
+        self.nodesets = sorted(schema.node_sets)
+        self.edgesets = sorted(schema.edge_sets)
+        ns_idx = {n: i for i, n in enumerate(self.nodesets)}
+        es_idx = {n: i for i, n in enumerate(self.edgesets)}
+        node_ns, first, num, e_es, e_rev, e_hw, e_child = _flatten_plan(plan, ns_idx, es_idx)
+        num_nodes = np.array([int(graph.node_sets[n].num_nodes) for n in self.nodesets], np.int64)
+        self._keep = []
+        srcs, dsts, tss, counts = [], [], [], []
+        for name in self.edgesets:
+            adj = np.ascontiguousarray(np.asarray(graph.edge_sets[name].adjacency).astype(np.int64))
+            s, d = np.ascontiguousarray(adj[0]), np.ascontiguousarray(adj[1])
+            t = None
+            if name in ets:
+                t = np.ascontiguousarray(np.asarray(graph.edge_sets[name].features[ets[name]], np.int64))
+            self._keep += [s, d, t]
+            srcs.append(_p(s))
+            dsts.append(_p(d))
+            tss.append(_p(t) if t is not None else None)
+            counts.append(len(s))
+        n_es = len(self.edgesets)
+        src_arr = (_p64 * max(1, n_es))(*srcs)
+        dst_arr = (_p64 * max(1, n_es))(*dsts)
+        ts_arr = (_p64 * max(1, n_es))(*tss)
+        cnt = np.array(counts + [0], np.int64)
+        if mode is None:
+            mode = MODE_FIRST if debug_sampling else MODE_RANDOM
+        mask_idx = es_idx[edgeset_to_mask] if edgeset_to_mask is not None else -1
+        self.h = self.lib.oracle_sampler_create(
+            len(self.nodesets), _p(num_nodes), n_es, src_arr, dst_arr, ts_arr, _p(cnt), len(node_ns), _ints(node_ns),
+            _ints(first), _ints(num), len(e_es), _ints(e_es), _ints(e_rev), _ints(e_hw), _ints(e_child),
+            int(bool(plan.with_replacement)), int(mode), int(num_threads), int(seed), mask_idx, int(bool(ets)),
+        )
+        if not self.h:
+            raise OracleError(_err(self.lib))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib.oracle_sampler_free(self.h)
+
+    def sample_raw(self, seeds, seed_ts=None, masks=None, threads: int = 1):
+        """Samples and returns the merged (sample-major) flat arrays:
+        (node_counts[B, NS], edge_counts[B, ES], nodes, esrc, edst)."""
+        seeds = np.ascontiguousarray(np.asarray(seeds, np.int64))
+        ts = None if seed_ts is None else np.ascontiguousarray(np.asarray(seed_ts, np.int64))
+        mk = None if masks is None else np.ascontiguousarray(np.asarray(masks, np.int64))
+        st = self.lib.oracle_sample(self.h, _p(seeds), _p(ts), _p(mk), len(seeds), int(threads))
+        if st != 0:
+            raise OracleError(_err(self.lib))
+        B = len(seeds)
+        nc = np.zeros((B, len(self.nodesets)), np.int64)
+        ec = np.zeros((B, len(self.edgesets)), np.int64)
+        self.lib.oracle_result_counts(self.h, _p(nc), _p(ec))
+        nodes = np.zeros(int(nc.sum()), np.int64)
+        esrc = np.zeros(int(ec.sum()), np.int64)
+        edst = np.zeros(int(ec.sum()), np.int64)
+        self.lib.oracle_result_copy(self.h, _p(nodes), _p(esrc), _p(edst))
+        return nc, ec, nodes, esrc, edst
+
+    def sample(self, seeds, seed_ts=None, masks=None, threads: int = 1):
+        """Per seed: ({nodeset: ids}, {edgeset: [2, E] adjacency})."""
+        nc, ec, nodes, esrc, edst = self.sample_raw(seeds, seed_ts, masks, threads)
+        out = []
+        a = b = 0
+        for i in range(nc.shape[0]):
+            ns = {}
+            for s, name in enumerate(self.nodesets):
+                ns[name] = nodes[a : a + nc[i, s]]
+                a += nc[i, s]
+            es = {}
+            for e, name in enumerate(self.edgesets):
+                es[name] = np.stack([esrc[b : b + ec[i, e]], edst[b : b + ec[i, e]]])
+                b += ec[i, e]
+            out.append((ns, es))
+        return out
+
+
+# ---------------------------------------------------------------------------
+# Aggregation (float64).
+# ---------------------------------------------------------------------------
+def segment_sum(data: np.ndarray, segment_ids: np.ndarray, num_segments: int, mean: bool = False) -> np.ndarray:
+    """jax.ops.segment_sum semantics in float64 (out-of-range ids dropped);
+    mean divides by max(count, 1) (hetero_gnn.py:288-295)."""
+    data = np.asarray(data, np.float64)
+    ids = np.asarray(segment_ids, np.int64)
+    keep = (ids >= 0) & (ids < num_segments)
+    out = np.zeros((num_segments,) + data.shape[1:], np.float64)
+    np.add.at(out, ids[keep], data[keep])
+    if mean:
+        cnt = np.bincount(ids[keep], minlength=num_segments).astype(np.float64)
+        out /= np.maximum(cnt, 1.0).reshape((-1,) + (1,) * (data.ndim - 1))
+    return out
+
+
+def csr_spmm(rowptr: np.ndarray, col: np.ndarray, x: np.ndarray, val: Optional[np.ndarray] = None,
+             normalize: bool = False) -> np.ndarray:
+    """Y[r] = scale_r * sum_j val_j * X[col_j] in float64 (scipy CSR)."""
+    import scipy.sparse as sp
+
+    rowptr = np.asarray(rowptr, np.int64)
+    n_rows = len(rowptr) - 1
+    v = np.ones(len(col), np.float64) if val is None else np.asarray(val, np.float64)
+    a = sp.csr_matrix((v, np.asarray(col, np.int64), rowptr), shape=(n_rows, x.shape[0]))
+    y = a @ np.asarray(x, np.float64)
+    if normalize:
+        deg = np.diff(rowptr).astype(np.float64)
+        y /= np.maximum(deg, 1.0)[:, None]
+    return y

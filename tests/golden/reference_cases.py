@@ -1,0 +1,180 @@
+"""Known-answer cases transcribed from the reference's own sampler tests.
+
+Each case cites the reference test it comes from (paths within the DGF
+project). The graphs are the tests' fixtures; the expected outputs are the
+tests' asserted values. These pin the oracle and, through it, the GPU path.
+"""
+
+import numpy as np
+
+# ---------------------------------------------------------------------------
+# Toy 3-edgeset graph: dgf/src/sampling/in_memory_sampler_test.py:35-82.
+# ---------------------------------------------------------------------------
+TOY_NODESETS = {"n1": 2, "n2": 3}
+TOY_EDGESETS = {
+    # name: (source, target, adjacency)
+    "e11": ("n1", "n1", [[1], [0]]),
+    "e12": ("n1", "n2", [[0, 0, 0], [0, 1, 2]]),
+    "e22": ("n2", "n2", [[0], [2]]),
+}
+TOY_FEATURES = {"n1": {"f1": np.array([10, 11])}, "n2": {"f2": np.array([20.0, 21.0, 22.0])}}
+
+# Sampler.__str__ of SimpleSamplingConfig(seed_nodeset="n1", num_hops=2)
+# (hop_width=5, reverse=True): in_memory_sampler_test.py:84-134.
+TOY_SAMPLER_STR = """\
+Sampler(
+  plan=SamplingPlan(root=
+Node(nodeset_idx=0, children=[
+  Edge(edgeset_idx=0, reversed=0, hop_width=5, node=
+    Node(nodeset_idx=0, children=[
+      Edge(edgeset_idx=0, reversed=0, hop_width=5, node=
+        Node(nodeset_idx=0, children=[])),
+      Edge(edgeset_idx=0, reversed=1, hop_width=5, node=
+        Node(nodeset_idx=0, children=[])),
+      Edge(edgeset_idx=1, reversed=0, hop_width=5, node=
+        Node(nodeset_idx=1, children=[]))
+    ])),
+  Edge(edgeset_idx=0, reversed=1, hop_width=5, node=
+    Node(nodeset_idx=0, children=[
+      Edge(edgeset_idx=0, reversed=0, hop_width=5, node=
+        Node(nodeset_idx=0, children=[])),
+      Edge(edgeset_idx=0, reversed=1, hop_width=5, node=
+        Node(nodeset_idx=0, children=[])),
+      Edge(edgeset_idx=1, reversed=0, hop_width=5, node=
+        Node(nodeset_idx=1, children=[]))
+    ])),
+  Edge(edgeset_idx=1, reversed=0, hop_width=5, node=
+    Node(nodeset_idx=1, children=[
+      Edge(edgeset_idx=1, reversed=1, hop_width=5, node=
+        Node(nodeset_idx=0, children=[])),
+      Edge(edgeset_idx=2, reversed=0, hop_width=5, node=
+        Node(nodeset_idx=1, children=[])),
+      Edge(edgeset_idx=2, reversed=1, hop_width=5, node=
+        Node(nodeset_idx=1, children=[]))
+    ]))
+]),
+  with_replacement=0
+),
+  nodeset_index={n1: 0, n2: 1},
+  edgeset_index={e11: 0, e12: 1, e22: 2},
+  nodesets=[{idx=0, num_nodes=2}, {idx=1, num_nodes=3}]
+)"""
+
+# BuildAdjacencyIndex string goldens: in_memory_sampler_test.py:136-195.
+# (adjacency, reversed, num_source_nodes, num_target_nodes, expected)
+INDEX_STRING_CASES = [
+    ([[], []], False, 2, 2, "AdjacencyIndex(source_blocks=(3)[0, 0, 0], target_node_idxs=(0)[])"),
+    ([[0, 0, 0], [0, 1, 2]], False, 2, 3,
+     "AdjacencyIndex(source_blocks=(3)[0, 3, 3], target_node_idxs=(3)[0, 1, 2])"),
+    ([[0, 0, 0], [0, 1, 2]], True, 2, 3,
+     "AdjacencyIndex(source_blocks=(4)[0, 1, 2, 3], target_node_idxs=(3)[0, 0, 0])"),
+    ([[0, 0, 1, 1], [0, 1, 0, 1]], False, 2, 2,
+     "AdjacencyIndex(source_blocks=(3)[0, 2, 4], target_node_idxs=(4)[0, 1, 0, 1])"),
+]
+
+# Deterministic (debug_sampling=True) sample goldens on the toy graph.
+# Each: (description, config kwargs, seeds, masked, edgeset_to_mask,
+#        expected per seed: ({nodeset: #idx}, {edgeset: adjacency})).
+TOY_SAMPLE_CASES = [
+    (
+        "1-hop deterministic, in_memory_sampler_test.py:255-297",
+        dict(seed_nodeset="n1", num_hops=1, hop_width=2),
+        [0], None, None,
+        [({"n1": [0, 1], "n2": [0, 1]}, {"e11": [[1], [0]], "e12": [[0, 0], [0, 1]], "e22": [[], []]})],
+    ),
+    (
+        "2-hop deterministic, in_memory_sampler_test.py:299-343",
+        dict(seed_nodeset="n1", num_hops=2, hop_width=2),
+        [0], None, None,
+        [({"n1": [0, 1], "n2": [0, 2, 1]}, {"e11": [[1], [0]], "e12": [[0, 0], [0, 2]], "e22": [[0], [1]]})],
+    ),
+    (
+        "2-hop deterministic with replacement, in_memory_sampler_test.py:345-389",
+        dict(seed_nodeset="n1", num_hops=2, hop_width=2, with_replacement=True),
+        [0], None, None,
+        [({"n1": [0, 1, 0, 0, 0], "n2": [0, 2, 1]},
+          {"e11": [[1, 1], [0, 2]], "e12": [[0, 0, 3, 4], [0, 2, 0, 2]], "e22": [[0], [1]]})],
+    ),
+    (
+        "multi-seed deterministic, in_memory_sampler_test.py:472-540",
+        dict(seed_nodeset="n1", num_hops=1, hop_width=2),
+        [0, 1], None, None,
+        [({"n1": [0, 1], "n2": [0, 1]}, {"e11": [[1], [0]], "e12": [[0, 0], [0, 1]], "e22": [[], []]}),
+         ({"n1": [1, 0], "n2": []}, {"e11": [[0], [1]], "e12": [[], []], "e22": [[], []]})],
+    ),
+    (
+        "0-hop, in_memory_sampler_test.py:197-219",
+        dict(seed_nodeset="n1", num_hops=0, hop_width=2),
+        [0], None, None,
+        [({"n1": [0], "n2": []}, {"e11": [[], []], "e12": [[], []], "e22": [[], []]})],
+    ),
+]
+
+# Masking goldens (only the node sets the tests assert).
+# in_memory_sampler_test.py:391-418 and :443-470.
+TOY_MASK_CASES = [
+    ("mask forward", dict(seed_nodeset="n1", num_hops=1, hop_width=2), 0, 1, "e12", {"n2": [0, 2]}),
+    ("mask reverse", dict(seed_nodeset="n2", num_hops=1, hop_width=2, reverse=True), 0, 0, "e12", {"n1": []}),
+]
+
+# ---------------------------------------------------------------------------
+# Temporal graph: dgf/src/util/gen_test_graph.py:2179-2250 (include_e2=True).
+# ---------------------------------------------------------------------------
+TEMPORAL_NODES = {"n1": 4}
+TEMPORAL_NODE_TS = np.array([10, 20, 30, 40], np.int64)
+TEMPORAL_NODE_FEAT = np.array([[1.0, 1.0], [2.0, 2.0], [3.0, 3.0], [4.0, 4.0]], np.float32)
+TEMPORAL_E1 = ([[0, 0, 1], [1, 2, 3]], np.array([15, 25, 35], np.int64))
+TEMPORAL_E2 = [[2, 3], [0, 1]]
+
+# test_temporal_sampling, in_memory_sampler_test.py:980-1086: plan
+# SimpleSamplingConfig(n1, num_hops=2, hop_width=2, reverse=False,
+# temporal_sampling=True), debug_sampling=True, seed node 0.
+TEMPORAL_CASES = {
+    10: ({"n1": [0]}, {"e1": [[], []], "e2": [[], []]}, [10], [[1.0, 1.0]]),
+    20: ({"n1": [0, 1]}, {"e1": [[0], [1]], "e2": [[], []]}, [10, 20], [[1.0, 1.0], [2.0, 2.0]]),
+    25: ({"n1": [0, 1, 2]}, {"e1": [[0, 0], [1, 2]], "e2": [[2], [0]]}, [10, 20, 30],
+         [[1.0, 1.0], [2.0, 2.0], [3.0, 3.0]]),
+    40: ({"n1": [0, 1, 3, 2]}, {"e1": [[0, 0, 1], [1, 3, 2]], "e2": [[3], [0]]}, [10, 20, 40, 30],
+         [[1.0, 1.0], [2.0, 2.0], [4.0, 4.0], [3.0, 3.0]]),
+}
+
+# ---------------------------------------------------------------------------
+# AdjacencyIndex known answers: dgf/src/sampling/in_memory_sampler_test.cc.
+# ---------------------------------------------------------------------------
+# (edges [(src, dst[, ts])], num_src, num_dst, source_blocks, targets, timestamps)
+CSR_CASES = [
+    ("BasicCase :93-102", [(0, 0), (0, 1), (2, 3)], 3, 4, [0, 2, 2, 3], [0, 1, 3], None),
+    ("EmptyEdges :104-111", [], 2, 2, [0, 0, 0], [], None),
+    ("SourceWithNoOutgoingEdges :113-121", [(0, 1), (2, 3)], 4, 4, [0, 1, 1, 2, 2], [1, 3], None),
+    ("DuplicateEdgesKept :123-132", [(0, 1), (0, 1), (0, 2)], 1, 3, [0, 3], [1, 1, 2], None),
+    ("EdgesOutOfOrder :134-143", [(2, 3), (0, 1), (0, 0)], 3, 4, [0, 2, 2, 3], [0, 1, 3], None),
+    ("Temporal :163-174", [(0, 1, 15), (0, 2, 25), (1, 3, 35)], 4, 4, [0, 2, 3, 3, 3], [1, 2, 3], [15, 25, 35]),
+]
+
+# Per-node sampler known answers on CreateTestIndex = {{0,3,3,5},
+# {10,11,12,20,21}} (in_memory_sampler_test.cc:24-82) and the masking /
+# temporal ones (:176-287). kind: 0 random, 1 first, 2 random+ts, 3 first+ts.
+PER_NODE_FIRST = [
+    ("SampleFirst_LessThanAvailable :35-40", 0, 2, [10, 11]),
+    ("SampleFirst_MoreThanAvailable :42-47", 0, 5, [10, 11, 12]),
+    ("SampleFirst_NoNeighbors :49-54", 1, 1, []),
+]
+PER_NODE_RANDOM = [
+    # (name, source, k, expected size, allowed superset)
+    ("SampleRandomUniform_LessThanAvailable :56-64", 0, 2, 2, [10, 11, 12]),
+    ("SampleRandomUniform_MoreThanAvailable :66-73", 0, 5, 3, [10, 11, 12]),
+    ("SampleRandomUniform_NoNeighbors :75-82", 1, 1, 0, []),
+]
+# Masked index: edges 0->1 (e0), 0->2 (e1), 0->3 (e2) (:194-268), and
+# 0->1..5 (e0..e4) for MoreCandidates (:270-287).
+MASK_FIRST = ("SampleFirst_WithMasking :194-206", 2, 1, [1, 3])
+MASK_RANDOM = [
+    # (name, targets, edge_idxs, k, masked, expected size, allowed)
+    ("WithMasking :208-222", [1, 2, 3], [0, 1, 2], 2, 1, 2, [1, 3]),
+    ("AllMasked :224-237", [1, 2, 3], [5, 5, 5], 2, 5, 0, []),
+    ("NoneMasked :239-253", [1, 2, 3], [0, 1, 2], 2, 5, 2, [1, 2, 3]),
+    ("NumSamplesLargerThanAvailable :255-268", [1, 2, 3], [0, 1, 2], 5, 1, 2, [1, 3]),
+    ("MoreCandidates :270-287", [1, 2, 3, 4, 5], [0, 1, 2, 3, 4], 2, 2, 2, [1, 2, 4, 5]),
+]
+# SampleWithTimestamp_FiltersFutureEdges :176-190.
+TEMPORAL_FILTER = ([(0, 1, 15), (0, 2, 25), (1, 3, 35)], 4, 4, 0, 20, 2, [1])
