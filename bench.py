@@ -1,0 +1,640 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 sampling + aggregation path.
+
+Headline (one JSON line on rank 0): sampled subgraphs/s of the large sharded
+workload — 111,059,956 nodes / 1,615,685,872 edges (Zipf(2.0) out-degrees),
+bf16 128-d features node-range partitioned across the ranks, 3-hop fanout
+[15, 10, 5], 8192 seeds per GPU per step, halo features gathered with NCCL
+all-to-all when N > 1. A step = sample one batch of seeds + gather the
+features of every sampled node. Synthetic inputs stand in for the dataset.
+
+At N = 1 the line also carries the standalone CSR SpMM (2,449,029 rows,
+61,859,140 nnz, 256 features, fp32 and bf16: achieved HBM GB/s) and the
+temporal 169K-node sampler (fanout [10, 5], 1024 seeds, cutoff = seed
+timestamp) next to their CPU baselines.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dgfx|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+B_SEEDS = 8192
+FANOUT = [15, 10, 5]
+FEAT_DIM = 128
+
+
+def log(*a):
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+                    capture_output=True, text=True, timeout=5,
+                ).stdout.strip()
+                if out:
+                    self.rows.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def timed(fn, steps, sync_fn, events=True):
+    """Device time (ms per call) of `steps` calls bracketed by syncs."""
+    import torch
+
+    sync_fn()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        fn(i)
+    e.record()
+    sync_fn()
+    return s.elapsed_time(e) / steps
+
+
+def count_dgfx_launches(fn):
+    """Kernels of this library launched by one call of fn (CUPTI via the
+    torch profiler; names in the dgfx namespace)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    return sum(1 for n in names if "dgfx" in n), len(names)
+
+
+# ---------------------------------------------------------------------------
+# Large sharded sampling (headline).
+# ---------------------------------------------------------------------------
+def large_spec(scale):
+    import dataclasses
+
+    from distributed_graph_flow_b200 import synth
+
+    s = synth.LARGE_SHARDED
+    if scale == 1.0:
+        return s
+    return dataclasses.replace(s, num_nodes=max(1000, int(s.num_nodes * scale)), num_edges=int(s.num_edges * scale))
+
+
+def setup_large(rank, world, dev, scale=1.0):
+    import torch
+
+    from distributed_graph_flow_b200 import driver, synth
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+    from distributed_graph_flow_b200.sampling import config as cfg
+
+    spec = large_spec(scale)
+    t0 = time.time()
+    index, _, _ = synth.build_graph(spec, dev)
+    t_graph = time.time() - t0
+    rpr = math.ceil(spec.num_nodes / world)
+    lo = rank * rpr
+    cnt = max(0, min(rpr, spec.num_nodes - lo))
+    table = synth.normal_features(lo, cnt, FEAT_DIM, spec.seed + 100, torch.bfloat16, dev)
+    plan = cfg.explicit_plan("paper", "cites", FANOUT)
+    cc = ext.create_device_sampler(plan, ["paper"], [spec.num_nodes], ["cites"], [index], [None],
+                                   ext._native.MODE_RANDOM, seed=1234)
+    feats = driver.HaloFeatures(table, rpr, rank, world)
+    sharded = driver.ShardedSampler(cc, feats, rank, world)
+    torch.cuda.synchronize()
+    log(f"[bench] large graph built in {t_graph:.1f}s; setup {time.time() - t0:.1f}s; T={cc.tree_size}")
+    return spec, index, table, cc, sharded, plan
+
+
+def bench_large(args, rank, world, dev):
+    import torch
+    import torch.distributed as dist
+
+    from distributed_graph_flow_b200 import _native, synth
+
+    spec, index, table, cc, sharded, plan = setup_large(rank, world, dev, args.scale)
+    W, K = args.warmup, args.steps
+    seeds = synth.uniform_int((W + K) * B_SEEDS, 0, spec.num_nodes, 77 + rank, 5, dev).view(W + K, B_SEEDS)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def sync():
+        torch.cuda.synchronize()
+        barrier()
+
+    for i in range(W):
+        sharded.step(seeds[i])
+    cc.check()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks.start()
+    ms = timed(lambda i: sharded.step(seeds[W + i]), K, sync)
+    clk = clocks.stop()
+    cc.check()
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = B_SEEDS * world / (ms_max / 1e3)
+
+    # Per-step sizes (for the byte counts) from one representative step.
+    merged, feats, _ = sharded.step(seeds[W])
+    torch.cuda.synchronize()
+    total_nodes = int(merged.node_offsets[-1].item())
+    total_edges = int(merged.edge_offsets[-1].item())
+    st = (ctypes_stats(cc))
+
+    # Kernel-level timings on the same inputs (dominant kernels).
+    ms_sample = timed(lambda i: cc.sample_merged(seeds[W + i], call_index=10_000 + i, check=False), K, sync)
+    st = ctypes_stats(cc)
+    ms_gather = None
+    if world == 1:
+        rng = merged.node_offsets[[0, -1]]
+        cap = int(merged.node_ids.numel())
+        out = torch.empty((cap, FEAT_DIM), dtype=torch.bfloat16, device=dev)
+
+        def g(_):
+            _native.check(_native.lib().dgfx_gather_rows_ranged(
+                _native.ptr(table), int(table.shape[0]), FEAT_DIM * 2, _native.ptr(merged.node_ids), _native.ptr(rng),
+                cap, _native.ptr(out), _native.stream_handle()))
+
+        ms_gather = timed(g, K, sync)
+
+    hbm, peak_kind = measured_peaks()
+    # Algorithmic bytes per launch.
+    sample_bytes = 16 * st[0] + 4 * st[1] + 8 * B_SEEDS + 8 * total_nodes + 16 * total_edges
+    gather_bytes = total_nodes * (2 * FEAT_DIM * 2 + 8)
+    kernels = {
+        "sampler": {"ms": ms_sample, "bytes_per_launch": sample_bytes, "gbs": sample_bytes / ms_sample / 1e6,
+                    "rows_expanded": st[0], "neighbours_sampled": st[1]},
+    }
+    if ms_gather is not None:
+        kernels["feature_gather"] = {"ms": ms_gather, "bytes_per_launch": gather_bytes,
+                                     "gbs": gather_bytes / ms_gather / 1e6}
+    dom = max(kernels, key=lambda k: kernels[k]["ms"])
+    traffic = ncu_traffic().get(dom, {}).get("bytes_per_launch")
+    roof = {"kernel": dom, "bound": "hbm", "achieved": round(kernels[dom]["gbs"], 1), "peak": hbm,
+            "peak_kind": peak_kind, "unit": "GB/s", "frac": round(kernels[dom]["gbs"] / hbm, 4),
+            "traffic": traffic}
+
+    # End to end through the public API with host buffers.
+    e2e = bench_large_e2e(sharded, seeds, W, K, dev, world, sync)
+
+    launches, all_k = count_dgfx_launches(lambda: sharded.step(seeds[W]))
+    res = {
+        "metric": "sampled subgraphs/sec",
+        "value": round(value, 1),
+        "unit": "subgraphs/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(ms_max, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int64 ids / bf16 features",
+        "data": "synthetic (seeded power-law graph with the sizes of the 1.6B-edge graph; N(0,1) bf16 features)",
+        "config": {"workload": "large sharded sampling: 111,059,956 nodes, 1,615,685,872 edges, Zipf(2.0), "
+                               "fanout [15,10,5], 8192 seeds/GPU, bf16 128-d features node-range partitioned",
+                   "seeds_per_gpu": B_SEEDS, "fanout": FANOUT, "nodes_per_step_rank0": total_nodes,
+                   "edges_per_step_rank0": total_edges, "l2": "inputs larger than L2 (7.4 GB CSR, 28 GB features)",
+                   "parallelism": f"seed-sharded dp{world}, topology replicated, features node-range partitioned"},
+        "clocks": clk,
+        "roofline": roof,
+        "kernels": kernels,
+        "e2e": e2e,
+        "gpu_launches": launches * K,
+        "gpu_launches_per_step": launches,
+    }
+    return res, (spec, index, table, cc, plan, seeds, W)
+
+
+def ctypes_stats(cc):
+    import ctypes
+
+    from distributed_graph_flow_b200 import _native
+
+    out = (ctypes.c_int64 * 3)()
+    _native.check(_native.lib().dgfx_sampler_stats(cc._handle, _native.stream_handle(), out))
+    return [int(x) for x in out]
+
+
+def bench_large_e2e(sharded, seeds_dev, W, K, dev, world, sync):
+    """Host seeds in, host topology + features out (pinned buffers), through
+    ShardedSampler.step; copies inside the timed region."""
+    import torch
+
+    host_seeds = seeds_dev.cpu().pin_memory()
+    cap_nodes = B_SEEDS * sharded.cc.tree_size
+    h_nodes = torch.empty(cap_nodes, dtype=torch.int64, pin_memory=True)
+    h_src = torch.empty(cap_nodes, dtype=torch.int64, pin_memory=True)
+    h_dst = torch.empty(cap_nodes, dtype=torch.int64, pin_memory=True)
+    h_feat = torch.empty((cap_nodes, FEAT_DIM), dtype=torch.bfloat16, pin_memory=True)
+    d_seeds = torch.empty(B_SEEDS, dtype=torch.int64, device=dev)
+    moved = {"h2d": 0, "d2h": 0}
+
+    def one(i):
+        d_seeds.copy_(host_seeds[W + i], non_blocking=True)
+        merged, feats, total = sharded.step(d_seeds)
+        off = merged.node_offsets[-1:].cpu()
+        eoff = merged.edge_offsets[-1:].cpu()
+        n = int(off.item())
+        m = int(eoff.item())
+        h_nodes[:n].copy_(merged.node_ids[:n], non_blocking=True)
+        h_src[:m].copy_(merged.edge_src[:m], non_blocking=True)
+        h_dst[:m].copy_(merged.edge_dst[:m], non_blocking=True)
+        if feats is not None:
+            h_feat[:n].copy_(feats[:n], non_blocking=True)
+        moved["h2d"] += B_SEEDS * 8
+        moved["d2h"] += n * 8 + m * 16 + 16 + (n * FEAT_DIM * 2 if feats is not None else 0)
+
+    for i in range(min(W, 2)):
+        one(i)
+    moved["h2d"] = moved["d2h"] = 0
+    sync()
+    t0 = time.perf_counter()
+    ms = timed(one, K, sync)
+    wall = (time.perf_counter() - t0) * 1e3 / K
+    t = torch.tensor([max(ms, wall)], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    return {"value": round(B_SEEDS * world / (ms_max / 1e3), 1), "unit": "subgraphs/s",
+            "h2d_bytes_per_step": moved["h2d"] // K, "d2h_bytes_per_step": moved["d2h"] // K,
+            "ms_per_step": round(ms_max, 3)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle / reference code on the host cores).
+# ---------------------------------------------------------------------------
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_sampler_from_index(index, num_nodes, plan, temporal=False, fill_threads=16):
+    from oracle import oracle as O
+
+    rowptr = index.rowptr.cpu().numpy()
+    col = index.col.cpu().numpy()
+    ts = index.ts.cpu().numpy() if (temporal and index.ts is not None) else None
+    ref = O.available(ref=True)
+    s = O.OracleSampler.from_csr([num_nodes], [plan.root.nodeset], [plan.root.children[0].edgeset],
+                                 {plan.root.children[0].edgeset: (rowptr, col, ts)}, plan, mode=O.MODE_RANDOM,
+                                 num_threads=host_cores(), seed=99, temporal=temporal, ref=ref,
+                                 fill_threads=fill_threads)
+    return s, ("reference" if ref else "port")
+
+
+def cpu_large_baseline(index, table_host, num_nodes, plan, seeds, budget_s=15.0, threads=None):
+    """Samples (topology via the reference's compiled samplers when built,
+    else the restatement) + numpy feature gather per sample, like
+    add_features_to_samples. Returns (subgraphs/s, cores, kind, sample desc)."""
+    threads = threads or host_cores()
+    need = (index.rowptr.numel() + index.col.numel()) * 8 * 1.6 / 1e9 + 4
+    if host_mem_gb() < need:
+        raise RuntimeError(f"CPU baseline infeasible at this size: needs ~{need:.0f} GB host memory, "
+                           f"{host_mem_gb():.0f} GB available")
+    s, kind = cpu_sampler_from_index(index, num_nodes, plan)
+    done = 0
+    t_sample = t_feat = 0.0
+    t_start = time.perf_counter()
+    i = 0
+    while time.perf_counter() - t_start < budget_s and i < len(seeds):
+        batch = seeds[i]
+        i += 1
+        t0 = time.perf_counter()
+        nc, ec, nodes, _, _ = s.sample_raw(batch, threads=threads)
+        t1 = time.perf_counter()
+        if table_host is not None:
+            off = 0
+            for c in nc[:, 0]:
+                _ = table_host[nodes[off:off + c]]
+                off += c
+        t_feat += time.perf_counter() - t1
+        t_sample += t1 - t0
+        done += len(batch)
+    rate = done / (t_sample + t_feat)
+    return rate, threads, kind, {"seeds": done, "batches": i, "sample_s": round(t_sample, 3),
+                                 "feature_gather_s": round(t_feat, 3), "features": table_host is not None}
+
+
+def host_mem_gb():
+    try:
+        import psutil
+
+        return psutil.virtual_memory().available / 1e9
+    except Exception:
+        return 0.0
+
+
+# ---------------------------------------------------------------------------
+# Standalone SpMM (products-sized).
+# ---------------------------------------------------------------------------
+def bench_spmm(dev, steps):
+    import torch
+
+    from distributed_graph_flow_b200 import aggregation, synth
+
+    spec = synth.PRODUCTS_SPMM
+    rowptr, _, _ = synth.rowptr_and_edges(spec, dev, with_edges=False)
+    nnz = int(rowptr[-1].item())
+    col = synth.uniform_int(nnz, 0, spec.num_nodes, 3, 7, dev).to(torch.int32)
+    deg = (rowptr[1:] - rowptr[:-1]).clamp_min(1).to(torch.float32)
+    row_of = torch.repeat_interleave(torch.arange(spec.num_nodes, device=dev), rowptr[1:] - rowptr[:-1])
+    val = (1.0 / deg)[row_of].contiguous()
+    del row_of
+    F = 256
+    hbm, peak_kind = measured_peaks()
+    out = {"workload": "CSR SpMM 2,449,029 x 2,449,029, 61,859,140 nnz (Zipf 1.9 rows, max 17,000), x256, "
+                       "vals = 1/row_degree", "nnz": nnz}
+    ws = aggregation.spmm_workspace(spec.num_nodes, nnz, F, dev)
+    for dt, name in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
+        x = synth.normal_features(0, spec.num_nodes, F, 5, dt, dev)
+        y = torch.empty_like(x)
+        for _ in range(3):
+            aggregation.csr_spmm(rowptr, col, x, val=val, out=y, workspace=ws)
+        ms = timed(lambda i: aggregation.csr_spmm(rowptr, col, x, val=val, out=y, workspace=ws), steps,
+                   torch.cuda.synchronize)
+        e = x.element_size()
+        alg = 8 * (spec.num_nodes + 1) + nnz * 8 + nnz * F * e + spec.num_nodes * F * e
+        gbs = alg / ms / 1e6
+        out[name] = {"ms": round(ms, 3), "algorithmic_bytes": alg, "achieved_gbs": round(gbs, 1), "peak_gbs": hbm,
+                     "peak_kind": peak_kind, "frac": round(gbs / hbm, 4),
+                     "traffic": ncu_traffic().get(f"spmm_{name}", {}).get("bytes_per_launch")}
+        del x, y
+    # CPU baseline: scipy CSR @ dense on a bounded row sample (fp32).
+    try:
+        import scipy.sparse as sp
+
+        rows = 200_000
+        rp = rowptr[: rows + 1].cpu().numpy()
+        c = col[: rp[-1]].cpu().numpy()
+        v = val[: rp[-1]].cpu().numpy()
+        xh = synth.normal_features(0, spec.num_nodes, F, 5, torch.float32, dev).cpu().numpy()
+        a = sp.csr_matrix((v, c, rp), shape=(rows, spec.num_nodes))
+        t0 = time.perf_counter()
+        _ = a @ xh
+        dt = time.perf_counter() - t0
+        alg = 8 * (rows + 1) + len(c) * 8 + len(c) * F * 4 + rows * F * 4
+        out["cpu_baseline"] = {"value": round(alg / dt / 1e9, 2), "unit": "GB/s (same byte count)", "cores": 1,
+                               "kind": "scipy CSR @ dense (jax is not installed; scipy stands in)",
+                               "sample": f"first {rows} rows, fp32"}
+    except Exception as exc:  # noqa: BLE001
+        out["cpu_baseline"] = {"unavailable": str(exc)}
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Temporal 169K-node sampler.
+# ---------------------------------------------------------------------------
+def bench_temporal(dev, steps):
+    import torch
+
+    from distributed_graph_flow_b200 import _native, synth
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+    from distributed_graph_flow_b200.sampling import config as cfg
+
+    spec = synth.TEMPORAL_169K
+    index, ts, _ = synth.build_graph(spec, dev)
+    node_ts = synth.uniform_int(spec.num_nodes, 0, 50, spec.seed, 12, dev)
+    table = synth.normal_features(0, spec.num_nodes, FEAT_DIM, 9, torch.float32, dev)
+    plan = cfg.explicit_plan("v", "e", [10, 5])
+    cc = ext.create_device_sampler(plan, ["v"], [spec.num_nodes], ["e"], [index], [None], _native.MODE_RANDOM,
+                                   seed=3, has_temporal=True)
+    B = 1024
+    nb = 8 + steps
+    seeds = synth.uniform_int(nb * B, 0, spec.num_nodes, 21, 9, dev).view(nb, B)
+    sts = node_ts[seeds]
+    feats = torch.empty((B * cc.tree_size, FEAT_DIM), dtype=torch.float32, device=dev)
+
+    def step(i):
+        m = cc.sample_merged(seeds[i], sts[i], None, call_index=i, check=False)
+        rng = m.node_offsets[[0, -1]]
+        _native.check(_native.lib().dgfx_gather_rows_ranged(
+            _native.ptr(table), spec.num_nodes, FEAT_DIM * 4, _native.ptr(m.node_ids), _native.ptr(rng),
+            int(m.node_ids.numel()), _native.ptr(feats), _native.stream_handle()))
+
+    for i in range(5):
+        step(i)
+    cc.check()
+    ms = timed(lambda i: step(8 + i), steps, torch.cuda.synchronize)
+    cc.check()
+    out = {"workload": "temporal 169,343 nodes / 1,166,243 edges, Zipf(2.1), ts in [0,50), fanout [10,5], "
+                       "1024 seeds, cutoff = seed ts, fp32 128-d features",
+           "value": round(B / (ms / 1e3), 1), "unit": "subgraphs/s", "ms_per_step": round(ms, 4)}
+    # CPU baseline on the same graph and seeds.
+    try:
+        from oracle import oracle as O
+
+        s, kind = cpu_sampler_from_index(index, spec.num_nodes, plan, temporal=True)
+        th = host_cores()
+        host_tab = table.cpu().numpy()
+        seeds_h = seeds.cpu().numpy()
+        sts_h = sts.cpu().numpy()
+        done, t_tot = 0, 0.0
+        i = 0
+        while t_tot < 10.0 and i < nb:
+            t0 = time.perf_counter()
+            nc, ec, nodes, _, _ = s.sample_raw(seeds_h[i], sts_h[i], threads=th)
+            off = 0
+            for c in nc[:, 0]:
+                _ = host_tab[nodes[off:off + c]]
+                off += c
+            t_tot += time.perf_counter() - t0
+            done += B
+            i += 1
+            if i == nb:
+                i = 0
+        out["cpu_baseline"] = {"value": round(done / t_tot, 1), "unit": "subgraphs/s", "cores": th, "kind": kind,
+                               "sample": f"{done} seeds, topology + numpy feature gather"}
+        out["speedup_vs_cpu"] = round(out["value"] / out["cpu_baseline"]["value"], 1)
+    except Exception as exc:  # noqa: BLE001
+        out["cpu_baseline"] = {"unavailable": str(exc)}
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Reference arm: the reference's CPU sampler on the host cores.
+# ---------------------------------------------------------------------------
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return None
+    import torch
+
+    from distributed_graph_flow_b200 import synth
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    spec = large_spec(args.scale)
+    need_gb = 14 + 30
+    avail = host_mem_gb()
+    from distributed_graph_flow_b200.sampling import config as cfg
+
+    plan = cfg.explicit_plan("paper", "cites", FANOUT)
+    # Inputs (untimed): the same seeded graph, built on the device and copied
+    # to the host in CreateFromEdgeList order.
+    index, _, _ = synth.build_graph(spec, dev)
+    table_host = None
+    if avail > need_gb + 20:
+        table_host = synth.normal_features(0, spec.num_nodes, FEAT_DIM, spec.seed + 100, torch.bfloat16, dev).cpu().view(
+            torch.int16).numpy()
+    seeds = synth.uniform_int((args.warmup + args.steps) * B_SEEDS, 0, spec.num_nodes, 77, 5, dev).view(
+        -1, B_SEEDS).cpu().numpy()
+    budget = max(20.0, 12.0 * args.steps)
+    rate, cores, kind, sample = cpu_large_baseline(index, table_host, spec.num_nodes, plan, seeds, budget_s=budget)
+    res = {
+        "impl": "reference",
+        "metric": "sampled subgraphs/sec",
+        "value": round(rate, 1),
+        "unit": "subgraphs/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int64 ids / bf16 features",
+        "data": "synthetic (same seeded graph as the dgfx arm)",
+        "config": {"workload": "large sharded sampling: 111,059,956 nodes, 1,615,685,872 edges, Zipf(2.0), "
+                               "fanout [15,10,5], 8192 seeds/GPU, bf16 128-d features node-range partitioned",
+                   "host_mem_available_gb": round(avail, 1)},
+        "cpu_baseline": {"value": round(rate, 1), "unit": "subgraphs/s", "cores": cores, "kind": kind,
+                         "sample": json.dumps(sample)},
+        "e2e": {"value": round(rate, 1), "unit": "subgraphs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="dgfx", choices=["dgfx", "reference"])
+    ap.add_argument("--no-extras", action="store_true", help="skip the SpMM / temporal sub-benchmarks")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--scale", type=float, default=1.0, help="shrink the large workload (debugging only)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    import torch
+
+    if args.impl == "reference":
+        # Rank 0 alone times the reference's CPU sampler; other ranks exit.
+        if rank == 0:
+            print(json.dumps(reference_arm(args, rank, world)), flush=True)
+        return
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+
+    res, ctx = bench_large(args, rank, world, dev)
+    if rank == 0 and world == 1:
+        spec, index, table, cc, plan, seeds, W = ctx
+        if not args.no_cpu:
+            table_host = None
+            if host_mem_gb() > 80:
+                table_host = table.cpu().view(torch.int16).numpy()
+            try:
+                rate, cores, kind, sample = cpu_large_baseline(index, table_host, spec.num_nodes, plan,
+                                                               seeds.cpu().numpy(), budget_s=15.0)
+                res["cpu_baseline"] = {"value": round(rate, 1), "unit": "subgraphs/s", "cores": cores, "kind": kind,
+                                       "sample": json.dumps(sample)}
+            except Exception as exc:  # noqa: BLE001
+                res["cpu_baseline"] = {"unavailable": str(exc)}
+            del table_host
+        del ctx, index, table, cc
+        torch.cuda.empty_cache()
+        if not args.no_extras:
+            res["spmm"] = bench_spmm(dev, max(5, args.steps // 2))
+            torch.cuda.empty_cache()
+            res["temporal_169k"] = bench_temporal(dev, args.steps)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

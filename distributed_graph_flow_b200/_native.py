@@ -87,12 +87,21 @@ SIGNATURES = {
     "dgfx_sampler_output_capacity": (_int, [_vp, _i64, _p_i64, _p_i64]),
     "dgfx_sampler_sample": (_int, [_vp, _vp, _vp, _vp, _i64, _u64, ctypes.POINTER(SampleOut), _vp, _sz, _vp]),
     "dgfx_sampler_check": (_int, [_vp, _vp]),
+    "dgfx_sampler_stats": (_int, [_vp, _vp, _p_i64]),
     "dgfx_gather_rows": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "dgfx_gather_rows_ranged": (_int, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
     "dgfx_spmm_workspace_size": (_int, [_i64, _i64, _i64, ctypes.POINTER(_sz)]),
     "dgfx_spmm_csr": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _int, _vp, _int, _i64, _i32, _vp, _sz, _vp]),
     "dgfx_segment_sum_workspace_size": (_int, [_i64, _i64, _i64, ctypes.POINTER(_sz)]),
     "dgfx_segment_sum": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _int, _vp, _sz, _vp]),
+    "dgfx_halo_partition_workspace_size": (_int, [_i64, _i32, ctypes.POINTER(_sz)]),
+    "dgfx_halo_partition": (_int, [_vp, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "dgfx_gather_rows_local": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp]),
+    "dgfx_scatter_rows": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "dgfx_synth_graph_workspace_size": (_int, [_i64, ctypes.POINTER(_sz)]),
+    "dgfx_synth_graph": (_int, [_i64, _i64, ctypes.c_double, _i64, _u64, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "dgfx_synth_uniform_int": (_int, [_i64, _i64, _i64, _u64, ctypes.c_uint32, _vp, _vp]),
+    "dgfx_synth_normal_features": (_int, [_i64, _i64, _i64, _u64, _int, _vp, _vp]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

@@ -58,6 +58,25 @@ __device__ __forceinline__ void store_vec(__nv_bfloat16* p, const float* o) {
   *reinterpret_cast<uint4*>(p) = v;
 }
 
+// Stores V consecutive fp32 accumulators as YT (V = 4 or 8).
+template <int V>
+__device__ __forceinline__ void store_span(float* p, const float* o) {
+#pragma unroll
+  for (int q = 0; q < V; q += 4) store_vec(p + q, o + q);
+}
+template <int V>
+__device__ __forceinline__ void store_span(__nv_bfloat16* p, const float* o) {
+  if constexpr (V == 8) {
+    store_vec(p, o);
+  } else {
+    uint2 v;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+    h[0] = __floats2bfloat162_rn(o[0], o[1]);
+    h[1] = __floats2bfloat162_rn(o[2], o[3]);
+    *reinterpret_cast<uint2*>(p) = v;
+  }
+}
+
 template <class T> struct Vec;
 template <> struct Vec<float> { static constexpr int n = 4; };
 template <> struct Vec<__nv_bfloat16> { static constexpr int n = 8; };
@@ -165,7 +184,7 @@ spmm_kernel(const int64_t* __restrict__ rowptr, const int32_t* __restrict__ col,
           float o[V];
 #pragma unroll
           for (int q = 0; q < V; ++q) o[q] = acc[c][q] * scale;
-          store_vec(out + ch * V, o);
+          store_span<V>(out + ch * V, o);
         }
       }
     } else {

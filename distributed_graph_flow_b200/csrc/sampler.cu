@@ -91,7 +91,8 @@ struct Params {
   int32_t* edge_cnt;         // [ES][B]
   char* global_work;         // per-CTA arrays when not in shared memory
   size_t work_stride;
-  unsigned long long* status;  // [0] first bad seed slot, [1] ts missing, [2] table overflow
+  unsigned long long* status;  // [0] first bad seed slot, [1] ts missing, [2] table overflow,
+                               // [3..5] expanded rows, sampled neighbours, timestamp probes
 };
 
 // Per-CTA working arrays (shared or global memory).
@@ -123,8 +124,10 @@ __device__ __forceinline__ uint64_t draw64(const Params& p, int32_t q, int32_t e
 
 // One expansion task: pick up to k neighbours of node v over plan edge e and
 // write them to the child slots base + j * stride (j < k).
+// stats[0..2] (shared) count expanded rows, sampled neighbours and timestamp
+// probes of this CTA.
 __device__ void expand_task(const Params& p, const Work& w, int32_t q, int32_t e, int32_t base, int64_t v,
-                            bool has_ts, int64_t seed_ts, int64_t mask, uint32_t slot) {
+                            bool has_ts, int64_t seed_ts, int64_t mask, uint32_t slot, unsigned int* stats) {
   const EdgeDev E = p.edges[e];
   const int32_t k = E.k, stride = E.stride;
   int32_t cnt = 0;
@@ -142,12 +145,15 @@ __device__ void expand_task(const Params& p, const Work& w, int32_t q, int32_t e
     if (temporal && n > 0) {
       // upper_bound(ts[rb..re), seed_ts): first position with ts > seed_ts.
       int64_t lo = 0, hi = n;
+      unsigned int probes = 0;
       while (lo < hi) {
         const int64_t mid = (lo + hi) >> 1;
         if (E.ts[rb + mid] <= seed_ts) lo = mid + 1;
         else hi = mid;
+        ++probes;
       }
       n = lo;
+      atomicAdd(&stats[2], probes);
     }
     int64_t moff = -1;
     if (!temporal && mask >= 0 && E.edgeset == p.mask_edgeset && E.edge_pos != nullptr && mask < E.num_edges) {
@@ -156,6 +162,8 @@ __device__ void expand_task(const Params& p, const Work& w, int32_t q, int32_t e
     }
     const int64_t nv = n - (moff >= 0 ? 1 : 0);
     cnt = static_cast<int32_t>(nv < k ? nv : k);
+    atomicAdd(&stats[0], 1u);
+    atomicAdd(&stats[1], static_cast<unsigned int>(cnt));
     const int mode = (p.mode == DGFX_MODE_MOST_RECENT && !temporal) ? DGFX_MODE_RANDOM : p.mode;
     if (cnt > 0) {
       if (mode == DGFX_MODE_RANDOM && cnt < nv) {
@@ -228,6 +236,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   __shared__ int32_t ns_count[kMaxNodesets];
   __shared__ int32_t ns_base[kMaxNodesets];
   __shared__ int32_t es_count[kMaxEdgesets];
+  __shared__ unsigned int stats[3];
 
   const int64_t sample = blockIdx.x;
   const int T = p.T;
@@ -242,6 +251,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
 
   for (int i = threadIdx.x; i < p.num_nodesets; i += blockDim.x) ns_count[i] = 0;
   for (int i = threadIdx.x; i < p.num_edgesets; i += blockDim.x) es_count[i] = 0;
+  if (threadIdx.x < 3) stats[threadIdx.x] = 0;
   if (threadIdx.x == 0) {
     bool ok = true;
     if (p.root_has_children && (seed < 0 || seed >= p.root_num_src)) {
@@ -257,7 +267,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
     const int t0 = p.level[d], t1 = p.level[d + 1];
     for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
       const int4 task = p.tasks[t];
-      expand_task(p, w, task.x, task.y, task.z, w.node[task.x], has_ts, sts, mask, slot);
+      expand_task(p, w, task.x, task.y, task.z, w.node[task.x], has_ts, sts, mask, slot, stats);
     }
     __syncthreads();
   }
@@ -402,6 +412,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
 
   for (int s = threadIdx.x; s < p.num_nodesets; s += blockDim.x) p.node_cnt[s * p.B + sample] = ns_count[s];
   for (int e = threadIdx.x; e < p.num_edgesets; e += blockDim.x) p.edge_cnt[e * p.B + sample] = es_count[e];
+  if (threadIdx.x < 3) atomicAdd(&p.status[3 + threadIdx.x], static_cast<unsigned long long>(stats[threadIdx.x]));
 }
 
 // Merged batch from the per-seed scratch: one warp per seed.
@@ -640,7 +651,7 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
   if (!tasks.empty()) DGFX_CUDA_TRY(cudaMemcpy(s->d_tasks, tasks.data(), sizeof(int4) * tasks.size(), cudaMemcpyHostToDevice));
   DGFX_CUDA_TRY(cudaMemcpy(s->d_level, level.data(), sizeof(int32_t) * level.size(), cudaMemcpyHostToDevice));
   DGFX_CUDA_TRY(cudaMemcpy(s->d_pos, pos.data(), sizeof(int2) * pos.size(), cudaMemcpyHostToDevice));
-  const unsigned long long init[3] = {~0ull, 0ull, 0ull};
+  const unsigned long long init[6] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
   DGFX_CUDA_TRY(cudaMemcpy(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice));
 
   // Threads per CTA: enough for the bitonic sort's N2/2 pairs, 32..256.
@@ -700,7 +711,7 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   if (d_workspace == nullptr || workspace_bytes < sample_ws_bytes(s, B)) {
     return fail(DGFX_ERR_WORKSPACE, "dgfx_sampler_sample: workspace too small");
   }
-  const unsigned long long init[3] = {~0ull, 0ull, 0ull};
+  const unsigned long long init[6] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
   DGFX_CUDA_TRY(cudaMemcpyAsync(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice, stream));
   s->last_B = B;
   s->last_seeds = d_seeds;
@@ -778,5 +789,15 @@ extern "C" int dgfx_sampler_check(dgfx_sampler* s, dgfx_stream stream_) {
                 "SampleRandomUniformWithTimestamp instead.");
   }
   if (st[2] != 0) return fail(DGFX_ERR_INTERNAL, "sampler: dedup table overflow");
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_sampler_stats(dgfx_sampler* s, dgfx_stream stream_, int64_t* out3) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (s == nullptr || out3 == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_stats: null argument");
+  unsigned long long st[6];
+  DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
+  DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
+  for (int i = 0; i < 3; ++i) out3[i] = static_cast<int64_t>(st[3 + i]);
   return DGFX_OK;
 }

@@ -1,0 +1,122 @@
+"""Single-box multi-GPU sampling driver.
+
+Replaces the reference's Beam driver (dgf/src/sampling/
+beam_semi_distributed_sampler_v2.py:51-158, 200-268): one process per GPU,
+seed batches sharded across ranks, the graph topology replicated in every
+GPU's HBM, node features node-range partitioned (rank r owns rows
+[r * rows_per_rank, (r + 1) * rows_per_rank)). The only exchange is the halo
+feature gather, replacing the Beam CoGroupByKey feature join
+(beam_semi_distributed_sampler_v2.py:271-387):
+  1. requested ids are stably partitioned by owner (dgfx_halo_partition);
+  2. counts, ids and rows move in NCCL all-to-alls over NVLink/NVSwitch;
+  3. owners gather their rows locally (dgfx_gather_rows_local) and the
+     received rows are scattered back to request order (dgfx_scatter_rows).
+With one rank the exchange degenerates to a local gather.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+from distributed_graph_flow_b200 import _native
+
+
+class HaloFeatures:
+    """Node features partitioned by node range across the process group."""
+
+    def __init__(self, local_table, rows_per_rank: int, rank: int, world: int, group=None):
+        self.table = local_table  # [local_rows, F] on this rank's GPU
+        self.rows_per_rank = int(rows_per_rank)
+        self.rank = int(rank)
+        self.world = int(world)
+        self.group = group
+        self.row_bytes = local_table.element_size() * int(local_table.shape[1])
+        if self.row_bytes % 16:
+            raise ValueError("feature rows must be a multiple of 16 bytes")
+        self._ws = None
+
+    def _workspace(self, n: int):
+        torch = _native.require_cuda()
+        need = ctypes.c_size_t()
+        _native.check(_native.lib().dgfx_halo_partition_workspace_size(n, self.world, ctypes.byref(need)))
+        if self._ws is None or self._ws.numel() < need.value:
+            self._ws = torch.empty(need.value, dtype=torch.uint8, device=self.table.device)
+        return self._ws, need.value
+
+    def gather(self, ids, out=None, stream=None):
+        """Rows for int64 ids (global node ids) in request order."""
+        torch = _native.require_cuda()
+        import torch.distributed as dist
+
+        n = int(ids.numel())
+        dev = self.table.device
+        F = int(self.table.shape[1])
+        if out is None:
+            out = torch.empty((max(n, 1), F), dtype=self.table.dtype, device=dev)[:n]
+        sh = _native.stream_handle(stream)
+        lib = _native.lib()
+        if self.world == 1:
+            _native.check(lib.dgfx_gather_rows_local(_native.ptr(self.table), int(self.table.shape[0]), self.row_bytes,
+                                                     _native.ptr(ids), n, 0, _native.ptr(out), sh))
+            return out
+        sorted_ids = torch.empty(max(n, 1), dtype=torch.int64, device=dev)
+        perm = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+        send_counts = torch.empty(self.world, dtype=torch.int64, device=dev)
+        ws, nbytes = self._workspace(n)
+        _native.check(lib.dgfx_halo_partition(_native.ptr(ids), n, self.rows_per_rank, self.world,
+                                              _native.ptr(sorted_ids), _native.ptr(perm), _native.ptr(send_counts),
+                                              _native.ptr(ws), nbytes, sh))
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        sc = send_counts.tolist()
+        rc = recv_counts.tolist()
+        n_recv = int(sum(rc))
+        recv_ids = torch.empty(max(n_recv, 1), dtype=torch.int64, device=dev)[:n_recv]
+        dist.all_to_all_single(recv_ids, sorted_ids[:n], rc, sc, group=self.group)
+        rows = torch.empty((max(n_recv, 1), F), dtype=self.table.dtype, device=dev)[:n_recv]
+        _native.check(lib.dgfx_gather_rows_local(_native.ptr(self.table), int(self.table.shape[0]), self.row_bytes,
+                                                 _native.ptr(recv_ids), n_recv, self.rank * self.rows_per_rank,
+                                                 _native.ptr(rows), sh))
+        back = torch.empty((max(n, 1), F), dtype=self.table.dtype, device=dev)[:n]
+        dist.all_to_all_single(back, rows, sc, rc, group=self.group)
+        _native.check(lib.dgfx_scatter_rows(_native.ptr(back), n, self.row_bytes, _native.ptr(perm), _native.ptr(out), sh))
+        return out
+
+
+class ShardedSampler:
+    """Per-rank sampler over the replicated topology plus halo features.
+
+    ``step(seeds)`` samples this rank's seed shard (int64 device tensor) and
+    returns (merged batch, features of every sampled node in merged order,
+    number of sampled nodes)."""
+
+    def __init__(self, cc_sampler, features: Optional[HaloFeatures], rank: int, world: int):
+        self.cc = cc_sampler
+        self.features = features
+        self.rank = rank
+        self.world = world
+        self._calls = 0
+
+    def step(self, seeds, seed_ts=None, stream=None):
+        call = self._calls * self.world + self.rank  # distinct random stream per rank and call
+        self._calls += 1
+        merged = self.cc.sample_merged(seeds, seed_ts, None, stream=stream, call_index=call, check=False)
+        feats = None
+        total = None
+        if self.features is not None:
+            if self.world == 1:
+                # No host round trip: bounds of the gather are read on the device.
+                torch = _native.require_cuda()
+                cap = int(merged.node_ids.numel())
+                F = int(self.features.table.shape[1])
+                feats = torch.empty((cap, F), dtype=self.features.table.dtype, device=self.features.table.device)
+                rng = merged.node_offsets[[0, -1]]
+                _native.check(_native.lib().dgfx_gather_rows_ranged(
+                    _native.ptr(self.features.table), int(self.features.table.shape[0]), self.features.row_bytes,
+                    _native.ptr(merged.node_ids), _native.ptr(rng), cap, _native.ptr(feats),
+                    _native.stream_handle(stream)))
+            else:
+                total = int(merged.node_offsets[-1].item())
+                feats = self.features.gather(merged.node_ids[:total], stream=stream)
+        return merged, feats, total

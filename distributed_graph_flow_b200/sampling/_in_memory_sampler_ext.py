@@ -467,10 +467,38 @@ def CreateSampler(
                 fwd[e] = BuildAdjacencyIndex(es.adjacency, ts, False, ns_src, ns_dst, e == mask_idx)
             if need_bwd[e]:
                 bwd[e] = BuildAdjacencyIndex(es.adjacency, ts, True, ns_src, ns_dst, e == mask_idx)
+    mode = _native.MODE_FIRST if debug_sampling else _native.MODE_RANDOM
+    if sampling_mode is not None:
+        mode = int(sampling_mode)
+    return create_device_sampler(
+        plan, nodeset_names, num_nodes, edgeset_names, fwd, bwd, mode, seed, mask_idx,
+        has_temporal=bool(edgeset_timestamp_features), device=dev, plan_arrays=plan_arrays,
+    )
 
-        mode = _native.MODE_FIRST if debug_sampling else _native.MODE_RANDOM
-        if sampling_mode is not None:
-            mode = int(sampling_mode)
+
+def create_device_sampler(
+    plan,
+    nodeset_names: List[str],
+    num_nodes: List[int],
+    edgeset_names: List[str],
+    fwd: List[Optional[AdjacencyIndex]],
+    bwd: List[Optional[AdjacencyIndex]],
+    mode: int,
+    seed: Optional[int],
+    mask_idx: int = -1,
+    has_temporal: bool = False,
+    device=None,
+    plan_arrays: Optional[_PlanArrays] = None,
+) -> Sampler:
+    """Sampler over indices already resident in HBM (e.g. built on the device
+    from a generated edge list). Node/edge set lists are in index order."""
+    torch = _torch()
+    nodeset_index = {n: i for i, n in enumerate(nodeset_names)}
+    edgeset_index = {n: i for i, n in enumerate(edgeset_names)}
+    if plan_arrays is None:
+        plan_arrays = _PlanArrays(plan, nodeset_index, edgeset_index)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
         if seed is None or seed < 0:
             seed = int.from_bytes(os.urandom(8), "little") >> 1
         empty = _native.CsrView()
@@ -499,7 +527,7 @@ def CreateSampler(
     s._fwd = fwd
     s._bwd = bwd
     s._mask_edgeset = mask_idx
-    s._has_temporal = bool(edgeset_timestamp_features)
+    s._has_temporal = bool(has_temporal)
     s._mode = mode
     s._seed = seed
     s._root_nodeset = plan.root.nodeset

@@ -166,6 +166,13 @@ int dgfx_sampler_sample(dgfx_sampler* sampler, const int64_t* d_seeds,
  * of bounds. Should be lower than 4"). */
 int dgfx_sampler_check(dgfx_sampler* sampler, dgfx_stream stream);
 
+/* Work counters of the last dgfx_sampler_sample (synchronises `stream`):
+ * out3[0] = adjacency rows expanded, out3[1] = neighbours sampled,
+ * out3[2] = timestamp binary-search probes. They feed the algorithmic-byte
+ * count of the sampler's roofline. No reference counterpart. */
+int dgfx_sampler_stats(dgfx_sampler* sampler, dgfx_stream stream,
+                       int64_t* out3);
+
 /* ------------------------------------------------------------------------
  * Feature gather: out[i, :] = table[row_ids[i], :] for row_bytes-wide rows
  * (row_bytes a multiple of 16). Replaces add_features_to_samples'
@@ -217,6 +224,52 @@ int dgfx_segment_sum(const void* d_data, int data_dtype,
                      int32_t indices_are_sorted, void* d_out, int out_dtype,
                      void* d_workspace, size_t workspace_bytes,
                      dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Halo feature exchange (node-range-partitioned features across ranks).
+ * Replaces the Beam CoGroupByKey feature join of
+ * dgf/src/sampling/beam_semi_distributed_sampler_v2.py:271-387; the rows
+ * themselves move in one NCCL all-to-all issued by the host driver.
+ * dgfx_halo_partition: stable sort of requested ids by owner
+ * (owner = id / rows_per_rank, clamped to [0, world)); d_sorted_ids[j] =
+ * d_ids[d_perm[j]]; d_counts[w] = ids owned by rank w.
+ * dgfx_gather_rows_local: out[i] = table[ids[i] - id_base] (zero row if
+ * outside [0, local_rows)).
+ * dgfx_scatter_rows: out[perm[i]] = rows[i].
+ * ------------------------------------------------------------------------ */
+int dgfx_halo_partition_workspace_size(int64_t n, int32_t world, size_t* bytes);
+int dgfx_halo_partition(const int64_t* d_ids, int64_t n, int64_t rows_per_rank,
+                        int32_t world, int64_t* d_sorted_ids, uint32_t* d_perm,
+                        int64_t* d_counts, void* d_workspace,
+                        size_t workspace_bytes, dgfx_stream stream);
+int dgfx_gather_rows_local(const void* d_table, int64_t local_rows,
+                           int64_t row_bytes, const int64_t* d_ids, int64_t n,
+                           int64_t id_base, void* d_out, dgfx_stream stream);
+int dgfx_scatter_rows(const void* d_rows, int64_t n, int64_t row_bytes,
+                      const uint32_t* d_perm, void* d_out, dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Seeded synthetic inputs (stand-ins for the benchmark datasets, the role of
+ * the reference's dgf/src/util/gen_test_graph.py generators at scale).
+ * dgfx_synth_graph: power-law out-degrees (P(d) ~ d^-alpha, capped at
+ * max_degree, rescaled to exactly num_edges), power-law target popularity;
+ * writes rowptr int64[num_nodes + 1] and, if non-NULL, the source-major edge
+ * list src/dst int64[num_edges]. Pure function of its arguments.
+ * dgfx_synth_uniform_int: out[i] uniform in [lo, hi) (Philox stream id).
+ * dgfx_synth_normal_features: rows [node_begin, node_begin + count) of a
+ * N(0,1) [*, dim] matrix keyed by node id (partition independent).
+ * ------------------------------------------------------------------------ */
+int dgfx_synth_graph_workspace_size(int64_t num_nodes, size_t* bytes);
+int dgfx_synth_graph(int64_t num_nodes, int64_t num_edges, double alpha,
+                     int64_t max_degree, uint64_t seed, int64_t* d_rowptr,
+                     int64_t* d_src, int64_t* d_dst, void* d_workspace,
+                     size_t workspace_bytes, dgfx_stream stream);
+int dgfx_synth_uniform_int(int64_t n, int64_t lo, int64_t hi, uint64_t seed,
+                           uint32_t stream_id, int64_t* d_out,
+                           dgfx_stream stream);
+int dgfx_synth_normal_features(int64_t node_begin, int64_t count, int64_t dim,
+                               uint64_t seed, int dtype, void* d_out,
+                               dgfx_stream stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

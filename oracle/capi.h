@@ -93,6 +93,97 @@ void* oracle_sampler_create(int n_nodesets, const std::int64_t* num_nodes,
   return h.release();
 }
 
+// Same as oracle_sampler_create, but the plan's indices are given as
+// prebuilt CSR arrays (rowptr int64[n+1], col int32[E], optional ts
+// int64[E]) per edgeset and direction (NULL rowptr: not walked). Used to
+// time the CPU sampler on graphs too large to sort on the host; the arrays
+// must already be in CreateFromEdgeList order.
+void* oracle_sampler_create_csr(int n_nodesets, const std::int64_t* num_nodes, int n_edgesets,
+                                const std::int64_t* const* fwd_rowptr, const std::int32_t* const* fwd_col,
+                                const std::int64_t* const* fwd_ts, const std::int64_t* const* bwd_rowptr,
+                                const std::int32_t* const* bwd_col, const std::int64_t* const* bwd_ts,
+                                const std::int64_t* num_edges, int n_plan_nodes, const int* node_nodeset,
+                                const int* node_first_edge, const int* node_num_edges, int n_plan_edges,
+                                const int* edge_edgeset, const int* edge_reversed, const int* edge_hop_width,
+                                const int* edge_child, int with_replacement, int mode, int num_threads,
+                                std::int64_t seed, int has_temporal, int fill_threads) {
+  auto h = std::make_unique<OracleHandle>();
+  auto& s = h->sampler;
+  s.plan.with_replacement = with_replacement != 0;
+  for (int i = 0; i < n_plan_nodes; ++i) {
+    dgf_oracle::PlanNode n;
+    n.nodeset = node_nodeset[i];
+    for (int j = 0; j < node_num_edges[i]; ++j) n.edges.push_back(node_first_edge[i] + j);
+    s.plan.nodes.push_back(n);
+  }
+  for (int i = 0; i < n_plan_edges; ++i) {
+    s.plan.edges.push_back({edge_edgeset[i], edge_reversed[i] != 0, edge_hop_width[i], edge_child[i]});
+  }
+  s.num_nodes.assign(num_nodes, num_nodes + n_nodesets);
+  s.mode = mode;
+  s.has_temporal = has_temporal != 0;
+  s.num_threads = num_threads;
+  s.num_steps = s.plan.nodes.size();
+  s.edgesets.assign(n_edgesets, {});
+  const int nt = std::max(1, fill_threads);
+  auto fill = [&](const std::int64_t* rp, const std::int32_t* col, const std::int64_t* ts, std::size_t nrows,
+                  std::size_t ne) {
+    OracleIndex idx;
+    idx.source_blocks.resize(nrows + 1);
+    idx.target_node_idxs.resize(ne);
+    if (ts != nullptr) idx.timestamps.resize(ne);
+    std::vector<std::thread> pool;
+    for (int t = 0; t < nt; ++t) {
+      pool.emplace_back([&, t]() {
+        const std::size_t lo = ne * t / nt, hi = ne * (t + 1) / nt;
+        for (std::size_t i = lo; i < hi; ++i) idx.target_node_idxs[i] = static_cast<dgf_oracle::InputIdx>(col[i]);
+        if (ts != nullptr) {
+          for (std::size_t i = lo; i < hi; ++i) idx.timestamps[i] = ts[i];
+        }
+        const std::size_t rlo = (nrows + 1) * t / nt, rhi = (nrows + 1) * (t + 1) / nt;
+        for (std::size_t i = rlo; i < rhi; ++i) idx.source_blocks[i] = static_cast<dgf_oracle::InputIdx>(rp[i]);
+      });
+    }
+    for (auto& th : pool) th.join();
+    return idx;
+  };
+  for (int e = 0; e < n_edgesets; ++e) {
+    auto& es = s.edgesets[e];
+    for (const auto& pe : s.plan.edges) {
+      if (pe.edgeset != e) continue;
+      (pe.reversed ? es.need_bwd : es.need_fwd) = true;
+    }
+    // Row counts come from the plan's node sets.
+    for (int i = 0; i < n_plan_nodes; ++i) {
+      for (int j : s.plan.nodes[i].edges) {
+        const auto& pe = s.plan.edges[j];
+        if (pe.edgeset != e) continue;
+        const int here = s.plan.nodes[i].nodeset, there = s.plan.nodes[pe.child].nodeset;
+        es.src_ns = pe.reversed ? there : here;
+        es.dst_ns = pe.reversed ? here : there;
+      }
+    }
+    const std::size_t ne = static_cast<std::size_t>(num_edges[e]);
+    if (es.need_fwd) {
+      if (fwd_rowptr == nullptr || fwd_rowptr[e] == nullptr) {
+        g_oracle_error = "missing forward CSR";
+        return nullptr;
+      }
+      es.fwd = fill(fwd_rowptr[e], fwd_col[e], fwd_ts != nullptr ? fwd_ts[e] : nullptr, s.num_nodes[es.src_ns], ne);
+    }
+    if (es.need_bwd) {
+      if (bwd_rowptr == nullptr || bwd_rowptr[e] == nullptr) {
+        g_oracle_error = "missing backward CSR";
+        return nullptr;
+      }
+      es.bwd = fill(bwd_rowptr[e], bwd_col[e], bwd_ts != nullptr ? bwd_ts[e] : nullptr, s.num_nodes[es.dst_ns], ne);
+    }
+  }
+  if (seed >= 0) s.rng.seed(static_cast<std::uint64_t>(seed));
+  else s.rng.seed(std::random_device()());
+  return h.release();
+}
+
 void oracle_sampler_free(void* h) { delete static_cast<OracleHandle*>(h); }
 
 // Samples n seeds; keeps the results in the handle. Returns 0 on success,

@@ -66,6 +66,14 @@ def _lib(ref: bool) -> ctypes.CDLL:
             ctypes.c_int64, ctypes.c_int, ctypes.c_int,
         ]
         lib.oracle_sampler_free.argtypes = [ctypes.c_void_p]
+        _p32 = ctypes.POINTER(ctypes.c_int32)
+        lib.oracle_sampler_create_csr.restype = ctypes.c_void_p
+        lib.oracle_sampler_create_csr.argtypes = [
+            ctypes.c_int, _p64, ctypes.c_int, ctypes.POINTER(_p64), ctypes.POINTER(_p32), ctypes.POINTER(_p64),
+            ctypes.POINTER(_p64), ctypes.POINTER(_p32), ctypes.POINTER(_p64), _p64, ctypes.c_int, _pi, _pi, _pi,
+            ctypes.c_int, _pi, _pi, _pi, _pi, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int,
+            ctypes.c_int,
+        ]
         lib.oracle_sample.restype = ctypes.c_int
         lib.oracle_sample.argtypes = [ctypes.c_void_p, _p64, _p64, _p64, ctypes.c_int64, ctypes.c_int]
         lib.oracle_result_counts.argtypes = [ctypes.c_void_p, _p64, _p64]
@@ -215,6 +223,44 @@ class OracleSampler:
         )
         if not self.h:
             raise OracleError(_err(self.lib))
+
+    @classmethod
+    def from_csr(cls, num_nodes, nodesets, edgesets, csr_fwd, plan, mode=MODE_RANDOM, num_threads=0, seed=0,
+                 temporal=False, ref=False, fill_threads=8):
+        """Sampler over prebuilt forward CSR arrays {edgeset: (rowptr int64,
+        col int32, ts int64 | None)} already in CreateFromEdgeList order."""
+        self = cls.__new__(cls)
+        self.lib = _lib(ref)
+        self.nodesets = list(nodesets)
+        self.edgesets = list(edgesets)
+        ns_idx = {n: i for i, n in enumerate(self.nodesets)}
+        es_idx = {n: i for i, n in enumerate(self.edgesets)}
+        node_ns, first, num, e_es, e_rev, e_hw, e_child = _flatten_plan(plan, ns_idx, es_idx)
+        nn = np.asarray(num_nodes, np.int64)
+        self._keep = []
+        _p32 = ctypes.POINTER(ctypes.c_int32)
+        rps, cols, tss, counts = [], [], [], []
+        for name in self.edgesets:
+            rp, col, ts = csr_fwd[name]
+            rp = np.ascontiguousarray(rp, np.int64)
+            col = np.ascontiguousarray(col, np.int32)
+            ts = None if ts is None else np.ascontiguousarray(ts, np.int64)
+            self._keep += [rp, col, ts]
+            rps.append(rp.ctypes.data_as(_p64))
+            cols.append(col.ctypes.data_as(_p32))
+            tss.append(None if ts is None else ts.ctypes.data_as(_p64))
+            counts.append(len(col))
+        n_es = len(self.edgesets)
+        cnt = np.array(counts + [0], np.int64)
+        self.h = self.lib.oracle_sampler_create_csr(
+            len(self.nodesets), _p(nn), n_es, (_p64 * n_es)(*rps), (_p32 * n_es)(*cols), (_p64 * n_es)(*tss),
+            None, None, None, _p(cnt), len(node_ns), _ints(node_ns), _ints(first), _ints(num), len(e_es), _ints(e_es),
+            _ints(e_rev), _ints(e_hw), _ints(e_child), int(bool(plan.with_replacement)), int(mode), int(num_threads),
+            int(seed), int(bool(temporal)), int(fill_threads),
+        )
+        if not self.h:
+            raise OracleError(_err(self.lib))
+        return self
 
     def __del__(self):
         if getattr(self, "h", None):
