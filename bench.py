@@ -102,18 +102,21 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def timed(fn, steps, sync_fn, events=True):
-    """Device time (ms per call) of `steps` calls bracketed by syncs."""
+def timed(fn, steps, sync_fn, name="timed"):
+    """Device time (ms per call) of `steps` calls bracketed by syncs, inside
+    an NVTX range (so profilers can be restricted to the timed region)."""
     import torch
 
     sync_fn()
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push(name)
     s.record()
     for i in range(steps):
         fn(i)
     e.record()
     sync_fn()
+    torch.cuda.nvtx.range_pop()
     return s.elapsed_time(e) / steps
 
 
@@ -193,7 +196,7 @@ def bench_large(args, rank, world, dev):
     cc.check()
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
     clocks.start()
-    ms = timed(lambda i: sharded.step(seeds[W + i]), K, sync)
+    ms = timed(lambda i: sharded.step(seeds[W + i]), K, sync, "step")
     clk = clocks.stop()
     cc.check()
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -210,7 +213,8 @@ def bench_large(args, rank, world, dev):
     st = (ctypes_stats(cc))
 
     # Kernel-level timings on the same inputs (dominant kernels).
-    ms_sample = timed(lambda i: cc.sample_merged(seeds[W + i], call_index=10_000 + i, check=False), K, sync)
+    ms_sample = timed(lambda i: cc.sample_merged(seeds[W + i], call_index=10_000 + i, check=False), K, sync,
+                      "kernel_sampler")
     st = ctypes_stats(cc)
     ms_gather = None
     if world == 1:
@@ -223,7 +227,7 @@ def bench_large(args, rank, world, dev):
                 _native.ptr(table), int(table.shape[0]), FEAT_DIM * 2, _native.ptr(merged.node_ids), _native.ptr(rng),
                 cap, _native.ptr(out), _native.stream_handle()))
 
-        ms_gather = timed(g, K, sync)
+        ms_gather = timed(g, K, sync, "kernel_gather")
 
     hbm, peak_kind = measured_peaks()
     # Algorithmic bytes per launch.
@@ -243,9 +247,11 @@ def bench_large(args, rank, world, dev):
             "traffic": traffic}
 
     # End to end through the public API with host buffers.
-    e2e = bench_large_e2e(sharded, seeds, W, K, dev, world, sync)
-
-    launches, all_k = count_dgfx_launches(lambda: sharded.step(seeds[W]))
+    if args.minimal:
+        e2e, launches = None, 0
+    else:
+        e2e = bench_large_e2e(sharded, seeds, W, K, dev, world, sync)
+        launches, _ = count_dgfx_launches(lambda: sharded.step(seeds[W]))
     res = {
         "metric": "sampled subgraphs/sec",
         "value": round(value, 1),
@@ -318,7 +324,7 @@ def bench_large_e2e(sharded, seeds_dev, W, K, dev, world, sync):
     moved["h2d"] = moved["d2h"] = 0
     sync()
     t0 = time.perf_counter()
-    ms = timed(one, K, sync)
+    ms = timed(one, K, sync, "e2e")
     wall = (time.perf_counter() - t0) * 1e3 / K
     t = torch.tensor([max(ms, wall)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -400,12 +406,21 @@ def host_mem_gb():
 # ---------------------------------------------------------------------------
 # Standalone SpMM (products-sized).
 # ---------------------------------------------------------------------------
-def bench_spmm(dev, steps):
+def _scaled(spec, scale):
+    import dataclasses
+
+    if scale == 1.0:
+        return spec
+    return dataclasses.replace(spec, num_nodes=max(1000, int(spec.num_nodes * scale)),
+                               num_edges=int(spec.num_edges * scale))
+
+
+def bench_spmm(dev, steps, scale=1.0):
     import torch
 
     from distributed_graph_flow_b200 import aggregation, synth
 
-    spec = synth.PRODUCTS_SPMM
+    spec = _scaled(synth.PRODUCTS_SPMM, scale)
     rowptr, _, _ = synth.rowptr_and_edges(spec, dev, with_edges=False)
     nnz = int(rowptr[-1].item())
     col = synth.uniform_int(nnz, 0, spec.num_nodes, 3, 7, dev).to(torch.int32)
@@ -424,7 +439,7 @@ def bench_spmm(dev, steps):
         for _ in range(3):
             aggregation.csr_spmm(rowptr, col, x, val=val, out=y, workspace=ws)
         ms = timed(lambda i: aggregation.csr_spmm(rowptr, col, x, val=val, out=y, workspace=ws), steps,
-                   torch.cuda.synchronize)
+                   torch.cuda.synchronize, f"spmm_{name}")
         e = x.element_size()
         alg = 8 * (spec.num_nodes + 1) + nnz * 8 + nnz * F * e + spec.num_nodes * F * e
         gbs = alg / ms / 1e6
@@ -457,14 +472,14 @@ def bench_spmm(dev, steps):
 # ---------------------------------------------------------------------------
 # Temporal 169K-node sampler.
 # ---------------------------------------------------------------------------
-def bench_temporal(dev, steps):
+def bench_temporal(dev, steps, scale=1.0):
     import torch
 
     from distributed_graph_flow_b200 import _native, synth
     from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
     from distributed_graph_flow_b200.sampling import config as cfg
 
-    spec = synth.TEMPORAL_169K
+    spec = _scaled(synth.TEMPORAL_169K, scale)
     index, ts, _ = synth.build_graph(spec, dev)
     node_ts = synth.uniform_int(spec.num_nodes, 0, 50, spec.seed, 12, dev)
     table = synth.normal_features(0, spec.num_nodes, FEAT_DIM, 9, torch.float32, dev)
@@ -487,7 +502,7 @@ def bench_temporal(dev, steps):
     for i in range(5):
         step(i)
     cc.check()
-    ms = timed(lambda i: step(8 + i), steps, torch.cuda.synchronize)
+    ms = timed(lambda i: step(8 + i), steps, torch.cuda.synchronize, "temporal")
     cc.check()
     out = {"workload": "temporal 169,343 nodes / 1,166,243 edges, Zipf(2.1), ts in [0,50), fanout [10,5], "
                        "1024 seeds, cutoff = seed ts, fp32 128-d features",
@@ -583,7 +598,11 @@ def main():
     ap.add_argument("--impl", default="dgfx", choices=["dgfx", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the SpMM / temporal sub-benchmarks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
-    ap.add_argument("--scale", type=float, default=1.0, help="shrink the large workload (debugging only)")
+    ap.add_argument("--scale", type=float, default=1.0, help="shrink the workload (profiling / debugging only)")
+    ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal"],
+                    help="run one workload and skip the rest (profiling)")
+    ap.add_argument("--minimal", action="store_true",
+                    help="timed steps only: no e2e leg, launch count or CPU baseline (for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -606,8 +625,14 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
 
+    if args.only in ("spmm", "temporal"):
+        # Single sub-benchmark (used for focused profiler captures).
+        fn = bench_spmm if args.only == "spmm" else bench_temporal
+        print(json.dumps(fn(dev, args.steps, args.scale)), flush=True)
+        return
+
     res, ctx = bench_large(args, rank, world, dev)
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.only is None:
         spec, index, table, cc, plan, seeds, W = ctx
         if not args.no_cpu:
             table_host = None

@@ -41,6 +41,7 @@
 #include <algorithm>
 #include <cstring>
 #include <functional>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -415,6 +416,21 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   if (threadIdx.x < 3) atomicAdd(&p.status[3 + threadIdx.x], static_cast<unsigned long long>(stats[threadIdx.x]));
 }
 
+// Largest row length of an index (the cap on useful slots per plan edge).
+__global__ void max_degree_kernel(const int64_t* __restrict__ rowptr, int64_t n, unsigned long long* out) {
+  unsigned long long m = 0;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const unsigned long long d = static_cast<unsigned long long>(rowptr[i + 1] - rowptr[i]);
+    m = d > m ? d : m;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, m, o);
+    m = x > m ? x : m;
+  }
+  if ((threadIdx.x & 31) == 0) atomicMax(out, m);
+}
+
 // Merged batch from the per-seed scratch: one warp per seed.
 __global__ void compact_kernel(Params p, const int64_t* __restrict__ node_off, const int64_t* __restrict__ edge_off,
                                int root_ns, int64_t* __restrict__ node_ids, int64_t* __restrict__ edge_src,
@@ -554,6 +570,32 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
   s->seed = seed;
   s->root_ns = node_nodeset[0];
 
+  // Slots per plan edge: hop_width capped by the largest row of the index it
+  // walks (no row can yield more), which keeps wide fanouts compact.
+  std::vector<int32_t> slots(num_plan_edges);
+  {
+    std::map<const int64_t*, int64_t> max_deg;
+    unsigned long long* d_max = nullptr;
+    for (int j = 0; j < num_plan_edges; ++j) {
+      const dgfx_csr_view& v = edge_reversed[j] ? backward[edge_edgeset[j]] : forward[edge_edgeset[j]];
+      auto it = max_deg.find(v.rowptr);
+      if (it == max_deg.end()) {
+        if (d_max == nullptr) DGFX_CUDA_TRY(cudaMalloc(&d_max, sizeof(unsigned long long)));
+        DGFX_CUDA_TRY(cudaMemset(d_max, 0, sizeof(unsigned long long)));
+        if (v.num_src > 0) {
+          const int64_t blocks = std::min<int64_t>(ceil_div(v.num_src, 256), 148 * 16);
+          max_degree_kernel<<<static_cast<unsigned>(blocks), 256>>>(v.rowptr, v.num_src, d_max);
+          DGFX_CUDA_TRY(cudaGetLastError());
+        }
+        unsigned long long m = 0;
+        DGFX_CUDA_TRY(cudaMemcpy(&m, d_max, sizeof(m), cudaMemcpyDeviceToHost));
+        it = max_deg.emplace(v.rowptr, static_cast<int64_t>(m)).first;
+      }
+      slots[j] = static_cast<int32_t>(std::min<int64_t>(edge_hop_width[j], it->second));
+    }
+    if (d_max != nullptr) cudaFree(d_max);
+  }
+
   // Padded subtree sizes Z(p): memoised recursion with a cycle guard.
   std::vector<int64_t> Z(num_plan_nodes, -1);
   std::vector<int> state(num_plan_nodes, 0);
@@ -566,7 +608,7 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
       const int j = node_first_edge[pn] + c;
       const int64_t zc = size_of(edge_child[j]);
       if (zc < 0) return -1;
-      z += static_cast<int64_t>(edge_hop_width[j]) * zc;
+      z += static_cast<int64_t>(slots[j]) * zc;
       if (z > kMaxPositions) return -1;
     }
     state[pn] = 2;
@@ -596,8 +638,8 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
       const int64_t zc = Z[edge_child[j]];
       if (static_cast<int>(tasks_by_depth.size()) <= depth) tasks_by_depth.resize(depth + 1);
       tasks_by_depth[depth].push_back(make_int4(static_cast<int>(q), j, static_cast<int>(off), 0));
-      for (int k = 0; k < edge_hop_width[j]; ++k) place(edge_child[j], off + k * zc, q, j, depth + 1);
-      off += static_cast<int64_t>(edge_hop_width[j]) * zc;
+      for (int k = 0; k < slots[j]; ++k) place(edge_child[j], off + k * zc, q, j, depth + 1);
+      off += static_cast<int64_t>(slots[j]) * zc;
     }
   };
   place(0, 0, -1, -1, 0);
@@ -624,7 +666,7 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
     E.ts = v.ts;
     E.edge_pos = (edge_edgeset[j] == edgeset_to_mask) ? v.edge_pos : nullptr;
     E.num_edges = v.num_edges;
-    E.k = edge_hop_width[j];
+    E.k = slots[j];
     E.stride = static_cast<int32_t>(Z[edge_child[j]]);
     E.edgeset = edge_edgeset[j];
     E.reversed = edge_reversed[j] != 0;
