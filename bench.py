@@ -218,14 +218,14 @@ def bench_large(args, rank, world, dev):
     st = ctypes_stats(cc)
     ms_gather = None
     if world == 1:
-        rng = merged.node_offsets[[0, -1]]
+        off = merged.node_offsets
         cap = int(merged.node_ids.numel())
         out = torch.empty((cap, FEAT_DIM), dtype=torch.bfloat16, device=dev)
 
         def g(_):
             _native.check(_native.lib().dgfx_gather_rows_ranged(
-                _native.ptr(table), int(table.shape[0]), FEAT_DIM * 2, _native.ptr(merged.node_ids), _native.ptr(rng),
-                cap, _native.ptr(out), _native.stream_handle()))
+                _native.ptr(table), int(table.shape[0]), FEAT_DIM * 2, _native.ptr(merged.node_ids),
+                _native.elem_ptr(off, 0), _native.elem_ptr(off, -1), cap, _native.ptr(out), _native.stream_handle()))
 
         ms_gather = timed(g, K, sync, "kernel_gather")
 
@@ -494,10 +494,10 @@ def bench_temporal(dev, steps, scale=1.0):
 
     def step(i):
         m = cc.sample_merged(seeds[i], sts[i], None, call_index=i, check=False)
-        rng = m.node_offsets[[0, -1]]
+        off = m.node_offsets
         _native.check(_native.lib().dgfx_gather_rows_ranged(
-            _native.ptr(table), spec.num_nodes, FEAT_DIM * 4, _native.ptr(m.node_ids), _native.ptr(rng),
-            int(m.node_ids.numel()), _native.ptr(feats), _native.stream_handle()))
+            _native.ptr(table), spec.num_nodes, FEAT_DIM * 4, _native.ptr(m.node_ids), _native.elem_ptr(off, 0),
+            _native.elem_ptr(off, -1), int(m.node_ids.numel()), _native.ptr(feats), _native.stream_handle()))
 
     for i in range(5):
         step(i)

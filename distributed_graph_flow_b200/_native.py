@@ -89,7 +89,7 @@ SIGNATURES = {
     "dgfx_sampler_check": (_int, [_vp, _vp]),
     "dgfx_sampler_stats": (_int, [_vp, _vp, _p_i64]),
     "dgfx_gather_rows": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
-    "dgfx_gather_rows_ranged": (_int, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
+    "dgfx_gather_rows_ranged": (_int, [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp]),
     "dgfx_spmm_workspace_size": (_int, [_i64, _i64, _i64, ctypes.POINTER(_sz)]),
     "dgfx_spmm_csr": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _int, _vp, _int, _i64, _i32, _vp, _sz, _vp]),
     "dgfx_segment_sum_workspace_size": (_int, [_i64, _i64, _i64, ctypes.POINTER(_sz)]),
@@ -159,3 +159,10 @@ def stream_handle(stream=None) -> int:
 def ptr(t) -> Optional[int]:
     """Device pointer of a torch tensor (None passes NULL)."""
     return None if t is None else int(t.data_ptr())
+
+
+def elem_ptr(t, i: int) -> int:
+    """Device pointer of element i of a 1-D tensor (negative i counts from the end)."""
+    if i < 0:
+        i += t.numel()
+    return int(t.data_ptr()) + i * t.element_size()

@@ -101,9 +101,29 @@ __global__ void spmm_fill_kernel(const int64_t* __restrict__ task_off, int64_t r
 }
 
 // ---- main kernel ----------------------------------------------------------
-// CPL = 16-byte chunks per lane (feature slice per warp = 32 * CPL * VEC).
-template <class XT, class YT, int CPL>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+// CPL = 16-byte chunks per lane (feature slice per warp = 32 * CPL * VEC);
+// U = gathered rows kept in flight per warp. Chunks stay raw (uint4) in
+// registers until their FMA so U * CPL loads fit in 64 registers, which keeps
+// four 256-thread CTAs (32 warps) resident per SM. The next 32 (col, val)
+// pairs are fetched while the current ones are consumed.
+__device__ __forceinline__ void unpack(const uint4& r, float* o, const float*) {
+  o[0] = __uint_as_float(r.x);
+  o[1] = __uint_as_float(r.y);
+  o[2] = __uint_as_float(r.z);
+  o[3] = __uint_as_float(r.w);
+}
+__device__ __forceinline__ void unpack(const uint4& r, float* o, const __nv_bfloat16*) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    o[2 * i] = f.x;
+    o[2 * i + 1] = f.y;
+  }
+}
+
+template <class XT, class YT, int CPL, int U>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 3)
 spmm_kernel(const int64_t* __restrict__ rowptr, const int32_t* __restrict__ col, const float* __restrict__ val,
             const XT* __restrict__ X, YT* __restrict__ Y, int64_t feat, int64_t f0, int64_t fw,
             const int64_t* __restrict__ task_off, const int32_t* __restrict__ task_row,
@@ -114,6 +134,16 @@ spmm_kernel(const int64_t* __restrict__ rowptr, const int32_t* __restrict__ col,
   const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
   const int64_t ntasks = task_off[rows];
   const int nchunks = static_cast<int>(fw / V);
+  auto fetch = [&](int64_t base, int64_t e, int32_t& c, float& w) {
+    const int64_t idx = base + lane;
+    const bool ok = idx < e;
+    c = ok ? (col != nullptr ? col[idx] : static_cast<int32_t>(idx)) : 0;
+    w = ok ? (val != nullptr ? val[idx] : 1.f) : 0.f;
+    if (c < 0 || c >= num_cols) {  // out-of-range column: no contribution
+      c = 0;
+      w = 0.f;
+    }
+  };
   for (int64_t t = blockIdx.x * static_cast<int64_t>(kWarpsPerBlock) + (threadIdx.x >> 5); t < ntasks; t += warps) {
     const int64_t r = task_row[t];
     const int64_t j = t - task_off[r];
@@ -125,52 +155,49 @@ spmm_kernel(const int64_t* __restrict__ rowptr, const int32_t* __restrict__ col,
     for (int c = 0; c < CPL; ++c)
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[c][i] = 0.f;
+    int32_t my_col;
+    float my_val;
+    fetch(b, e, my_col, my_val);
     for (int64_t base = b; base < e; base += 32) {
       const int m = static_cast<int>(e - base < 32 ? e - base : 32);
-      const int64_t idx = base + lane;
-      int32_t my_col = lane < m ? (col != nullptr ? col[idx] : static_cast<int32_t>(idx)) : 0;
-      float my_val = lane < m ? (val != nullptr ? val[idx] : 1.f) : 0.f;
-      if (my_col < 0 || my_col >= num_cols) {  // out-of-range column: no contribution
-        my_col = 0;
-        my_val = 0.f;
-      }
-      int i = 0;
-      for (; i + 4 <= m; i += 4) {
-        float x[4][CPL][V];
-        float wv[4];
+      int32_t nx_col;
+      float nx_val;
+      fetch(base + 32, e, nx_col, nx_val);
+      for (int i = 0; i < m; i += U) {
+        uint4 raw[U][CPL];
+        float wv[U];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int64_t cc = __shfl_sync(0xffffffffu, my_col, i + u);
-          wv[u] = __shfl_sync(0xffffffffu, my_val, i + u);
-          const XT* row = X + cc * feat + f0;
+        for (int u = 0; u < U; ++u) {
+          const int src = (i + u) & 31;
+          const int64_t cc = __shfl_sync(0xffffffffu, my_col, src);
+          wv[u] = __shfl_sync(0xffffffffu, my_val, src);
+          if (i + u < m) {
+            const uint4* row = reinterpret_cast<const uint4*>(X + cc * feat + f0);
 #pragma unroll
-          for (int c = 0; c < CPL; ++c) {
-            const int ch = lane + 32 * c;
-            if (ch < nchunks) load_vec(row + ch * V, x[u][c]);
+            for (int c = 0; c < CPL; ++c) {
+              const int ch = lane + 32 * c;
+              if (ch < nchunks) raw[u][c] = __ldg(row + ch);
+            }
           }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < U; ++u) {
+          if (i + u < m) {
 #pragma unroll
-          for (int c = 0; c < CPL; ++c)
+            for (int c = 0; c < CPL; ++c) {
+              const int ch = lane + 32 * c;
+              if (ch < nchunks) {
+                float x[V];
+                unpack(raw[u][c], x, X);
 #pragma unroll
-            for (int q = 0; q < V; ++q) acc[c][q] = fmaf(wv[u], x[u][c][q], acc[c][q]);
-      }
-      for (; i < m; ++i) {
-        const int64_t cc = __shfl_sync(0xffffffffu, my_col, i);
-        const float wv = __shfl_sync(0xffffffffu, my_val, i);
-        const XT* row = X + cc * feat + f0;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          const int ch = lane + 32 * c;
-          if (ch < nchunks) {
-            float x[V];
-            load_vec(row + ch * V, x);
-#pragma unroll
-            for (int q = 0; q < V; ++q) acc[c][q] = fmaf(wv, x[q], acc[c][q]);
+                for (int q = 0; q < V; ++q) acc[c][q] = fmaf(wv[u], x[q], acc[c][q]);
+              }
+            }
           }
         }
       }
+      my_col = nx_col;
+      my_val = nx_val;
     }
     const int64_t ntask_r = task_off[r + 1] - task_off[r];
     if (ntask_r == 1) {
@@ -304,13 +331,13 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ table, int64_t num_
   }
 }
 
-// Rows [range[0], range[1]) of ids (bounds read on the device, at most
-// max_rows): out[i] = table[ids[range[0] + i]].
+// Rows [*begin, *end) of ids (bounds read on the device, at most max_rows):
+// out[i] = table[ids[*begin + i]].
 __global__ void gather_rows_ranged_kernel(const uint4* __restrict__ table, int64_t num_table_rows, int64_t vec_per_row,
-                                          const int64_t* __restrict__ ids, const int64_t* __restrict__ range,
-                                          int64_t max_rows, uint4* __restrict__ out) {
-  const int64_t lo = range[0];
-  int64_t n = range[1] - lo;
+                                          const int64_t* __restrict__ ids, const int64_t* __restrict__ begin,
+                                          const int64_t* __restrict__ end, int64_t max_rows, uint4* __restrict__ out) {
+  const int64_t lo = *begin;
+  int64_t n = *end - lo;
   n = n < max_rows ? n : max_rows;
   const int64_t total = n * vec_per_row;
   for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < total;
@@ -378,24 +405,24 @@ int launch_spmm(const int64_t* rowptr, const int32_t* col, const float* val, int
                 const void* x, void* y, int64_t feat, int normalize, const SpmmBufs& b, cudaStream_t stream, int xdtype) {
   constexpr int V = Vec<XT>::n;
   const int64_t fb = feat_block(feat, xdtype);
-  const unsigned grid = static_cast<unsigned>(sm_count() * 8);
+  const unsigned grid = static_cast<unsigned>(sm_count() * 3);  // persistent: 3 resident CTAs per SM
   for (int64_t f0 = 0; f0 < feat; f0 += fb) {
     const int64_t fw = std::min(fb, feat - f0);
     const int64_t chunks = fw / V;
     const XT* X = static_cast<const XT*>(x);
     YT* Y = static_cast<YT*>(y);
     if (chunks <= 32) {
-      spmm_kernel<XT, YT, 1><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
-                                                                        b.task_off, b.task_row, b.split_off,
-                                                                        b.partial, rows, normalize, num_cols);
+      spmm_kernel<XT, YT, 1, 8><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
+                                                                           b.task_off, b.task_row, b.split_off,
+                                                                           b.partial, rows, normalize, num_cols);
     } else if (chunks <= 64) {
-      spmm_kernel<XT, YT, 2><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
-                                                                        b.task_off, b.task_row, b.split_off,
-                                                                        b.partial, rows, normalize, num_cols);
+      spmm_kernel<XT, YT, 2, 4><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
+                                                                           b.task_off, b.task_row, b.split_off,
+                                                                           b.partial, rows, normalize, num_cols);
     } else {
-      spmm_kernel<XT, YT, 4><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
-                                                                        b.task_off, b.task_row, b.split_off,
-                                                                        b.partial, rows, normalize, num_cols);
+      spmm_kernel<XT, YT, 4, 2><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
+                                                                           b.task_off, b.task_row, b.split_off,
+                                                                           b.partial, rows, normalize, num_cols);
     }
     DGFX_CUDA_TRY(cudaGetLastError());
     spmm_fixup_kernel<YT><<<grid_for(rows * 32, 256), 256, 0, stream>>>(rowptr, b.split_off, b.partial, Y, rows,
@@ -430,10 +457,11 @@ extern "C" int dgfx_gather_rows(const void* d_table, int64_t num_table_rows, int
 }
 
 extern "C" int dgfx_gather_rows_ranged(const void* d_table, int64_t num_table_rows, int64_t row_bytes,
-                                       const int64_t* d_row_ids, const int64_t* d_range, int64_t max_rows,
-                                       void* d_out, dgfx_stream stream_) {
+                                       const int64_t* d_row_ids, const int64_t* d_begin, const int64_t* d_end,
+                                       int64_t max_rows, void* d_out, dgfx_stream stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  if (row_bytes <= 0 || row_bytes % 16 != 0 || max_rows < 0 || num_table_rows < 0 || d_range == nullptr) {
+  if (row_bytes <= 0 || row_bytes % 16 != 0 || max_rows < 0 || num_table_rows < 0 || d_begin == nullptr ||
+      d_end == nullptr) {
     return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_gather_rows_ranged: bad arguments");
   }
   if (max_rows == 0) return DGFX_OK;
@@ -442,7 +470,7 @@ extern "C" int dgfx_gather_rows_ranged(const void* d_table, int64_t num_table_ro
   }
   const int64_t vpr = row_bytes / 16;
   gather_rows_ranged_kernel<<<grid_for(max_rows * vpr, 256), 256, 0, stream>>>(
-      static_cast<const uint4*>(d_table), num_table_rows, vpr, d_row_ids, d_range, max_rows,
+      static_cast<const uint4*>(d_table), num_table_rows, vpr, d_row_ids, d_begin, d_end, max_rows,
       static_cast<uint4*>(d_out));
   DGFX_CUDA_TRY(cudaGetLastError());
   return DGFX_OK;

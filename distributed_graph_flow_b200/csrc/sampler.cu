@@ -23,12 +23,13 @@
 //   2. relabel: hash table keyed by (nodeset, node) keeps the minimum position
 //      (atomicMin), then a block scan numbers first discoveries per nodeset
 //      (with_replacement: every occupied position is a new node);
-//   3. edges: one 64-bit key (edgeset, src_local, dst_local) per occupied
-//      non-root position, bitonic-sorted in the block, then deduplicated; this
-//      equals the reference's btree_set iteration order;
+//   3. edges: one key (edgeset | src_local | dst_local) per occupied non-root
+//      position, sorted by a block-level stable LSD radix sort (8 bits per
+//      pass, ceil((bits(#edgesets) + 2 * bits(T)) / 8) passes) and
+//      deduplicated; this equals the reference's btree_set iteration order;
 //   4. per-seed results go to a scratch slice; two scans and a compaction
 //      kernel produce the merged batch.
-// Arrays live in shared memory when the tree is small enough (T <= 4096),
+// Arrays live in shared memory when the tree is small enough (T <= 8192),
 // otherwise in a per-CTA slice of the workspace.
 //
 // Random mode draws from Philox4x32-10 keyed by the sampler seed with counter
@@ -55,7 +56,7 @@ namespace {
 constexpr uint64_t kEmptyKey = ~0ull;
 constexpr int kMaxNodesets = 64;
 constexpr int kMaxEdgesets = 256;
-constexpr int kMaxSmemPositions = 4096;
+constexpr int kMaxSmemPositions = 8192;
 constexpr int64_t kMaxPositions = int64_t(1) << 24;
 
 struct EdgeDev {
@@ -94,27 +95,37 @@ struct Params {
   size_t work_stride;
   unsigned long long* status;  // [0] first bad seed slot, [1] ts missing, [2] table overflow,
                                // [3..5] expanded rows, sampled neighbours, timestamp probes
+  int32_t pbits;               // bits of a local id (local ids < T <= 2^pbits)
+  int32_t keybits;             // bits of an edge sort key (edgeset | src | dst)
+  uint32_t ns_key_base[kMaxNodesets];  // node set offsets of the 32-bit dedup keys
 };
 
-// Per-CTA working arrays (shared or global memory).
+// Per-CTA working arrays (shared or global memory). The dedup table packs
+// (key << 32 | minimum position) into one 64-bit word per slot; after the
+// relabel the same words hold the edge sort keys and their sort buffer
+// (2 * T <= H words).
 struct Work {
-  int32_t* node;    // [T]
-  int32_t* local;   // [T]
-  uint64_t* hkey;   // [H]   (reused as the edge-key array, N2 <= H)
-  int32_t* hval;    // [H]
+  unsigned long long* slot;  // [H]
+  int32_t* node;             // [T]
+  int32_t* local;            // [T]
 };
 
 __host__ __device__ inline size_t work_bytes(int T, int H) {
-  return static_cast<size_t>(T) * 8 + static_cast<size_t>(H) * 12 + 64;
+  return static_cast<size_t>(H) * 8 + static_cast<size_t>(T) * 8 + 64;
 }
 
 __device__ inline Work carve_work(char* base, int T, int H) {
   Work w;
-  w.hkey = reinterpret_cast<uint64_t*>(base);
-  w.hval = reinterpret_cast<int32_t*>(base + static_cast<size_t>(H) * 8);
-  w.node = reinterpret_cast<int32_t*>(base + static_cast<size_t>(H) * 12);
+  w.slot = reinterpret_cast<unsigned long long*>(base);
+  w.node = reinterpret_cast<int32_t*>(base + static_cast<size_t>(H) * 8);
   w.local = w.node + T;
   return w;
+}
+
+// Shared memory of one CTA: radix-sort counters, then (if the tree fits)
+// the working arrays.
+__host__ __device__ inline size_t counter_bytes(int threads) {
+  return static_cast<size_t>(threads / 32) * 256 * 4 + 256 * 4;
 }
 
 __device__ __forceinline__ uint64_t draw64(const Params& p, int32_t q, int32_t e, uint32_t m, uint32_t slot) {
@@ -231,6 +242,83 @@ __device__ uint64_t block_scan_items(int n, V value, S sink, uint64_t* smem33) {
   return total;
 }
 
+// Stable LSD radix sort of n 64-bit keys (bits [0, nbits)) by one CTA, 8 bits
+// per pass. Warp w owns items [w * chunk, (w + 1) * chunk), visited in rounds
+// of 32 consecutive items, so (warp, round, lane) order is input order; ranks
+// within a round come from __match_any_sync. cnt has (blockDim.x / 32) * 256
+// entries and dbase 256. Returns the buffer holding the sorted keys.
+__device__ unsigned long long* block_radix_sort(unsigned long long* a, unsigned long long* b, int n, int nbits,
+                                                int32_t* cnt, int32_t* dbase) {
+  const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunk = (n + nw - 1) / nw;
+  const int lo = min(n, warp * chunk), hi = min(n, lo + chunk);
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int shift = 0; shift < nbits; shift += 8) {
+    for (int i = threadIdx.x; i < nw * 256; i += blockDim.x) cnt[i] = 0;
+    __syncthreads();
+    for (int base = lo; base < hi; base += 32) {
+      const int i = base + lane;
+      const bool v = i < hi;
+      const uint32_t d = v ? static_cast<uint32_t>(a[i] >> shift) & 255u : 256u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, d);
+      if (v && (peers & lt) == 0) cnt[warp * 256 + d] += __popc(peers);
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < 256; d += blockDim.x) {
+      int s = 0;
+      for (int w = 0; w < nw; ++w) s += cnt[w * 256 + d];
+      dbase[d] = s;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int v[8];
+      int s = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[j] = dbase[lane * 8 + j];
+        s += v[j];
+      }
+      int pre = warp_inclusive_scan(s) - s;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        dbase[lane * 8 + j] = pre;
+        pre += v[j];
+      }
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < 256; d += blockDim.x) {
+      int run = dbase[d];
+      for (int w = 0; w < nw; ++w) {
+        const int c = cnt[w * 256 + d];
+        cnt[w * 256 + d] = run;
+        run += c;
+      }
+    }
+    __syncthreads();
+    for (int base = lo; base < hi; base += 32) {
+      const int i = base + lane;
+      const bool v = i < hi;
+      const unsigned long long k = v ? a[i] : 0ull;
+      const uint32_t d = v ? static_cast<uint32_t>(k >> shift) & 255u : 256u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, d);
+      const int rank = __popc(peers & lt);
+      int start = 0;
+      if (v) start = cnt[warp * 256 + d];
+      __syncwarp();
+      if (v) {
+        b[start + rank] = k;
+        if (rank == 0) cnt[warp * 256 + d] = start + __popc(peers);
+      }
+      __syncwarp();
+    }
+    __syncthreads();
+    unsigned long long* t = a;
+    a = b;
+    b = t;
+  }
+  return a;
+}
+
 __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   extern __shared__ __align__(16) char smem_dyn[];
   __shared__ uint64_t scan_tmp[33];
@@ -241,7 +329,10 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
 
   const int64_t sample = blockIdx.x;
   const int T = p.T;
-  char* base = p.global_work != nullptr ? p.global_work + static_cast<size_t>(sample) * p.work_stride : smem_dyn;
+  int32_t* cnt = reinterpret_cast<int32_t*>(smem_dyn);
+  int32_t* dbase = cnt + (blockDim.x >> 5) * 256;
+  char* base = p.global_work != nullptr ? p.global_work + static_cast<size_t>(sample) * p.work_stride
+                                        : smem_dyn + counter_bytes(blockDim.x);
   const Work w = carve_work(base, T, p.H);
   const uint32_t slot = static_cast<uint32_t>(sample);
 
@@ -273,15 +364,14 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
     __syncthreads();
   }
 
-  // 2. Relabel.
+  // 2. Relabel. Dedup slot word = (node key << 32) | smallest position;
+  //    after numbering, the low word holds 0x80000000 | local id (never a
+  //    position, so later first-discovery tests fail for every position).
   if (p.with_replacement) {
     for (int q = threadIdx.x; q < T; q += blockDim.x) w.local[q] = -1;
     __syncthreads();
   } else {
-    for (int i = threadIdx.x; i < p.H; i += blockDim.x) {
-      w.hkey[i] = kEmptyKey;
-      w.hval[i] = 0x7fffffff;
-    }
+    for (int i = threadIdx.x; i < p.H; i += blockDim.x) w.slot[i] = kEmptyKey;
     __syncthreads();
     const uint32_t hmask = static_cast<uint32_t>(p.H - 1);
     for (int q = threadIdx.x; q < T; q += blockDim.x) {
@@ -289,12 +379,17 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
       int32_t slot_q = -1;
       if (v >= 0) {
         const int ns = p.pos_info[q].y & 0xFF;
-        const uint64_t key = (static_cast<uint64_t>(ns) << 32) | static_cast<uint32_t>(v);
-        uint32_t h = static_cast<uint32_t>((key * 0x9E3779B97F4A7C15ull) >> (64 - p.log2H)) & hmask;
+        const uint32_t key = p.ns_key_base[ns] + static_cast<uint32_t>(v);
+        const unsigned long long entry = (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(q);
+        uint32_t h = ((key * 0x9E3779B1u) >> (32 - p.log2H)) & hmask;
         for (int probe = 0; probe < p.H; ++probe) {
-          const unsigned long long prev = atomicCAS(reinterpret_cast<unsigned long long*>(&w.hkey[h]), kEmptyKey, key);
-          if (prev == kEmptyKey || prev == key) {
-            atomicMin(&w.hval[h], q);
+          const unsigned long long prev = atomicCAS(&w.slot[h], kEmptyKey, entry);
+          if (prev == kEmptyKey) {
+            slot_q = static_cast<int32_t>(h);
+            break;
+          }
+          if (static_cast<uint32_t>(prev >> 32) == key) {
+            atomicMin(&w.slot[h], entry);
             slot_q = static_cast<int32_t>(h);
             break;
           }
@@ -315,7 +410,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
     auto first = [&](int q) -> bool {
       if (p.with_replacement) return w.node[q] >= 0;
       const int32_t s = w.local[q];
-      return s >= 0 && w.hval[s] == q;
+      return s >= 0 && static_cast<uint32_t>(w.slot[s]) == static_cast<uint32_t>(q);
     };
     auto value = [&](int q) -> uint64_t {
       const int ns = p.pos_info[q].y & 0xFF;
@@ -325,9 +420,13 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
     auto sink = [&](int q, uint64_t pre) {
       const int ns = p.pos_info[q].y & 0xFF;
       if (ns < g || ns >= g + per_pass || !first(q)) return;
-      const int32_t rank = static_cast<int32_t>((pre >> ((ns - g) * fbits)) & fmask);
-      if (p.with_replacement) w.local[q] = rank;
-      else w.hval[w.local[q]] = -(rank + 1);
+      const uint32_t rank = static_cast<uint32_t>((pre >> ((ns - g) * fbits)) & fmask);
+      if (p.with_replacement) {
+        w.local[q] = static_cast<int32_t>(rank);
+      } else {
+        const int32_t s = w.local[q];
+        w.slot[s] = (w.slot[s] & 0xFFFFFFFF00000000ull) | (0x80000000u | rank);
+      }
     };
     const uint64_t tot = block_scan_items(T, value, sink, scan_tmp);
     if (threadIdx.x == 0) {
@@ -340,7 +439,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   if (!p.with_replacement) {
     for (int q = threadIdx.x; q < T; q += blockDim.x) {
       const int32_t s = w.local[q];
-      w.local[q] = s >= 0 ? -w.hval[s] - 1 : -1;
+      w.local[q] = s >= 0 ? static_cast<int32_t>(static_cast<uint32_t>(w.slot[s]) & 0x7FFFFFFFu) : -1;
     }
   }
   if (threadIdx.x == 0) {
@@ -363,53 +462,45 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
     if (l >= 0) out_nodes[ns_base[ns] + l] = v;
   }
 
-  // 3. Edge keys (edgeset, src_local, dst_local), sorted and deduplicated.
-  uint64_t* ek = w.hkey;
-  __syncthreads();
-  for (int i = threadIdx.x; i < p.N2; i += blockDim.x) {
-    uint64_t key = kEmptyKey;
+  // 3. Edge keys (edgeset | src_local | dst_local) of positions 1..T-1,
+  //    radix-sorted and deduplicated. Empty positions get the key
+  //    num_edgesets << 2*pbits, which sorts after every real edge.
+  const int n_keys = T - 1;
+  const int pb = p.pbits;
+  const unsigned long long invalid = static_cast<unsigned long long>(p.num_edgesets) << (2 * pb);
+  unsigned long long* keys = w.slot;
+  unsigned long long* tmp = w.slot + T;
+  for (int i = threadIdx.x; i < n_keys; i += blockDim.x) {
+    unsigned long long key = invalid;
     const int q = i + 1;
-    if (q < T && w.node[q] >= 0 && w.local[q] >= 0) {
+    if (w.node[q] >= 0 && w.local[q] >= 0) {
       const int2 info = p.pos_info[q];
       const int e = info.y >> 8;
       const EdgeDev& E = p.edges[e];
-      const uint64_t a = static_cast<uint32_t>(w.local[info.x]);
-      const uint64_t b = static_cast<uint32_t>(w.local[q]);
-      const uint64_t src = E.reversed ? b : a, dst = E.reversed ? a : b;
-      key = (static_cast<uint64_t>(E.edgeset) << 48) | (src << 24) | dst;
+      const unsigned long long a = static_cast<uint32_t>(w.local[info.x]);
+      const unsigned long long b = static_cast<uint32_t>(w.local[q]);
+      const unsigned long long src = E.reversed ? b : a, dst = E.reversed ? a : b;
+      key = (static_cast<unsigned long long>(E.edgeset) << (2 * pb)) | (src << pb) | dst;
     }
-    ek[i] = key;
+    keys[i] = key;
   }
   __syncthreads();
-  for (int kk = 2; kk <= p.N2; kk <<= 1) {
-    for (int j = kk >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < p.N2; i += blockDim.x) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t a = ek[i], b = ek[ixj];
-          const bool up = (i & kk) == 0;
-          if ((a > b) == up) {
-            ek[i] = b;
-            ek[ixj] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
+  const unsigned long long* ek = block_radix_sort(keys, tmp, n_keys, p.keybits, cnt, dbase);
   uint64_t* out_edges = p.scratch_edges + sample * static_cast<int64_t>(T);
+  const unsigned long long lmask = (1ull << pb) - 1;
   auto is_new = [&](int i) -> uint64_t {
-    const uint64_t k = ek[i];
-    return (k != kEmptyKey && (i == 0 || ek[i - 1] != k)) ? 1ull : 0ull;
+    const unsigned long long k = ek[i];
+    return (k != invalid && (i == 0 || ek[i - 1] != k)) ? 1ull : 0ull;
   };
   auto put = [&](int i, uint64_t pre) {
-    const uint64_t k = ek[i];
-    if (k != kEmptyKey && (i == 0 || ek[i - 1] != k)) {
-      out_edges[pre] = k;
-      atomicAdd(&es_count[static_cast<int>(k >> 48)], 1);
+    const unsigned long long k = ek[i];
+    if (k != invalid && (i == 0 || ek[i - 1] != k)) {
+      const unsigned long long es = k >> (2 * pb);
+      out_edges[pre] = (es << 48) | (((k >> pb) & lmask) << 24) | (k & lmask);
+      atomicAdd(&es_count[static_cast<int>(es)], 1);
     }
   };
-  block_scan_items(p.N2, is_new, put, scan_tmp);
+  block_scan_items(n_keys, is_new, put, scan_tmp);
 
   for (int s = threadIdx.x; s < p.num_nodesets; s += blockDim.x) p.node_cnt[s * p.B + sample] = ns_count[s];
   for (int e = threadIdx.x; e < p.num_edgesets; e += blockDim.x) p.edge_cnt[e * p.B + sample] = es_count[e];
@@ -482,6 +573,9 @@ struct dgfx_sampler {
   uint64_t seed = 0;
   bool use_smem = true;
   int threads = 256;
+  size_t smem_bytes = 0;
+  int32_t pbits = 1, keybits = 2;
+  uint32_t ns_key_base[kMaxNodesets] = {};
   // Device tables (one allocation).
   void* d_tables = nullptr;
   EdgeDev* d_edges = nullptr;
@@ -671,7 +765,19 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
     E.edgeset = edge_edgeset[j];
     E.reversed = edge_reversed[j] != 0;
   }
-  (void)num_nodes;
+  // Dedup keys: node ids of all node sets laid end to end in 32 bits.
+  {
+    uint64_t acc = 0;
+    for (int i = 0; i < num_nodesets; ++i) {
+      s->ns_key_base[i] = static_cast<uint32_t>(acc);
+      acc += static_cast<uint64_t>(num_nodes[i] < 0 ? 0 : num_nodes[i]);
+    }
+    if (acc >= 0xFFFFFFFFull) {
+      return fail(DGFX_ERR_UNSUPPORTED, "dgfx_sampler_create: more than 2^32 - 2 nodes over all node sets");
+    }
+  }
+  s->pbits = std::max(1, bit_length(static_cast<uint64_t>(T - 1)));
+  s->keybits = bit_length(static_cast<uint64_t>(num_edgesets)) + 2 * s->pbits;
 
   // One device allocation for all tables.
   const size_t b_edges = align_up(sizeof(EdgeDev) * std::max<size_t>(1, s->h_edges.size()), 256);
@@ -696,14 +802,12 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
   const unsigned long long init[6] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
   DGFX_CUDA_TRY(cudaMemcpy(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice));
 
-  // Threads per CTA: enough for the bitonic sort's N2/2 pairs, 32..256.
-  s->threads = std::min(256, std::max(32, s->N2 / 2));
-  if (s->use_smem) {
-    const size_t smem = work_bytes(s->T, s->H);
-    if (smem > 48 * 1024) {
-      DGFX_CUDA_TRY(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
-    }
+  // Threads per CTA: about one per eight tree positions, 32..256.
+  s->threads = std::min(256, std::max(32, s->N2 / 8));
+  s->smem_bytes = counter_bytes(s->threads) + (s->use_smem ? work_bytes(s->T, s->H) : 0);
+  if (s->smem_bytes > 48 * 1024) {
+    DGFX_CUDA_TRY(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(s->smem_bytes)));
   }
   *out = s.release();
   return DGFX_OK;
@@ -797,7 +901,10 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   p.global_work = b.global_work;
   p.work_stride = work_bytes(s->T, s->H);
   p.status = s->d_status;
-  const size_t smem = s->use_smem ? work_bytes(s->T, s->H) : 0;
+  p.pbits = s->pbits;
+  p.keybits = s->keybits;
+  for (int i = 0; i < kMaxNodesets; ++i) p.ns_key_base[i] = s->ns_key_base[i];
+  const size_t smem = s->smem_bytes;
   sample_kernel<<<static_cast<unsigned>(B), s->threads, smem, stream>>>(p);
   DGFX_CUDA_TRY(cudaGetLastError());
   const size_t mark = arena.used;

@@ -111,11 +111,11 @@ class ShardedSampler:
                 cap = int(merged.node_ids.numel())
                 F = int(self.features.table.shape[1])
                 feats = torch.empty((cap, F), dtype=self.features.table.dtype, device=self.features.table.device)
-                rng = merged.node_offsets[[0, -1]]
+                off = merged.node_offsets
                 _native.check(_native.lib().dgfx_gather_rows_ranged(
                     _native.ptr(self.features.table), int(self.features.table.shape[0]), self.features.row_bytes,
-                    _native.ptr(merged.node_ids), _native.ptr(rng), cap, _native.ptr(feats),
-                    _native.stream_handle(stream)))
+                    _native.ptr(merged.node_ids), _native.elem_ptr(off, 0), _native.elem_ptr(off, -1), cap,
+                    _native.ptr(feats), _native.stream_handle(stream)))
             else:
                 total = int(merged.node_offsets[-1].item())
                 feats = self.features.gather(merged.node_ids[:total], stream=stream)

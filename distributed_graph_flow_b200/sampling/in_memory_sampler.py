@@ -246,14 +246,15 @@ class Sampler:
                 tables = store.tables.get(ns_name, {})
                 if not tables:
                     continue
-                rng = merged.node_offsets[s * B : (s + 1) * B + 1 : B]
+                off = merged.node_offsets
                 feats[ns_name] = {}
                 for fname, (table, row_bytes, padded, dtype, shape) in tables.items():
                     rows = torch.empty((max(cap, 1), padded), dtype=torch.uint8, device=store.device)
                     _native.check(
                         _native.lib().dgfx_gather_rows_ranged(
                             _native.ptr(table), int(table.shape[0]), padded, _native.ptr(merged.node_ids),
-                            _native.ptr(rng.contiguous()), cap, _native.ptr(rows), sh,
+                            _native.elem_ptr(off, s * B), _native.elem_ptr(off, (s + 1) * B), cap,
+                            _native.ptr(rows), sh,
                         )
                     )
                     feats[ns_name][fname] = (rows, row_bytes, dtype, shape)

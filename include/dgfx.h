@@ -183,14 +183,14 @@ int dgfx_gather_rows(const void* d_table, int64_t num_table_rows,
                      int64_t row_bytes, const int64_t* d_row_ids,
                      int64_t num_rows, void* d_out, dgfx_stream stream);
 
-/* Same, for the rows [d_range[0], d_range[1]) of d_row_ids with the bounds
- * read on the device (at most max_rows rows; out row i <- d_row_ids[
- * d_range[0] + i]). Lets a node set of a merged batch be gathered without
- * a host synchronisation. */
+/* Same, for the rows [*d_begin, *d_end) of d_row_ids with both bounds read
+ * on the device (at most max_rows rows; out row i <- d_row_ids[*d_begin + i]).
+ * Lets a node set of a merged batch be gathered straight from the batch's
+ * offsets, without a host synchronisation. */
 int dgfx_gather_rows_ranged(const void* d_table, int64_t num_table_rows,
                             int64_t row_bytes, const int64_t* d_row_ids,
-                            const int64_t* d_range, int64_t max_rows,
-                            void* d_out, dgfx_stream stream);
+                            const int64_t* d_begin, const int64_t* d_end,
+                            int64_t max_rows, void* d_out, dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
  * Aggregation.

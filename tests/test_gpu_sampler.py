@@ -320,9 +320,9 @@ def test_large_tree_global_memory_path(sampling):
     """A plan whose padded tree exceeds the shared-memory limit runs from the
     workspace and still matches the oracle (first mode)."""
     graph, schema = random_hetero_graph(8, temporal=False, sizes={"a": 60, "b": 30, "c": 9})
-    conf = dict(seed_nodeset="a", num_hops=3, hop_width=6)
+    conf = dict(seed_nodeset="a", num_hops=3, hop_width=8)
     plan = sampling.simple_sampling_config_to_sampling_plan(sampling.SimpleSamplingConfig(**conf), schema)
     s = sampling.create_sampler(graph, plan, schema, return_features=False, return_node_idxs=True, batch_size=8,
                                 debug_sampling=True)
-    assert s._cc_sampler.tree_size > 4096
+    assert s._cc_sampler.tree_size > 8192
     _compare(sampling, graph, schema, conf, sampling.MODE_FIRST, False, np.arange(20))
