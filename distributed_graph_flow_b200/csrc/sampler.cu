@@ -44,6 +44,7 @@
 #include <functional>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -949,4 +950,66 @@ extern "C" int dgfx_sampler_stats(dgfx_sampler* s, dgfx_stream stream_, int64_t*
   DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
   for (int i = 0; i < 3; ++i) out3[i] = static_cast<int64_t>(st[3 + i]);
   return DGFX_OK;
+}
+
+// ===========================================================================
+// Allocation-free sampling entry point.
+//
+// Some callers cannot allocate device memory at the point where they sample:
+// code running under a framework that owns the whole device memory pool
+// (a JAX/XLA process that preallocates HBM, a serving runtime with a fixed
+// arena) or a plugin invoked where allocation is forbidden. They cannot
+// provide dgfx_sampler_sample's workspace, so this variant takes its scratch
+// from one file-scope device array instead. The array is fixed at
+// kNoAllocScratchBytes (64 MiB) and every GPU that loads this library holds
+// it until the process exits. Its device address is looked up with
+// cudaGetSymbolAddress once per device, on the first call made with that
+// device current; make that first call before any stream capture.
+// All calls share the array and it keeps the previous call's contents; the
+// sampler writes every scratch word it later reads, so nothing needs
+// clearing. Calls whose executions overlap on the GPU (two streams, or two
+// host threads) race on the array and must be serialised by the caller.
+// ===========================================================================
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  DGFX_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(DGFX_ERR_UNSUPPORTED, "dgfx_sampler_sample_noalloc: device id");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      return fail(DGFX_ERR_CUDA, std::string("dgfx_sampler_sample_noalloc: cudaGetSymbolAddress failed: ") +
+                                     cudaGetErrorString(e));
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return DGFX_OK;
+}
+}  // namespace
+
+extern "C" int dgfx_sampler_sample_noalloc(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_ts,
+                                           const int64_t* d_masked_edges, int64_t B, uint64_t call_index,
+                                           const dgfx_sample_out* out, dgfx_stream stream) {
+  if (s == nullptr || B < 0) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_sample_noalloc: bad arguments");
+  const size_t need = sample_ws_bytes(s, B);
+  if (need > kNoAllocScratchBytes) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT,
+                "dgfx_sampler_sample_noalloc: " + std::to_string(B) + " seeds need " + std::to_string(need) +
+                    " bytes of scratch, more than the fixed " + std::to_string(kNoAllocScratchBytes) +
+                    " bytes; use fewer seeds per call or dgfx_sampler_sample with a workspace");
+  }
+  void* scratch = nullptr;
+  DGFX_TRY(noalloc_scratch(&scratch));
+  return dgfx_sampler_sample(s, d_seeds, d_seed_ts, d_masked_edges, B, call_index, out, scratch,
+                             kNoAllocScratchBytes, stream);
 }

@@ -161,6 +161,22 @@ int dgfx_sampler_sample(dgfx_sampler* sampler, const int64_t* d_seeds,
                         const dgfx_sample_out* out, void* d_workspace,
                         size_t workspace_bytes, dgfx_stream stream);
 
+/* Same as dgfx_sampler_sample but allocates nothing and takes no workspace:
+ * for callers that cannot allocate device memory when they sample (a
+ * framework that owns the device's memory pool, a fixed-arena serving
+ * runtime, a plugin called where allocation is not allowed). Its scratch is
+ * one file-scope 64 MiB device array of this library, held on every GPU that
+ * loads the library until exit; a call whose dgfx_sampler_workspace_size
+ * exceeds 64 MiB fails with DGFX_ERR_INVALID_ARGUMENT. The array's address
+ * is looked up on the first call on each device (make that call before any
+ * stream capture). Calls share the array: calls that overlap on the GPU
+ * race. This entry point has no counterpart in the reference. */
+int dgfx_sampler_sample_noalloc(dgfx_sampler* sampler, const int64_t* d_seeds,
+                                const int64_t* d_seed_ts,
+                                const int64_t* d_masked_edges,
+                                int64_t num_seeds, uint64_t call_index,
+                                const dgfx_sample_out* out, dgfx_stream stream);
+
 /* Synchronises `stream` and reports the latched status of the last
  * dgfx_sampler_sample (reference messages, e.g. "The source node idx 7 is out
  * of bounds. Should be lower than 4"). */
