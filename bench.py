@@ -148,7 +148,7 @@ def large_spec(scale):
     return dataclasses.replace(s, num_nodes=max(1000, int(s.num_nodes * scale)), num_edges=int(s.num_edges * scale))
 
 
-def setup_large(rank, world, dev, scale=1.0):
+def setup_large(rank, world, dev, scale=1.0, halo="p2p"):
     import torch
 
     from distributed_graph_flow_b200 import driver, synth
@@ -162,11 +162,17 @@ def setup_large(rank, world, dev, scale=1.0):
     rpr = math.ceil(spec.num_nodes / world)
     lo = rank * rpr
     cnt = max(0, min(rpr, spec.num_nodes - lo))
-    table = synth.normal_features(lo, cnt, FEAT_DIM, spec.seed + 100, torch.bfloat16, dev)
     plan = cfg.explicit_plan("paper", "cites", FANOUT)
     cc = ext.create_device_sampler(plan, ["paper"], [spec.num_nodes], ["cites"], [index], [None],
                                    ext._native.MODE_RANDOM, seed=1234)
-    feats = driver.HaloFeatures(table, rpr, rank, world)
+    if halo == "nccl":
+        table = synth.normal_features(lo, cnt, FEAT_DIM, spec.seed + 100, torch.bfloat16, dev)
+        feats = driver.HaloFeatures(table, rpr, rank, world)
+    else:
+        feats = driver.PeerFeatures(cnt, FEAT_DIM, torch.bfloat16, rpr, spec.num_nodes, rank, world, dev)
+        synth.normal_features(lo, cnt, FEAT_DIM, spec.seed + 100, torch.bfloat16, dev, out=feats.table)
+        feats.connect()
+        table = feats.table
     sharded = driver.ShardedSampler(cc, feats, rank, world)
     torch.cuda.synchronize()
     log(f"[bench] large graph built in {t_graph:.1f}s; setup {time.time() - t0:.1f}s; T={cc.tree_size}")
@@ -179,7 +185,7 @@ def bench_large(args, rank, world, dev):
 
     from distributed_graph_flow_b200 import _native, synth
 
-    spec, index, table, cc, sharded, plan = setup_large(rank, world, dev, args.scale)
+    spec, index, table, cc, sharded, plan = setup_large(rank, world, dev, args.scale, args.halo)
     W, K = args.warmup, args.steps
     seeds = synth.uniform_int((W + K) * B_SEEDS, 0, spec.num_nodes, 77 + rank, 5, dev).view(W + K, B_SEEDS)
 
@@ -217,17 +223,24 @@ def bench_large(args, rank, world, dev):
                       "kernel_sampler")
     st = ctypes_stats(cc)
     ms_gather = None
-    if world == 1:
-        off = merged.node_offsets
-        cap = int(merged.node_ids.numel())
-        out = torch.empty((cap, FEAT_DIM), dtype=torch.bfloat16, device=dev)
+    from distributed_graph_flow_b200 import driver
 
+    off = merged.node_offsets
+    cap = int(merged.node_ids.numel())
+    out = torch.empty((cap, FEAT_DIM), dtype=torch.bfloat16, device=dev)
+    g = None
+    if isinstance(sharded.features, driver.PeerFeatures):
+        def g(_):
+            sharded.features.gather_range(merged.node_ids, _native.elem_ptr(off, 0), _native.elem_ptr(off, -1), cap,
+                                          out)
+    elif world == 1:
         def g(_):
             _native.check(_native.lib().dgfx_gather_rows_ranged(
                 _native.ptr(table), int(table.shape[0]), FEAT_DIM * 2, _native.ptr(merged.node_ids),
                 _native.elem_ptr(off, 0), _native.elem_ptr(off, -1), cap, _native.ptr(out), _native.stream_handle()))
-
+    if g is not None:
         ms_gather = timed(g, K, sync, "kernel_gather")
+        del out
 
     hbm, peak_kind = measured_peaks()
     # Algorithmic bytes per launch.
@@ -277,7 +290,9 @@ def bench_large(args, rank, world, dev):
         "gpu_launches": launches * K,
         "gpu_launches_per_step": launches,
     }
-    return res, (spec, index, table, cc, plan, seeds, W)
+    res["config"]["halo"] = ("peer loads over NVLink (one gather kernel)" if args.halo == "p2p"
+                             else "NCCL all-to-all halo exchange")
+    return res, (spec, index, table, cc, plan, seeds, W, sharded)
 
 
 def ctypes_stats(cc):
@@ -601,6 +616,8 @@ def main():
     ap.add_argument("--scale", type=float, default=1.0, help="shrink the workload (profiling / debugging only)")
     ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal"],
                     help="run one workload and skip the rest (profiling)")
+    ap.add_argument("--halo", default="p2p", choices=["p2p", "nccl"],
+                    help="feature halo: peer loads over NVLink (default) or NCCL all-to-all")
     ap.add_argument("--minimal", action="store_true",
                     help="timed steps only: no e2e leg, launch count or CPU baseline (for profiler captures)")
     args = ap.parse_args()
@@ -632,8 +649,8 @@ def main():
         return
 
     res, ctx = bench_large(args, rank, world, dev)
+    spec, index, table, cc, plan, seeds, W, sharded = ctx
     if rank == 0 and world == 1 and args.only is None:
-        spec, index, table, cc, plan, seeds, W = ctx
         if not args.no_cpu:
             table_host = None
             if host_mem_gb() > 80:
@@ -646,8 +663,14 @@ def main():
             except Exception as exc:  # noqa: BLE001
                 res["cpu_baseline"] = {"unavailable": str(exc)}
             del table_host
-        del ctx, index, table, cc
-        torch.cuda.empty_cache()
+    # Peer-mapped partitions are unmapped and freed on every rank together.
+    from distributed_graph_flow_b200 import driver as _driver
+
+    if isinstance(sharded.features, _driver.PeerFeatures):
+        sharded.features.close()
+    del ctx, index, table, cc, sharded
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and args.only is None:
         if not args.no_extras:
             res["spmm"] = bench_spmm(dev, max(5, args.steps // 2))
             torch.cuda.empty_cache()

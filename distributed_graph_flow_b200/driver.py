@@ -84,6 +84,111 @@ class HaloFeatures:
         return out
 
 
+class DeviceBuffer:
+    """A cudaMalloc'd allocation (dgfx_device_alloc) seen by torch through
+    __cuda_array_interface__. Needed for CUDA IPC, which shares whole
+    allocations, not sub-blocks of torch's caching allocator."""
+
+    def __init__(self, nbytes: int, device):
+        self.device = device
+        ptr = ctypes.c_void_p()
+        _native.check(_native.lib().dgfx_device_alloc(int(nbytes), ctypes.byref(ptr)))
+        self.ptr = int(ptr.value)
+        self.nbytes = int(nbytes)
+        self.__cuda_array_interface__ = {"shape": (max(1, self.nbytes),), "typestr": "|u1",
+                                         "data": (self.ptr, False), "version": 3}
+
+    def tensor(self, shape, dtype):
+        torch = _native.require_cuda()
+        raw = torch.as_tensor(self, device=self.device)
+        n = 1
+        for s in shape:
+            n *= int(s)
+        return raw[: n * torch.empty(0, dtype=dtype).element_size()].view(dtype).view(*shape)
+
+    def free(self):
+        if self.ptr:
+            _native.check(_native.lib().dgfx_device_free(self.ptr))
+            self.ptr = 0
+
+
+class PeerFeatures:
+    """Node-range-partitioned features gathered with peer loads.
+
+    Each rank's partition lives in its own allocation whose CUDA IPC handle is
+    shared with the other ranks once (all_gather of the 64-byte handles), so
+    every rank holds pointers to all partitions and one kernel
+    (dgfx_gather_rows_p2p) fetches any row from its owner over NVLink. Call
+    ``close()`` on every rank before the process group is destroyed.
+    """
+
+    def __init__(self, local_rows: int, dim: int, dtype, rows_per_rank: int, num_nodes: int, rank: int,
+                 world: int, device, group=None):
+        torch = _native.require_cuda()
+        self.rank, self.world, self.group = int(rank), int(world), group
+        self.rows_per_rank, self.num_nodes, self.dim = int(rows_per_rank), int(num_nodes), int(dim)
+        self.dtype = dtype
+        self.device = device
+        self.row_bytes = torch.empty(0, dtype=dtype).element_size() * self.dim
+        if self.row_bytes % 16:
+            raise ValueError("feature rows must be a multiple of 16 bytes")
+        self.buffer = DeviceBuffer(max(1, local_rows) * self.row_bytes, device)
+        self.table = self.buffer.tensor((local_rows, self.dim), dtype)
+        self._peers = []
+        self._ptrs = None
+
+    def connect(self):
+        """Exchanges IPC handles (collective over the group). Call after the
+        local partition is filled."""
+        torch = _native.require_cuda()
+        lib = _native.lib()
+        ptrs = [0] * self.world
+        ptrs[self.rank] = self.buffer.ptr
+        if self.world > 1:
+            import torch.distributed as dist
+
+            h = (ctypes.c_uint8 * 64)()
+            _native.check(lib.dgfx_ipc_get_handle(self.buffer.ptr, ctypes.cast(h, ctypes.c_void_p)))
+            mine = torch.tensor(list(bytes(h)), dtype=torch.uint8, device=self.device)
+            allh = torch.empty((self.world, 64), dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(allh, mine, group=self.group)
+            allh = allh.cpu().numpy()
+            for r in range(self.world):
+                if r == self.rank:
+                    continue
+                buf = (ctypes.c_uint8 * 64)(*allh[r].tolist())
+                p = ctypes.c_void_p()
+                _native.check(lib.dgfx_ipc_open(ctypes.cast(buf, ctypes.c_void_p), ctypes.byref(p)))
+                ptrs[r] = int(p.value)
+                self._peers.append(int(p.value))
+        self._ptrs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        torch.cuda.synchronize(self.device)
+        return self
+
+    def gather_range(self, ids, begin_ptr: int, end_ptr: int, max_rows: int, out, stream=None):
+        """out[i] = feature row of ids[*begin + i] for i < min(*end - *begin, max_rows)."""
+        _native.check(_native.lib().dgfx_gather_rows_p2p(
+            _native.ptr(self._ptrs), self.world, self.rows_per_rank, self.num_nodes, self.row_bytes,
+            _native.ptr(ids), begin_ptr, end_ptr, int(max_rows), _native.ptr(out), _native.stream_handle(stream)))
+        return out
+
+    def close(self):
+        """Unmaps the peers' partitions and frees this rank's (collective)."""
+        torch = _native.require_cuda()
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(group=self.group)
+            for p in self._peers:
+                _native.check(_native.lib().dgfx_ipc_close(p))
+            self._peers = []
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+        self.table = None
+        self.buffer.free()
+
+
 class ShardedSampler:
     """Per-rank sampler over the replicated topology plus halo features.
 
@@ -104,7 +209,16 @@ class ShardedSampler:
         merged = self.cc.sample_merged(seeds, seed_ts, None, stream=stream, call_index=call, check=False)
         feats = None
         total = None
-        if self.features is not None:
+        if isinstance(self.features, PeerFeatures):
+            # One kernel, bounds read on the device: local rows from HBM,
+            # remote rows by peer loads. No host round trip at any world size.
+            torch = _native.require_cuda()
+            cap = int(merged.node_ids.numel())
+            feats = torch.empty((cap, self.features.dim), dtype=self.features.dtype, device=self.features.device)
+            off = merged.node_offsets
+            self.features.gather_range(merged.node_ids, _native.elem_ptr(off, 0), _native.elem_ptr(off, -1), cap,
+                                       feats, stream=stream)
+        elif self.features is not None:
             if self.world == 1:
                 # No host round trip: bounds of the gather are read on the device.
                 torch = _native.require_cuda()

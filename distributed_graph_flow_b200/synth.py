@@ -66,10 +66,11 @@ def uniform_int(n: int, lo: int, hi: int, seed: int, stream_id: int, device, str
     return out
 
 
-def normal_features(node_begin: int, count: int, dim: int, seed: int, dtype, device, stream=None):
+def normal_features(node_begin: int, count: int, dim: int, seed: int, dtype, device, stream=None, out=None):
     torch = _native.require_cuda()
     code = _native.BF16 if dtype == torch.bfloat16 else _native.F32
-    out = torch.empty((max(count, 1), dim), dtype=dtype, device=device)[:count]
+    if out is None:
+        out = torch.empty((max(count, 1), dim), dtype=dtype, device=device)[:count]
     _native.check(
         _native.lib().dgfx_synth_normal_features(node_begin, count, dim, seed, code, _native.ptr(out), _stream(stream))
     )

@@ -265,6 +265,29 @@ int dgfx_scatter_rows(const void* d_rows, int64_t n, int64_t row_bytes,
                       const uint32_t* d_perm, void* d_out, dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Peer-memory feature gather (one kernel instead of the all-to-all halo
+ * exchange when the ranks' GPUs have peer access, e.g. over NVSwitch).
+ * Each rank allocates its feature partition with dgfx_device_alloc, shares
+ * it with dgfx_ipc_get_handle (64-byte CUDA IPC handle) and opens the other
+ * ranks' handles with dgfx_ipc_open; d_tables is a device array of the
+ * `world` partition pointers (its own included). dgfx_gather_rows_p2p:
+ * out[i] = partition(o)[id - o * rows_per_rank] for id = d_row_ids[*d_begin
+ * + i], o = id / rows_per_rank (zero row for ids outside [0, num_nodes)),
+ * at most max_rows rows, bounds read on the device. Remote rows are read
+ * with plain loads over NVLink (no TMA, no multicast).
+ * ------------------------------------------------------------------------ */
+int dgfx_device_alloc(size_t bytes, void** d_ptr);
+int dgfx_device_free(void* d_ptr);
+int dgfx_ipc_get_handle(const void* d_ptr, void* handle64);
+int dgfx_ipc_open(const void* handle64, void** d_ptr);
+int dgfx_ipc_close(void* d_ptr);
+int dgfx_gather_rows_p2p(const void* const* d_tables, int32_t world,
+                         int64_t rows_per_rank, int64_t num_nodes,
+                         int64_t row_bytes, const int64_t* d_row_ids,
+                         const int64_t* d_begin, const int64_t* d_end,
+                         int64_t max_rows, void* d_out, dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
  * Seeded synthetic inputs (stand-ins for the benchmark datasets, the role of
  * the reference's dgf/src/util/gen_test_graph.py generators at scale).
  * dgfx_synth_graph: power-law out-degrees (P(d) ~ d^-alpha, capped at

@@ -61,11 +61,53 @@ def _worker(rank, world, port, q):
             cc.check()
             assert total == int(merged.node_offsets[-1].item())
             assert torch.equal(feats[:total], full[merged.node_ids[:total]])
+        # Peer-load gather over the same partition.
+        pf = driver.PeerFeatures(hi - lo, F, torch.bfloat16, rpr, spec.num_nodes, rank, world, dev)
+        pf.table.copy_(full[lo:hi])
+        pf.connect()
+        ids = torch.from_numpy(rng.integers(-3, spec.num_nodes + 3, 20_000)).to(dev)
+        bounds = torch.tensor([5, 19_000], dtype=torch.int64, device=dev)
+        out = torch.zeros((20_000, F), dtype=torch.bfloat16, device=dev)
+        from distributed_graph_flow_b200 import _native
+
+        pf.gather_range(ids, _native.elem_ptr(bounds, 0), _native.elem_ptr(bounds, 1), 20_000, out)
+        sel = ids[5:19_000]
+        ok = (sel >= 0) & (sel < spec.num_nodes)
+        exp = torch.zeros((len(sel), F), dtype=torch.bfloat16, device=dev)
+        exp[ok] = full[sel[ok]]
+        assert torch.equal(out[: len(sel)], exp), f"p2p gather rank {rank}"
+        ss2 = driver.ShardedSampler(cc, pf, rank, world)
+        merged, feats, _ = ss2.step(seeds)
+        cc.check()
+        total = int(merged.node_offsets[-1].item())
+        assert torch.equal(feats[:total], full[merged.node_ids[:total]])
+        pf.close()
         q.put((rank, "ok"))
     except Exception as exc:  # noqa: BLE001
         q.put((rank, repr(exc)))
     finally:
         dist.destroy_process_group()
+
+
+def test_peer_gather_single_rank(cuda):
+    """The peer-load gather kernel with one partition (no IPC): rows in request
+    order, zero rows for ids outside the graph, bounds read on the device."""
+    from distributed_graph_flow_b200 import _native, driver, synth
+
+    dev = torch.device("cuda", 0)
+    n, F = 5000, 128
+    pf = driver.PeerFeatures(n, F, torch.bfloat16, n, n, 0, 1, dev)
+    synth.normal_features(0, n, F, 4, torch.bfloat16, dev, out=pf.table)
+    pf.connect()
+    full = pf.table.clone()
+    ids = torch.tensor([7, -1, 4999, 5000, 0, 7], dtype=torch.int64, device=dev)
+    bounds = torch.tensor([0, 6], dtype=torch.int64, device=dev)
+    out = torch.full((8, F), 3.0, dtype=torch.bfloat16, device=dev)
+    pf.gather_range(ids, _native.elem_ptr(bounds, 0), _native.elem_ptr(bounds, 1), 8, out)
+    assert torch.equal(out[0], full[7]) and torch.equal(out[2], full[4999]) and torch.equal(out[4], full[0])
+    assert torch.count_nonzero(out[1]) == 0 and torch.count_nonzero(out[3]) == 0
+    assert torch.equal(out[6], torch.full((F,), 3.0, dtype=torch.bfloat16, device=dev))  # past *end: untouched
+    pf.close()
 
 
 def test_halo_exchange_two_gpus(cuda):
