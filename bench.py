@@ -102,9 +102,10 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def timed(fn, steps, sync_fn, name="timed"):
+def timed(fn, steps, sync_fn, name="timed", finish=None):
     """Device time (ms per call) of `steps` calls bracketed by syncs, inside
-    an NVTX range (so profilers can be restricted to the timed region)."""
+    an NVTX range (so profilers can be restricted to the timed region).
+    `finish` joins side streams into the timing stream before the end event."""
     import torch
 
     sync_fn()
@@ -114,6 +115,8 @@ def timed(fn, steps, sync_fn, name="timed"):
     s.record()
     for i in range(steps):
         fn(i)
+    if finish is not None:
+        finish()
     e.record()
     sync_fn()
     torch.cuda.nvtx.range_pop()
@@ -197,12 +200,17 @@ def bench_large(args, rank, world, dev):
         torch.cuda.synchronize()
         barrier()
 
+    # Steps are pipelined: the feature gather of step i (second stream)
+    # overlaps the sampling of step i + 1; the timed region ends when both
+    # streams are done.
+    step = sharded.step_overlapped if args.overlap else sharded.step
     for i in range(W):
-        sharded.step(seeds[i])
+        step(seeds[i])
+    sharded.drain()
     cc.check()
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
     clocks.start()
-    ms = timed(lambda i: sharded.step(seeds[W + i]), K, sync, "step")
+    ms = timed(lambda i: step(seeds[W + i]), K, sync, "step", finish=sharded.drain)
     clk = clocks.stop()
     cc.check()
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -282,7 +290,11 @@ def bench_large(args, rank, world, dev):
                                "fanout [15,10,5], 8192 seeds/GPU, bf16 128-d features node-range partitioned",
                    "seeds_per_gpu": B_SEEDS, "fanout": FANOUT, "nodes_per_step_rank0": total_nodes,
                    "edges_per_step_rank0": total_edges, "l2": "inputs larger than L2 (7.4 GB CSR, 28 GB features)",
-                   "parallelism": f"seed-sharded dp{world}, topology replicated, features node-range partitioned"},
+                   "parallelism": f"seed-sharded dp{world}, topology replicated, features node-range partitioned",
+                   "pipelined": bool(args.overlap and world >= 1),
+                   "step": "sample a batch + gather every sampled node's features (gather of step i overlaps "
+                           "sampling of step i+1 on a second stream)" if args.overlap else
+                           "sample a batch + gather every sampled node's features"},
         "clocks": clk,
         "roofline": roof,
         "kernels": kernels,
@@ -618,6 +630,8 @@ def main():
                     help="run one workload and skip the rest (profiling)")
     ap.add_argument("--halo", default="p2p", choices=["p2p", "nccl"],
                     help="feature halo: peer loads over NVLink (default) or NCCL all-to-all")
+    ap.add_argument("--no-overlap", dest="overlap", action="store_false",
+                    help="run each step's feature gather on the sampling stream (no pipelining)")
     ap.add_argument("--minimal", action="store_true",
                     help="timed steps only: no e2e leg, launch count or CPU baseline (for profiler captures)")
     args = ap.parse_args()

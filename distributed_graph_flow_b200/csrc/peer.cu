@@ -18,27 +18,50 @@ namespace dgfx {
 namespace {
 
 // out[i] = partition(owner)[row] for ids[*begin + i], owner = id / rows_per_rank.
-__global__ void gather_p2p_kernel(const uint4* const* __restrict__ tables, int32_t world, int64_t rows_per_rank,
-                                  int64_t num_nodes, int64_t vpr, const int64_t* __restrict__ ids,
-                                  const int64_t* __restrict__ begin, const int64_t* __restrict__ end,
-                                  int64_t max_rows, uint4* __restrict__ out) {
+// Each thread keeps U independent (id load -> row load) chains in flight to
+// cover NVLink latency; 16-byte vectors per row = 1 << lvpr (row widths are
+// powers of two here; other widths use the division path).
+// Small CTAs (64 threads, <= 32 registers) so the gather can run beside a
+// resident sampler kernel (it fills shared memory but leaves registers and
+// threads for a few such CTAs per SM) when steps are pipelined.
+constexpr int kGatherThreads = 64;
+
+template <int U>
+__global__ void __launch_bounds__(kGatherThreads, 32) gather_p2p_kernel(const uint4* const* __restrict__ tables, int32_t world,
+                                                          uint32_t rows_per_rank, uint32_t num_nodes, int64_t vpr,
+                                                          int lvpr, const int64_t* __restrict__ ids,
+                                                          const int64_t* __restrict__ begin,
+                                                          const int64_t* __restrict__ end, int64_t max_rows,
+                                                          uint4* __restrict__ out) {
   const int64_t lo = *begin;
   int64_t n = *end - lo;
   n = n < max_rows ? n : max_rows;
   const int64_t total = n * vpr;
-  for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < total;
-       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t i = v / vpr, c = v - i * vpr;
-    const int64_t id = ids[lo + i];
-    uint4 x = make_uint4(0, 0, 0, 0);
-    if (id >= 0 && id < num_nodes) {
-      const int64_t o = id / rows_per_rank;
-      if (o < world) {
-        const uint4* t = tables[o];
-        x = t[(id - o * rows_per_rank) * vpr + c];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; base < total;
+       base += stride * U) {
+    uint4 x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = base + u * stride;
+      x[u] = make_uint4(0, 0, 0, 0);
+      if (v < total) {
+        const int64_t i = lvpr >= 0 ? (v >> lvpr) : v / vpr;
+        const int64_t c = v - i * vpr;
+        const int64_t id = ids[lo + i];
+        if (id >= 0 && id < num_nodes) {
+          const uint32_t o = static_cast<uint32_t>(id) / rows_per_rank;
+          if (o < static_cast<uint32_t>(world)) {
+            x[u] = __ldg(tables[o] + (static_cast<int64_t>(static_cast<uint32_t>(id) - o * rows_per_rank) * vpr + c));
+          }
+        }
       }
     }
-    out[v] = x;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = base + u * stride;
+      if (v < total) out[v] = x[u];
+    }
   }
 }
 
@@ -92,14 +115,23 @@ extern "C" int dgfx_gather_rows_p2p(const void* const* d_tables, int32_t world, 
     return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_gather_rows_p2p: bad arguments");
   }
   if (max_rows == 0) return DGFX_OK;
+  if (num_nodes >= (int64_t(1) << 32) || rows_per_rank >= (int64_t(1) << 32)) {
+    return fail(DGFX_ERR_UNSUPPORTED, "dgfx_gather_rows_p2p: more than 2^32 - 1 nodes");
+  }
   const int64_t vpr = row_bytes / 16;
+  int lvpr = -1;
+  for (int b = 0; b < 31; ++b) {
+    if ((int64_t(1) << b) == vpr) lvpr = b;
+  }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t blocks = std::min<int64_t>(ceil_div(max_rows * vpr, 256), static_cast<int64_t>(sms) * 16);
-  gather_p2p_kernel<<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), 256, 0, stream>>>(
-      reinterpret_cast<const uint4* const*>(d_tables), world, rows_per_rank, num_nodes, vpr, d_row_ids, d_begin,
-      d_end, max_rows, static_cast<uint4*>(d_out));
+  constexpr int U = 3;
+  const int64_t blocks =
+      std::min<int64_t>(ceil_div(max_rows * vpr, kGatherThreads * U), static_cast<int64_t>(sms) * 24);
+  gather_p2p_kernel<U><<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), kGatherThreads, 0, stream>>>(
+      reinterpret_cast<const uint4* const*>(d_tables), world, static_cast<uint32_t>(rows_per_rank),
+      static_cast<uint32_t>(num_nodes), vpr, lvpr, d_row_ids, d_begin, d_end, max_rows, static_cast<uint4*>(d_out));
   DGFX_CUDA_TRY(cudaGetLastError());
   return DGFX_OK;
 }

@@ -203,6 +203,39 @@ class ShardedSampler:
         self.world = world
         self._calls = 0
 
+    def step_overlapped(self, seeds, seed_ts=None):
+        """Like step(), but the feature gather runs on a second stream so it
+        overlaps the sampling of the next call (the sampler is latency-bound,
+        the gather bandwidth-bound). Results are valid once the caller's
+        stream has waited on ``gather_stream`` (``drain()``)."""
+        torch = _native.require_cuda()
+        if not isinstance(self.features, PeerFeatures):
+            return self.step(seeds, seed_ts)
+        dev = self.features.device
+        if getattr(self, "gather_stream", None) is None:
+            self.gather_stream = torch.cuda.Stream(device=dev)
+        main = torch.cuda.current_stream(dev)
+        call = self._calls * self.world + self.rank
+        self._calls += 1
+        merged = self.cc.sample_merged(seeds, seed_ts, None, call_index=call, check=False)
+        self.gather_stream.wait_stream(main)
+        cap = int(merged.node_ids.numel())
+        with torch.cuda.stream(self.gather_stream):
+            feats = torch.empty((cap, self.features.dim), dtype=self.features.dtype, device=dev)
+            off = merged.node_offsets
+            self.features.gather_range(merged.node_ids, _native.elem_ptr(off, 0), _native.elem_ptr(off, -1), cap,
+                                       feats, stream=self.gather_stream)
+        for t in (merged.node_ids, merged.node_offsets):
+            t.record_stream(self.gather_stream)
+        return merged, feats, None
+
+    def drain(self):
+        """Makes the current stream wait for every overlapped gather."""
+        torch = _native.require_cuda()
+        gs = getattr(self, "gather_stream", None)
+        if gs is not None:
+            torch.cuda.current_stream(gs.device).wait_stream(gs)
+
     def step(self, seeds, seed_ts=None, stream=None):
         call = self._calls * self.world + self.rank  # distinct random stream per rank and call
         self._calls += 1
