@@ -151,7 +151,7 @@ def large_spec(scale):
     return dataclasses.replace(s, num_nodes=max(1000, int(s.num_nodes * scale)), num_edges=int(s.num_edges * scale))
 
 
-def setup_large(rank, world, dev, scale=1.0, halo="p2p"):
+def setup_large(rank, world, dev, scale=1.0, halo="exchange"):
     import torch
 
     from distributed_graph_flow_b200 import driver, synth
@@ -172,7 +172,10 @@ def setup_large(rank, world, dev, scale=1.0, halo="p2p"):
         table = synth.normal_features(lo, cnt, FEAT_DIM, spec.seed + 100, torch.bfloat16, dev)
         feats = driver.HaloFeatures(table, rpr, rank, world)
     else:
-        feats = driver.PeerFeatures(cnt, FEAT_DIM, torch.bfloat16, rpr, spec.num_nodes, rank, world, dev)
+        # Exchange slots sized to the sampler's batch capacity: never overflow.
+        slot = B_SEEDS * cc.tree_size if halo == "exchange" else 0
+        feats = driver.PeerFeatures(cnt, FEAT_DIM, torch.bfloat16, rpr, spec.num_nodes, rank, world, dev,
+                                    exchange_rows=slot)
         synth.normal_features(lo, cnt, FEAT_DIM, spec.seed + 100, torch.bfloat16, dev, out=feats.table)
         feats.connect()
         table = feats.table
@@ -213,6 +216,8 @@ def bench_large(args, rank, world, dev):
     ms = timed(lambda i: step(seeds[W + i]), K, sync, "step", finish=sharded.drain)
     clk = clocks.stop()
     cc.check()
+    if hasattr(sharded.features, "check"):
+        sharded.features.check()
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -302,8 +307,11 @@ def bench_large(args, rank, world, dev):
         "gpu_launches": launches * K,
         "gpu_launches_per_step": launches,
     }
-    res["config"]["halo"] = ("peer loads over NVLink (one gather kernel)" if args.halo == "p2p"
-                             else "NCCL all-to-all halo exchange")
+    res["config"]["halo"] = {"p2p": "peer loads over NVLink (one gather kernel)",
+                             "exchange": "bulk peer exchange (bucket by owner, owner-local gather, sequential "
+                                         "NVLink pulls; NCCL one-word barriers)" if world > 1 else
+                                         "local gather (one rank)",
+                             "nccl": "NCCL all-to-all halo exchange"}[args.halo]
     return res, (spec, index, table, cc, plan, seeds, W, sharded)
 
 
@@ -628,8 +636,8 @@ def main():
     ap.add_argument("--scale", type=float, default=1.0, help="shrink the workload (profiling / debugging only)")
     ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal"],
                     help="run one workload and skip the rest (profiling)")
-    ap.add_argument("--halo", default="p2p", choices=["p2p", "nccl"],
-                    help="feature halo: peer loads over NVLink (default) or NCCL all-to-all")
+    ap.add_argument("--halo", default="exchange", choices=["exchange", "p2p", "nccl"],
+                    help="feature halo: bulk peer exchange (default), direct peer loads, or NCCL all-to-all")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="run each step's feature gather on the sampling stream (no pipelining)")
     ap.add_argument("--minimal", action="store_true",

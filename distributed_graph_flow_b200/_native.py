@@ -105,6 +105,12 @@ SIGNATURES = {
     "dgfx_ipc_open": (_int, [_vp, ctypes.POINTER(_vp)]),
     "dgfx_ipc_close": (_int, [_vp]),
     "dgfx_gather_rows_p2p": (_int, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp]),
+    "dgfx_exchange_buffer_size": (_int, [_i32, _i64, _i64, ctypes.POINTER(_sz)]),
+    "dgfx_exchange_partition": (_int, [_vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
+    "dgfx_exchange_serve": (_int, [_vp, _i32, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "dgfx_exchange_scatter": (_int, [_vp, _i32, _i32, _i64, _i64, _vp, _vp, _vp]),
+    "dgfx_exchange_barrier": (_int, [_vp, _i32, _i32, ctypes.c_uint32, _u64, _vp]),
+    "dgfx_exchange_check": (_int, [_vp, _i32, _vp]),
     "dgfx_synth_graph_workspace_size": (_int, [_i64, ctypes.POINTER(_sz)]),
     "dgfx_synth_graph": (_int, [_i64, _i64, ctypes.c_double, _i64, _u64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "dgfx_synth_uniform_int": (_int, [_i64, _i64, _i64, _u64, ctypes.c_uint32, _vp, _vp]),

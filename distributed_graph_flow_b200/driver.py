@@ -6,12 +6,19 @@ seed batches sharded across ranks, the graph topology replicated in every
 GPU's HBM, node features node-range partitioned (rank r owns rows
 [r * rows_per_rank, (r + 1) * rows_per_rank)). The only exchange is the halo
 feature gather, replacing the Beam CoGroupByKey feature join
-(beam_semi_distributed_sampler_v2.py:271-387):
-  1. requested ids are stably partitioned by owner (dgfx_halo_partition);
-  2. counts, ids and rows move in NCCL all-to-alls over NVLink/NVSwitch;
-  3. owners gather their rows locally (dgfx_gather_rows_local) and the
-     received rows are scattered back to request order (dgfx_scatter_rows).
-With one rank the exchange degenerates to a local gather.
+(beam_semi_distributed_sampler_v2.py:271-387). Three interchangeable paths:
+  * HaloFeatures: requested ids are stably partitioned by owner
+    (dgfx_halo_partition); counts, ids and rows move in NCCL all-to-alls;
+    owners gather locally (dgfx_gather_rows_local) and received rows are
+    scattered back to request order (dgfx_scatter_rows). Needs host-side
+    counts (one device-to-host read per step).
+  * PeerFeatures, peer loads: one kernel reads every row from its owner's
+    partition through CUDA IPC mappings (dgfx_gather_rows_p2p).
+  * PeerFeatures, bulk exchange: the same all-to-all done by three kernels
+    over the IPC mappings (dgfx_exchange_*) with device-side counts and a
+    device barrier; NVLink traffic moves in contiguous runs. The default at
+    more than one rank.
+With one rank every path degenerates to a local gather.
 """
 
 from __future__ import annotations
@@ -113,42 +120,62 @@ class DeviceBuffer:
 
 
 class PeerFeatures:
-    """Node-range-partitioned features gathered with peer loads.
+    """Node-range-partitioned features gathered from peer memory.
 
     Each rank's partition lives in its own allocation whose CUDA IPC handle is
     shared with the other ranks once (all_gather of the 64-byte handles), so
-    every rank holds pointers to all partitions and one kernel
-    (dgfx_gather_rows_p2p) fetches any row from its owner over NVLink. Call
-    ``close()`` on every rank before the process group is destroyed.
+    every rank holds pointers to all partitions. Two gather paths:
+
+    * peer loads (``exchange_rows=0``): one kernel (dgfx_gather_rows_p2p)
+      fetches any row from its owner over NVLink;
+    * bulk exchange (``exchange_rows > 0``, more than one rank): requests are
+      bucketed by owner; owners gather their rows locally and write them into
+      each requester's inbox; requesters scatter the inbox into request order
+      (dgfx_exchange_*), so every byte crossing NVLink moves in contiguous
+      runs. Three stream-ordered launches separated by a device barrier over
+      peer flags (``barrier="device"``, bounded wait, no host round trip) or
+      a one-element NCCL all-reduce (``barrier="nccl"``). ``exchange_rows`` is
+      the capacity of one (requester, owner) slot; the batch capacity never
+      overflows it. ``check()`` reports overflow and barrier timeouts.
+
+    Call ``close()`` on every rank before the process group is destroyed.
     """
 
     def __init__(self, local_rows: int, dim: int, dtype, rows_per_rank: int, num_nodes: int, rank: int,
-                 world: int, device, group=None):
+                 world: int, device, group=None, exchange_rows: int = 0, barrier: str = "device",
+                 barrier_timeout_s: float = 10.0):
         torch = _native.require_cuda()
         self.rank, self.world, self.group = int(rank), int(world), group
         self.rows_per_rank, self.num_nodes, self.dim = int(rows_per_rank), int(num_nodes), int(dim)
+        self.local_rows = int(local_rows)
         self.dtype = dtype
         self.device = device
         self.row_bytes = torch.empty(0, dtype=dtype).element_size() * self.dim
         if self.row_bytes % 16:
             raise ValueError("feature rows must be a multiple of 16 bytes")
+        self.exchange_rows = int(exchange_rows) if self.world > 1 else 0
+        if barrier not in ("device", "nccl"):
+            raise ValueError(f"barrier must be 'device' or 'nccl', got {barrier!r}")
+        self.barrier = barrier
+        self.barrier_timeout_ns = int(barrier_timeout_s * 1e9)
+        self._epoch = 0
         self.buffer = DeviceBuffer(max(1, local_rows) * self.row_bytes, device)
         self.table = self.buffer.tensor((local_rows, self.dim), dtype)
         self._peers = []
         self._ptrs = None
+        self._ex = None
 
-    def connect(self):
-        """Exchanges IPC handles (collective over the group). Call after the
-        local partition is filled."""
+    def _share(self, local_ptr: int):
+        """All ranks' pointers to the allocation each rank passes (collective)."""
         torch = _native.require_cuda()
         lib = _native.lib()
         ptrs = [0] * self.world
-        ptrs[self.rank] = self.buffer.ptr
+        ptrs[self.rank] = local_ptr
         if self.world > 1:
             import torch.distributed as dist
 
             h = (ctypes.c_uint8 * 64)()
-            _native.check(lib.dgfx_ipc_get_handle(self.buffer.ptr, ctypes.cast(h, ctypes.c_void_p)))
+            _native.check(lib.dgfx_ipc_get_handle(local_ptr, ctypes.cast(h, ctypes.c_void_p)))
             mine = torch.tensor(list(bytes(h)), dtype=torch.uint8, device=self.device)
             allh = torch.empty((self.world, 64), dtype=torch.uint8, device=self.device)
             dist.all_gather_into_tensor(allh, mine, group=self.group)
@@ -161,19 +188,72 @@ class PeerFeatures:
                 _native.check(lib.dgfx_ipc_open(ctypes.cast(buf, ctypes.c_void_p), ctypes.byref(p)))
                 ptrs[r] = int(p.value)
                 self._peers.append(int(p.value))
-        self._ptrs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        return torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+
+    def connect(self):
+        """Exchanges IPC handles (collective over the group). Call after the
+        local partition is filled."""
+        torch = _native.require_cuda()
+        self._ptrs = self._share(self.buffer.ptr)
+        if self.exchange_rows > 0:
+            need = ctypes.c_size_t()
+            _native.check(_native.lib().dgfx_exchange_buffer_size(self.world, self.exchange_rows, self.row_bytes,
+                                                                  ctypes.byref(need)))
+            self._ex = DeviceBuffer(need.value, self.device)
+            self._ex.tensor((need.value,), torch.uint8).zero_()
+            self._ex_ptrs = self._share(self._ex.ptr)
+            self._req_pos = torch.empty(self.world * self.exchange_rows, dtype=torch.int32, device=self.device)
+            self._bar = torch.zeros(1, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
         return self
 
     def gather_range(self, ids, begin_ptr: int, end_ptr: int, max_rows: int, out, stream=None):
         """out[i] = feature row of ids[*begin + i] for i < min(*end - *begin, max_rows)."""
-        _native.check(_native.lib().dgfx_gather_rows_p2p(
-            _native.ptr(self._ptrs), self.world, self.rows_per_rank, self.num_nodes, self.row_bytes,
-            _native.ptr(ids), begin_ptr, end_ptr, int(max_rows), _native.ptr(out), _native.stream_handle(stream)))
+        if self._ex is None:
+            _native.check(_native.lib().dgfx_gather_rows_p2p(
+                _native.ptr(self._ptrs), self.world, self.rows_per_rank, self.num_nodes, self.row_bytes,
+                _native.ptr(ids), begin_ptr, end_ptr, int(max_rows), _native.ptr(out), _native.stream_handle(stream)))
+            return out
+        torch = _native.require_cuda()
+        import torch.distributed as dist
+
+        s = torch.cuda.current_stream(self.device) if stream is None else stream
+        sh = int(s.cuda_stream)
+        lib = _native.lib()
+        _native.check(lib.dgfx_exchange_partition(
+            self._ex.ptr, self.world, self.exchange_rows, self.rows_per_rank, self.num_nodes, self.row_bytes,
+            _native.ptr(ids), begin_ptr, end_ptr, int(max_rows), _native.ptr(self._req_pos), _native.ptr(out), sh))
+        self._group_barrier(s)
+        _native.check(lib.dgfx_exchange_serve(
+            _native.ptr(self._ex_ptrs), self.world, self.rank, self.exchange_rows, self.rows_per_rank, self.row_bytes,
+            self.buffer.ptr, self.local_rows, _native.ptr(self._req_pos), _native.ptr(out), sh))
+        self._group_barrier(s)
+        _native.check(lib.dgfx_exchange_scatter(
+            _native.ptr(self._ex_ptrs), self.world, self.rank, self.exchange_rows, self.row_bytes,
+            _native.ptr(self._req_pos), _native.ptr(out), sh))
         return out
 
+    def _group_barrier(self, s):
+        """Stream-ordered barrier over the group (every rank calls it in the same order)."""
+        if self.barrier == "device":
+            self._epoch = (self._epoch % 0x7FFFFFFF) + 1
+            _native.check(_native.lib().dgfx_exchange_barrier(_native.ptr(self._ex_ptrs), self.world, self.rank,
+                                                              self._epoch, self.barrier_timeout_ns, int(s.cuda_stream)))
+        else:
+            torch = _native.require_cuda()
+            import torch.distributed as dist
+
+            with torch.cuda.stream(s):
+                dist.all_reduce(self._bar, op=dist.ReduceOp.MAX, group=self.group)
+
+    def check(self, stream=None):
+        """Raises if an exchange slot overflowed or a barrier wait timed out
+        since the last check (synchronises)."""
+        if self._ex is not None:
+            _native.check(_native.lib().dgfx_exchange_check(self._ex.ptr, self.world, _native.stream_handle(stream)))
+
     def close(self):
-        """Unmaps the peers' partitions and frees this rank's (collective)."""
+        """Unmaps the peers' allocations and frees this rank's (collective)."""
         torch = _native.require_cuda()
         torch.cuda.synchronize(self.device)
         if self.world > 1:
@@ -187,6 +267,9 @@ class PeerFeatures:
             dist.barrier(group=self.group)
         self.table = None
         self.buffer.free()
+        if self._ex is not None:
+            self._ex.free()
+            self._ex = None
 
 
 class ShardedSampler:
@@ -213,7 +296,9 @@ class ShardedSampler:
             return self.step(seeds, seed_ts)
         dev = self.features.device
         if getattr(self, "gather_stream", None) is None:
-            self.gather_stream = torch.cuda.Stream(device=dev)
+            # High priority: the gather's CTAs are scheduled ahead of the
+            # queued sampler CTAs of the next call as SM slots free up.
+            self.gather_stream = torch.cuda.Stream(device=dev, priority=-1)
         main = torch.cuda.current_stream(dev)
         call = self._calls * self.world + self.rank
         self._calls += 1

@@ -288,6 +288,60 @@ int dgfx_gather_rows_p2p(const void* const* d_tables, int32_t world,
                          int64_t max_rows, void* d_out, dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Bulk peer exchange of feature rows (same result as dgfx_gather_rows_p2p;
+ * every byte that crosses NVLink moves in contiguous runs, every random row
+ * access is to this GPU's own HBM). Each rank owns one exchange buffer of
+ * dgfx_exchange_buffer_size bytes (dgfx_device_alloc, shared by CUDA IPC like
+ * the partitions, zeroed once): per-owner request counts, per-owner request-id
+ * slots of slot_rows ids, barrier flags and per-owner row inboxes of slot_rows
+ * rows. A step is three stream-ordered launches separated by group barriers
+ * (dgfx_exchange_barrier, or any group-wide barrier on the same stream):
+ *   dgfx_exchange_partition (requester): zeroes this rank's counts and puts
+ *     ids[*d_begin + i] (i < min(*d_end - *d_begin, max_rows)) into the slot
+ *     of its owner o = id / rows_per_rank; d_req_pos[o * slot_rows + k] = i.
+ *     Ids outside [0, num_nodes) get a zero row in d_out here.
+ *   -- barrier --
+ *   dgfx_exchange_serve (owner): reads every requester's slot for this rank
+ *     (contiguous peer reads), gathers the rows from the local partition and
+ *     writes them into that requester's inbox (contiguous peer stores); its
+ *     own requests go straight to d_out.
+ *   -- barrier --
+ *   dgfx_exchange_scatter (requester): d_out[d_req_pos[...]] = inbox rows.
+ * dgfx_exchange_barrier: every rank publishes `epoch` (increasing per call,
+ * same sequence on all ranks, starting at 1) in the other ranks' flags and
+ * waits for theirs, at most max_wait_ns; a wait that runs out sets the
+ * timeout flag instead of hanging.
+ * dgfx_exchange_check (synchronises the stream) reports and clears the flags:
+ * slot overflow (a slot needed more than slot_rows ids; rows were dropped) as
+ * DGFX_ERR_WORKSPACE, barrier timeout as DGFX_ERR_FAILED_PRECONDITION.
+ * d_exchanges is a device array of the `world` exchange-buffer pointers (own
+ * included); d_req_pos holds world * slot_rows int32 and stays on this rank.
+ * world <= 16.
+ * ------------------------------------------------------------------------ */
+int dgfx_exchange_buffer_size(int32_t world, int64_t slot_rows,
+                              int64_t row_bytes, size_t* bytes);
+int dgfx_exchange_partition(void* d_exchange, int32_t world, int64_t slot_rows,
+                            int64_t rows_per_rank, int64_t num_nodes,
+                            int64_t row_bytes, const int64_t* d_row_ids,
+                            const int64_t* d_begin, const int64_t* d_end,
+                            int64_t max_rows, int32_t* d_req_pos, void* d_out,
+                            dgfx_stream stream);
+int dgfx_exchange_serve(const void* const* d_exchanges, int32_t world,
+                        int32_t rank, int64_t slot_rows, int64_t rows_per_rank,
+                        int64_t row_bytes, const void* d_table,
+                        int64_t local_rows, const int32_t* d_req_pos,
+                        void* d_out, dgfx_stream stream);
+int dgfx_exchange_scatter(const void* const* d_exchanges, int32_t world,
+                          int32_t rank, int64_t slot_rows, int64_t row_bytes,
+                          const int32_t* d_req_pos, void* d_out,
+                          dgfx_stream stream);
+int dgfx_exchange_barrier(const void* const* d_exchanges, int32_t world,
+                          int32_t rank, uint32_t epoch, uint64_t max_wait_ns,
+                          dgfx_stream stream);
+int dgfx_exchange_check(const void* d_exchange, int32_t world,
+                        dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
  * Seeded synthetic inputs (stand-ins for the benchmark datasets, the role of
  * the reference's dgf/src/util/gen_test_graph.py generators at scale).
  * dgfx_synth_graph: power-law out-degrees (P(d) ~ d^-alpha, capped at

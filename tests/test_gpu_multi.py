@@ -1,10 +1,14 @@
 """Multi-GPU halo feature exchange with the real kernels and NCCL.
 
-Runs only where at least two GPUs are visible: two spawned ranks each hold a
-node-range partition of a feature table; rows gathered through
-HaloFeatures (partition by owner, NCCL all-to-alls, local gather, scatter)
-must equal the rows of the full table, and ShardedSampler steps on every rank
-must produce features that match their sampled node ids.
+The two-rank test runs only where at least two GPUs are visible: two spawned
+ranks each hold a node-range partition of a feature table; rows gathered
+through HaloFeatures (NCCL all-to-alls), PeerFeatures peer loads and the
+PeerFeatures bulk exchange must equal the rows of the full table, and
+ShardedSampler steps on every rank must produce features that match their
+sampled node ids. The exchange kernels are also run for several ranks
+emulated on one GPU (no waits between them: stream order is the barrier),
+and the device barrier's bounded wait is run out on one GPU with a flag that
+nothing sets.
 """
 
 import os
@@ -82,6 +86,28 @@ def _worker(rank, world, port, q):
         total = int(merged.node_offsets[-1].item())
         assert torch.equal(feats[:total], full[merged.node_ids[:total]])
         pf.close()
+        # Bulk exchange over the same partition (IPC-shared exchange buffers),
+        # with the device barrier and with NCCL all-reduce barriers, direct
+        # and through pipelined steps.
+        cap_nodes = int(merged.node_ids.numel())
+        for barrier in ("device", "nccl"):
+            pe = driver.PeerFeatures(hi - lo, F, torch.bfloat16, rpr, spec.num_nodes, rank, world, dev,
+                                     exchange_rows=max(20_000, cap_nodes), barrier=barrier)
+            pe.table.copy_(full[lo:hi])
+            pe.connect()
+            out.fill_(0)
+            pe.gather_range(ids, _native.elem_ptr(bounds, 0), _native.elem_ptr(bounds, 1), 20_000, out)
+            torch.cuda.synchronize()
+            assert torch.equal(out[: len(sel)], exp), f"exchange gather rank {rank} ({barrier})"
+            ss3 = driver.ShardedSampler(cc, pe, rank, world)
+            for _ in range(3):
+                merged, feats, _ = ss3.step_overlapped(seeds)
+                ss3.drain()
+                torch.cuda.synchronize()
+                total = int(merged.node_offsets[-1].item())
+                assert torch.equal(feats[:total], full[merged.node_ids[:total]]), f"exchange step {rank} ({barrier})"
+            pe.check()
+            pe.close()
         q.put((rank, "ok"))
     except Exception as exc:  # noqa: BLE001
         q.put((rank, repr(exc)))
@@ -108,6 +134,123 @@ def test_peer_gather_single_rank(cuda):
     assert torch.count_nonzero(out[1]) == 0 and torch.count_nonzero(out[3]) == 0
     assert torch.equal(out[6], torch.full((F,), 3.0, dtype=torch.bfloat16, device=dev))  # past *end: untouched
     pf.close()
+
+
+def _run_exchange(lib, W, rpr, N, row_bytes, parts, ids, bounds, caps, outs, slot, sh):
+    """The three exchange launches for W ranks whose buffers all live on one
+    GPU; issuing every rank's step before the next step's launches (one
+    stream) is the barrier."""
+    import ctypes
+
+    import torch
+
+    from distributed_graph_flow_b200 import _native
+
+    need = ctypes.c_size_t()
+    _native.check(lib.dgfx_exchange_buffer_size(W, slot, row_bytes, ctypes.byref(need)))
+    dev = outs[0].device
+    bufs = [torch.zeros(need.value, dtype=torch.uint8, device=dev) for _ in range(W)]
+    ptrs = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=dev)
+    pos = [torch.empty(W * slot, dtype=torch.int32, device=dev) for _ in range(W)]
+    for r in range(W):
+        _native.check(lib.dgfx_exchange_partition(
+            _native.ptr(bufs[r]), W, slot, rpr, N, row_bytes, _native.ptr(ids[r]), _native.elem_ptr(bounds[r], 0),
+            _native.elem_ptr(bounds[r], 1), caps[r], _native.ptr(pos[r]), _native.ptr(outs[r]), sh))
+    for r in range(W):
+        _native.check(lib.dgfx_exchange_serve(
+            _native.ptr(ptrs), W, r, slot, rpr, row_bytes, _native.ptr(parts[r]), int(parts[r].shape[0]),
+            _native.ptr(pos[r]), _native.ptr(outs[r]), sh))
+    for r in range(W):
+        _native.check(lib.dgfx_exchange_scatter(_native.ptr(ptrs), W, r, slot, row_bytes, _native.ptr(pos[r]),
+                                                _native.ptr(outs[r]), sh))
+    return bufs
+
+
+def test_exchange_emulated_ranks(cuda):
+    """Bulk peer exchange (dgfx_exchange_partition / serve / scatter) for 1, 3
+    and 8 ranks emulated on one GPU: every rank's rows equal the full table's
+    rows in request order, ids outside the graph give zero rows, rows past
+    min(*end - *begin, max_rows) stay untouched, buffers are reusable, and a
+    slot smaller than a rank's requests to one owner is reported (and the
+    flag cleared) by dgfx_exchange_check."""
+    from distributed_graph_flow_b200 import _native, synth
+
+    lib = _native.lib()
+    dev = torch.device("cuda", 0)
+    sh = _native.stream_handle()
+    N, F = 20_011, 64
+    row_bytes = F * 2
+    full = synth.normal_features(0, N, F, 4, torch.bfloat16, dev)
+    rng = np.random.default_rng(11)
+    for W in (1, 3, 8):
+        rpr = -(-N // W)
+        parts = [full[r * rpr:min(N, (r + 1) * rpr)].contiguous() for r in range(W)]
+        sizes = [int(x) for x in rng.choice([0, 1, 33, 4000, 9000], W)]
+        sizes[0] = 9000
+        ids, bounds, caps, outs = [], [], [], []
+        for r in range(W):
+            lo = int(rng.integers(0, 5))
+            n = sizes[r]
+            ids.append(torch.from_numpy(rng.integers(-3, N + 3, n + lo + 4)).to(dev))
+            bounds.append(torch.tensor([lo, lo + n], dtype=torch.int64, device=dev))
+            caps.append(n if r % 2 == 0 else max(0, n - 5))  # odd ranks: max_rows below the bound count
+            outs.append(torch.full((n + 2, F), 3.0, dtype=torch.bfloat16, device=dev))
+        slot = max(max(caps), 1)
+        for _rep in range(2):
+            for o in outs:
+                o.fill_(3.0)
+            bufs = _run_exchange(lib, W, rpr, N, row_bytes, parts, ids, bounds, caps, outs, slot, sh)
+            torch.cuda.synchronize()
+            for r in range(W):
+                lo, n = int(bounds[r][0]), caps[r]
+                sel = ids[r][lo:lo + n]
+                ok = (sel >= 0) & (sel < N)
+                exp = torch.zeros((n, F), dtype=torch.bfloat16, device=dev)
+                exp[ok] = full[sel[ok]]
+                assert torch.equal(outs[r][:n], exp), f"W={W} rank {r}"
+                assert bool((outs[r][n:] == 3.0).all()), f"W={W} rank {r}: rows past the end written"
+                _native.check(lib.dgfx_exchange_check(_native.ptr(bufs[r]), W, sh))
+        if W > 1:
+            small = 16
+            bufs = _run_exchange(lib, W, rpr, N, row_bytes, parts, ids, bounds, caps, outs, small, sh)
+            with pytest.raises(RuntimeError, match="overflowed"):
+                _native.check(lib.dgfx_exchange_check(_native.ptr(bufs[0]), W, sh))
+            _native.check(lib.dgfx_exchange_check(_native.ptr(bufs[0]), W, sh))  # flag cleared
+
+
+def test_exchange_barrier_single_gpu(cuda):
+    """dgfx_exchange_barrier on one GPU: with one rank it passes at once; with
+    two ranks whose peer flag already holds the epoch it passes; with a peer
+    flag that nothing sets, the bounded wait runs out and dgfx_exchange_check
+    reports the timeout (and clears it) while the context stays usable."""
+    import ctypes
+    import time
+
+    from distributed_graph_flow_b200 import _native
+
+    lib = _native.lib()
+    dev = torch.device("cuda", 0)
+    sh = _native.stream_handle()
+    need = ctypes.c_size_t()
+    _native.check(lib.dgfx_exchange_buffer_size(2, 64, 128, ctypes.byref(need)))
+    buf = torch.zeros(need.value, dtype=torch.uint8, device=dev)
+    ptrs = torch.tensor([buf.data_ptr(), buf.data_ptr()], dtype=torch.int64, device=dev)
+    one = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
+    for epoch in (1, 2, 3):
+        _native.check(lib.dgfx_exchange_barrier(_native.ptr(one), 1, 0, epoch, 10**9, sh))
+    _native.check(lib.dgfx_exchange_check(buf.data_ptr(), 1, sh))
+    flags = buf[192:256].view(torch.int32)  # arrival epochs, one uint32 per rank
+    flags[1] = 7
+    _native.check(lib.dgfx_exchange_barrier(_native.ptr(ptrs), 2, 0, 7, 10**9, sh))
+    _native.check(lib.dgfx_exchange_check(buf.data_ptr(), 2, sh))
+    flags[1] = 0
+    t0 = time.time()
+    _native.check(lib.dgfx_exchange_barrier(_native.ptr(ptrs), 2, 0, 8, 2 * 10**6, sh))  # 2 ms bound
+    with pytest.raises(ValueError, match="timed out"):
+        _native.check(lib.dgfx_exchange_check(buf.data_ptr(), 2, sh))
+    assert time.time() - t0 < 5.0
+    _native.check(lib.dgfx_exchange_check(buf.data_ptr(), 2, sh))  # cleared
+    assert torch.cuda.is_available() and int(flags[0].item()) == 8
 
 
 def test_halo_exchange_two_gpus(cuda):
