@@ -76,6 +76,8 @@ struct Params {
   const EdgeDev* edges;
   const int4* tasks;       // (parent position, plan edge, first child slot, 0)
   const int32_t* level;    // tasks of depth d: [level[d], level[d+1])
+  const int32_t* children; // child slots of the depth-d tasks: [clevel[d], clevel[d+1])
+  const int32_t* clevel;
   int32_t depth;           // number of expansion levels
   const int2* pos_info;    // (parent position, plan edge << 8 | nodeset)
   int32_t T, N2, H, log2H;
@@ -135,11 +137,14 @@ __device__ __forceinline__ uint64_t draw64(const Params& p, int32_t q, int32_t e
   return (m & 1u) ? (static_cast<uint64_t>(r.w) << 32 | r.z) : (static_cast<uint64_t>(r.y) << 32 | r.x);
 }
 
-// One expansion task: pick up to k neighbours of node v over plan edge e and
-// write them to the child slots base + j * stride (j < k).
+// One expansion task, first half: choose up to k neighbours of node v over
+// plan edge e and record their CSR positions (int64, -1 = empty) in the
+// child slots base + j * stride (j < k) of the pick array `at`. The column
+// loads happen afterwards, one child slot per thread (load_children), so a
+// task costs one dependent global load (its row bounds), not k.
 // stats[0..2] (shared) count expanded rows, sampled neighbours and timestamp
 // probes of this CTA.
-__device__ void expand_task(const Params& p, const Work& w, int32_t q, int32_t e, int32_t base, int64_t v,
+__device__ void expand_task(const Params& p, long long* at, int32_t q, int32_t e, int32_t base, int64_t v,
                             bool has_ts, int64_t seed_ts, int64_t mask, uint32_t slot, unsigned int* stats) {
   const EdgeDev E = p.edges[e];
   const int32_t k = E.k, stride = E.stride;
@@ -187,40 +192,65 @@ __device__ void expand_task(const Params& p, const Work& w, int32_t q, int32_t e
           const uint64_t r = draw64(p, q, e, static_cast<uint32_t>(taken), slot);
           int64_t t = static_cast<int64_t>(bounded64(r, static_cast<uint64_t>(j + 1)));
           for (int32_t i = 0; i < taken; ++i) {
-            if (w.node[base + i * stride] == t) {
+            if (at[base + i * stride] == t) {
               t = j;
               break;
             }
           }
-          w.node[base + taken * stride] = static_cast<int32_t>(t);
+          at[base + taken * stride] = t;
           ++taken;
         }
         // Adjacency order (insertion sort over the slots).
         for (int32_t i = 1; i < cnt; ++i) {
-          const int32_t x = w.node[base + i * stride];
+          const long long x = at[base + i * stride];
           int32_t j = i - 1;
-          while (j >= 0 && w.node[base + j * stride] > x) {
-            w.node[base + (j + 1) * stride] = w.node[base + j * stride];
+          while (j >= 0 && at[base + j * stride] > x) {
+            at[base + (j + 1) * stride] = at[base + j * stride];
             --j;
           }
-          w.node[base + (j + 1) * stride] = x;
+          at[base + (j + 1) * stride] = x;
         }
         for (int32_t i = 0; i < cnt; ++i) {
-          int64_t off = w.node[base + i * stride];
+          long long off = at[base + i * stride];
           if (moff >= 0 && off >= moff) ++off;
-          w.node[base + i * stride] = E.col[rb + off];
+          at[base + i * stride] = rb + off;
         }
       } else {
         const int64_t first = (mode == DGFX_MODE_MOST_RECENT) ? nv - cnt : 0;
         for (int32_t i = 0; i < cnt; ++i) {
           int64_t off = first + i;
           if (moff >= 0 && off >= moff) ++off;
-          w.node[base + i * stride] = E.col[rb + off];
+          at[base + i * stride] = rb + off;
         }
       }
     }
   }
-  for (int32_t i = cnt; i < k; ++i) w.node[base + i * stride] = -1;
+  for (int32_t i = cnt; i < k; ++i) at[base + i * stride] = -1;
+}
+
+// Expansion, second half: node[q] = col[at[q]] for the child slots
+// children[c0..c1), four independent loads in flight per thread.
+__device__ void load_children(const Params& p, const Work& w, const long long* at, int c0, int c1) {
+  constexpr int kIlp = 4;
+  const int bd = blockDim.x;
+  for (int i0 = c0 + threadIdx.x; i0 < c1; i0 += kIlp * bd) {
+    int32_t q[kIlp];
+    int32_t v[kIlp];
+#pragma unroll
+    for (int u = 0; u < kIlp; ++u) {
+      const int i = i0 + u * bd;
+      q[u] = i < c1 ? p.children[i] : -1;
+      v[u] = -1;
+      if (q[u] >= 0) {
+        const long long a = at[q[u]];
+        if (a >= 0) v[u] = p.edges[p.pos_info[q[u]].y >> 8].col[a];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kIlp; ++u) {
+      if (q[u] >= 0) w.node[q[u]] = v[u];
+    }
+  }
 }
 
 // Exclusive scan over items [0, n) of a block: value(i) is read twice (must
@@ -327,6 +357,8 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   __shared__ int32_t ns_base[kMaxNodesets];
   __shared__ int32_t es_count[kMaxEdgesets];
   __shared__ unsigned int stats[3];
+  __shared__ int32_t wtot[8];
+  __shared__ int lbits_s;
 
   const int64_t sample = blockIdx.x;
   const int T = p.T;
@@ -355,13 +387,18 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   }
   __syncthreads();
 
-  // 1. Level-synchronous expansion.
+  // 1. Level-synchronous expansion: picks (CSR positions, in the dedup
+  //    table's words, which are free until the relabel), then the column
+  //    loads of all picks of the level in parallel.
+  long long* at = reinterpret_cast<long long*>(w.slot);
   for (int d = 0; d < p.depth; ++d) {
     const int t0 = p.level[d], t1 = p.level[d + 1];
     for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
       const int4 task = p.tasks[t];
-      expand_task(p, w, task.x, task.y, task.z, w.node[task.x], has_ts, sts, mask, slot, stats);
+      expand_task(p, at, task.x, task.y, task.z, w.node[task.x], has_ts, sts, mask, slot, stats);
     }
+    __syncthreads();
+    load_children(p, w, at, p.clevel[d], p.clevel[d + 1]);
     __syncthreads();
   }
 
@@ -402,53 +439,79 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
     }
     __syncthreads();
   }
-  // Number first discoveries per nodeset, up to 4 nodesets per pass (16-bit
-  // fields; T <= 65535 here) or 2 per pass (32-bit fields).
-  const int per_pass = T < 65536 ? 4 : 2;
-  const int fbits = 64 / per_pass;
-  const uint64_t fmask = (fbits == 64) ? ~0ull : ((1ull << fbits) - 1);
-  for (int g = 0; g < p.num_nodesets; g += per_pass) {
-    auto first = [&](int q) -> bool {
-      if (p.with_replacement) return w.node[q] >= 0;
-      const int32_t s = w.local[q];
-      return s >= 0 && static_cast<uint32_t>(w.slot[s]) == static_cast<uint32_t>(q);
-    };
-    auto value = [&](int q) -> uint64_t {
-      const int ns = p.pos_info[q].y & 0xFF;
-      if (ns < g || ns >= g + per_pass || !first(q)) return 0;
-      return 1ull << ((ns - g) * fbits);
-    };
-    auto sink = [&](int q, uint64_t pre) {
-      const int ns = p.pos_info[q].y & 0xFF;
-      if (ns < g || ns >= g + per_pass || !first(q)) return;
-      const uint32_t rank = static_cast<uint32_t>((pre >> ((ns - g) * fbits)) & fmask);
+  // Number first discoveries per nodeset in position order. Warps own
+  // contiguous position ranges (rounds of 32); pass 1 counts first
+  // discoveries per (warp, nodeset), pass 2 ranks them: rank = first
+  // discoveries of the nodeset in earlier warps + earlier rounds + earlier
+  // lanes. A position is a first discovery iff the dedup word of its node
+  // still holds it as the minimum position (the rank written by pass 2 has
+  // bit 31 set, so it never equals a position).
+  const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  const int NS = p.num_nodesets;
+  int32_t* wcnt = cnt;  // [nw][NS]; the radix-sort counters are free here
+  const int pchunk = ((T + nw - 1) / nw + 31) & ~31;
+  const int plo = min(T, warp * pchunk), phi = min(T, plo + pchunk);
+  auto first_ns = [&](int q) -> int {
+    if (q >= phi) return -1;
+    if (p.with_replacement) {
+      if (w.node[q] < 0) return -1;
+    } else {
+      const int32_t sl = w.local[q];
+      if (sl < 0 || static_cast<uint32_t>(w.slot[sl]) != static_cast<uint32_t>(q)) return -1;
+    }
+    return p.pos_info[q].y & 0xFF;
+  };
+  for (int i = threadIdx.x; i < nw * NS; i += blockDim.x) wcnt[i] = 0;
+  __syncthreads();
+  for (int b = plo; b < phi; b += 32) {
+    const int ns = first_ns(b + lane);
+    const uint32_t peers = __match_any_sync(0xffffffffu, ns);
+    if (ns >= 0 && (peers & lt) == 0) wcnt[warp * NS + ns] += __popc(peers);
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < NS; g += blockDim.x) {
+    int32_t run = 0;
+    for (int v = 0; v < nw; ++v) {
+      const int32_t c = wcnt[v * NS + g];
+      wcnt[v * NS + g] = run;
+      run += c;
+    }
+    ns_count[g] = run;
+  }
+  __syncthreads();
+  for (int b = plo; b < phi; b += 32) {
+    const int q = b + lane;
+    const int ns = first_ns(q);
+    const uint32_t peers = __match_any_sync(0xffffffffu, ns);
+    if (ns >= 0) {
+      const uint32_t rank = static_cast<uint32_t>(wcnt[warp * NS + ns]) + __popc(peers & lt);
       if (p.with_replacement) {
         w.local[q] = static_cast<int32_t>(rank);
       } else {
-        const int32_t s = w.local[q];
-        w.slot[s] = (w.slot[s] & 0xFFFFFFFF00000000ull) | (0x80000000u | rank);
-      }
-    };
-    const uint64_t tot = block_scan_items(T, value, sink, scan_tmp);
-    if (threadIdx.x == 0) {
-      for (int s = g; s < g + per_pass && s < p.num_nodesets; ++s) {
-        ns_count[s] = static_cast<int32_t>((tot >> ((s - g) * fbits)) & fmask);
+        const int32_t sl = w.local[q];
+        w.slot[sl] = (w.slot[sl] & 0xFFFFFFFF00000000ull) | (0x80000000u | rank);
       }
     }
+    __syncwarp();
+    if (ns >= 0 && (peers & lt) == 0) wcnt[warp * NS + ns] += __popc(peers);
+    __syncwarp();
   }
   __syncthreads();
   if (!p.with_replacement) {
     for (int q = threadIdx.x; q < T; q += blockDim.x) {
-      const int32_t s = w.local[q];
-      w.local[q] = s >= 0 ? static_cast<int32_t>(static_cast<uint32_t>(w.slot[s]) & 0x7FFFFFFFu) : -1;
+      const int32_t sl = w.local[q];
+      w.local[q] = sl >= 0 ? static_cast<int32_t>(static_cast<uint32_t>(w.slot[sl]) & 0x7FFFFFFFu) : -1;
     }
   }
   if (threadIdx.x == 0) {
-    int32_t acc = 0;
-    for (int s = 0; s < p.num_nodesets; ++s) {
-      ns_base[s] = acc;
-      acc += ns_count[s];
+    int32_t acc = 0, most = 1;
+    for (int g = 0; g < NS; ++g) {
+      ns_base[g] = acc;
+      acc += ns_count[g];
+      most = ns_count[g] > most ? ns_count[g] : most;
     }
+    lbits_s = max(1, 32 - __clz(most - 1));
   }
   __syncthreads();
 
@@ -463,41 +526,53 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
     if (l >= 0) out_nodes[ns_base[ns] + l] = v;
   }
 
-  // 3. Edge keys (edgeset | src_local | dst_local) of positions 1..T-1,
-  //    radix-sorted and deduplicated. Empty positions get the key
-  //    num_edgesets << 2*pbits, which sorts after every real edge.
-  const int n_keys = T - 1;
-  const int pb = p.pbits;
-  const unsigned long long invalid = static_cast<unsigned long long>(p.num_edgesets) << (2 * pb);
+  // 3. Edge keys (edgeset | src_local | dst_local), local ids in lb bits (the
+  //    widest local id of this sample), one per occupied non-root position,
+  //    compacted in position order by warp ballots, radix-sorted (stable)
+  //    and deduplicated. The dedup table's words are free again.
+  const int lb = lbits_s;
+  const int esbits = p.keybits - 2 * p.pbits;
   unsigned long long* keys = w.slot;
   unsigned long long* tmp = w.slot + T;
-  for (int i = threadIdx.x; i < n_keys; i += blockDim.x) {
-    unsigned long long key = invalid;
-    const int q = i + 1;
-    if (w.node[q] >= 0 && w.local[q] >= 0) {
-      const int2 info = p.pos_info[q];
-      const int e = info.y >> 8;
-      const EdgeDev& E = p.edges[e];
-      const unsigned long long a = static_cast<uint32_t>(w.local[info.x]);
-      const unsigned long long b = static_cast<uint32_t>(w.local[q]);
-      const unsigned long long src = E.reversed ? b : a, dst = E.reversed ? a : b;
-      key = (static_cast<unsigned long long>(E.edgeset) << (2 * pb)) | (src << pb) | dst;
-    }
-    keys[i] = key;
+  auto edge_key = [&](int q, unsigned long long* key) -> bool {
+    if (q < 1 || q >= phi || w.node[q] < 0 || w.local[q] < 0) return false;
+    const int2 info = p.pos_info[q];
+    const EdgeDev& E = p.edges[info.y >> 8];
+    const unsigned long long a = static_cast<uint32_t>(w.local[info.x]);
+    const unsigned long long b = static_cast<uint32_t>(w.local[q]);
+    const unsigned long long src = E.reversed ? b : a, dst = E.reversed ? a : b;
+    *key = (static_cast<unsigned long long>(E.edgeset) << (2 * lb)) | (src << lb) | dst;
+    return true;
+  };
+  int32_t wsum = 0;
+  for (int b = plo; b < phi; b += 32) {
+    unsigned long long key;
+    wsum += __popc(__ballot_sync(0xffffffffu, edge_key(b + lane, &key)));
+  }
+  if (lane == 0) wtot[warp] = wsum;
+  __syncthreads();
+  int32_t wbase = 0, n_keys = 0;
+  for (int v = 0; v < nw; ++v) {
+    wbase += v < warp ? wtot[v] : 0;
+    n_keys += wtot[v];
+  }
+  for (int b = plo; b < phi; b += 32) {
+    unsigned long long key = 0;
+    const bool ok = edge_key(b + lane, &key);
+    const uint32_t m = __ballot_sync(0xffffffffu, ok);
+    if (ok) keys[wbase + __popc(m & lt)] = key;
+    wbase += __popc(m);
   }
   __syncthreads();
-  const unsigned long long* ek = block_radix_sort(keys, tmp, n_keys, p.keybits, cnt, dbase);
+  const unsigned long long* ek = block_radix_sort(keys, tmp, n_keys, esbits + 2 * lb, cnt, dbase);
   uint64_t* out_edges = p.scratch_edges + sample * static_cast<int64_t>(T);
-  const unsigned long long lmask = (1ull << pb) - 1;
-  auto is_new = [&](int i) -> uint64_t {
-    const unsigned long long k = ek[i];
-    return (k != invalid && (i == 0 || ek[i - 1] != k)) ? 1ull : 0ull;
-  };
+  const unsigned long long lmask = (1ull << lb) - 1;
+  auto is_new = [&](int i) -> uint64_t { return (i == 0 || ek[i - 1] != ek[i]) ? 1ull : 0ull; };
   auto put = [&](int i, uint64_t pre) {
     const unsigned long long k = ek[i];
-    if (k != invalid && (i == 0 || ek[i - 1] != k)) {
-      const unsigned long long es = k >> (2 * pb);
-      out_edges[pre] = (es << 48) | (((k >> pb) & lmask) << 24) | (k & lmask);
+    if (i == 0 || ek[i - 1] != k) {
+      const unsigned long long es = k >> (2 * lb);
+      out_edges[pre] = (es << 48) | (((k >> lb) & lmask) << 24) | (k & lmask);
       atomicAdd(&es_count[static_cast<int>(es)], 1);
     }
   };
@@ -582,6 +657,8 @@ struct dgfx_sampler {
   EdgeDev* d_edges = nullptr;
   int4* d_tasks = nullptr;
   int32_t* d_level = nullptr;
+  int32_t* d_children = nullptr;
+  int32_t* d_clevel = nullptr;
   int2* d_pos = nullptr;
   unsigned long long* d_status = nullptr;
   int64_t last_B = 0;
@@ -741,9 +818,16 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
   if (num_plan_edges >= (1 << 23)) return fail(DGFX_ERR_UNSUPPORTED, "dgfx_sampler_create: too many plan edges");
   std::vector<int4> tasks;
   std::vector<int32_t> level{0};
+  std::vector<int32_t> children;
+  std::vector<int32_t> clevel{0};
   for (auto& v : tasks_by_depth) {
     tasks.insert(tasks.end(), v.begin(), v.end());
     level.push_back(static_cast<int32_t>(tasks.size()));
+    for (const int4& t : v) {
+      const int32_t zc = static_cast<int32_t>(Z[edge_child[t.y]]);
+      for (int k = 0; k < slots[t.y]; ++k) children.push_back(t.z + k * zc);
+    }
+    clevel.push_back(static_cast<int32_t>(children.size()));
   }
   s->depth = static_cast<int32_t>(tasks_by_depth.size());
   s->root_has_children = node_num_edges[0] > 0;
@@ -785,21 +869,30 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
   const size_t b_tasks = align_up(sizeof(int4) * std::max<size_t>(1, tasks.size()), 256);
   const size_t b_level = align_up(sizeof(int32_t) * level.size(), 256);
   const size_t b_pos = align_up(sizeof(int2) * pos.size(), 256);
+  const size_t b_children = align_up(sizeof(int32_t) * std::max<size_t>(1, children.size()), 256);
+  const size_t b_clevel = align_up(sizeof(int32_t) * clevel.size(), 256);
   const size_t b_status = 256;
   char* d = nullptr;
-  DGFX_CUDA_TRY(cudaMalloc(&d, b_edges + b_tasks + b_level + b_pos + b_status));
+  DGFX_CUDA_TRY(cudaMalloc(&d, b_edges + b_tasks + b_level + b_pos + b_children + b_clevel + b_status));
   s->d_tables = d;
   s->d_edges = reinterpret_cast<EdgeDev*>(d);
   s->d_tasks = reinterpret_cast<int4*>(d + b_edges);
   s->d_level = reinterpret_cast<int32_t*>(d + b_edges + b_tasks);
   s->d_pos = reinterpret_cast<int2*>(d + b_edges + b_tasks + b_level);
-  s->d_status = reinterpret_cast<unsigned long long*>(d + b_edges + b_tasks + b_level + b_pos);
+  s->d_children = reinterpret_cast<int32_t*>(d + b_edges + b_tasks + b_level + b_pos);
+  s->d_clevel = reinterpret_cast<int32_t*>(d + b_edges + b_tasks + b_level + b_pos + b_children);
+  s->d_status =
+      reinterpret_cast<unsigned long long*>(d + b_edges + b_tasks + b_level + b_pos + b_children + b_clevel);
   if (!s->h_edges.empty()) {
     DGFX_CUDA_TRY(cudaMemcpy(s->d_edges, s->h_edges.data(), sizeof(EdgeDev) * s->h_edges.size(), cudaMemcpyHostToDevice));
   }
   if (!tasks.empty()) DGFX_CUDA_TRY(cudaMemcpy(s->d_tasks, tasks.data(), sizeof(int4) * tasks.size(), cudaMemcpyHostToDevice));
   DGFX_CUDA_TRY(cudaMemcpy(s->d_level, level.data(), sizeof(int32_t) * level.size(), cudaMemcpyHostToDevice));
   DGFX_CUDA_TRY(cudaMemcpy(s->d_pos, pos.data(), sizeof(int2) * pos.size(), cudaMemcpyHostToDevice));
+  if (!children.empty()) {
+    DGFX_CUDA_TRY(cudaMemcpy(s->d_children, children.data(), sizeof(int32_t) * children.size(), cudaMemcpyHostToDevice));
+  }
+  DGFX_CUDA_TRY(cudaMemcpy(s->d_clevel, clevel.data(), sizeof(int32_t) * clevel.size(), cudaMemcpyHostToDevice));
   const unsigned long long init[6] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
   DGFX_CUDA_TRY(cudaMemcpy(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice));
 
@@ -874,6 +967,8 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   p.edges = s->d_edges;
   p.tasks = s->d_tasks;
   p.level = s->d_level;
+  p.children = s->d_children;
+  p.clevel = s->d_clevel;
   p.depth = s->depth;
   p.pos_info = s->d_pos;
   p.T = s->T;
