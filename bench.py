@@ -4,14 +4,16 @@
 Headline (one JSON line on rank 0): sampled subgraphs/s of the large sharded
 workload — 111,059,956 nodes / 1,615,685,872 edges (Zipf(2.0) out-degrees),
 bf16 128-d features node-range partitioned across the ranks, 3-hop fanout
-[15, 10, 5], 8192 seeds per GPU per step, halo features gathered with NCCL
-all-to-all when N > 1. A step = sample one batch of seeds + gather the
-features of every sampled node. Synthetic inputs stand in for the dataset.
+[15, 10, 5], 8192 seeds per GPU per step; when N > 1 the feature halo moves
+in the bulk peer exchange over NVLink (driver.PeerFeatures). A step = sample
+one batch of seeds + gather the features of every sampled node. Synthetic
+inputs stand in for the dataset.
 
 At N = 1 the line also carries the standalone CSR SpMM (2,449,029 rows,
-61,859,140 nnz, 256 features, fp32 and bf16: achieved HBM GB/s) and the
-temporal 169K-node sampler (fanout [10, 5], 1024 seeds, cutoff = seed
-timestamp) next to their CPU baselines.
+61,859,140 nnz, 256 features, fp32 and bf16: achieved HBM GB/s), the temporal
+169K-node sampler (fanout [10, 5], 1024 seeds, cutoff = seed timestamp) and
+the heterogeneous temporal sampler (4 node sets, 4 edge types, 4096 seeds)
+next to their CPU baselines.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dgfx|reference]
 """
@@ -573,6 +575,88 @@ def bench_temporal(dev, steps, scale=1.0):
     return out
 
 
+def bench_hetero(dev, steps, scale=1.0):
+    """Heterogeneous temporal sampling: 4 node sets / 4 edge types, edge
+    times propagated from node set A's creation years, A seeds with cutoff =
+    seed year, both directions of every edge type, per-hop widths [15, 10];
+    fp32 128-d features of every sampled A node gathered."""
+    import torch
+
+    from distributed_graph_flow_b200 import _native, synth
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+
+    spec = synth.scaled_hetero(synth.HETERO_TEMPORAL, scale)
+    t0 = time.time()
+    g = synth.build_hetero_graph(spec, dev)
+    t_build = time.time() - t0
+    plan = synth.hetero_plan(spec, "A", [15, 10])
+    cc = ext.create_device_sampler(plan, g.nodeset_names, g.num_nodes, g.edgeset_names, g.fwd, g.bwd,
+                                   _native.MODE_RANDOM, seed=3, has_temporal=True)
+    a = g.nodeset_names.index("A")
+    n_a = g.num_nodes[a]
+    table = g.features["A"]
+    B = 4096
+    nb = 8 + steps
+    seeds = synth.uniform_int(nb * B, 0, n_a, 23, 9, dev).view(nb, B)
+    sts = g.node_ts["A"][seeds]
+    feats = torch.empty((B * cc.tree_size, FEAT_DIM), dtype=torch.float32, device=dev)
+
+    def step(i):
+        m = cc.sample_merged(seeds[i], sts[i], None, call_index=i, check=False)
+        off = m.node_offsets  # node set A's rows: [off[a * B], off[(a + 1) * B])
+        _native.check(_native.lib().dgfx_gather_rows_ranged(
+            _native.ptr(table), n_a, FEAT_DIM * 4, _native.ptr(m.node_ids), _native.elem_ptr(off, a * B),
+            _native.elem_ptr(off, (a + 1) * B), int(m.node_ids.numel()), _native.ptr(feats),
+            _native.stream_handle()))
+
+    for i in range(5):
+        step(i)
+    cc.check()
+    ms = timed(lambda i: step(8 + i), steps, torch.cuda.synchronize, "hetero")
+    cc.check()
+    m = cc.sample_merged(seeds[8], sts[8], None, call_index=8, check=False)
+    nodes = int(m.node_offsets[-1].item())
+    out = {"workload": "heterogeneous temporal: A 736,389 / B 1,134,649 / C 8,740 / D 59,965 nodes; edges B->A "
+                       "7,145,660, A->A 5,416,271, A->D 7,505,078, B->C 1,043,998 (Zipf 2.1); edge ts = "
+                       "propagated A creation years; both directions, fanout [15,10]; 4096 A seeds, cutoff = seed "
+                       "year; fp32 128-d A features",
+           "value": round(B / (ms / 1e3), 1), "unit": "subgraphs/s", "ms_per_step": round(ms, 4),
+           "nodes_per_step": nodes, "tree_positions": cc.tree_size, "graph_build_s": round(t_build, 2)}
+    try:
+        from oracle import oracle as O
+
+        fwd, bwd = {}, {}
+        for name, f, b in zip(g.edgeset_names, g.fwd, g.bwd):
+            fwd[name] = (f.rowptr.cpu().numpy(), f.col.cpu().numpy(), None if f.ts is None else f.ts.cpu().numpy())
+            bwd[name] = (b.rowptr.cpu().numpy(), b.col.cpu().numpy(), None if b.ts is None else b.ts.cpu().numpy())
+        ref = O.available(ref=True)
+        th = host_cores()
+        s = O.OracleSampler.from_csr(g.num_nodes, g.nodeset_names, g.edgeset_names, fwd, plan, mode=O.MODE_RANDOM,
+                                     num_threads=th, seed=99, temporal=True, ref=ref, csr_bwd=bwd)
+        host_tab = table.cpu().numpy()
+        seeds_h = seeds.cpu().numpy()
+        sts_h = sts.cpu().numpy()
+        done, t_tot, i = 0, 0.0, 0
+        while t_tot < 10.0:
+            t1 = time.perf_counter()
+            nc, _, nodes_h, _, _ = s.sample_raw(seeds_h[i % nb], sts_h[i % nb], threads=th)
+            off = 0
+            for row in nc:  # per sample, node sets in order: gather A's rows
+                lo = off + int(row[:a].sum())
+                _ = host_tab[nodes_h[lo:lo + int(row[a])]]
+                off += int(row.sum())
+            t_tot += time.perf_counter() - t1
+            done += B
+            i += 1
+        out["cpu_baseline"] = {"value": round(done / t_tot, 1), "unit": "subgraphs/s", "cores": th,
+                               "kind": "reference" if ref else "port",
+                               "sample": f"{done} seeds, topology + numpy gather of A features"}
+        out["speedup_vs_cpu"] = round(out["value"] / out["cpu_baseline"]["value"], 1)
+    except Exception as exc:  # noqa: BLE001
+        out["cpu_baseline"] = {"unavailable": str(exc)}
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Reference arm: the reference's CPU sampler on the host cores.
 # ---------------------------------------------------------------------------
@@ -634,7 +718,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the SpMM / temporal sub-benchmarks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--scale", type=float, default=1.0, help="shrink the workload (profiling / debugging only)")
-    ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal"],
+    ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal", "hetero"],
                     help="run one workload and skip the rest (profiling)")
     ap.add_argument("--halo", default="exchange", choices=["exchange", "p2p", "nccl"],
                     help="feature halo: bulk peer exchange (default), direct peer loads, or NCCL all-to-all")
@@ -664,9 +748,9 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
 
-    if args.only in ("spmm", "temporal"):
+    if args.only in ("spmm", "temporal", "hetero"):
         # Single sub-benchmark (used for focused profiler captures).
-        fn = bench_spmm if args.only == "spmm" else bench_temporal
+        fn = {"spmm": bench_spmm, "temporal": bench_temporal, "hetero": bench_hetero}[args.only]
         print(json.dumps(fn(dev, args.steps, args.scale)), flush=True)
         return
 
@@ -697,6 +781,8 @@ def main():
             res["spmm"] = bench_spmm(dev, max(5, args.steps // 2))
             torch.cuda.empty_cache()
             res["temporal_169k"] = bench_temporal(dev, args.steps)
+            torch.cuda.empty_cache()
+            res["hetero_temporal"] = bench_hetero(dev, args.steps)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -31,7 +31,8 @@ NVCC_FLAGS = ARCH + [
     "-fvisibility=hidden",
     f"-I{INCLUDE}",
 ]
-SOURCES = ["capi.cu", "primitives.cu", "csr_build.cu", "sampler.cu", "aggregate.cu", "halo.cu", "peer.cu", "synth.cu"]
+SOURCES = ["capi.cu", "primitives.cu", "csr_build.cu", "sampler.cu", "aggregate.cu", "halo.cu", "peer.cu", "synth.cu",
+           "transform.cu"]
 
 
 def nvcc() -> str:

@@ -53,20 +53,22 @@ __global__ void scale_rowptr_kernel(int64_t* __restrict__ rowptr, int64_t n, int
   }
 }
 
-// Edge list in source-major order: src[j] = row of j, dst[j] = popular node.
-__global__ void edges_kernel(const int64_t* __restrict__ rowptr, int64_t n, uint64_t perm_a, uint64_t perm_b,
-                             uint32_t k0, uint32_t k1, int64_t* __restrict__ src, int64_t* __restrict__ dst) {
+// Edge list in source-major order: src[j] = row of j, dst[j] = popular node
+// among m targets (rank m * u^3 through an affine permutation of [0, m)).
+__global__ void edges_kernel(const int64_t* __restrict__ rowptr, int64_t n, int64_t m, uint64_t perm_a,
+                             uint64_t perm_b, uint32_t k0, uint32_t k1, int64_t* __restrict__ src,
+                             int64_t* __restrict__ dst) {
   for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < n;
        v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t b = rowptr[v], e = rowptr[v + 1];
     for (int64_t j = b; j < e; ++j) {
       const U4 r = philox4x32_10(U4{static_cast<uint32_t>(j), static_cast<uint32_t>(j >> 32), 0xd57u, 2u}, k0, k1);
       const double u = u01(r.x, r.y);
-      int64_t rank = static_cast<int64_t>(static_cast<double>(n) * u * u * u);
-      rank = rank < n ? rank : n - 1;
+      int64_t rank = static_cast<int64_t>(static_cast<double>(m) * u * u * u);
+      rank = rank < m ? rank : m - 1;
       const unsigned __int128 t = static_cast<unsigned __int128>(perm_a) * static_cast<uint64_t>(rank) + perm_b;
       src[j] = v;
-      dst[j] = static_cast<int64_t>(t % static_cast<uint64_t>(n));
+      dst[j] = static_cast<int64_t>(t % static_cast<uint64_t>(m));
     }
   }
 }
@@ -133,37 +135,52 @@ extern "C" int dgfx_synth_graph_workspace_size(int64_t num_nodes, size_t* bytes)
   return DGFX_OK;
 }
 
-extern "C" int dgfx_synth_graph(int64_t num_nodes, int64_t num_edges, double alpha, int64_t max_degree, uint64_t seed,
-                                int64_t* d_rowptr, int64_t* d_src, int64_t* d_dst, void* d_workspace,
-                                size_t workspace_bytes, dgfx_stream stream_) {
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  if (num_nodes < 1 || num_edges < 0 || !(alpha > 1.0) || max_degree < 1 || d_rowptr == nullptr) {
+namespace {
+int synth_graph(int64_t num_src, int64_t num_dst, int64_t num_edges, double alpha, int64_t max_degree, uint64_t seed,
+                int64_t* d_rowptr, int64_t* d_src, int64_t* d_dst, void* d_workspace, size_t workspace_bytes,
+                cudaStream_t stream) {
+  if (num_src < 1 || num_dst < 1 || num_edges < 0 || !(alpha > 1.0) || max_degree < 1 || d_rowptr == nullptr) {
     return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_synth_graph: bad arguments");
   }
   size_t need = 0;
-  DGFX_TRY(dgfx_synth_graph_workspace_size(num_nodes, &need));
+  DGFX_TRY(dgfx_synth_graph_workspace_size(num_src, &need));
   if (d_workspace == nullptr || workspace_bytes < need) return fail(DGFX_ERR_WORKSPACE, "dgfx_synth_graph: workspace");
   Arena arena(d_workspace, workspace_bytes);
-  int64_t* deg = arena.take<int64_t>(static_cast<size_t>(num_nodes + 1));
+  int64_t* deg = arena.take<int64_t>(static_cast<size_t>(num_src + 1));
   const uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
-  raw_degree_kernel<<<blocks_for(num_nodes), 256, 0, stream>>>(num_nodes, 1.0 / (alpha - 1.0), max_degree, k0, k1,
-                                                                deg);
+  raw_degree_kernel<<<blocks_for(num_src), 256, 0, stream>>>(num_src, 1.0 / (alpha - 1.0), max_degree, k0, k1, deg);
   DGFX_CUDA_TRY(cudaGetLastError());
   int64_t* total = arena.take<int64_t>(1);
-  DGFX_TRY(exclusive_scan<int64_t>(deg, d_rowptr, num_nodes, true, arena, stream));
-  DGFX_CUDA_TRY(cudaMemcpyAsync(total, d_rowptr + num_nodes, sizeof(int64_t), cudaMemcpyDeviceToDevice, stream));
-  scale_rowptr_kernel<<<blocks_for(num_nodes + 1), 256, 0, stream>>>(d_rowptr, num_nodes, num_edges, total);
+  DGFX_TRY(exclusive_scan<int64_t>(deg, d_rowptr, num_src, true, arena, stream));
+  DGFX_CUDA_TRY(cudaMemcpyAsync(total, d_rowptr + num_src, sizeof(int64_t), cudaMemcpyDeviceToDevice, stream));
+  scale_rowptr_kernel<<<blocks_for(num_src + 1), 256, 0, stream>>>(d_rowptr, num_src, num_edges, total);
   DGFX_CUDA_TRY(cudaGetLastError());
   if (d_src != nullptr && d_dst != nullptr) {
-    // Affine permutation multiplier coprime with N.
-    uint64_t a = (0x9E3779B97F4A7C15ull ^ seed) % static_cast<uint64_t>(num_nodes);
+    // Affine permutation multiplier coprime with the target count.
+    const uint64_t m = static_cast<uint64_t>(num_dst);
+    uint64_t a = (0x9E3779B97F4A7C15ull ^ seed) % m;
     if (a < 2) a = 2;
-    while (gcd64(a, static_cast<uint64_t>(num_nodes)) != 1) ++a;
-    const uint64_t b = (seed * 0xD1B54A32D192ED03ull) % static_cast<uint64_t>(num_nodes);
-    edges_kernel<<<blocks_for(num_nodes), 256, 0, stream>>>(d_rowptr, num_nodes, a, b, k0, k1, d_src, d_dst);
+    while (gcd64(a, m) != 1) ++a;
+    const uint64_t b = (seed * 0xD1B54A32D192ED03ull) % m;
+    edges_kernel<<<blocks_for(num_src), 256, 0, stream>>>(d_rowptr, num_src, num_dst, a, b, k0, k1, d_src, d_dst);
     DGFX_CUDA_TRY(cudaGetLastError());
   }
   return DGFX_OK;
+}
+}  // namespace
+
+extern "C" int dgfx_synth_graph(int64_t num_nodes, int64_t num_edges, double alpha, int64_t max_degree, uint64_t seed,
+                                int64_t* d_rowptr, int64_t* d_src, int64_t* d_dst, void* d_workspace,
+                                size_t workspace_bytes, dgfx_stream stream_) {
+  return synth_graph(num_nodes, num_nodes, num_edges, alpha, max_degree, seed, d_rowptr, d_src, d_dst, d_workspace,
+                     workspace_bytes, reinterpret_cast<cudaStream_t>(stream_));
+}
+
+extern "C" int dgfx_synth_bipartite(int64_t num_src, int64_t num_dst, int64_t num_edges, double alpha,
+                                    int64_t max_degree, uint64_t seed, int64_t* d_rowptr, int64_t* d_src,
+                                    int64_t* d_dst, void* d_workspace, size_t workspace_bytes, dgfx_stream stream_) {
+  return synth_graph(num_src, num_dst, num_edges, alpha, max_degree, seed, d_rowptr, d_src, d_dst, d_workspace,
+                     workspace_bytes, reinterpret_cast<cudaStream_t>(stream_));
 }
 
 extern "C" int dgfx_synth_uniform_int(int64_t n, int64_t lo, int64_t hi, uint64_t seed, uint32_t stream_id,

@@ -342,12 +342,30 @@ int dgfx_exchange_check(const void* d_exchange, int32_t world,
                         dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Edge creation times from node creation times. Replaces the numpy body of
+ * propagate_timestamp_to_edges (dgf/src/transform/temporal.py:95-103):
+ * d_out[e] = max(d_src_ts[d_src[e]], d_dst_ts[d_dst[e]]); with one of the
+ * two node timestamp arrays NULL, the other endpoint's time. Endpoint ids are
+ * bounds-checked against num_src / num_dst; the first edge with an
+ * out-of-range id is reported as DGFX_ERR_INVALID_ARGUMENT. d_workspace:
+ * 8 bytes. Synchronises `stream` once.
+ * ------------------------------------------------------------------------ */
+int dgfx_edge_timestamps(const int64_t* d_src_ts, int64_t num_src,
+                         const int64_t* d_dst_ts, int64_t num_dst,
+                         const int64_t* d_src, const int64_t* d_dst,
+                         int64_t num_edges, int64_t* d_out, void* d_workspace,
+                         dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
  * Seeded synthetic inputs (stand-ins for the benchmark datasets, the role of
  * the reference's dgf/src/util/gen_test_graph.py generators at scale).
  * dgfx_synth_graph: power-law out-degrees (P(d) ~ d^-alpha, capped at
  * max_degree, rescaled to exactly num_edges), power-law target popularity;
  * writes rowptr int64[num_nodes + 1] and, if non-NULL, the source-major edge
  * list src/dst int64[num_edges]. Pure function of its arguments.
+ * dgfx_synth_bipartite: the same with sources [0, num_src) and targets
+ * drawn from [0, num_dst) (an edge type between two node sets; workspace as
+ * dgfx_synth_graph_workspace_size(num_src)).
  * dgfx_synth_uniform_int: out[i] uniform in [lo, hi) (Philox stream id).
  * dgfx_synth_normal_features: rows [node_begin, node_begin + count) of a
  * N(0,1) [*, dim] matrix keyed by node id (partition independent).
@@ -357,6 +375,11 @@ int dgfx_synth_graph(int64_t num_nodes, int64_t num_edges, double alpha,
                      int64_t max_degree, uint64_t seed, int64_t* d_rowptr,
                      int64_t* d_src, int64_t* d_dst, void* d_workspace,
                      size_t workspace_bytes, dgfx_stream stream);
+int dgfx_synth_bipartite(int64_t num_src, int64_t num_dst, int64_t num_edges,
+                         double alpha, int64_t max_degree, uint64_t seed,
+                         int64_t* d_rowptr, int64_t* d_src, int64_t* d_dst,
+                         void* d_workspace, size_t workspace_bytes,
+                         dgfx_stream stream);
 int dgfx_synth_uniform_int(int64_t n, int64_t lo, int64_t hi, uint64_t seed,
                            uint32_t stream_id, int64_t* d_out,
                            dgfx_stream stream);

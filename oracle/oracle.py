@@ -16,6 +16,8 @@ And a float64 numpy restatement of the aggregation math:
   * CSR SpMM (sparse_deferred SparseMatrix @ dense,
     homo_gnn_sparse_deferred.py:138-161) as the same segment sum with
     row = target, col = source.
+And a numpy restatement of the edge-time propagation,
+dgf/src/transform/temporal.py:95-103.
 """
 
 from __future__ import annotations
@@ -226,9 +228,11 @@ class OracleSampler:
 
     @classmethod
     def from_csr(cls, num_nodes, nodesets, edgesets, csr_fwd, plan, mode=MODE_RANDOM, num_threads=0, seed=0,
-                 temporal=False, ref=False, fill_threads=8):
-        """Sampler over prebuilt forward CSR arrays {edgeset: (rowptr int64,
-        col int32, ts int64 | None)} already in CreateFromEdgeList order."""
+                 temporal=False, ref=False, fill_threads=8, csr_bwd=None):
+        """Sampler over prebuilt CSR arrays {edgeset: (rowptr int64, col
+        int32, ts int64 | None)} already in CreateFromEdgeList order: forward
+        indices in csr_fwd, backward (reversed) ones in csr_bwd, each only for
+        the edge sets the plan walks in that direction."""
         self = cls.__new__(cls)
         self.lib = _lib(ref)
         self.nodesets = list(nodesets)
@@ -239,22 +243,37 @@ class OracleSampler:
         nn = np.asarray(num_nodes, np.int64)
         self._keep = []
         _p32 = ctypes.POINTER(ctypes.c_int32)
-        rps, cols, tss, counts = [], [], [], []
-        for name in self.edgesets:
-            rp, col, ts = csr_fwd[name]
-            rp = np.ascontiguousarray(rp, np.int64)
-            col = np.ascontiguousarray(col, np.int32)
-            ts = None if ts is None else np.ascontiguousarray(ts, np.int64)
-            self._keep += [rp, col, ts]
-            rps.append(rp.ctypes.data_as(_p64))
-            cols.append(col.ctypes.data_as(_p32))
-            tss.append(None if ts is None else ts.ctypes.data_as(_p64))
-            counts.append(len(col))
+        csr_bwd = csr_bwd or {}
+
+        def arrays(table):
+            rps, cols, tss, counts = [], [], [], []
+            for name in self.edgesets:
+                if name not in table:
+                    rps.append(None)
+                    cols.append(None)
+                    tss.append(None)
+                    counts.append(None)
+                    continue
+                rp, col, ts = table[name]
+                rp = np.ascontiguousarray(rp, np.int64)
+                col = np.ascontiguousarray(col, np.int32)
+                ts = None if ts is None else np.ascontiguousarray(ts, np.int64)
+                self._keep += [rp, col, ts]
+                rps.append(rp.ctypes.data_as(_p64))
+                cols.append(col.ctypes.data_as(_p32))
+                tss.append(None if ts is None else ts.ctypes.data_as(_p64))
+                counts.append(len(col))
+            return rps, cols, tss, counts
+
+        f_rp, f_col, f_ts, f_cnt = arrays(csr_fwd)
+        b_rp, b_col, b_ts, b_cnt = arrays(csr_bwd)
         n_es = len(self.edgesets)
+        counts = [f if f is not None else (b if b is not None else 0) for f, b in zip(f_cnt, b_cnt)]
         cnt = np.array(counts + [0], np.int64)
         self.h = self.lib.oracle_sampler_create_csr(
-            len(self.nodesets), _p(nn), n_es, (_p64 * n_es)(*rps), (_p32 * n_es)(*cols), (_p64 * n_es)(*tss),
-            None, None, None, _p(cnt), len(node_ns), _ints(node_ns), _ints(first), _ints(num), len(e_es), _ints(e_es),
+            len(self.nodesets), _p(nn), n_es, (_p64 * n_es)(*f_rp), (_p32 * n_es)(*f_col), (_p64 * n_es)(*f_ts),
+            (_p64 * n_es)(*b_rp), (_p32 * n_es)(*b_col), (_p64 * n_es)(*b_ts), _p(cnt), len(node_ns), _ints(node_ns),
+            _ints(first), _ints(num), len(e_es), _ints(e_es),
             _ints(e_rev), _ints(e_hw), _ints(e_child), int(bool(plan.with_replacement)), int(mode), int(num_threads),
             int(seed), int(bool(temporal)), int(fill_threads),
         )
@@ -334,3 +353,17 @@ def csr_spmm(rowptr: np.ndarray, col: np.ndarray, x: np.ndarray, val: Optional[n
         deg = np.diff(rowptr).astype(np.float64)
         y /= np.maximum(deg, 1.0)[:, None]
     return y
+
+
+# ---------------------------------------------------------------------------
+# Edge creation times (dgf/src/transform/temporal.py:95-103).
+# ---------------------------------------------------------------------------
+def edge_timestamps(src_ts: Optional[np.ndarray], tgt_ts: Optional[np.ndarray], adjacency: np.ndarray) -> np.ndarray:
+    """max(src_ts[src], tgt_ts[tgt]); the one side given when the other is
+    None (temporal.py:95-103)."""
+    src, tgt = adjacency
+    if src_ts is not None and tgt_ts is not None:
+        return np.maximum(src_ts[src], tgt_ts[tgt])
+    if src_ts is not None:
+        return src_ts[src]
+    return tgt_ts[tgt]

@@ -178,3 +178,15 @@ MASK_RANDOM = [
 ]
 # SampleWithTimestamp_FiltersFutureEdges :176-190.
 TEMPORAL_FILTER = ([(0, 1, 15), (0, 2, 25), (1, 3, 35)], 4, 4, 0, 20, 2, [1])
+
+# ---------------------------------------------------------------------------
+# propagate_timestamp_to_edges: dgf/src/transform/temporal_test.py:27-238.
+# (name, n1 node ts or None, n2 node ts or None, adjacency, target_feature,
+#  expected edge ts or the ValueError message fragment)
+# ---------------------------------------------------------------------------
+EDGE_TS_CASES = [
+    ("basic :27-81", ("timestamps", [10, 20]), ("timestamps", [5, 25]), [[0, 1], [1, 0]], "timestamps", [25, 20]),
+    ("single_node_timestamp :83-119", ("timestamps", [10, 20]), None, [[0, 1], [1, 0]], "timestamps", [10, 20]),
+    ("custom_names :145-199", ("time", [10, 20]), ("ts", [5, 25]), [[0, 1], [1, 0]], "edge_ts", [25, 20]),
+    ("fail_no_timestamps :121-143", None, None, [[0, 1], [1, 0]], "timestamps", "Neither source nodeset"),
+]
