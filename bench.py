@@ -575,6 +575,104 @@ def bench_temporal(dev, steps, scale=1.0):
     return out
 
 
+def bench_sage(dev, steps, scale=1.0):
+    """GraphSAGE-mean layer forward: mean SpMM over in-neighbours (bf16 out)
+    then relu(concat[x, agg] @ W^T + b) on the tensor cores. 2,000,000 nodes,
+    40,000,000 edges (Zipf 2.1 generator), bf16 x [N, 256], W [256, 512]
+    Glorot-uniform (seeded)."""
+    import torch
+
+    from distributed_graph_flow_b200 import aggregation, synth
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+
+    N = max(1024, int(2_000_000 * scale))
+    E = max(1024, int(40_000_000 * scale))
+    F, F_OUT = 256, 256
+    spec = synth.GraphSpec(N, E, 2.1, 20_000, seed=5)
+    _, src, dst = synth.rowptr_and_edges(spec, dev)
+    idx = ext.build_adjacency_index_device(src, dst, None, N, N, True, False)  # rows = targets
+    del src, dst
+    x = synth.normal_features(0, N, F, 6, torch.bfloat16, dev)
+    g = torch.Generator(device=dev).manual_seed(11)
+    lim = (6.0 / (2 * F + F_OUT)) ** 0.5
+    w = ((torch.rand((F_OUT, 2 * F), generator=g, device=dev) * 2 - 1) * lim).to(torch.bfloat16)
+    b = torch.zeros(F_OUT, dtype=torch.float32, device=dev)
+    agg = torch.empty((N, F), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((N, F_OUT), dtype=torch.bfloat16, device=dev)
+    ws = aggregation.spmm_workspace(N, E, F, dev)
+    rowptr, col = idx.rowptr, idx.col
+
+    def layer(_):
+        aggregation.sage_mean_linear_relu(rowptr, col, x, w, b, agg=agg, workspace=ws, out=y)
+
+    def spmm(_):
+        aggregation.csr_spmm(rowptr, col, x, normalize=True, out=agg, workspace=ws)
+
+    def dense(_):
+        aggregation.dense_concat(x, agg, w, b, relu=True, out=y)
+
+    for _ in range(3):
+        layer(0)
+    aggregation.dense_check()
+    ms_layer = timed(layer, steps, torch.cuda.synchronize, "sage_layer")
+    ms_spmm = timed(spmm, steps, torch.cuda.synchronize, "sage_spmm")
+    ms_dense = timed(dense, steps, torch.cuda.synchronize, "sage_dense")
+    aggregation.dense_check()
+    hbm, kind = measured_peaks()
+    tflops_peak = measured_tflops()
+    spmm_bytes = 8 * (N + 1) + 4 * E + 2 * F * E + 2 * F * N
+    dense_flops = 2.0 * N * (2 * F) * F_OUT
+    dense_bytes = 2 * N * (2 * F) + 2 * N * F_OUT + 2 * F_OUT * 2 * F
+    out = {"workload": "GraphSAGE-mean forward: 2,000,000 nodes, 40,000,000 edges (Zipf 2.1), bf16 x [N,256], "
+                       "mean SpMM -> concat[x, agg] [N,512] -> Dense 512->256 (tcgen05, fp32 accum) + ReLU",
+           "value": round(N / (ms_layer / 1e3), 1), "unit": "nodes/s", "ms_per_layer": round(ms_layer, 4),
+           "spmm": {"ms": round(ms_spmm, 4), "bytes": spmm_bytes, "gbs": round(spmm_bytes / ms_spmm / 1e6, 1),
+                    "frac_hbm": round(spmm_bytes / ms_spmm / 1e6 / hbm, 4), "bound": "hbm"},
+           "dense": {"ms": round(ms_dense, 4), "tflops": round(dense_flops / ms_dense / 1e9, 1),
+                     "frac_tensor": round(dense_flops / ms_dense / 1e9 / tflops_peak, 4),
+                     "gbs": round(dense_bytes / ms_dense / 1e6, 1),
+                     "frac_hbm": round(dense_bytes / ms_dense / 1e6 / hbm, 4),
+                     "bound": "hbm (AI = 2*512*256/(2*(512+256)) = 170 flop/B, below the ridge)"},
+           "peaks": {"hbm_gbs": hbm, "bf16_tflops": tflops_peak, "kind": kind}}
+    # CPU baseline: the same layer in torch fp32 on the host cores, on a
+    # bounded sample of target rows (their in-edges and rows of x).
+    try:
+        th = host_cores()
+        torch.set_num_threads(th)
+        rows = min(N, 50_000)
+        rp = rowptr[: rows + 1].cpu()
+        c = col[: int(rp[-1])].cpu().long()
+        xh = x.float().cpu()
+        wh = w.float().cpu()
+        bh = b.cpu()
+        seg = torch.repeat_interleave(torch.arange(rows), torch.diff(rp))
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 10.0:
+            aggh = torch.zeros((rows, F)).index_add_(0, seg, xh[c])
+            aggh /= torch.diff(rp).clamp(min=1).float()[:, None]
+            _ = torch.relu(torch.cat([xh[:rows], aggh], 1) @ wh.t() + bh)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        out["cpu_baseline"] = {"value": round(rows / dt, 1), "unit": "nodes/s", "cores": th, "kind": "port",
+                               "sample": f"{rows} target rows ({int(rp[-1])} in-edges), torch fp32 index_add_ "
+                                         f"mean + matmul + relu, {reps} reps"}
+        out["speedup_vs_cpu"] = round(out["value"] / out["cpu_baseline"]["value"], 1)
+    except Exception as exc:  # noqa: BLE001
+        out["cpu_baseline"] = {"unavailable": str(exc)}
+    return out
+
+
+def measured_tflops():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        for k in ("bf16_tflops", "bf16_tflops_burst"):
+            if k in d:
+                return float(d[k])
+    return 1590.0
+
+
 def bench_hetero(dev, steps, scale=1.0):
     """Heterogeneous temporal sampling: 4 node sets / 4 edge types, edge
     times propagated from node set A's creation years, A seeds with cutoff =
@@ -718,7 +816,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the SpMM / temporal sub-benchmarks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--scale", type=float, default=1.0, help="shrink the workload (profiling / debugging only)")
-    ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal", "hetero"],
+    ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal", "hetero", "sage"],
                     help="run one workload and skip the rest (profiling)")
     ap.add_argument("--halo", default="exchange", choices=["exchange", "p2p", "nccl"],
                     help="feature halo: bulk peer exchange (default), direct peer loads, or NCCL all-to-all")
@@ -748,9 +846,9 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
 
-    if args.only in ("spmm", "temporal", "hetero"):
+    if args.only in ("spmm", "temporal", "hetero", "sage"):
         # Single sub-benchmark (used for focused profiler captures).
-        fn = {"spmm": bench_spmm, "temporal": bench_temporal, "hetero": bench_hetero}[args.only]
+        fn = {"spmm": bench_spmm, "temporal": bench_temporal, "hetero": bench_hetero, "sage": bench_sage}[args.only]
         print(json.dumps(fn(dev, args.steps, args.scale)), flush=True)
         return
 
@@ -783,6 +881,8 @@ def main():
             res["temporal_169k"] = bench_temporal(dev, args.steps)
             torch.cuda.empty_cache()
             res["hetero_temporal"] = bench_hetero(dev, args.steps)
+            torch.cuda.empty_cache()
+            res["sage_mean_2m"] = bench_sage(dev, args.steps)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

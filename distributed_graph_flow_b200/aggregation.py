@@ -102,3 +102,51 @@ def gather_rows(table, ids, stream=None):
         )
     )
     return out
+
+
+def dense_concat(x1, x2, weight, bias=None, relu: bool = True, out=None, stream=None):
+    """act(concat[x1, x2] @ weight.T + bias) in bf16 on the tensor cores
+    (tcgen05, fp32 accumulation): the Dense(+ReLU) update after aggregation
+    (hetero_gnn.py:302-312). x1 [M, K1], x2 [M, K2] or None, weight [N, K1+K2]
+    (torch Linear layout), bias fp32 [N] or None; K1, K2 and N multiples of 64.
+    The concat is read from the two inputs, never materialised."""
+    torch = _native.require_cuda()
+    if x1.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or (x2 is not None and x2.dtype != torch.bfloat16):
+        raise ValueError("dense_concat: x1, x2 and weight must be bfloat16")
+    m, k1 = int(x1.shape[0]), int(x1.shape[1])
+    k2 = 0 if x2 is None else int(x2.shape[1])
+    if x2 is not None and int(x2.shape[0]) != m:
+        raise ValueError("dense_concat: x1 and x2 must have the same number of rows")
+    n = int(weight.shape[0])
+    if int(weight.shape[1]) != k1 + k2:
+        raise ValueError(f"dense_concat: weight is [{n}, {int(weight.shape[1])}], expected [N, {k1 + k2}]")
+    for t in (x1, x2, weight):
+        if t is not None and not t.is_contiguous():
+            raise ValueError("dense_concat: inputs must be contiguous")
+    if bias is not None and (bias.dtype != torch.float32 or int(bias.numel()) != n):
+        raise ValueError("dense_concat: bias must be float32 [N]")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x1.device)
+    _native.check(_native.lib().dgfx_dense_concat_bf16(
+        _native.ptr(x1), k1, _native.ptr(x2), k2, m, _native.ptr(weight), _native.ptr(bias), n, int(bool(relu)),
+        _native.ptr(out), _native.stream_handle(stream)))
+    return out
+
+
+def dense_check(stream=None):
+    """Raises if a dense_concat launch hit a pipeline timeout since the last
+    check (synchronises the stream)."""
+    _native.check(_native.lib().dgfx_dense_check(_native.stream_handle(stream)))
+
+
+def sage_mean_linear_relu(rowptr, col, x, weight, bias=None, agg=None, workspace=None, out=None, stream=None):
+    """GraphSAGE-mean layer: agg = mean over in-neighbours (CSR rows = target
+    nodes, col = source nodes) of x, then relu(concat[x, agg] @ weight.T +
+    bias). x bf16 [N, F]; weight bf16 [N_out, 2F]. Two launches: the SpMM
+    (HBM-bound gather, bf16 out) and the tensor-core dense layer."""
+    torch = _native.require_cuda()
+    n_rows = int(rowptr.numel()) - 1
+    if agg is None:
+        agg = torch.empty((n_rows, int(x.shape[1])), dtype=torch.bfloat16, device=x.device)
+    csr_spmm(rowptr, col, x, normalize=True, out=agg, workspace=workspace, stream=stream)
+    return dense_concat(x[:n_rows], agg, weight, bias, relu=True, out=out, stream=stream)

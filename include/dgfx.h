@@ -242,6 +242,25 @@ int dgfx_segment_sum(const void* d_data, int data_dtype,
                      dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Dense layer after aggregation on the tensor cores (tcgen05, sm_100a).
+ * Replaces the nn.Dense (+ activation) that follows the neighbour
+ * aggregation (dgf/src/learning/jax/layers/hetero_gnn.py:302-312,
+ * standard.py:238-270): d_y[m, n] = act(concat[d_x1, d_x2] @ d_w^T + d_bias)
+ * with d_x1 bf16 [m, k1], d_x2 bf16 [m, k2] (NULL when k2 = 0), d_w bf16
+ * [n, k1 + k2] (output-major, torch Linear layout), d_bias fp32 [n] or NULL,
+ * act = ReLU when relu != 0 else identity; fp32 accumulation, bf16 output
+ * (round to nearest). k1 >= 64; k1, k2 and n multiples of 64; all operands
+ * 16-byte aligned. A pipeline wait that runs out (2 s) is latched and
+ * reported by dgfx_dense_check (synchronises the stream) as
+ * DGFX_ERR_INTERNAL.
+ * ------------------------------------------------------------------------ */
+int dgfx_dense_concat_bf16(const void* d_x1, int64_t k1, const void* d_x2,
+                           int64_t k2, int64_t m, const void* d_w,
+                           const float* d_bias, int64_t n, int32_t relu,
+                           void* d_y, dgfx_stream stream);
+int dgfx_dense_check(dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
  * Halo feature exchange (node-range-partitioned features across ranks).
  * Replaces the Beam CoGroupByKey feature join of
  * dgf/src/sampling/beam_semi_distributed_sampler_v2.py:271-387; the rows
