@@ -61,7 +61,9 @@ def ncu_traffic():
 
 
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+    """Samples SM clocks and clock-event (throttle) reasons while the timed
+    region runs: NVML every millisecond (read-only queries), else nvidia-smi
+    every 200 ms."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -69,39 +71,74 @@ class ClockSampler:
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
-        self.rows = []
+        self.rows = []  # (sm_mhz, max_mhz, set of active reason names)
         self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = None
+            try:  # the torch device's own GPU (NVML ignores CUDA_VISIBLE_DEVICES)
+                import torch
+
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{torch.cuda.get_device_properties(gpu_index).uuid}")
+            except Exception:  # noqa: BLE001
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+            self._max = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._bits = {
+                "hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap,
+            }
+        except Exception:  # noqa: BLE001
+            self._nvml = None
 
     def start(self):
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
 
+    def _sample_nvml(self):
+        nv = self._nvml
+        sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+        mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        self.rows.append((float(sm), float(self._max), {k for k, bit in self._bits.items() if mask & bit}))
+
+    def _sample_smi(self):
+        out = subprocess.run(
+            ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+            capture_output=True, text=True, timeout=5,
+        ).stdout.strip()
+        if out:
+            r = [x.strip() for x in out.split(",")]
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            if r[1].replace(".", "").isdigit() and r[2].replace(".", "").isdigit():
+                self.rows.append((float(r[1]), float(r[2]),
+                                  {n for n, v in zip(names, r[5:9]) if v.lower() == "active"}))
+
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(
-                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
-                    capture_output=True, text=True, timeout=5,
-                ).stdout.strip()
-                if out:
-                    self.rows.append([x.strip() for x in out.split(",")])
-            except Exception:
+                if self._nvml is not None:
+                    self._sample_nvml()
+                else:
+                    self._sample_smi()
+            except Exception:  # noqa: BLE001
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.001 if self._nvml is not None else 0.2)
 
     def stop(self):
         self._stop.set()
         if self._t:
             self._t.join(timeout=10)
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
+                "reasons": sorted(set().union(*(r[2] for r in self.rows))), "samples": len(self.rows),
+                "source": "nvml" if self._nvml is not None else "nvidia-smi"}
 
 
 def timed(fn, steps, sync_fn, name="timed", finish=None):
