@@ -190,7 +190,7 @@ def large_spec(scale):
     return dataclasses.replace(s, num_nodes=max(1000, int(s.num_nodes * scale)), num_edges=int(s.num_edges * scale))
 
 
-def setup_large(rank, world, dev, scale=1.0, halo="exchange"):
+def setup_large(rank, world, dev, scale=1.0, halo="exchange", cache=0.0):
     import torch
 
     from distributed_graph_flow_b200 import driver, synth
@@ -218,6 +218,12 @@ def setup_large(rank, world, dev, scale=1.0, halo="exchange"):
         synth.normal_features(lo, cnt, FEAT_DIM, spec.seed + 100, torch.bfloat16, dev, out=feats.table)
         feats.connect()
         table = feats.table
+        if cache > 0 and world > 1 and halo == "exchange":
+            # Read-only copy of the most-referenced rows on every GPU.
+            hot = driver.hot_rows(index, int(cache * spec.num_nodes))
+            feats.cache_info = {"fraction": cache, "rows": int(hot.numel()),
+                                "gb_per_gpu": round(feats.replicate(hot) / 1e9, 2)}
+            del hot
     sharded = driver.ShardedSampler(cc, feats, rank, world)
     torch.cuda.synchronize()
     log(f"[bench] large graph built in {t_graph:.1f}s; setup {time.time() - t0:.1f}s; T={cc.tree_size}")
@@ -230,7 +236,7 @@ def bench_large(args, rank, world, dev):
 
     from distributed_graph_flow_b200 import _native, synth
 
-    spec, index, table, cc, sharded, plan = setup_large(rank, world, dev, args.scale, args.halo)
+    spec, index, table, cc, sharded, plan = setup_large(rank, world, dev, args.scale, args.halo, args.halo_cache)
     W, K = args.warmup, args.steps
     seeds = synth.uniform_int((W + K) * B_SEEDS, 0, spec.num_nodes, 77 + rank, 5, dev).view(W + K, B_SEEDS)
 
@@ -346,6 +352,11 @@ def bench_large(args, rank, world, dev):
         "gpu_launches": launches * K,
         "gpu_launches_per_step": launches,
     }
+    cache_info = getattr(sharded.features, "cache_info", None)
+    if cache_info is not None:
+        res["config"]["halo_cache"] = dict(cache_info, what="replicated read-only copy of the most-referenced "
+                                                            "feature rows (by in-degree); ownership stays "
+                                                            "node-range partitioned")
     res["config"]["halo"] = {"p2p": "peer loads over NVLink (one gather kernel)",
                              "exchange": "bulk peer exchange (bucket by owner, owner-local gather, sequential "
                                          "NVLink pulls; NCCL one-word barriers)" if world > 1 else
@@ -857,6 +868,9 @@ def main():
                     help="run one workload and skip the rest (profiling)")
     ap.add_argument("--halo", default="exchange", choices=["exchange", "p2p", "nccl"],
                     help="feature halo: bulk peer exchange (default), direct peer loads, or NCCL all-to-all")
+    ap.add_argument("--halo-cache", type=float, default=0.2,
+                    help="N > 1 with the bulk exchange: fraction of nodes (most in-edges first) whose feature rows "
+                         "every GPU keeps a read-only copy of (0 disables)")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="run each step's feature gather on the sampling stream (no pipelining)")
     ap.add_argument("--minimal", action="store_true",

@@ -108,8 +108,8 @@ SIGNATURES = {
     "dgfx_ipc_close": (_int, [_vp]),
     "dgfx_gather_rows_p2p": (_int, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp]),
     "dgfx_exchange_buffer_size": (_int, [_i32, _i64, _i64, ctypes.POINTER(_sz)]),
-    "dgfx_exchange_partition": (_int, [_vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
-    "dgfx_exchange_serve": (_int, [_vp, _i32, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "dgfx_exchange_partition": (_int, [_vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
+    "dgfx_exchange_serve": (_int, [_vp, _i32, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp]),
     "dgfx_exchange_scatter": (_int, [_vp, _i32, _i32, _i64, _i64, _vp, _vp, _vp]),
     "dgfx_exchange_barrier": (_int, [_vp, _i32, _i32, ctypes.c_uint32, _u64, _vp]),
     "dgfx_exchange_check": (_int, [_vp, _i32, _vp]),

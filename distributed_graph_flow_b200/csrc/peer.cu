@@ -77,19 +77,25 @@ __global__ void __launch_bounds__(kGatherThreads, 32) gather_p2p_kernel(const ui
 // (peer flags, bounded wait) or any group-wide barrier on the same stream.
 //
 // Exchange buffer layout, identical on every rank (S = slot_rows):
-//   [0, 8 * world)                       int64 request count per owner
+//   [0, 8 * (world + 1))                 int64 request count per owner, then
+//                                        per local replica (slot `world`)
 //   [kExStatusOff, +4)                   uint32 status: 1 slot overflow, 2 barrier timeout
 //   [kExFlagsOff, + 4 * world)           uint32 barrier arrival epoch per rank
-//   [kExIdsOff, + 8 * world * S)         int64 request ids; slot o = ids owned by rank o
+//   [kExIdsOff, + 8 * (world + 1) * S)   int64 request ids; slot o = ids owned by
+//                                        rank o, slot `world` = replica rows
 //   [rows_off, + world * S * row_bytes)  inbox rows; slot o = rows sent by owner o
+// Requests whose node has a row in the optional local replica table (a
+// read-only copy of frequently requested rows, hot_slot[id] >= 0) never
+// cross NVLink: they go to slot `world` and are copied locally by the serve
+// launch.
 // ---------------------------------------------------------------------------
 constexpr int kMaxWorld = 16;
-constexpr int64_t kExStatusOff = 128;
-constexpr int64_t kExFlagsOff = 192;
-constexpr int64_t kExIdsOff = 256;
+constexpr int64_t kExStatusOff = 256;
+constexpr int64_t kExFlagsOff = 320;
+constexpr int64_t kExIdsOff = 512;
 
 inline int64_t ex_rows_off(int32_t world, int64_t slot_rows) {
-  return (kExIdsOff + 8 * static_cast<int64_t>(world) * slot_rows + 255) / 256 * 256;
+  return (kExIdsOff + 8 * static_cast<int64_t>(world + 1) * slot_rows + 255) / 256 * 256;
 }
 
 constexpr int kPartThreads = 256;
@@ -101,15 +107,15 @@ constexpr int kPartItems = 8;
 __global__ void __launch_bounds__(kPartThreads) exchange_partition_kernel(
     char* __restrict__ ex, int32_t world, int64_t slot_rows, uint32_t rows_per_rank, uint32_t num_nodes, int64_t vpr,
     const int64_t* __restrict__ ids, const int64_t* __restrict__ begin, const int64_t* __restrict__ end,
-    int64_t max_rows, int32_t* __restrict__ req_pos, uint4* __restrict__ out) {
-  __shared__ int s_cnt[kMaxWorld];
-  __shared__ unsigned long long s_base[kMaxWorld];
+    int64_t max_rows, const int32_t* __restrict__ hot_slot, int32_t* __restrict__ req_pos, uint4* __restrict__ out) {
+  __shared__ int s_cnt[kMaxWorld + 1];
+  __shared__ unsigned long long s_base[kMaxWorld + 1];
   const int64_t lo = *begin;
   int64_t n = *end - lo;
   n = n < max_rows ? n : max_rows;
   const int64_t tile = static_cast<int64_t>(blockIdx.x) * (kPartThreads * kPartItems);
   if (tile >= n) return;  // uniform over the CTA
-  if (threadIdx.x < kMaxWorld) s_cnt[threadIdx.x] = 0;
+  if (threadIdx.x <= kMaxWorld) s_cnt[threadIdx.x] = 0;
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
@@ -123,8 +129,17 @@ __global__ void __launch_bounds__(kPartThreads) exchange_partition_kernel(
     int64_t id = -1;
     if (i < n) {
       id = ids[lo + i];
-      if (id >= 0 && id < num_nodes) o = static_cast<int>(static_cast<uint32_t>(id) / rows_per_rank);
-      if (o >= world) o = -1;
+      if (id >= 0 && id < num_nodes) {
+        o = static_cast<int>(static_cast<uint32_t>(id) / rows_per_rank);
+        if (o >= world) o = -1;
+        if (o >= 0 && hot_slot != nullptr) {
+          const int32_t h = __ldg(hot_slot + id);
+          if (h >= 0) {  // served from the local replica: store its row
+            o = world;
+            id = h;
+          }
+        }
+      }
       if (o < 0) {
         for (int64_t c = 0; c < vpr; ++c) out[i * vpr + c] = make_uint4(0, 0, 0, 0);
       }
@@ -139,7 +154,7 @@ __global__ void __launch_bounds__(kPartThreads) exchange_partition_kernel(
     idv[k] = id;
   }
   __syncthreads();
-  if (threadIdx.x < world) {
+  if (threadIdx.x <= world) {
     s_base[threadIdx.x] = atomicAdd(reinterpret_cast<unsigned long long*>(ex) + threadIdx.x,
                                     static_cast<unsigned long long>(s_cnt[threadIdx.x]));
   }
@@ -161,7 +176,11 @@ __global__ void __launch_bounds__(kPartThreads) exchange_partition_kernel(
   if (over) atomicOr(reinterpret_cast<unsigned*>(ex + kExStatusOff), 1u);
 }
 
-constexpr int kCopyThreads = 128;
+// Small CTAs (2 warps, <= 80 registers) so one fits on every SM beside a
+// resident sampler kernel when steps are pipelined; 8 loads in flight per
+// lane keep enough bytes moving per SM for NVLink.
+constexpr int kCopyThreads = 64;
+constexpr int kCopyUnroll = 8;
 constexpr int kChunk = 32;
 
 // Serve (kServe): segments over requesters p, rows = ids in p's slot for this
@@ -173,17 +192,22 @@ constexpr int kChunk = 32;
 // with U loads in flight per lane. Data other ranks wrote (counts, ids) is
 // read with ld.global.cv.
 template <bool kServe, int U>
-__global__ void __launch_bounds__(kCopyThreads) exchange_copy_kernel(
+__global__ void __launch_bounds__(kCopyThreads, 8) exchange_copy_kernel(
     const char* const* __restrict__ exs, int32_t world, int32_t rank, int64_t slot_rows, int64_t vpr, int lvpr,
     int64_t rows_off, const uint4* __restrict__ table, int64_t row_base, int64_t local_rows,
-    const int32_t* __restrict__ req_pos, uint4* __restrict__ out) {
-  __shared__ int64_t s_cnt[kMaxWorld];
-  __shared__ int64_t s_pre[kMaxWorld + 1];
-  if (threadIdx.x < world) {
+    const uint4* __restrict__ replica, int64_t replica_rows, const int32_t* __restrict__ req_pos,
+    uint4* __restrict__ out) {
+  // Segments: ranks 0..world-1, then (serve only) this rank's replica slot.
+  __shared__ int64_t s_cnt[kMaxWorld + 1];
+  __shared__ int64_t s_pre[kMaxWorld + 2];
+  const int nseg = kServe ? world + 1 : world;
+  if (threadIdx.x < nseg) {
     const int p = threadIdx.x;
     int64_t c = 0;
-    if (kServe) {
+    if (kServe && p < world) {
       c = __ldcv(reinterpret_cast<const long long*>(exs[p]) + rank);
+    } else if (kServe) {
+      c = reinterpret_cast<const int64_t*>(exs[rank])[world];
     } else if (p != rank) {
       c = reinterpret_cast<const int64_t*>(exs[rank])[p];
     }
@@ -192,26 +216,32 @@ __global__ void __launch_bounds__(kCopyThreads) exchange_copy_kernel(
   __syncthreads();
   if (threadIdx.x == 0) {
     int64_t a = 0;
-    for (int p = 0; p < world; ++p) {
+    for (int p = 0; p < nseg; ++p) {
       s_pre[p] = a;
       a += (s_cnt[p] + kChunk - 1) / kChunk;
     }
-    s_pre[world] = a;
+    s_pre[nseg] = a;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kCopyThreads / 32);
-  const int64_t chunks = s_pre[world];
+  const int64_t chunks = s_pre[nseg];
   for (int64_t ch = static_cast<int64_t>(blockIdx.x) * (kCopyThreads / 32) + (threadIdx.x >> 5); ch < chunks;
        ch += warps) {
     int p = 0;
-    while (p + 1 < world && s_pre[p + 1] <= ch) ++p;
+    while (p + 1 < nseg && s_pre[p + 1] <= ch) ++p;
     const int64_t k0 = (ch - s_pre[p]) * kChunk;
     const int64_t left = s_cnt[p] - k0;
     const int rows = left < kChunk ? static_cast<int>(left) : kChunk;
+    const bool rep = kServe && p == world;  // replica slot: local copy straight to d_out
     int64_t src = -1, dst = 0;
     if (lane < rows) {
-      if (kServe) {
+      if (rep) {
+        const int64_t h =
+            reinterpret_cast<const int64_t*>(exs[rank] + kExIdsOff)[static_cast<int64_t>(world) * slot_rows + k0 + lane];
+        src = (h >= 0 && h < replica_rows) ? h : -1;
+        dst = req_pos[static_cast<int64_t>(world) * slot_rows + k0 + lane];
+      } else if (kServe) {
         const int64_t id =
             __ldcv(reinterpret_cast<const long long*>(exs[p] + kExIdsOff) + static_cast<int64_t>(rank) * slot_rows + k0 + lane);
         const int64_t r = id - row_base;
@@ -223,8 +253,8 @@ __global__ void __launch_bounds__(kCopyThreads) exchange_copy_kernel(
         dst = req_pos[static_cast<int64_t>(p) * slot_rows + k0 + lane];
       }
     }
-    const uint4* sbase = kServe ? table : reinterpret_cast<const uint4*>(exs[rank] + rows_off);
-    uint4* dbase = (kServe && p != rank) ? reinterpret_cast<uint4*>(const_cast<char*>(exs[p]) + rows_off) : out;
+    const uint4* sbase = rep ? replica : (kServe ? table : reinterpret_cast<const uint4*>(exs[rank] + rows_off));
+    uint4* dbase = (kServe && !rep && p != rank) ? reinterpret_cast<uint4*>(const_cast<char*>(exs[p]) + rows_off) : out;
     const int64_t nv = static_cast<int64_t>(rows) * vpr;
     for (int64_t b = 0; b < nv; b += 32 * U) {
       uint4 x[U];
@@ -318,7 +348,8 @@ extern "C" int dgfx_exchange_buffer_size(int32_t world, int64_t slot_rows, int64
 extern "C" int dgfx_exchange_partition(void* d_exchange, int32_t world, int64_t slot_rows, int64_t rows_per_rank,
                                        int64_t num_nodes, int64_t row_bytes, const int64_t* d_row_ids,
                                        const int64_t* d_begin, const int64_t* d_end, int64_t max_rows,
-                                       int32_t* d_req_pos, void* d_out, dgfx_stream stream_) {
+                                       const int32_t* d_hot_slot, int32_t* d_req_pos, void* d_out,
+                                       dgfx_stream stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (d_exchange == nullptr || !ex_args_ok(world, slot_rows, row_bytes) || rows_per_rank < 1 || num_nodes < 0 ||
       num_nodes > rows_per_rank * world || max_rows < 0 || d_begin == nullptr || d_end == nullptr) {
@@ -327,12 +358,12 @@ extern "C" int dgfx_exchange_partition(void* d_exchange, int32_t world, int64_t 
   if (num_nodes >= (int64_t(1) << 32) || max_rows >= (int64_t(1) << 31)) {
     return fail(DGFX_ERR_UNSUPPORTED, "dgfx_exchange_partition: more than 2^32 - 1 nodes or 2^31 - 1 rows");
   }
-  DGFX_CUDA_TRY(cudaMemsetAsync(d_exchange, 0, 8 * static_cast<size_t>(world), stream));
+  DGFX_CUDA_TRY(cudaMemsetAsync(d_exchange, 0, 8 * static_cast<size_t>(world + 1), stream));
   if (max_rows == 0) return DGFX_OK;
   const int64_t blocks = ceil_div(max_rows, static_cast<int64_t>(kPartThreads * kPartItems));
   exchange_partition_kernel<<<static_cast<unsigned>(blocks), kPartThreads, 0, stream>>>(
       static_cast<char*>(d_exchange), world, slot_rows, static_cast<uint32_t>(rows_per_rank),
-      static_cast<uint32_t>(num_nodes), row_bytes / 16, d_row_ids, d_begin, d_end, max_rows, d_req_pos,
+      static_cast<uint32_t>(num_nodes), row_bytes / 16, d_row_ids, d_begin, d_end, max_rows, d_hot_slot, d_req_pos,
       static_cast<uint4*>(d_out));
   DGFX_CUDA_TRY(cudaGetLastError());
   return DGFX_OK;
@@ -341,20 +372,21 @@ extern "C" int dgfx_exchange_partition(void* d_exchange, int32_t world, int64_t 
 namespace {
 int launch_exchange_copy(bool serve, const void* const* d_exchanges, int32_t world, int32_t rank, int64_t slot_rows,
                          int64_t row_bytes, const void* d_table, int64_t row_base, int64_t local_rows,
-                         const int32_t* d_req_pos, void* d_out, cudaStream_t stream) {
+                         const void* d_replica, int64_t replica_rows, const int32_t* d_req_pos, void* d_out,
+                         cudaStream_t stream) {
   const int64_t vpr = row_bytes / 16;
-  const int64_t chunks = static_cast<int64_t>(world) * ceil_div(std::max<int64_t>(slot_rows, 1), int64_t(kChunk));
+  const int64_t chunks = static_cast<int64_t>(world + 1) * ceil_div(std::max<int64_t>(slot_rows, 1), int64_t(kChunk));
   const int64_t blocks =
-      std::max<int64_t>(1, std::min<int64_t>(ceil_div(chunks, int64_t(kCopyThreads / 32)), int64_t(sm_count()) * 8));
+      std::max<int64_t>(1, std::min<int64_t>(ceil_div(chunks, int64_t(kCopyThreads / 32)), int64_t(sm_count()) * 2));
   const auto exs = reinterpret_cast<const char* const*>(d_exchanges);
   const int64_t rows_off = ex_rows_off(world, slot_rows);
   if (serve) {
-    exchange_copy_kernel<true, 4><<<static_cast<unsigned>(blocks), kCopyThreads, 0, stream>>>(
+    exchange_copy_kernel<true, kCopyUnroll><<<static_cast<unsigned>(blocks), kCopyThreads, 0, stream>>>(
         exs, world, rank, slot_rows, vpr, lvpr_of(vpr), rows_off, static_cast<const uint4*>(d_table), row_base,
-        local_rows, d_req_pos, static_cast<uint4*>(d_out));
+        local_rows, static_cast<const uint4*>(d_replica), replica_rows, d_req_pos, static_cast<uint4*>(d_out));
   } else {
-    exchange_copy_kernel<false, 4><<<static_cast<unsigned>(blocks), kCopyThreads, 0, stream>>>(
-        exs, world, rank, slot_rows, vpr, lvpr_of(vpr), rows_off, nullptr, 0, 0, d_req_pos,
+    exchange_copy_kernel<false, kCopyUnroll><<<static_cast<unsigned>(blocks), kCopyThreads, 0, stream>>>(
+        exs, world, rank, slot_rows, vpr, lvpr_of(vpr), rows_off, nullptr, 0, 0, nullptr, 0, d_req_pos,
         static_cast<uint4*>(d_out));
   }
   DGFX_CUDA_TRY(cudaGetLastError());
@@ -364,14 +396,16 @@ int launch_exchange_copy(bool serve, const void* const* d_exchanges, int32_t wor
 
 extern "C" int dgfx_exchange_serve(const void* const* d_exchanges, int32_t world, int32_t rank, int64_t slot_rows,
                                    int64_t rows_per_rank, int64_t row_bytes, const void* d_table, int64_t local_rows,
-                                   const int32_t* d_req_pos, void* d_out, dgfx_stream stream_) {
+                                   const void* d_replica, int64_t replica_rows, const int32_t* d_req_pos, void* d_out,
+                                   dgfx_stream stream_) {
   if (d_exchanges == nullptr || !ex_args_ok(world, slot_rows, row_bytes) || rank < 0 || rank >= world ||
-      rows_per_rank < 1 || local_rows < 0 || (local_rows > 0 && d_table == nullptr) || d_req_pos == nullptr) {
+      rows_per_rank < 1 || local_rows < 0 || (local_rows > 0 && d_table == nullptr) || d_req_pos == nullptr ||
+      replica_rows < 0 || (replica_rows > 0 && d_replica == nullptr)) {
     return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_exchange_serve: bad arguments");
   }
   return launch_exchange_copy(true, d_exchanges, world, rank, slot_rows, row_bytes, d_table,
-                              static_cast<int64_t>(rank) * rows_per_rank, local_rows, d_req_pos, d_out,
-                              reinterpret_cast<cudaStream_t>(stream_));
+                              static_cast<int64_t>(rank) * rows_per_rank, local_rows, d_replica, replica_rows,
+                              d_req_pos, d_out, reinterpret_cast<cudaStream_t>(stream_));
 }
 
 extern "C" int dgfx_exchange_scatter(const void* const* d_exchanges, int32_t world, int32_t rank, int64_t slot_rows,
@@ -381,8 +415,8 @@ extern "C" int dgfx_exchange_scatter(const void* const* d_exchanges, int32_t wor
     return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_exchange_scatter: bad arguments");
   }
   if (world == 1) return DGFX_OK;
-  return launch_exchange_copy(false, d_exchanges, world, rank, slot_rows, row_bytes, nullptr, 0, 0, d_req_pos, d_out,
-                              reinterpret_cast<cudaStream_t>(stream_));
+  return launch_exchange_copy(false, d_exchanges, world, rank, slot_rows, row_bytes, nullptr, 0, 0, nullptr, 0,
+                              d_req_pos, d_out, reinterpret_cast<cudaStream_t>(stream_));
 }
 
 extern "C" int dgfx_exchange_barrier(const void* const* d_exchanges, int32_t world, int32_t rank, uint32_t epoch,

@@ -164,6 +164,8 @@ class PeerFeatures:
         self._peers = []
         self._ptrs = None
         self._ex = None
+        self._replica = None
+        self._hot_slot = None
 
     def _share(self, local_ptr: int):
         """All ranks' pointers to the allocation each rank passes (collective)."""
@@ -202,7 +204,7 @@ class PeerFeatures:
             self._ex = DeviceBuffer(need.value, self.device)
             self._ex.tensor((need.value,), torch.uint8).zero_()
             self._ex_ptrs = self._share(self._ex.ptr)
-            self._req_pos = torch.empty(self.world * self.exchange_rows, dtype=torch.int32, device=self.device)
+            self._req_pos = torch.empty((self.world + 1) * self.exchange_rows, dtype=torch.int32, device=self.device)
             self._bar = torch.zeros(1, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
         return self
@@ -220,18 +222,47 @@ class PeerFeatures:
         s = torch.cuda.current_stream(self.device) if stream is None else stream
         sh = int(s.cuda_stream)
         lib = _native.lib()
+        rep_rows = 0 if self._replica is None else int(self._replica.shape[0])
         _native.check(lib.dgfx_exchange_partition(
             self._ex.ptr, self.world, self.exchange_rows, self.rows_per_rank, self.num_nodes, self.row_bytes,
-            _native.ptr(ids), begin_ptr, end_ptr, int(max_rows), _native.ptr(self._req_pos), _native.ptr(out), sh))
+            _native.ptr(ids), begin_ptr, end_ptr, int(max_rows), _native.ptr(self._hot_slot),
+            _native.ptr(self._req_pos), _native.ptr(out), sh))
         self._group_barrier(s)
         _native.check(lib.dgfx_exchange_serve(
             _native.ptr(self._ex_ptrs), self.world, self.rank, self.exchange_rows, self.rows_per_rank, self.row_bytes,
-            self.buffer.ptr, self.local_rows, _native.ptr(self._req_pos), _native.ptr(out), sh))
+            self.buffer.ptr, self.local_rows, _native.ptr(self._replica), rep_rows, _native.ptr(self._req_pos),
+            _native.ptr(out), sh))
         self._group_barrier(s)
         _native.check(lib.dgfx_exchange_scatter(
             _native.ptr(self._ex_ptrs), self.world, self.rank, self.exchange_rows, self.row_bytes,
             _native.ptr(self._req_pos), _native.ptr(out), sh))
         return out
+
+    def replicate(self, hot_ids):
+        """Keeps a read-only copy of the rows of ``hot_ids`` (int64 CUDA
+        tensor, identical on every rank) in this GPU's HBM; requests for them
+        are then served locally instead of crossing NVLink (bulk exchange
+        only). Collective: every rank calls it with the same ids. Returns
+        the bytes the copy takes on this GPU."""
+        torch = _native.require_cuda()
+        if self._ex is None:
+            return 0  # one rank, or peer loads: nothing crosses an exchange
+        n = int(hot_ids.numel())
+        self._hot_slot = None
+        self._replica = None
+        replica = torch.empty((max(n, 1), self.dim), dtype=self.dtype, device=self.device)[:n]
+        bounds = torch.zeros(2, dtype=torch.int64, device=self.device)
+        for lo in range(0, n, self.exchange_rows):
+            hi = min(n, lo + self.exchange_rows)
+            bounds[0], bounds[1] = lo, hi
+            self.gather_range(hot_ids, _native.elem_ptr(bounds, 0), _native.elem_ptr(bounds, 1), hi - lo,
+                              replica[lo:hi])
+        hot_slot = torch.full((self.num_nodes,), -1, dtype=torch.int32, device=self.device)
+        hot_slot[hot_ids] = torch.arange(n, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)
+        self.check()
+        self._replica, self._hot_slot = replica, hot_slot
+        return n * self.row_bytes + self.num_nodes * 4
 
     def _group_barrier(self, s):
         """Stream-ordered barrier over the group (every rank calls it in the same order)."""
@@ -266,10 +297,24 @@ class PeerFeatures:
             torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
         self.table = None
+        self._replica = None
+        self._hot_slot = None
         self.buffer.free()
         if self._ex is not None:
             self._ex.free()
             self._ex = None
+
+
+def hot_rows(index, count: int):
+    """The ``count`` nodes with the most in-edges of a forward adjacency
+    index (int64 CUDA tensor, ties broken by node id): the rows a sampler
+    walking that index requests most often. Deterministic, so every rank
+    computes the same set."""
+    torch = _native.require_cuda()
+    num = int(index.num_dst)  # column ids of a forward index are target node ids
+    deg = torch.bincount(index.col, minlength=num)
+    order = torch.sort(deg, descending=True, stable=True).indices
+    return order[: max(0, min(int(count), num))].to(torch.int64).contiguous()
 
 
 class ShardedSampler:

@@ -330,11 +330,17 @@ int dgfx_gather_rows_p2p(const void* const* d_tables, int32_t world,
  * same sequence on all ranks, starting at 1) in the other ranks' flags and
  * waits for theirs, at most max_wait_ns; a wait that runs out sets the
  * timeout flag instead of hanging.
+ * Local replica (optional): d_hot_slot int32[num_nodes] maps a node to its
+ * row in this rank's d_replica table (a read-only copy of frequently
+ * requested rows, replica_rows x row_bytes), -1 elsewhere. Requests for such
+ * nodes never cross NVLink: the partition puts them in an extra slot and the
+ * serve launch copies their rows locally. NULL / 0 disables it.
  * dgfx_exchange_check (synchronises the stream) reports and clears the flags:
  * slot overflow (a slot needed more than slot_rows ids; rows were dropped) as
  * DGFX_ERR_WORKSPACE, barrier timeout as DGFX_ERR_FAILED_PRECONDITION.
  * d_exchanges is a device array of the `world` exchange-buffer pointers (own
- * included); d_req_pos holds world * slot_rows int32 and stays on this rank.
+ * included); d_req_pos holds (world + 1) * slot_rows int32 and stays on this
+ * rank.
  * world <= 16.
  * ------------------------------------------------------------------------ */
 int dgfx_exchange_buffer_size(int32_t world, int64_t slot_rows,
@@ -343,12 +349,14 @@ int dgfx_exchange_partition(void* d_exchange, int32_t world, int64_t slot_rows,
                             int64_t rows_per_rank, int64_t num_nodes,
                             int64_t row_bytes, const int64_t* d_row_ids,
                             const int64_t* d_begin, const int64_t* d_end,
-                            int64_t max_rows, int32_t* d_req_pos, void* d_out,
+                            int64_t max_rows, const int32_t* d_hot_slot,
+                            int32_t* d_req_pos, void* d_out,
                             dgfx_stream stream);
 int dgfx_exchange_serve(const void* const* d_exchanges, int32_t world,
                         int32_t rank, int64_t slot_rows, int64_t rows_per_rank,
                         int64_t row_bytes, const void* d_table,
-                        int64_t local_rows, const int32_t* d_req_pos,
+                        int64_t local_rows, const void* d_replica,
+                        int64_t replica_rows, const int32_t* d_req_pos,
                         void* d_out, dgfx_stream stream);
 int dgfx_exchange_scatter(const void* const* d_exchanges, int32_t world,
                           int32_t rank, int64_t slot_rows, int64_t row_bytes,

@@ -95,6 +95,10 @@ def _worker(rank, world, port, q):
                                      exchange_rows=max(20_000, cap_nodes), barrier=barrier)
             pe.table.copy_(full[lo:hi])
             pe.connect()
+            if barrier == "device":
+                # A replica of the 5,000 nodes with most in-edges (served locally).
+                nbytes = pe.replicate(driver.hot_rows(index, 5000))
+                assert nbytes > 0
             out.fill_(0)
             pe.gather_range(ids, _native.elem_ptr(bounds, 0), _native.elem_ptr(bounds, 1), 20_000, out)
             torch.cuda.synchronize()
@@ -136,10 +140,11 @@ def test_peer_gather_single_rank(cuda):
     pf.close()
 
 
-def _run_exchange(lib, W, rpr, N, row_bytes, parts, ids, bounds, caps, outs, slot, sh):
+def _run_exchange(lib, W, rpr, N, row_bytes, parts, ids, bounds, caps, outs, slot, sh, hot=None, replica=None):
     """The three exchange launches for W ranks whose buffers all live on one
     GPU; issuing every rank's step before the next step's launches (one
-    stream) is the barrier."""
+    stream) is the barrier. hot / replica: a shared node -> replica-row map
+    and replica table used by every emulated rank."""
     import ctypes
 
     import torch
@@ -151,15 +156,16 @@ def _run_exchange(lib, W, rpr, N, row_bytes, parts, ids, bounds, caps, outs, slo
     dev = outs[0].device
     bufs = [torch.zeros(need.value, dtype=torch.uint8, device=dev) for _ in range(W)]
     ptrs = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=dev)
-    pos = [torch.empty(W * slot, dtype=torch.int32, device=dev) for _ in range(W)]
+    pos = [torch.empty((W + 1) * slot, dtype=torch.int32, device=dev) for _ in range(W)]
+    rep_rows = 0 if replica is None else int(replica.shape[0])
     for r in range(W):
         _native.check(lib.dgfx_exchange_partition(
             _native.ptr(bufs[r]), W, slot, rpr, N, row_bytes, _native.ptr(ids[r]), _native.elem_ptr(bounds[r], 0),
-            _native.elem_ptr(bounds[r], 1), caps[r], _native.ptr(pos[r]), _native.ptr(outs[r]), sh))
+            _native.elem_ptr(bounds[r], 1), caps[r], _native.ptr(hot), _native.ptr(pos[r]), _native.ptr(outs[r]), sh))
     for r in range(W):
         _native.check(lib.dgfx_exchange_serve(
             _native.ptr(ptrs), W, r, slot, rpr, row_bytes, _native.ptr(parts[r]), int(parts[r].shape[0]),
-            _native.ptr(pos[r]), _native.ptr(outs[r]), sh))
+            _native.ptr(replica), rep_rows, _native.ptr(pos[r]), _native.ptr(outs[r]), sh))
     for r in range(W):
         _native.check(lib.dgfx_exchange_scatter(_native.ptr(ptrs), W, r, slot, row_bytes, _native.ptr(pos[r]),
                                                 _native.ptr(outs[r]), sh))
@@ -210,6 +216,23 @@ def test_exchange_emulated_ranks(cuda):
                 assert torch.equal(outs[r][:n], exp), f"W={W} rank {r}"
                 assert bool((outs[r][n:] == 3.0).all()), f"W={W} rank {r}: rows past the end written"
                 _native.check(lib.dgfx_exchange_check(_native.ptr(bufs[r]), W, sh))
+        # With a replica of 30 % of the nodes (hot rows served locally).
+        hot_ids = torch.from_numpy(rng.choice(N, N * 3 // 10, replace=False)).to(dev)
+        hot = torch.full((N,), -1, dtype=torch.int32, device=dev)
+        hot[hot_ids] = torch.arange(len(hot_ids), dtype=torch.int32, device=dev)
+        replica = full[hot_ids].contiguous()
+        for o in outs:
+            o.fill_(3.0)
+        bufs = _run_exchange(lib, W, rpr, N, row_bytes, parts, ids, bounds, caps, outs, slot, sh, hot, replica)
+        torch.cuda.synchronize()
+        for r in range(W):
+            lo, n = int(bounds[r][0]), caps[r]
+            sel = ids[r][lo:lo + n]
+            ok = (sel >= 0) & (sel < N)
+            exp = torch.zeros((n, F), dtype=torch.bfloat16, device=dev)
+            exp[ok] = full[sel[ok]]
+            assert torch.equal(outs[r][:n], exp), f"W={W} rank {r} with replica"
+            _native.check(lib.dgfx_exchange_check(_native.ptr(bufs[r]), W, sh))
         if W > 1:
             small = 16
             bufs = _run_exchange(lib, W, rpr, N, row_bytes, parts, ids, bounds, caps, outs, small, sh)
@@ -239,7 +262,7 @@ def test_exchange_barrier_single_gpu(cuda):
     for epoch in (1, 2, 3):
         _native.check(lib.dgfx_exchange_barrier(_native.ptr(one), 1, 0, epoch, 10**9, sh))
     _native.check(lib.dgfx_exchange_check(buf.data_ptr(), 1, sh))
-    flags = buf[192:256].view(torch.int32)  # arrival epochs, one uint32 per rank
+    flags = buf[320:384].view(torch.int32)  # arrival epochs, one uint32 per rank (exchange buffer byte 320)
     flags[1] = 7
     _native.check(lib.dgfx_exchange_barrier(_native.ptr(ptrs), 2, 0, 7, 10**9, sh))
     _native.check(lib.dgfx_exchange_check(buf.data_ptr(), 2, sh))
