@@ -30,6 +30,8 @@ ERR_UNSUPPORTED = 102
 F32 = 0
 BF16 = 1
 
+CALL_INDEX_DEVICE = (1 << 64) - 1  # DGFX_CALL_INDEX_DEVICE
+
 MODE_RANDOM = 0
 MODE_FIRST = 1
 MODE_MOST_RECENT = 2

@@ -90,6 +90,7 @@ struct Params {
   const int64_t* masks;
   int64_t B;
   uint32_t key0, key1, call_lo, call_hi;
+  unsigned long long* call_dev;  // non-null: the call index is this device word (advanced by compact_kernel)
   int32_t* scratch_nodes;    // [B][T]
   uint64_t* scratch_edges;   // [B][T]
   int32_t* node_cnt;         // [NS][B]
@@ -131,9 +132,10 @@ __host__ __device__ inline size_t counter_bytes(int threads) {
   return static_cast<size_t>(threads / 32) * 256 * 4 + 256 * 4;
 }
 
-__device__ __forceinline__ uint64_t draw64(const Params& p, int32_t q, int32_t e, uint32_t m, uint32_t slot) {
-  U4 c{static_cast<uint32_t>(q), static_cast<uint32_t>(e) | ((m >> 1) << 16), slot, p.call_lo};
-  const U4 r = philox4x32_10(c, p.key0 ^ p.call_hi, p.key1);
+__device__ __forceinline__ uint64_t draw64(const Params& p, int32_t q, int32_t e, uint32_t m, uint32_t slot,
+                                           uint2 call) {
+  U4 c{static_cast<uint32_t>(q), static_cast<uint32_t>(e) | ((m >> 1) << 16), slot, call.x};
+  const U4 r = philox4x32_10(c, p.key0 ^ call.y, p.key1);
   return (m & 1u) ? (static_cast<uint64_t>(r.w) << 32 | r.z) : (static_cast<uint64_t>(r.y) << 32 | r.x);
 }
 
@@ -145,7 +147,8 @@ __device__ __forceinline__ uint64_t draw64(const Params& p, int32_t q, int32_t e
 // stats[0..2] (shared) count expanded rows, sampled neighbours and timestamp
 // probes of this CTA.
 __device__ void expand_task(const Params& p, long long* at, int32_t q, int32_t e, int32_t base, int64_t v,
-                            bool has_ts, int64_t seed_ts, int64_t mask, uint32_t slot, unsigned int* stats) {
+                            bool has_ts, int64_t seed_ts, int64_t mask, uint32_t slot, uint2 call, int32_t pre_n,
+                            unsigned int* stats) {
   const EdgeDev E = p.edges[e];
   const int32_t k = E.k, stride = E.stride;
   int32_t cnt = 0;
@@ -160,7 +163,9 @@ __device__ void expand_task(const Params& p, long long* at, int32_t q, int32_t e
       atomicOr(&p.status[1], 1ull);
       n = 0;
     }
-    if (temporal && n > 0) {
+    if (temporal && n > 0 && pre_n >= 0) {
+      n = pre_n;  // cutoff found by the cooperative pre-pass
+    } else if (temporal && n > 0) {
       // upper_bound(ts[rb..re), seed_ts): first position with ts > seed_ts.
       int64_t lo = 0, hi = n;
       unsigned int probes = 0;
@@ -189,7 +194,7 @@ __device__ void expand_task(const Params& p, long long* at, int32_t q, int32_t e
         // already taken, else take j. Chosen offsets go to the child slots.
         int32_t taken = 0;
         for (int64_t j = nv - cnt; j < nv; ++j) {
-          const uint64_t r = draw64(p, q, e, static_cast<uint32_t>(taken), slot);
+          const uint64_t r = draw64(p, q, e, static_cast<uint32_t>(taken), slot, call);
           int64_t t = static_cast<int64_t>(bounded64(r, static_cast<uint64_t>(j + 1)));
           for (int32_t i = 0; i < taken; ++i) {
             if (at[base + i * stride] == t) {
@@ -226,6 +231,50 @@ __device__ void expand_task(const Params& p, long long* at, int32_t q, int32_t e
     }
   }
   for (int32_t i = cnt; i < k; ++i) at[base + i * stride] = -1;
+}
+
+// Temporal cutoff of every task of one level, eight lanes per task: each
+// round the group probes 8 pivots of the remaining interval of the
+// time-sorted row (a 9-ary search; rows of <= 8 remaining entries are read
+// whole), so a row of d edges costs ceil(log9(d)) dependent loads instead of
+// log2(d). cut[t - t0] = number of row entries with ts <= seed_ts, or -1
+// when the task's edge set has no timestamps / the node is absent.
+__device__ void cutoff_prepass(const Params& p, const Work& w, int32_t* cut, int t0, int t1, int64_t seed_ts,
+                               unsigned int* stats) {
+  const int gl = threadIdx.x & 7;
+  const int ngroups = blockDim.x >> 3;
+  const int shift = threadIdx.x & 24;
+  const unsigned gmask = 0xFFu << shift;
+  for (int t = t0 + (threadIdx.x >> 3); t < t1; t += ngroups) {
+    const int4 task = p.tasks[t];
+    const int32_t v = w.node[task.x];
+    const EdgeDev& E = p.edges[task.y];
+    int32_t res = -1;
+    if (v >= 0 && E.ts != nullptr) {
+      const int64_t rb = E.rowptr[v];
+      const int64_t* ts = E.ts + rb;
+      int64_t lo = 0, hi = E.rowptr[v + 1] - rb;
+      unsigned int probes = 0;
+      while (lo < hi) {
+        const int64_t len = hi - lo;
+        if (len <= 8) {
+          const bool le = gl < len && ts[lo + gl] <= seed_ts;
+          lo += __popc(__ballot_sync(gmask, le));
+          probes += static_cast<unsigned int>(len);
+          break;
+        }
+        const bool le = ts[lo + ((gl + 1) * len) / 9] <= seed_ts;
+        const int c = __popc((__ballot_sync(gmask, le) >> shift) & 0xFFu);  // pivots <= cut form a prefix
+        const int64_t base = lo;
+        if (c > 0) lo = base + (c * len) / 9 + 1;
+        if (c < 8) hi = base + ((c + 1) * len) / 9;
+        probes += 8;
+      }
+      res = static_cast<int32_t>(lo);
+      if (gl == 0) atomicAdd(&stats[2], probes);
+    }
+    if (gl == 0) cut[t - t0] = res;
+  }
 }
 
 // Expansion, second half: node[q] = col[at[q]] for the child slots
@@ -369,6 +418,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   const Work w = carve_work(base, T, p.H);
   const uint32_t slot = static_cast<uint32_t>(sample);
 
+  __shared__ uint2 call_s;
   const int64_t seed = p.seeds[sample];
   const bool has_ts = p.seed_ts != nullptr;
   const int64_t sts = has_ts ? p.seed_ts[sample] : 0;
@@ -378,6 +428,9 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   for (int i = threadIdx.x; i < p.num_edgesets; i += blockDim.x) es_count[i] = 0;
   if (threadIdx.x < 3) stats[threadIdx.x] = 0;
   if (threadIdx.x == 0) {
+    const unsigned long long cidx =
+        p.call_dev != nullptr ? *p.call_dev : ((static_cast<unsigned long long>(p.call_hi) << 32) | p.call_lo);
+    call_s = make_uint2(static_cast<uint32_t>(cidx), static_cast<uint32_t>(cidx >> 32));
     bool ok = true;
     if (p.root_has_children && (seed < 0 || seed >= p.root_num_src)) {
       atomicMin(&p.status[0], static_cast<unsigned long long>(sample));
@@ -391,11 +444,20 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   //    table's words, which are free until the relabel), then the column
   //    loads of all picks of the level in parallel.
   long long* at = reinterpret_cast<long long*>(w.slot);
+  const uint2 call = call_s;
   for (int d = 0; d < p.depth; ++d) {
     const int t0 = p.level[d], t1 = p.level[d + 1];
+    // Temporal cutoffs first (local ids are not numbered yet: their array
+    // is free and holds one cutoff per task of the level).
+    const bool pre = has_ts && (t1 - t0) <= T;
+    if (pre) {
+      cutoff_prepass(p, w, w.local, t0, t1, sts, stats);
+      __syncthreads();
+    }
     for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
       const int4 task = p.tasks[t];
-      expand_task(p, at, task.x, task.y, task.z, w.node[task.x], has_ts, sts, mask, slot, stats);
+      expand_task(p, at, task.x, task.y, task.z, w.node[task.x], has_ts, sts, mask, slot, call,
+                  pre ? w.local[t - t0] : -1, stats);
     }
     __syncthreads();
     load_children(p, w, at, p.clevel[d], p.clevel[d + 1]);
@@ -604,6 +666,8 @@ __global__ void compact_kernel(Params p, const int64_t* __restrict__ node_off, c
                                int64_t* __restrict__ edge_dst) {
   const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  // Every sample_kernel CTA has read the call index by now.
+  if (p.call_dev != nullptr && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(p.call_dev, 1ull);
   if (warp >= p.B) return;
   const int64_t i = warp;
   const int32_t* src_nodes = p.scratch_nodes + i * static_cast<int64_t>(p.T);
@@ -893,7 +957,8 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
     DGFX_CUDA_TRY(cudaMemcpy(s->d_children, children.data(), sizeof(int32_t) * children.size(), cudaMemcpyHostToDevice));
   }
   DGFX_CUDA_TRY(cudaMemcpy(s->d_clevel, clevel.data(), sizeof(int32_t) * clevel.size(), cudaMemcpyHostToDevice));
-  const unsigned long long init[6] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
+  // Status: first bad seed, ts missing, table overflow, 3 stats, device call index.
+  const unsigned long long init[7] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
   DGFX_CUDA_TRY(cudaMemcpy(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice));
 
   // Threads per CTA: about one per eight tree positions, 32..256.
@@ -951,8 +1016,9 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   if (d_workspace == nullptr || workspace_bytes < sample_ws_bytes(s, B)) {
     return fail(DGFX_ERR_WORKSPACE, "dgfx_sampler_sample: workspace too small");
   }
-  const unsigned long long init[6] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
-  DGFX_CUDA_TRY(cudaMemcpyAsync(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice, stream));
+  // Status words 0..5 (memsets, so the call can be captured in a CUDA graph).
+  DGFX_CUDA_TRY(cudaMemsetAsync(s->d_status, 0xFF, sizeof(unsigned long long), stream));
+  DGFX_CUDA_TRY(cudaMemsetAsync(s->d_status + 1, 0, 5 * sizeof(unsigned long long), stream));
   s->last_B = B;
   s->last_seeds = d_seeds;
   Arena arena(d_workspace, workspace_bytes);
@@ -990,6 +1056,7 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   p.key1 = static_cast<uint32_t>(s->seed >> 32);
   p.call_lo = static_cast<uint32_t>(call_index);
   p.call_hi = static_cast<uint32_t>(call_index >> 32);
+  p.call_dev = call_index == ~0ull ? s->d_status + 6 : nullptr;
   p.scratch_nodes = b.scratch_nodes;
   p.scratch_edges = b.scratch_edges;
   p.node_cnt = b.node_cnt;

@@ -281,6 +281,8 @@ class Sampler:
 
         seeds / seed_ts / masks are int64 device tensors. With check=False the
         call stays asynchronous (errors are latched; call ``check()``).
+        call_index=_native.CALL_INDEX_DEVICE takes the random-stream index from
+        a device counter that every call advances (for CUDA-graph capture).
         """
         torch = _torch()
         lib = _native.lib()
@@ -343,6 +345,91 @@ class Sampler:
 
     def RandomWalkNegativeSampling(self, seed_node_idxs, target_edgeset_idx, num_walks, num_negatives_per_seed):
         raise NotImplementedError("RandomWalkNegativeSampling is not implemented on the B200 sampler yet")
+
+
+class CapturedSampleStep:
+    """``sample_merged`` calls, plus optional gathers of the sampled nodes'
+    feature rows, captured once in a CUDA graph over static buffers.
+
+    With a list of K samplers the graph forks K independent batches of
+    ``batch_size`` seeds onto K streams and joins them: one ``run`` samples K
+    batches concurrently for the host cost of one graph launch. ``run(seeds,
+    seed_ts)`` copies the inputs ([K, batch_size] or [batch_size] int64) into
+    the static buffers and replays the graph; the random streams advance on
+    every replay (device call index). Results are the static outputs, valid
+    until the next ``run``: a list of K (MergedBatch, feature rows) pairs, or
+    one pair for a single sampler. Each sampler handle belongs to this step
+    (handles serialise their calls). ``table`` is a [num_rows, F] feature
+    matrix of node set ``feature_nodeset``."""
+
+    def __init__(self, samplers, batch_size: int, with_timestamps: bool, table=None, feature_nodeset: int = 0,
+                 stream=None):
+        torch = _torch()
+        self.single = not isinstance(samplers, (list, tuple))
+        self.samplers = [samplers] if self.single else list(samplers)
+        K = len(self.samplers)
+        dev = self.samplers[0]._device
+        self.B = int(batch_size)
+        self.stream = stream if stream is not None else torch.cuda.Stream(device=dev)
+        self.branches = [self.stream] + [torch.cuda.Stream(device=dev) for _ in range(K - 1)]
+        self.seeds = torch.zeros((K, self.B), dtype=torch.int64, device=dev)
+        self.seed_ts = torch.zeros((K, self.B), dtype=torch.int64, device=dev) if with_timestamps else None
+        ns = int(feature_nodeset)
+        self.features = [None] * K
+        if table is not None:
+            for k, smp in enumerate(self.samplers):
+                cap = self.B * smp.tree_size
+                self.features[k] = torch.empty((cap, int(table.shape[1])), dtype=table.dtype, device=dev)
+
+        def body(k):
+            smp = self.samplers[k]
+            batch = smp.sample_merged(self.seeds[k], None if self.seed_ts is None else self.seed_ts[k], None,
+                                      call_index=_native.CALL_INDEX_DEVICE, check=False)
+            if table is not None:
+                off = batch.node_offsets
+                _native.check(_native.lib().dgfx_gather_rows_ranged(
+                    _native.ptr(table), int(table.shape[0]), int(table.shape[1]) * table.element_size(),
+                    _native.ptr(batch.node_ids), _native.elem_ptr(off, ns * self.B),
+                    _native.elem_ptr(off, (ns + 1) * self.B), int(batch.node_ids.numel()),
+                    _native.ptr(self.features[k]), _native.stream_handle()))
+            return batch
+
+        for k in range(K):  # allocates each sampler's workspace outside the capture
+            with torch.cuda.stream(self.branches[k]):
+                body(k)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        self.batches = [None] * K
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            for k in range(1, K):  # fork
+                self.branches[k].wait_stream(self.stream)
+            for k in range(K):
+                with torch.cuda.stream(self.branches[k]):
+                    self.batches[k] = body(k)
+            for k in range(1, K):  # join
+                self.stream.wait_stream(self.branches[k])
+        torch.cuda.synchronize(dev)
+
+    def run(self, seeds, seed_ts=None):
+        """Samples ``seeds`` after the caller's current stream."""
+        torch = _torch()
+        self.stream.wait_stream(torch.cuda.current_stream(self.seeds.device))
+        with torch.cuda.stream(self.stream):
+            self.seeds.copy_(seeds.view(self.seeds.shape), non_blocking=True)
+            if self.seed_ts is not None:
+                self.seed_ts.copy_(seed_ts.view(self.seed_ts.shape), non_blocking=True)
+            self.graph.replay()
+        out = list(zip(self.batches, self.features))
+        return out[0] if self.single else out
+
+    def wait(self):
+        """Makes the caller's current stream wait for the last run."""
+        torch = _torch()
+        torch.cuda.current_stream(self.seeds.device).wait_stream(self.stream)
+
+    @property
+    def sampler(self):
+        return self.samplers[0]
 
 
 def batch_to_host(batch: MergedBatch):

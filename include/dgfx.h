@@ -152,9 +152,13 @@ typedef struct dgfx_sample_out {
  * cutoff (edge ts <= seed ts); d_masked_edges (int64[B], -1 = none) masks one
  * edge of the masked edgeset per seed. call_index selects the random stream
  * (Philox4x32-10 keyed by the sampler seed; counter = (call, seed slot, tree
- * position, plan edge)). Asynchronous: device-side failures (seed out of
- * range, timestamps missing for a temporal index) are latched and reported
- * by dgfx_sampler_check. */
+ * position, plan edge)); call_index == DGFX_CALL_INDEX_DEVICE takes it from
+ * a counter in device memory that each call advances, so a call captured in
+ * a CUDA graph draws a new stream on every replay (the call issues only
+ * kernels and memsets; no host synchronisation). Asynchronous: device-side
+ * failures (seed out of range, timestamps missing for a temporal index) are
+ * latched and reported by dgfx_sampler_check. */
+#define DGFX_CALL_INDEX_DEVICE (~0ull)
 int dgfx_sampler_sample(dgfx_sampler* sampler, const int64_t* d_seeds,
                         const int64_t* d_seed_ts, const int64_t* d_masked_edges,
                         int64_t num_seeds, uint64_t call_index,
