@@ -478,7 +478,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
       const int32_t v = w.node[q];
       int32_t slot_q = -1;
       if (v >= 0) {
-        const int ns = p.pos_info[q].y & 0xFF;
+        const int ns = p.num_nodesets == 1 ? 0 : (p.pos_info[q].y & 0xFF);
         const uint32_t key = p.ns_key_base[ns] + static_cast<uint32_t>(v);
         const unsigned long long entry = (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(q);
         uint32_t h = ((key * 0x9E3779B1u) >> (32 - p.log2H)) & hmask;
@@ -522,7 +522,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
       const int32_t sl = w.local[q];
       if (sl < 0 || static_cast<uint32_t>(w.slot[sl]) != static_cast<uint32_t>(q)) return -1;
     }
-    return p.pos_info[q].y & 0xFF;
+    return NS == 1 ? 0 : (p.pos_info[q].y & 0xFF);
   };
   for (int i = threadIdx.x; i < nw * NS; i += blockDim.x) wcnt[i] = 0;
   __syncthreads();
@@ -583,7 +583,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   for (int q = threadIdx.x; q < T; q += blockDim.x) {
     const int32_t v = w.node[q];
     if (v < 0) continue;
-    const int ns = p.pos_info[q].y & 0xFF;
+    const int ns = NS == 1 ? 0 : (p.pos_info[q].y & 0xFF);
     const int32_t l = w.local[q];
     if (l >= 0) out_nodes[ns_base[ns] + l] = v;
   }
@@ -606,10 +606,18 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
     *key = (static_cast<unsigned long long>(E.edgeset) << (2 * lb)) | (src << lb) | dst;
     return true;
   };
+  // Pass 1 computes each position's key once (staged by position in the
+  // sort's spare half; a real key is < 2^56, ~0 marks none) and counts them
+  // per warp; pass 2 compacts the staged keys in position order.
+  unsigned long long* staged = tmp;
   int32_t wsum = 0;
+#pragma unroll 4
   for (int b = plo; b < phi; b += 32) {
-    unsigned long long key;
-    wsum += __popc(__ballot_sync(0xffffffffu, edge_key(b + lane, &key)));
+    const int q = b + lane;
+    unsigned long long key = ~0ull;
+    const bool ok = edge_key(q, &key);
+    if (q < phi) staged[q] = ok ? key : ~0ull;
+    wsum += __popc(__ballot_sync(0xffffffffu, ok));
   }
   if (lane == 0) wtot[warp] = wsum;
   __syncthreads();
@@ -619,14 +627,33 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
     n_keys += wtot[v];
   }
   for (int b = plo; b < phi; b += 32) {
-    unsigned long long key = 0;
-    const bool ok = edge_key(b + lane, &key);
+    const int q = b + lane;
+    const unsigned long long key = q < phi ? staged[q] : ~0ull;
+    const bool ok = key != ~0ull;
     const uint32_t m = __ballot_sync(0xffffffffu, ok);
     if (ok) keys[wbase + __popc(m & lt)] = key;
     wbase += __popc(m);
   }
   __syncthreads();
-  const unsigned long long* ek = block_radix_sort(keys, tmp, n_keys, esbits + 2 * lb, cnt, dbase);
+  const unsigned long long* ek;
+  if (n_keys <= static_cast<int>(blockDim.x)) {
+    // Few keys (the usual case): one key per thread, stable rank = keys
+    // smaller, or equal at a smaller index; one pass, no digit passes.
+    if (static_cast<int>(threadIdx.x) < n_keys) {
+      const int me = static_cast<int>(threadIdx.x);
+      const unsigned long long k = keys[me];
+      int rank = 0;
+      for (int j = 0; j < n_keys; ++j) {
+        const unsigned long long kj = keys[j];
+        rank += (kj < k || (kj == k && j < me)) ? 1 : 0;
+      }
+      tmp[rank] = k;
+    }
+    __syncthreads();
+    ek = tmp;
+  } else {
+    ek = block_radix_sort(keys, tmp, n_keys, esbits + 2 * lb, cnt, dbase);
+  }
   uint64_t* out_edges = p.scratch_edges + sample * static_cast<int64_t>(T);
   const unsigned long long lmask = (1ull << lb) - 1;
   auto is_new = [&](int i) -> uint64_t { return (i == 0 || ek[i - 1] != ek[i]) ? 1ull : 0ull; };
