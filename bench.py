@@ -739,6 +739,67 @@ def bench_sage(dev, steps, scale=1.0):
     return out
 
 
+def bench_gat(dev, steps, scale=1.0):
+    """Graph-attention aggregation (segment softmax + weighted segment sum):
+    2,000,000 target nodes, 40,000,000 edges grouped by target (in-degrees
+    from the Zipf 2.1 generator's popularity), 8 heads x 32 dims, bf16
+    messages, fp32 logits, bf16 output."""
+    import torch
+
+    from distributed_graph_flow_b200 import aggregation, synth
+
+    N = max(1024, int(2_000_000 * scale))
+    E = max(1024, int(40_000_000 * scale))
+    H, D = 8, 32
+    spec = synth.GraphSpec(N, E, 2.1, 20_000, seed=8)
+    _, _, dst = synth.rowptr_and_edges(spec, dev)
+    ids = torch.sort(dst).values
+    del dst
+    g = torch.Generator(device=dev).manual_seed(5)
+    logits = torch.randn((E, H), generator=g, device=dev)
+    msgs = synth.normal_features(0, E, H * D, 12, torch.bfloat16, dev).view(E, H, D)
+    out = torch.empty((N, H, D), dtype=torch.bfloat16, device=dev)
+
+    def run(_):
+        aggregation.segment_softmax(logits, msgs, ids, N, indices_are_sorted=True)
+
+    for _ in range(3):
+        run(0)
+    ms = timed(run, max(5, steps // 2), torch.cuda.synchronize, "gat")
+    hbm, kind = measured_peaks()
+    nbytes = E * (H * D * 2 + H * 4 + 8) + N * H * D * 2 + 8 * (N + 1)
+    res = {"workload": "segment softmax + weighted segment sum (GAT relation attention): 2,000,000 targets, "
+                       "40,000,000 edges grouped by target, 8 heads x 32, bf16 messages, fp32 logits",
+           "ms": round(ms, 4), "algorithmic_bytes": nbytes, "achieved_gbs": round(nbytes / ms / 1e6, 1),
+           "peak_gbs": hbm, "peak_kind": kind, "frac": round(nbytes / ms / 1e6 / hbm, 4), "bound": "hbm"}
+    del out
+    try:  # torch-CPU fp32 on a bounded prefix of the segments
+        th = host_cores()
+        torch.set_num_threads(th)
+        rows = min(N, 100_000)
+        n_items = int(torch.searchsorted(ids, torch.tensor(rows, device=dev)).item())
+        li, mi, ti = logits[:n_items].cpu(), msgs[:n_items].float().cpu(), ids[:n_items].cpu()
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 8.0:
+            mx = torch.full((rows, H), -float("inf")).scatter_reduce(0, ti[:, None].expand(-1, H), li, reduce="amax")
+            ex = torch.exp(li - mx[ti])
+            den = torch.zeros((rows, H)).index_add_(0, ti, ex)
+            w = ex / (den[ti] + 1e-9)
+            _ = torch.zeros((rows, H, D)).index_add_(0, ti, w[..., None] * mi)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        cpu_gbs = (n_items * (H * D * 4 + H * 4 + 8) + rows * H * D * 4) / dt / 1e9
+        res["cpu_baseline"] = {"value": round(n_items / dt, 1), "unit": "edges/s", "cores": th, "kind": "port",
+                               "sample": f"{rows} segments ({n_items} edges), torch fp32 scatter_reduce/index_add_, "
+                                         f"{reps} reps ({cpu_gbs:.1f} GB/s)"}
+        res["edges_per_s"] = round(E / (ms / 1e3), 1)
+        res["speedup_vs_cpu"] = round(res["edges_per_s"] / res["cpu_baseline"]["value"], 1)
+    except Exception as exc:  # noqa: BLE001
+        res["cpu_baseline"] = {"unavailable": str(exc)}
+    return res
+
+
 def measured_tflops():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -892,7 +953,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the SpMM / temporal sub-benchmarks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--scale", type=float, default=1.0, help="shrink the workload (profiling / debugging only)")
-    ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal", "hetero", "sage"],
+    ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal", "hetero", "sage", "gat"],
                     help="run one workload and skip the rest (profiling)")
     ap.add_argument("--halo", default="exchange", choices=["exchange", "p2p", "nccl"],
                     help="feature halo: bulk peer exchange (default), direct peer loads, or NCCL all-to-all")
@@ -925,9 +986,10 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
 
-    if args.only in ("spmm", "temporal", "hetero", "sage"):
+    if args.only in ("spmm", "temporal", "hetero", "sage", "gat"):
         # Single sub-benchmark (used for focused profiler captures).
-        fn = {"spmm": bench_spmm, "temporal": bench_temporal, "hetero": bench_hetero, "sage": bench_sage}[args.only]
+        fn = {"spmm": bench_spmm, "temporal": bench_temporal, "hetero": bench_hetero, "sage": bench_sage,
+              "gat": bench_gat}[args.only]
         print(json.dumps(fn(dev, args.steps, args.scale)), flush=True)
         return
 
@@ -962,6 +1024,8 @@ def main():
             res["hetero_temporal"] = bench_hetero(dev, args.steps)
             torch.cuda.empty_cache()
             res["sage_mean_2m"] = bench_sage(dev, args.steps)
+            torch.cuda.empty_cache()
+            res["gat_attention_2m"] = bench_gat(dev, args.steps)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -97,6 +97,8 @@ SIGNATURES = {
     "dgfx_spmm_csr": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _int, _vp, _int, _i64, _i32, _vp, _sz, _vp]),
     "dgfx_segment_sum_workspace_size": (_int, [_i64, _i64, _i64, ctypes.POINTER(_sz)]),
     "dgfx_segment_sum": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _int, _vp, _sz, _vp]),
+    "dgfx_segment_softmax_workspace_size": (_int, [_i64, _i64, _i32, _i64, _int, _i32, ctypes.POINTER(_sz)]),
+    "dgfx_segment_softmax": (_int, [_vp, _i32, _vp, _int, _i64, _vp, _i64, _i64, _i32, _vp, _int, _vp, _sz, _vp]),
     "dgfx_dense_concat_bf16": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i32, _vp, _vp]),
     "dgfx_dense_check": (_int, [_vp]),
     "dgfx_halo_partition_workspace_size": (_int, [_i64, _i32, ctypes.POINTER(_sz)]),

@@ -88,6 +88,33 @@ def segment_sum(data, segment_ids, num_segments: int, mean: bool = False, indice
     return out
 
 
+def segment_softmax(logits, messages, segment_ids, num_segments: int, indices_are_sorted: bool = False,
+                    out_dtype=None, stream=None):
+    """Attention-weighted segment sum (hetero_graph_attention_network.py:
+    242-263): softmax of ``logits`` [E, H] over the items of each segment
+    (per head, max-subtracted, + 1e-9 in the denominator) weighting
+    ``messages`` [E, H, D]; returns [num_segments, H, D]. One pass over the
+    items (online softmax), fp32 accumulation."""
+    torch = _native.require_cuda()
+    if logits.dtype != torch.float32:
+        raise ValueError("segment_softmax: logits must be float32")
+    E, H = int(logits.shape[0]), int(logits.shape[1])
+    if messages.dim() != 3 or int(messages.shape[0]) != E or int(messages.shape[1]) != H:
+        raise ValueError("segment_softmax: messages must be [E, H, D] matching logits [E, H]")
+    D = int(messages.shape[2])
+    out = torch.empty((num_segments, H, D), dtype=out_dtype or messages.dtype, device=messages.device)
+    ids = segment_ids.to(torch.int64).contiguous()
+    need = ctypes.c_size_t()
+    _native.check(_native.lib().dgfx_segment_softmax_workspace_size(
+        E, num_segments, H, D, _dtype_code(messages.dtype), int(bool(indices_are_sorted)), ctypes.byref(need)))
+    ws = torch.empty(max(1, need.value), dtype=torch.uint8, device=messages.device)
+    _native.check(_native.lib().dgfx_segment_softmax(
+        _native.ptr(logits.contiguous()), H, _native.ptr(messages.contiguous()), _dtype_code(messages.dtype), D,
+        _native.ptr(ids), E, int(num_segments), int(bool(indices_are_sorted)), _native.ptr(out),
+        _dtype_code(out.dtype), _native.ptr(ws), need.value, _native.stream_handle(stream)))
+    return out
+
+
 def gather_rows(table, ids, stream=None):
     """out[i] = table[ids[i]] (rows of any dtype whose byte width is a
     multiple of 16; ids outside the table give zero rows)."""

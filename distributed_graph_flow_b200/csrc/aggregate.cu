@@ -361,6 +361,187 @@ int sm_count() {
   return n;
 }
 
+// ---- segment softmax aggregation (attention) ------------------------------
+// out[t, h, :] = sum_e w[e, h] * msg[e, h, :] over the items e of segment t,
+// w[e, h] = exp(l[e, h] - m[t, h]) / (sum_e' exp(l[e', h] - m[t, h]) + 1e-9),
+// m[t, h] = max_e l[e, h]: the relation attention of
+// dgf/src/learning/jax/layers/hetero_graph_attention_network.py:242-263.
+// One warp per segment over its items in CSR order (perm[j] = item of slot j,
+// nullptr = identity); lane l owns the 16-byte slices v = l + 32 i of the
+// H x D message row, each inside one head. Online softmax: per slice a running
+// (max, sum, weighted sum) rescaled when the max grows, so every message row
+// is read once and no [E, H] weight array is materialised.
+template <class MT>
+__device__ __forceinline__ void unpack16(const uint4& x, float* f);
+template <>
+__device__ __forceinline__ void unpack16<float>(const uint4& x, float* f) {
+  f[0] = __uint_as_float(x.x);
+  f[1] = __uint_as_float(x.y);
+  f[2] = __uint_as_float(x.z);
+  f[3] = __uint_as_float(x.w);
+}
+template <>
+__device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& x, float* f) {
+  const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// Online-softmax state of one 16-byte message slice: running max, running
+// sum of exp(l - max) and running weighted sum of the slice's elements.
+template <int EPV>
+struct SoftmaxState {
+  float m, s, acc[EPV];
+  __device__ __forceinline__ void init() {
+    m = -INFINITY;
+    s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) acc[k] = 0.0f;
+  }
+  __device__ __forceinline__ void add(float l, const float* x) {
+    const float mn = fmaxf(m, l);
+    if (mn == -INFINITY) return;  // every logit so far is -inf
+    const float sc = expf(m - mn);
+    const float p = expf(l - mn);
+    s = s * sc + p;
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) acc[k] = acc[k] * sc + p * x[k];
+    m = mn;
+  }
+  __device__ __forceinline__ void merge(float m2, float s2, const float* acc2) {
+    const float mn = fmaxf(m, m2);
+    if (mn == -INFINITY) return;
+    const float a = expf(m - mn), b = expf(m2 - mn);
+    s = s * a + s2 * b;
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) acc[k] = acc[k] * a + acc2[k] * b;
+    m = mn;
+  }
+};
+
+// One warp per task: a chunk of at most kChunk items of one segment (the
+// SpMM task plan), four message rows in flight. A segment of one task writes
+// its output; chunks of a split segment write their states (per slice: max,
+// sum, EPV weighted sums) for segment_softmax_fixup_kernel.
+template <class MT, class OT, int VPL>
+__global__ void __launch_bounds__(256) segment_softmax_kernel(
+    const int64_t* __restrict__ rowptr, const int64_t* __restrict__ task_off, const int64_t* __restrict__ split_off,
+    const int32_t* __restrict__ task_row, const int64_t* __restrict__ num_tasks, const uint32_t* __restrict__ perm,
+    const float* __restrict__ logits, int heads, const uint4* __restrict__ msg, int64_t vpr, int head_dim,
+    float* __restrict__ partial, OT* __restrict__ out) {
+  constexpr int EPV = 16 / sizeof(MT);
+  constexpr int kU = 4;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  int head[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) head[i] = static_cast<int>(((lane + 32 * i) * EPV) / head_dim);
+  const int64_t ntot = *num_tasks;  // task_off[nseg]: the exact plan size
+  for (int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; t < ntot; t += warps) {
+    const int64_t r = task_row[t];
+    const int64_t c = t - task_off[r];
+    const int64_t ntask = task_off[r + 1] - task_off[r];
+    const int64_t lo = rowptr[r] + c * kChunk;
+    const int64_t hi = min(rowptr[r + 1], lo + kChunk);
+    SoftmaxState<EPV> st[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) st[i].init();
+    for (int64_t j0 = lo; j0 < hi; j0 += kU) {
+      float l[kU][VPL];
+      uint4 x[kU][VPL];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t j = j0 + u;
+        const int64_t e = j < hi ? (perm != nullptr ? static_cast<int64_t>(perm[j]) : j) : -1;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+          const int64_t v = lane + 32 * i;
+          l[u][i] = -INFINITY;
+          x[u][i] = make_uint4(0, 0, 0, 0);
+          if (e >= 0 && v < vpr) {
+            l[u][i] = __ldg(logits + e * heads + head[i]);
+            x[u][i] = __ldg(msg + e * vpr + v);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (j0 + u < hi) {
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) {
+            if (lane + 32 * i < vpr) {
+              float f[EPV];
+              unpack16<MT>(x[u][i], f);
+              st[i].add(l[u][i], f);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int64_t v = lane + 32 * i;
+      if (v >= vpr) continue;
+      if (ntask == 1) {
+        const float inv = 1.0f / (st[i].s + 1e-9f);
+        OT* o = out + (r * vpr + v) * EPV;
+#pragma unroll
+        for (int k = 0; k < EPV; ++k) o[k] = static_cast<OT>(st[i].acc[k] * inv);
+      } else {
+        float* p = partial + ((split_off[r] + c) * vpr + v) * (2 + EPV);
+        p[0] = st[i].m;
+        p[1] = st[i].s;
+#pragma unroll
+        for (int k = 0; k < EPV; ++k) p[2 + k] = st[i].acc[k];
+      }
+    }
+  }
+}
+
+// Split segments: merge their chunk states in chunk order (deterministic).
+template <class MT, class OT, int VPL>
+__global__ void __launch_bounds__(256) segment_softmax_fixup_kernel(const int64_t* __restrict__ task_off,
+                                                                    const int64_t* __restrict__ split_off,
+                                                                    int64_t nseg, int64_t vpr,
+                                                                    const float* __restrict__ partial,
+                                                                    OT* __restrict__ out) {
+  constexpr int EPV = 16 / sizeof(MT);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; r < nseg; r += warps) {
+    const int64_t ntask = task_off[r + 1] - task_off[r];
+    if (ntask <= 1) continue;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int64_t v = lane + 32 * i;
+      if (v >= vpr) continue;
+      SoftmaxState<EPV> st;
+      st.init();
+      for (int64_t c = 0; c < ntask; ++c) {
+        const float* p = partial + ((split_off[r] + c) * vpr + v) * (2 + EPV);
+        st.merge(p[0], p[1], p + 2);
+      }
+      const float inv = 1.0f / (st.s + 1e-9f);
+      OT* o = out + (r * vpr + v) * EPV;
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) o[k] = static_cast<OT>(st.acc[k] * inv);
+    }
+  }
+}
+
+__global__ void softmax_sort_input_kernel(const int64_t* __restrict__ ids, int64_t n, int64_t nseg,
+                                          uint64_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t id = ids[i];
+    keys[i] = (id >= 0 && id < nseg) ? static_cast<uint64_t>(id) : static_cast<uint64_t>(nseg);
+    vals[i] = static_cast<uint32_t>(i);
+  }
+}
+
 unsigned grid_for(int64_t work, int threads) {
   const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
   const int64_t b = ceil_div(std::max<int64_t>(work, 1), threads);
@@ -580,4 +761,141 @@ extern "C" int dgfx_segment_sum(const void* d_data, int data_dtype, const int64_
   }
   DGFX_CUDA_TRY(cudaGetLastError());
   return DGFX_OK;
+}
+
+namespace dgfx {
+namespace {
+size_t softmax_ws(int64_t n, int64_t nseg, bool sorted, int64_t vpr, int64_t epv) {
+  Arena a(nullptr, 0);
+  a.take<int64_t>(static_cast<size_t>(nseg + 1));  // rowptr
+  if (!sorted) {
+    a.take<uint64_t>(static_cast<size_t>(std::max<int64_t>(n, 1)));
+    a.take<uint32_t>(static_cast<size_t>(std::max<int64_t>(n, 1)));
+    a.take<uint64_t>(static_cast<size_t>(std::max<int64_t>(n, 1)));
+    a.take<uint32_t>(static_cast<size_t>(std::max<int64_t>(n, 1)));
+  }
+  a.take<int32_t>(static_cast<size_t>(nseg));                       // cnt
+  a.take<int32_t>(static_cast<size_t>(nseg));                       // split_cnt
+  a.take<int64_t>(static_cast<size_t>(nseg + 1));                   // task_off
+  a.take<int64_t>(static_cast<size_t>(nseg + 1));                   // split_off
+  a.take<int32_t>(static_cast<size_t>(max_tasks(nseg, n)));         // task_row
+  a.take<float>(static_cast<size_t>(max_split_tasks(n) * vpr * (2 + epv)));  // chunk states
+  return a.used + std::max(scan_workspace_bytes(nseg + 1), sorted ? size_t(0) : radix_sort_workspace_bytes(n)) +
+         2048;
+}
+
+template <class MT, class OT>
+int launch_softmax(const int64_t* rowptr, const uint32_t* perm, int64_t nseg, int64_t n, const float* logits,
+                   int heads, const void* msg, int64_t vpr, int head_dim, void* out, Arena& arena,
+                   cudaStream_t stream) {
+  constexpr int64_t EPV = 16 / sizeof(MT);
+  int32_t* cnt = arena.take<int32_t>(static_cast<size_t>(nseg));
+  int32_t* split_cnt = arena.take<int32_t>(static_cast<size_t>(nseg));
+  int64_t* task_off = arena.take<int64_t>(static_cast<size_t>(nseg + 1));
+  int64_t* split_off = arena.take<int64_t>(static_cast<size_t>(nseg + 1));
+  int32_t* task_row = arena.take<int32_t>(static_cast<size_t>(max_tasks(nseg, n)));
+  float* partial = arena.take<float>(static_cast<size_t>(max_split_tasks(n) * vpr * (2 + EPV)));
+  spmm_count_kernel<<<grid_for(nseg, 256), 256, 0, stream>>>(rowptr, nseg, cnt, split_cnt);
+  DGFX_CUDA_TRY(cudaGetLastError());
+  const size_t mark = arena.used;
+  DGFX_TRY(exclusive_scan<int32_t>(cnt, task_off, nseg, true, arena, stream));
+  arena.used = mark;
+  DGFX_TRY(exclusive_scan<int32_t>(split_cnt, split_off, nseg, true, arena, stream));
+  spmm_fill_kernel<<<grid_for(nseg, 256), 256, 0, stream>>>(task_off, nseg, task_row);
+  DGFX_CUDA_TRY(cudaGetLastError());
+  // Grid sized for the largest possible plan; the kernel reads the exact task
+  // count (task_off[nseg]) on the device.
+  const int64_t tasks = max_tasks(nseg, n);
+  const unsigned blocks = grid_for(tasks * 32, 256);
+  auto m = static_cast<const uint4*>(msg);
+  auto o = static_cast<OT*>(out);
+  const int vpl = static_cast<int>(ceil_div(vpr, int64_t(32)));
+#define DGFX_SOFTMAX_LAUNCH(V)                                                                                \
+  segment_softmax_kernel<MT, OT, V><<<blocks, 256, 0, stream>>>(rowptr, task_off, split_off, task_row,         \
+                                                                 task_off + nseg, perm, logits, heads, m, vpr,  \
+                                                                 head_dim, partial, o);                        \
+  DGFX_CUDA_TRY(cudaGetLastError());                                                                           \
+  segment_softmax_fixup_kernel<MT, OT, V><<<grid_for(nseg * 32, 256), 256, 0, stream>>>(task_off, split_off,   \
+                                                                                        nseg, vpr, partial, o);
+  if (vpl <= 1) {
+    DGFX_SOFTMAX_LAUNCH(1)
+  } else if (vpl == 2) {
+    DGFX_SOFTMAX_LAUNCH(2)
+  } else {
+    DGFX_SOFTMAX_LAUNCH(4)
+  }
+#undef DGFX_SOFTMAX_LAUNCH
+  DGFX_CUDA_TRY(cudaGetLastError());
+  return DGFX_OK;
+}
+}  // namespace
+}  // namespace dgfx
+
+extern "C" int dgfx_segment_softmax_workspace_size(int64_t num_items, int64_t num_segments, int32_t heads,
+                                                   int64_t head_dim, int msg_dtype, int32_t sorted, size_t* bytes) {
+  if (bytes == nullptr || num_items < 0 || num_segments < 0 || heads < 1 || head_dim < 1 || !check_dtype(msg_dtype)) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_segment_softmax_workspace_size: bad arguments");
+  }
+  const int64_t epv = msg_dtype == DGFX_F32 ? 4 : 8;
+  *bytes = softmax_ws(num_items, num_segments, sorted != 0, ceil_div(heads * head_dim, epv), epv);
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_segment_softmax(const float* d_logits, int32_t heads, const void* d_messages, int msg_dtype,
+                                    int64_t head_dim, const int64_t* d_ids, int64_t n, int64_t nseg, int32_t sorted,
+                                    void* d_out, int out_dtype, void* d_workspace, size_t workspace_bytes,
+                                    dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!check_dtype(msg_dtype) || !check_dtype(out_dtype)) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_segment_softmax: dtype");
+  }
+  const int64_t epv = msg_dtype == DGFX_F32 ? 4 : 8;
+  if (n < 0 || nseg < 0 || heads < 1 || head_dim < 1 || head_dim % epv != 0 ||
+      (n > 0 && (d_logits == nullptr || d_messages == nullptr || d_ids == nullptr)) ||
+      (nseg > 0 && d_out == nullptr)) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT,
+                "dgfx_segment_softmax: bad arguments (head_dim must be a multiple of 4 for fp32, 8 for bf16 messages)");
+  }
+  const int64_t vpr = heads * head_dim / epv;
+  if (vpr > 128 || n >= (int64_t(1) << 31)) {
+    return fail(DGFX_ERR_UNSUPPORTED, "dgfx_segment_softmax: heads * head_dim rows above 2 KB or 2^31 items");
+  }
+  if (nseg == 0) return DGFX_OK;
+  if (d_workspace == nullptr || workspace_bytes < softmax_ws(n, nseg, sorted != 0, vpr, epv)) {
+    return fail(DGFX_ERR_WORKSPACE, "dgfx_segment_softmax: workspace too small");
+  }
+  Arena arena(d_workspace, workspace_bytes);
+  int64_t* rowptr = arena.take<int64_t>(static_cast<size_t>(nseg + 1));
+  const uint32_t* perm = nullptr;
+  if (sorted || n == 0) {
+    sorted_bounds_kernel<<<grid_for(nseg + 1, 256), 256, 0, stream>>>(d_ids, n, nseg, rowptr);
+  } else {
+    uint64_t* k0 = arena.take<uint64_t>(static_cast<size_t>(n));
+    uint32_t* v0 = arena.take<uint32_t>(static_cast<size_t>(n));
+    uint64_t* k1 = arena.take<uint64_t>(static_cast<size_t>(n));
+    uint32_t* v1 = arena.take<uint32_t>(static_cast<size_t>(n));
+    softmax_sort_input_kernel<<<grid_for(n, 256), 256, 0, stream>>>(d_ids, n, nseg, k0, v0);
+    DGFX_CUDA_TRY(cudaGetLastError());
+    bool in1 = false;
+    DGFX_TRY(radix_sort_pairs(k0, v0, k1, v1, n, 0, std::max(1, bit_length(static_cast<uint64_t>(nseg))), &in1,
+                              arena, stream));
+    const uint64_t* ks = in1 ? k1 : k0;
+    perm = in1 ? v1 : v0;
+    sorted_bounds_kernel<<<grid_for(nseg + 1, 256), 256, 0, stream>>>(reinterpret_cast<const int64_t*>(ks), n, nseg,
+                                                                       rowptr);
+  }
+  DGFX_CUDA_TRY(cudaGetLastError());
+  const int hd = static_cast<int>(head_dim);
+  if (msg_dtype == DGFX_F32) {
+    return out_dtype == DGFX_F32
+               ? launch_softmax<float, float>(rowptr, perm, nseg, n, d_logits, heads, d_messages, vpr, hd, d_out,
+                                              arena, stream)
+               : launch_softmax<float, __nv_bfloat16>(rowptr, perm, nseg, n, d_logits, heads, d_messages, vpr, hd,
+                                                      d_out, arena, stream);
+  }
+  return out_dtype == DGFX_F32
+             ? launch_softmax<__nv_bfloat16, float>(rowptr, perm, nseg, n, d_logits, heads, d_messages, vpr, hd,
+                                                    d_out, arena, stream)
+             : launch_softmax<__nv_bfloat16, __nv_bfloat16>(rowptr, perm, nseg, n, d_logits, heads, d_messages, vpr,
+                                                            hd, d_out, arena, stream);
 }

@@ -246,6 +246,33 @@ int dgfx_segment_sum(const void* d_data, int data_dtype,
                      dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Segment softmax aggregation (graph attention). Replaces the relation
+ * attention of dgf/src/learning/jax/layers/hetero_graph_attention_network.py:
+ * 242-263 (segment_max, exp, segment_sum, divide, weighted segment_sum):
+ *   d_out[t, h, :] = sum_{e: id(e) = t} w[e, h] * msg[e, h, :]
+ *   w[e, h] = exp(l[e, h] - m[t, h]) / (sum_{e'} exp(l[e', h] - m[t, h]) + 1e-9)
+ *   m[t, h] = max_{e: id(e) = t} l[e, h]
+ * d_logits fp32 [n, heads]; d_messages [n, heads, head_dim] (msg_dtype;
+ * head_dim a multiple of 4 for fp32, 8 for bf16; heads * head_dim * element
+ * size <= 2 KB); d_ids int64 [n] (ids outside [0, nseg) are dropped;
+ * sorted != 0 promises ascending ids); d_out [nseg, heads, head_dim]
+ * (out_dtype), zero rows for empty segments. Segments are split into
+ * chunks of 256 items (one warp each, online softmax); chunk states merge in
+ * chunk order, so results are deterministic. Segments whose logits are all
+ * -inf give zero rows.
+ * ------------------------------------------------------------------------ */
+int dgfx_segment_softmax_workspace_size(int64_t num_items, int64_t num_segments,
+                                        int32_t heads, int64_t head_dim,
+                                        int msg_dtype, int32_t sorted,
+                                        size_t* bytes);
+int dgfx_segment_softmax(const float* d_logits, int32_t heads,
+                         const void* d_messages, int msg_dtype, int64_t head_dim,
+                         const int64_t* d_ids, int64_t n, int64_t nseg,
+                         int32_t sorted, void* d_out, int out_dtype,
+                         void* d_workspace, size_t workspace_bytes,
+                         dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
  * Dense layer after aggregation on the tensor cores (tcgen05, sm_100a).
  * Replaces the nn.Dense (+ activation) that follows the neighbour
  * aggregation (dgf/src/learning/jax/layers/hetero_gnn.py:302-312,

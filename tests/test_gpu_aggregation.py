@@ -6,6 +6,7 @@ sum_j |val_j * x_j| so that cancellation does not inflate the error."""
 
 import numpy as np
 import pytest
+import torch
 
 from oracle import oracle as O
 
@@ -110,3 +111,67 @@ def test_gather_rows(agg, cuda):
     assert torch.count_nonzero(out[4:]) == 0
     tb = torch.randn(50, 128, device="cuda").to(torch.bfloat16)
     assert torch.equal(agg.gather_rows(tb, torch.arange(49, -1, -1, device="cuda")), tb.flip(0))
+
+
+# ---------------------------------------------------------------------------
+# Segment softmax (graph attention), hetero_graph_attention_network.py:242-263
+# ---------------------------------------------------------------------------
+def _softmax_reference(logits, messages, ids, nseg):
+    """The reference's sequence in torch fp32: segment_max, exp, segment_sum,
+    divide (+1e-9), weighted segment_sum. Items outside [0, nseg) dropped."""
+    keep = (ids >= 0) & (ids < nseg)
+    l, m, t = logits[keep].double(), messages[keep].double(), ids[keep]
+    H = logits.shape[1]
+    mx = torch.full((nseg, H), -float("inf"), dtype=torch.float64, device=l.device)
+    mx = mx.scatter_reduce(0, t[:, None].expand(-1, H), l, reduce="amax")
+    ex = torch.exp(l - mx[t])
+    den = torch.zeros((nseg, H), dtype=torch.float64, device=l.device).index_add_(0, t, ex)
+    w = ex / (den[t] + 1e-9)
+    out = torch.zeros((nseg,) + tuple(messages.shape[1:]), dtype=torch.float64, device=l.device)
+    return out.index_add_(0, t, w[..., None] * m)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+@pytest.mark.parametrize("sorted_ids", [False, True])
+@pytest.mark.parametrize("H,D", [(1, 8), (4, 32), (8, 32), (2, 64)])
+def test_segment_softmax(cuda, dtype, sorted_ids, H, D):
+    from distributed_graph_flow_b200 import aggregation
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device="cuda").manual_seed(H * 100 + D)
+    E, nseg = 50_000, 3_001
+    dt = getattr(torch, dtype)
+    # Skewed segment sizes, some empty segments, a few ids out of range.
+    ids = (torch.rand(E, generator=g, device=dev) ** 3 * (nseg + 20)).long() - 10
+    if sorted_ids:
+        ids = torch.sort(ids).values
+    logits = torch.randn((E, H), generator=g, device=dev) * 4
+    msgs = torch.randn((E, H, D), generator=g, device=dev).to(dt)
+    got = aggregation.segment_softmax(logits, msgs, ids, nseg, indices_are_sorted=sorted_ids, out_dtype=torch.float32)
+    ref = _softmax_reference(logits, msgs.float(), ids, nseg)
+    tol = 1e-5 if dtype == "float32" else 1e-2
+    # Relative to the row scale: sum of |w * m| over the segment.
+    err = (got.double() - ref).abs()
+    scale = ref.abs().amax(dim=-1, keepdim=True).clamp(min=1e-3)
+    assert float((err / scale).max()) <= tol, float((err / scale).max())
+    # bf16 output rounds once more.
+    got16 = aggregation.segment_softmax(logits, msgs, ids, nseg, indices_are_sorted=sorted_ids)
+    assert got16.dtype == dt
+    assert float(((got16.double() - ref).abs() / scale).max()) <= (1e-5 if dtype == "float32" else 2e-2)
+
+
+def test_segment_softmax_deterministic_and_empty(cuda):
+    from distributed_graph_flow_b200 import aggregation
+
+    dev = torch.device("cuda", 0)
+    ids = torch.tensor([5, 2, 5, 2, 5], device=dev)
+    logits = torch.tensor([[1.0], [2.0], [3.0], [-1.0], [0.5]], device=dev)
+    msgs = torch.arange(5 * 8, dtype=torch.float32, device=dev).view(5, 1, 8)
+    a = aggregation.segment_softmax(logits, msgs, ids, 7)
+    b = aggregation.segment_softmax(logits, msgs, ids, 7)
+    assert torch.equal(a, b)
+    assert torch.count_nonzero(a[[0, 1, 3, 4, 6]]) == 0
+    ref = _softmax_reference(logits, msgs, ids, 7)
+    assert torch.allclose(a.double(), ref, rtol=1e-6, atol=1e-6)
+    empty = aggregation.segment_softmax(logits[:0], msgs[:0], ids[:0], 3)
+    assert torch.count_nonzero(empty) == 0
