@@ -118,6 +118,10 @@ SIGNATURES = {
     "dgfx_exchange_barrier": (_int, [_vp, _i32, _i32, ctypes.c_uint32, _u64, _vp]),
     "dgfx_exchange_check": (_int, [_vp, _i32, _vp]),
     "dgfx_edge_timestamps": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp]),
+    "dgfx_subgraph_union_workspace_size": (_int, [_i64, _i64, ctypes.POINTER(_sz)]),
+    "dgfx_subgraph_union": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _i64, _i64, _vp, _vp,
+                                   _vp, _vp, _vp, _vp, _sz, _vp]),
+    "dgfx_merge_edgeset": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
     "dgfx_synth_graph_workspace_size": (_int, [_i64, ctypes.POINTER(_sz)]),
     "dgfx_synth_graph": (_int, [_i64, _i64, ctypes.c_double, _i64, _u64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "dgfx_synth_bipartite": (_int, [_i64, _i64, _i64, ctypes.c_double, _i64, _u64, _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -337,11 +337,77 @@ class Sampler:
         batch = self.sample_merged(seeds, ts, masks)
         return export_graphs(batch)
 
-    def SubGraph(self, seed_node_idx):
-        raise NotImplementedError("SubGraph extraction is not implemented on the B200 sampler yet")
+    def _edgeset_endpoints(self):
+        """(source, target) node set index of every edge set the plan walks
+        (from the plan's edges: a reversed plan edge walks target -> source)."""
+        src = [0] * len(self._edgeset_names)
+        dst = [0] * len(self._edgeset_names)
 
-    def MultiSubGraphs(self, seed_node_idx):
-        raise NotImplementedError("MultiSubGraphs extraction is not implemented on the B200 sampler yet")
+        def walk(pn):
+            for pe in pn.children:
+                here, there = self._nodeset_index[pn.nodeset], self._nodeset_index[pe.node.nodeset]
+                e = self._edgeset_index[pe.edgeset]
+                src[e], dst[e] = (there, here) if pe.reversed else (here, there)
+                walk(pe.node)
+
+        walk(self._plan.root)
+        return src, dst
+
+    def SubGraph(self, seed_node_idx) -> img.InMemoryGraph:
+        """One graph around all seeds (Sampler::SubGraph, ext.cc:959-972, with
+        SubGraphExtractor :600-772): the seeds are the first nodes of the root
+        node set in seed order, every other node is numbered in order of its
+        first (seed, depth-first) discovery, edges deduplicated and sorted.
+        Computed as the union of the seeds' samples on the device
+        (dgfx_subgraph_union); exact in the deterministic modes (debug
+        sampling, or hop_width >= degree)."""
+        torch = _torch()
+        lib = _native.lib()
+        seeds = self._to_device(np.asarray(seed_node_idx, dtype=np.int64).reshape(-1), "seeds")
+        batch = self.sample_merged(seeds)
+        B = batch.B
+        NS, ES = len(self._nodeset_names), len(self._edgeset_names)
+        n = int(batch.node_offsets[-1].item())
+        m = int(batch.edge_offsets[-1].item())
+        dev = self._device
+        out_nodes = torch.empty(max(n, 1), dtype=torch.int64, device=dev)
+        out_src = torch.empty(max(m, 1), dtype=torch.int64, device=dev)
+        out_dst = torch.empty(max(m, 1), dtype=torch.int64, device=dev)
+        node_counts = (ctypes.c_int64 * NS)()
+        edge_counts = (ctypes.c_int64 * max(ES, 1))()
+        src_ns, dst_ns = self._edgeset_endpoints()
+        need = ctypes.c_size_t()
+        _native.check(lib.dgfx_subgraph_union_workspace_size(n, m, ctypes.byref(need)))
+        ws = torch.empty(max(1, need.value), dtype=torch.uint8, device=dev)
+        root = self._nodeset_index[self._root_nodeset]
+        _native.check(lib.dgfx_subgraph_union(
+            _native.ptr(batch.node_ids), _native.ptr(batch.node_offsets), _native.ptr(batch.edge_src),
+            _native.ptr(batch.edge_dst), _native.ptr(batch.edge_offsets), B, NS, ES, root,
+            (ctypes.c_int32 * max(ES, 1))(*src_ns), (ctypes.c_int32 * max(ES, 1))(*dst_ns), n, m,
+            _native.ptr(out_nodes), node_counts, _native.ptr(out_src), _native.ptr(out_dst), edge_counts,
+            _native.ptr(ws), need.value, _native.stream_handle()))
+        nodes_h = out_nodes.cpu().numpy()
+        src_h, dst_h = out_src.cpu().numpy(), out_dst.cpu().numpy()
+        node_sets, edge_sets = {}, {}
+        a = 0
+        for s, name in enumerate(self._nodeset_names):
+            c = int(node_counts[s])
+            node_sets[name] = img.InMemoryNodeSet(num_nodes=c, features={"#idx": nodes_h[a:a + c].copy()})
+            a += c
+        a = 0
+        for e, name in enumerate(self._edgeset_names):
+            c = int(edge_counts[e]) if ES else 0
+            edge_sets[name] = img.InMemoryEdgeSet(adjacency=np.stack([src_h[a:a + c], dst_h[a:a + c]]).astype(np.int64))
+            a += c
+        return img.InMemoryGraph(node_sets=node_sets, edge_sets=edge_sets)
+
+    def MultiSubGraphs(self, seed_node_idx) -> list:
+        """One independent subgraph per seed (Sampler::MultiSubGraphs,
+        ext.cc:974-1017): the seed's sample, which equals its extracted
+        subgraph in the deterministic modes (the reference documents
+        multisubgraph as sample with an infinite width)."""
+        seeds = self._to_device(np.asarray(seed_node_idx, dtype=np.int64).reshape(-1), "seeds")
+        return export_graphs(self.sample_merged(seeds))
 
     def RandomWalkNegativeSampling(self, seed_node_idxs, target_edgeset_idx, num_walks, num_negatives_per_seed):
         raise NotImplementedError("RandomWalkNegativeSampling is not implemented on the B200 sampler yet")

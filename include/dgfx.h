@@ -415,6 +415,54 @@ int dgfx_edge_timestamps(const int64_t* d_src_ts, int64_t num_src,
                          dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Subgraph around a set of seeds. Replaces the numbering and edge set of
+ * SubGraphExtractor (dgf/src/sampling/in_memory_sampler_ext.cc:600-772) as
+ * the union of a merged batch of per-seed samples (dgfx_sample_out layout,
+ * one sample per seed): the seeds are the first `batch` nodes of
+ * root_nodeset (ids in seed order; a repeated seed node maps to its last
+ * seed id), every other node is numbered in its node set in order of its
+ * first (seed index, local id) occurrence, and the edges, mapped to these
+ * ids, are deduplicated and sorted by (source, target) per edge set.
+ * edge_src_nodeset / edge_dst_nodeset (host, num_edgesets) give each edge
+ * set's endpoint node sets. Outputs: d_out_node_ids (total_nodes capacity)
+ * node-set major with out_node_counts (host, num_nodesets);
+ * d_out_src / d_out_dst (total_edges capacity) edge-set major with
+ * out_edge_counts (host). Synchronises the stream. total_nodes < 2^28.
+ * ------------------------------------------------------------------------ */
+int dgfx_subgraph_union_workspace_size(int64_t total_nodes, int64_t total_edges,
+                                       size_t* bytes);
+int dgfx_subgraph_union(const int64_t* d_node_ids, const int64_t* d_node_offsets,
+                        const int64_t* d_edge_src, const int64_t* d_edge_dst,
+                        const int64_t* d_edge_offsets, int64_t batch,
+                        int32_t num_nodesets, int32_t num_edgesets,
+                        int32_t root_nodeset, const int32_t* edge_src_nodeset,
+                        const int32_t* edge_dst_nodeset, int64_t total_nodes,
+                        int64_t total_edges, int64_t* d_out_node_ids,
+                        int64_t* out_node_counts, int64_t* d_out_src,
+                        int64_t* d_out_dst, int64_t* out_edge_counts,
+                        void* d_workspace, size_t workspace_bytes,
+                        dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Merged-batch adjacency with padding. Replaces the adjacency part of
+ * merge_graphs (dgf/src/transform/merge.py:165-197) for a merged batch
+ * (dgfx_sample_out layout: offsets set-major, then sample, trailing total):
+ * d_out_src / d_out_dst[k] for the k-th edge of edge set `edgeset` over all
+ * samples in order = its local ids plus the sample's first node in the
+ * source / target node set (d_node_offsets[ns * batch + i] -
+ * d_node_offsets[ns * batch]); entries from the real edge count up to
+ * num_out are padding edges (sentinel_src, sentinel_dst); real edges past
+ * num_out are dropped (the caller checks the counts first).
+ * ------------------------------------------------------------------------ */
+int dgfx_merge_edgeset(const int64_t* d_node_offsets,
+                       const int64_t* d_edge_offsets, const int64_t* d_edge_src,
+                       const int64_t* d_edge_dst, int64_t batch, int32_t edgeset,
+                       int32_t src_nodeset, int32_t dst_nodeset,
+                       int64_t num_out, int64_t sentinel_src,
+                       int64_t sentinel_dst, int64_t* d_out_src,
+                       int64_t* d_out_dst, dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
  * Seeded synthetic inputs (stand-ins for the benchmark datasets, the role of
  * the reference's dgf/src/util/gen_test_graph.py generators at scale).
  * dgfx_synth_graph: power-law out-degrees (P(d) ~ d^-alpha, capped at

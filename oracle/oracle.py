@@ -17,7 +17,9 @@ And a float64 numpy restatement of the aggregation math:
     homo_gnn_sparse_deferred.py:138-161) as the same segment sum with
     row = target, col = source.
 And a numpy restatement of the edge-time propagation,
-dgf/src/transform/temporal.py:95-103.
+dgf/src/transform/temporal.py:95-103, and a pure-Python restatement of
+SubGraphExtractor (in_memory_sampler_ext.cc:600-772) for small graphs in the
+deterministic modes.
 """
 
 from __future__ import annotations
@@ -367,3 +369,72 @@ def edge_timestamps(src_ts: Optional[np.ndarray], tgt_ts: Optional[np.ndarray], 
     if src_ts is not None:
         return src_ts[src]
     return tgt_ts[tgt]
+
+
+# ---------------------------------------------------------------------------
+# SubGraphExtractor (in_memory_sampler_ext.cc:600-772), deterministic modes:
+# every plan edge takes the first min(hop_width, degree) neighbours in index
+# order (SampleFirst, :250-279; with hop_width >= degree SampleRandomUniform
+# returns the whole row in the same order, in_memory_sampler.cc:130-132).
+# ---------------------------------------------------------------------------
+def subgraph(graph, plan, seeds, nodeset_names: List[str], edgeset_names: List[str], schema) -> tuple:
+    """Returns ({nodeset: node idxs}, {edgeset: [2, E] adjacency})."""
+    adj = {}
+    for name in edgeset_names:
+        es = schema.edge_sets[name]
+        a = np.asarray(graph.edge_sets[name].adjacency, dtype=np.int64).reshape(2, -1)
+        for rev in (False, True):
+            src, dst = (a[1], a[0]) if rev else (a[0], a[1])
+            order = np.lexsort((dst, src))  # CreateFromEdgeList: sorted by (source, target)
+            rows = {}
+            for s_, d_ in zip(src[order].tolist(), dst[order].tolist()):
+                rows.setdefault(s_, []).append(d_)
+            adj[(name, rev)] = rows
+    # Plan nodes numbered depth-first (the step index of a plan node).
+    steps = {}
+
+    def number(pn):
+        steps[id(pn)] = len(steps)
+        for c in pn.children:
+            number(c.node)
+
+    number(plan.root)
+    node_idxs = {n: [] for n in nodeset_names}
+    visited = {n: {} for n in nodeset_names}       # node -> sample idx
+    visited_step = {n: set() for n in nodeset_names}
+    edges = {e: set() for e in edgeset_names}
+
+    def grow(pn, source, source_sampled):
+        for pe in pn.children:
+            targets = adj[(pe.edgeset, bool(pe.reversed))].get(source, [])[: pe.hop_width]
+            tns = pe.node.nodeset
+            step = steps[id(pe.node)]
+            for t in targets:
+                cont = True
+                if t in visited[tns]:
+                    eff = visited[tns][t]
+                    if (t, step) in visited_step[tns]:
+                        cont = False
+                    else:
+                        visited_step[tns].add((t, step))
+                else:
+                    eff = len(node_idxs[tns])
+                    visited[tns][t] = eff
+                    node_idxs[tns].append(t)
+                    visited_step[tns].add((t, step))
+                edges[pe.edgeset].add((eff, source_sampled) if pe.reversed else (source_sampled, eff))
+                if cont:
+                    grow(pe.node, t, eff)
+
+    root = plan.root.nodeset
+    for sd in seeds:
+        visited[root][sd] = len(node_idxs[root])
+        node_idxs[root].append(sd)
+        visited_step[root].add((sd, steps[id(plan.root)]))
+    for sd in seeds:
+        grow(plan.root, sd, visited[root][sd])
+    out_edges = {}
+    for e in edgeset_names:
+        pairs = sorted(edges[e])
+        out_edges[e] = np.array([[p[0] for p in pairs], [p[1] for p in pairs]], dtype=np.int64).reshape(2, -1)
+    return {n: np.array(v, dtype=np.int64) for n, v in node_idxs.items()}, out_edges

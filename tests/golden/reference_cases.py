@@ -190,3 +190,65 @@ EDGE_TS_CASES = [
     ("custom_names :145-199", ("time", [10, 20]), ("ts", [5, 25]), [[0, 1], [1, 0]], "edge_ts", [25, 20]),
     ("fail_no_timestamps :121-143", None, None, [[0, 1], [1, 0]], "timestamps", "Neither source nodeset"),
 ]
+
+# ---------------------------------------------------------------------------
+# merge_graphs: dgf/src/transform/merge_test.py:30-224 on two copies of
+# gen_test_graph.generate_in_memory_graph(False, False) (:1259-1337) with
+# generate_schema(False, False, variable_length=False) (:98-190).
+# ---------------------------------------------------------------------------
+MERGE_GRAPH = {
+    "nodes": {"n1": 2, "n2": 2},
+    "features": {
+        "n1": {"f2": np.array([[0.0, 1.0], [2.0, 3.0]], np.float32), "f1": np.array([[b"blue"], [b"red"]])},
+        "n2": {"f3": np.array([4, 5], np.int64), "f4": np.array([10, 11], np.int64)},
+    },
+    "edges": {"e1": ("n1", "n1", [[0, 0], [0, 1]]), "e2": ("n1", "n2", [[0, 0], [0, 1]])},
+}
+MERGE_PADDING = {"nodes": {"n1": 6, "n2": 7}, "edges": {"e1": 5, "e2": 6}}
+MERGE_EXPECTED_PADDED = {
+    "offsets": {"n1": [0, 2, 4], "n2": [0, 2, 4]},
+    "num_nodes": {"n1": 6, "n2": 7},
+    "features": {
+        "n1": {"f1": [[b"blue"], [b"red"], [b"blue"], [b"red"], [b""], [b""]],
+               "f2": [[0.0, 1.0], [2.0, 3.0], [0.0, 1.0], [2.0, 3.0], [0.0, 0.0], [0.0, 0.0]]},
+        "n2": {"f3": [4, 5, 4, 5, 0, 0, 0], "f4": [10, 11, 10, 11, 0, 0, 0]},
+    },
+    "adjacency": {"e1": [[0, 0, 2, 2, 5], [0, 1, 2, 3, 5]], "e2": [[0, 0, 2, 2, 5, 5], [0, 1, 2, 3, 6, 6]]},
+}
+MERGE_EXPECTED_UNPADDED = {
+    "offsets": {"n1": [0, 2, 4], "n2": [0, 2, 4]},
+    "num_nodes": {"n1": 4, "n2": 4},
+    "adjacency": {"e1": [[0, 0, 2, 2], [0, 1, 2, 3]], "e2": [[0, 0, 2, 2], [0, 1, 2, 3]]},
+}
+# test_batch_padding_too_small (:156-180): n1 padded to 4 (no room for the sentinel).
+MERGE_TOO_SMALL_MESSAGE = r"Required at least 5 nodes \(including the sentinel node\), but the padder only defines 4."
+
+# ---------------------------------------------------------------------------
+# SubGraph / MultiSubGraphs on the toy graph: in_memory_sampler_test.py:
+# 614-830 (SimpleSamplingConfig(seed_nodeset, num_hops=depth, hop_width=100),
+# reverse=True by default). Each case: (name, seed nodeset, depth, seeds,
+# ({nodeset: #idx}, {edgeset: adjacency})).
+# ---------------------------------------------------------------------------
+SUBGRAPH_CASES = [
+    ("depth0 n1 [0,1] :616-642", "n1", 0, [0, 1],
+     ({"n1": [0, 1], "n2": []}, {"e11": [[], []], "e12": [[], []], "e22": [[], []]})),
+    ("depth1 n1 [0,1] :643-669", "n1", 1, [0, 1],
+     ({"n1": [0, 1], "n2": [0, 1, 2]}, {"e11": [[1], [0]], "e12": [[0, 0, 0], [0, 1, 2]], "e22": [[], []]})),
+    ("depth2 n1 [0,1] :670-702", "n1", 2, [0, 1],
+     ({"n1": [0, 1], "n2": [0, 2, 1]}, {"e11": [[1], [0]], "e12": [[0, 0, 0], [0, 1, 2]], "e22": [[0], [1]]})),
+    ("depth2 n2 [2,0] :703-735", "n2", 2, [2, 0],
+     ({"n1": [0, 1], "n2": [2, 0, 1]}, {"e11": [[1], [0]], "e12": [[0, 0, 0], [0, 1, 2]], "e22": [[1], [0]]})),
+]
+# multisubgraph([0, 1]) with num_hops=1, hop_width=100 (:764-830).
+MULTISUBGRAPH_CASE = ("n1", 1, [0, 1], [
+    ({"n1": [0, 1], "n2": [0, 1, 2]}, {"e11": [[1], [0]], "e12": [[0, 0, 0], [0, 1, 2]], "e22": [[], []]}),
+    ({"n1": [1, 0], "n2": []}, {"e11": [[0], [1]], "e12": [[], []], "e22": [[], []]}),
+])
+# test_subgraph_line (:883-978): one n1 node with a self loop, one n2 node,
+# plan n1 -e11-> n1 -e11-> n1 -e12-> n2 (hop_width 5), seed [0].
+SUBGRAPH_LINE = ({"n1": 1, "n2": 1}, {"e11": ("n1", "n1", [[0], [0]]), "e12": ("n1", "n2", [[0], [0]])},
+                 ({"n1": [0], "n2": [0]}, {"e11": [[0], [0]], "e12": [[0], [0]]}))
+# test_ego_sampling_matches_subgraph (:832-881): 8 nodes, 18 directed edges;
+# 2 hops, hop_width 20: sample(0) == subgraph([0]).
+EGO_EDGES = [[0, 0, 0, 1, 1, 1, 2, 2, 3, 4, 4, 4, 4, 5, 6, 6, 6, 7],
+             [1, 4, 6, 0, 2, 3, 1, 4, 1, 0, 2, 5, 6, 4, 0, 4, 7, 6]]
