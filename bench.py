@@ -800,6 +800,64 @@ def bench_gat(dev, steps, scale=1.0):
     return res
 
 
+def bench_rw_negatives(dev, steps, scale=1.0):
+    """Random-walk negative sampling for link prediction on the 169,343-node
+    Zipf(2.1) graph (no timestamps: walks ignore them): plan fanout [10, 5]
+    (two hops), 5 negatives per seed, 10 walks per negative (the link
+    generator's default: 50 walks), 16,384 seeds per call."""
+    import dataclasses
+
+    import torch
+
+    from distributed_graph_flow_b200 import _native, synth
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+    from distributed_graph_flow_b200.sampling import config as cfg
+
+    spec = dataclasses.replace(_scaled(synth.TEMPORAL_169K, scale), ts_range=None)
+    index, _, _ = synth.build_graph(spec, dev)
+    plan = cfg.explicit_plan("v", "e", [10, 5])
+    cc = ext.create_device_sampler(plan, ["v"], [spec.num_nodes], ["e"], [index], [None], _native.MODE_RANDOM, seed=5)
+    B, K, W = 16384, 5, 50
+    nb = 4 + steps
+    seeds = synth.uniform_int(nb * B, 0, spec.num_nodes, 23, 9, dev).view(nb, B)
+
+    def step(i):
+        cc.random_walk_negatives(seeds[i], 0, W, K, call_index=i, check=False)
+
+    for i in range(3):
+        step(i)
+    cc.check_random_walk_negatives()
+    ms = timed(lambda i: step(4 + i), steps, torch.cuda.synchronize, "rw_negatives")
+    cc.check_random_walk_negatives()
+    steps_per_walk = 2
+    res = {"workload": "random-walk negatives: 169,343 nodes / 1,166,243 edges Zipf(2.1), plan fanout [10,5], "
+                       "5 negatives x 10 walks per seed, 16,384 seeds per call",
+           "value": round(B / (ms / 1e3), 1), "unit": "seeds/s", "ms_per_call": round(ms, 4),
+           "walk_steps_per_s": round(B * W * steps_per_walk / (ms / 1e3), 1), "bound": "latency (dependent "
+           "random row loads per walk step)"}
+    try:
+        from oracle import oracle as O
+
+        s, kind = cpu_sampler_from_index(index, spec.num_nodes, plan)
+        th = host_cores()
+        seeds_h = seeds.cpu().numpy()
+        done, t_tot, i = 0, 0.0, 0
+        while t_tot < 10.0 and i < nb:
+            t0 = time.perf_counter()
+            s.random_walk_negatives(seeds_h[i], 0, W, K, kind=0, threads=th)
+            t_tot += time.perf_counter() - t0
+            done += B
+            i += 1
+        res["cpu_baseline"] = {"value": round(done / t_tot, 1), "unit": "seeds/s", "cores": th, "kind": "port",
+                               "sample": f"{done} seeds; restated RandomWalkNegativeSamplerHelper (std::mt19937_64)"
+                                         + (" over the reference's compiled AdjacencyIndex" if kind == "reference"
+                                            else "")}
+        res["speedup_vs_cpu"] = round(res["value"] / res["cpu_baseline"]["value"], 1)
+    except Exception as exc:  # noqa: BLE001
+        res["cpu_baseline"] = {"unavailable": str(exc)}
+    return res
+
+
 def measured_tflops():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -953,7 +1011,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the SpMM / temporal sub-benchmarks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--scale", type=float, default=1.0, help="shrink the workload (profiling / debugging only)")
-    ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal", "hetero", "sage", "gat"],
+    ap.add_argument("--only", default=None, choices=["large", "spmm", "temporal", "hetero", "sage", "gat", "negatives"],
                     help="run one workload and skip the rest (profiling)")
     ap.add_argument("--halo", default="exchange", choices=["exchange", "p2p", "nccl"],
                     help="feature halo: bulk peer exchange (default), direct peer loads, or NCCL all-to-all")
@@ -986,10 +1044,10 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
 
-    if args.only in ("spmm", "temporal", "hetero", "sage", "gat"):
+    if args.only in ("spmm", "temporal", "hetero", "sage", "gat", "negatives"):
         # Single sub-benchmark (used for focused profiler captures).
         fn = {"spmm": bench_spmm, "temporal": bench_temporal, "hetero": bench_hetero, "sage": bench_sage,
-              "gat": bench_gat}[args.only]
+              "gat": bench_gat, "negatives": bench_rw_negatives}[args.only]
         print(json.dumps(fn(dev, args.steps, args.scale)), flush=True)
         return
 
@@ -1026,6 +1084,8 @@ def main():
             res["sage_mean_2m"] = bench_sage(dev, args.steps)
             torch.cuda.empty_cache()
             res["gat_attention_2m"] = bench_gat(dev, args.steps)
+            torch.cuda.empty_cache()
+            res["rw_negatives_169k"] = bench_rw_negatives(dev, args.steps)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -50,6 +50,7 @@
 
 #include "common.cuh"
 #include "primitives.cuh"
+#include "walk_plan.cuh"
 
 namespace dgfx {
 namespace {
@@ -755,7 +756,10 @@ struct dgfx_sampler {
   int64_t last_B = 0;
   const int64_t* last_seeds = nullptr;
   std::vector<EdgeDev> h_edges;
+  WalkPlan walk;  // for random-walk negative sampling
 };
+
+const dgfx::WalkPlan* dgfx_sampler_walk_plan(const dgfx_sampler* s) { return s == nullptr ? nullptr : &s->walk; }
 
 namespace {
 
@@ -988,6 +992,47 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
   const unsigned long long init[7] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
   DGFX_CUDA_TRY(cudaMemcpy(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice));
 
+  // The plan as random walks see it (plan nodes, plan edges with their CSR,
+  // forward indices and endpoints per edge set).
+  {
+    WalkPlan& w = s->walk;
+    w.num_nodesets = num_nodesets;
+    w.num_edgesets = num_edgesets;
+    w.seed = seed;
+    w.node_nodeset.assign(node_nodeset, node_nodeset + num_plan_nodes);
+    w.node_first_edge.assign(node_first_edge, node_first_edge + num_plan_nodes);
+    w.node_num_edges.assign(node_num_edges, node_num_edges + num_plan_nodes);
+    w.edge_edgeset.assign(edge_edgeset, edge_edgeset + num_plan_edges);
+    w.edge_reversed.assign(edge_reversed, edge_reversed + num_plan_edges);
+    w.edge_child.assign(edge_child, edge_child + num_plan_edges);
+    w.num_nodes.assign(num_nodes, num_nodes + num_nodesets);
+    w.forward.assign(forward, forward + num_edgesets);
+    w.es_src.assign(num_edgesets, -1);
+    w.es_dst.assign(num_edgesets, -1);
+    std::vector<WalkNode> hn(num_plan_nodes);
+    std::vector<WalkEdge> he(std::max(1, num_plan_edges));
+    for (int i = 0; i < num_plan_nodes; ++i) {
+      hn[i] = WalkNode{node_nodeset[i], node_first_edge[i], node_num_edges[i], 0};
+      for (int c = 0; c < node_num_edges[i]; ++c) {
+        const int j = node_first_edge[i] + c;
+        const int here = node_nodeset[i], there = node_nodeset[edge_child[j]];
+        w.es_src[edge_edgeset[j]] = edge_reversed[j] ? there : here;
+        w.es_dst[edge_edgeset[j]] = edge_reversed[j] ? here : there;
+      }
+    }
+    for (int j = 0; j < num_plan_edges; ++j) {
+      const dgfx_csr_view& v = edge_reversed[j] ? backward[edge_edgeset[j]] : forward[edge_edgeset[j]];
+      he[j] = WalkEdge{v.rowptr, v.col, edge_child[j], node_nodeset[edge_child[j]]};
+    }
+    const size_t b_nodes = align_up(sizeof(WalkNode) * hn.size(), 256);
+    char* dw = nullptr;
+    DGFX_CUDA_TRY(cudaMalloc(&dw, b_nodes + sizeof(WalkEdge) * he.size()));
+    w.d_nodes = reinterpret_cast<WalkNode*>(dw);
+    w.d_edges = reinterpret_cast<WalkEdge*>(dw + b_nodes);
+    DGFX_CUDA_TRY(cudaMemcpy(w.d_nodes, hn.data(), sizeof(WalkNode) * hn.size(), cudaMemcpyHostToDevice));
+    DGFX_CUDA_TRY(cudaMemcpy(w.d_edges, he.data(), sizeof(WalkEdge) * he.size(), cudaMemcpyHostToDevice));
+  }
+
   // Threads per CTA: about one per eight tree positions, 32..256.
   s->threads = std::min(256, std::max(32, s->N2 / 8));
   s->smem_bytes = counter_bytes(s->threads) + (s->use_smem ? work_bytes(s->T, s->H) : 0);
@@ -1002,6 +1047,7 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
 extern "C" void dgfx_sampler_destroy(dgfx_sampler* s) {
   if (s == nullptr) return;
   if (s->d_tables != nullptr) cudaFree(s->d_tables);
+  if (s->walk.d_nodes != nullptr) cudaFree(s->walk.d_nodes);
   delete s;
 }
 

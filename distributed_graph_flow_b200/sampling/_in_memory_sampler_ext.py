@@ -409,8 +409,50 @@ class Sampler:
         seeds = self._to_device(np.asarray(seed_node_idx, dtype=np.int64).reshape(-1), "seeds")
         return export_graphs(self.sample_merged(seeds))
 
+    def random_walk_negatives(self, seeds, target_edgeset_idx: int, num_walks: int, num_negatives_per_seed: int,
+                              stream=None, call_index: Optional[int] = None, check: bool = True):
+        """Random-walk negatives for device int64 seeds: an int64 CUDA tensor
+        [num_seeds, num_negatives_per_seed] (dgfx_random_walk_negatives).
+        With check=False the call stays asynchronous; call
+        ``check_random_walk_negatives()`` before trusting the rows."""
+        torch = _torch()
+        lib = _native.lib()
+        e = int(target_edgeset_idx)
+        if e < 0 or e >= len(self._edgeset_names):
+            raise ValueError("Invalid target_edgeset_idx")
+        if self._fwd[e] is None:
+            raise ValueError(f"Edgeset '{self._edgeset_names[e]}' does not have a forward index. "
+                             "Ensure it is traversed forward in the SamplingPlan.")
+        B, W, K = int(seeds.numel()), int(num_walks), int(num_negatives_per_seed)
+        need = ctypes.c_size_t()
+        _native.check(lib.dgfx_random_walk_negatives_workspace_size(self._handle, B, e, W, K, ctypes.byref(need)))
+        ws = self._buffers.get("rw_ws")
+        if ws is None or ws.numel() < need.value:
+            ws = torch.empty(max(256, need.value), dtype=torch.uint8, device=self._device)
+            self._buffers["rw_ws"] = ws
+        out = torch.empty((B, K), dtype=torch.int64, device=self._device)
+        if call_index is None:
+            call_index = self._calls
+            self._calls += 1
+        _native.check(lib.dgfx_random_walk_negatives(self._handle, _native.ptr(seeds), B, e, W, K,
+                                                     int(call_index) & ((1 << 64) - 1), _native.ptr(out),
+                                                     _native.ptr(ws), ws.numel(), _native.stream_handle(stream)))
+        if check:
+            self.check_random_walk_negatives(stream)
+        return out
+
+    def check_random_walk_negatives(self, stream=None) -> None:
+        ws = self._buffers.get("rw_ws")
+        if ws is not None:
+            _native.check(_native.lib().dgfx_random_walk_negatives_check(_native.ptr(ws), _native.stream_handle(stream)))
+
     def RandomWalkNegativeSampling(self, seed_node_idxs, target_edgeset_idx, num_walks, num_negatives_per_seed):
-        raise NotImplementedError("RandomWalkNegativeSampling is not implemented on the B200 sampler yet")
+        """Sampler::RandomWalkNegativeSampling (ext.cc:875-948): int64 numpy
+        [num_seeds, num_negatives_per_seed] of negative target nodes per seed
+        (visit-ranked random-walk nodes the seed does not link to, then
+        uniform fallback draws)."""
+        seeds = self._to_device(np.asarray(seed_node_idxs, dtype=np.int64).reshape(-1), "seeds")
+        return self.random_walk_negatives(seeds, target_edgeset_idx, num_walks, num_negatives_per_seed).cpu().numpy()
 
 
 class CapturedSampleStep:

@@ -415,6 +415,38 @@ int dgfx_edge_timestamps(const int64_t* d_src_ts, int64_t num_src,
                          dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Random-walk negative sampling. Replaces Sampler::RandomWalkNegativeSampling
+ * with RandomWalkNegativeSamplerHelper (dgf/src/sampling/
+ * in_memory_sampler_ext.cc:774-948): per seed, num_walks walks down the
+ * sampler's plan (uniform plan edge, uniform neighbour, stop at a node
+ * without neighbours); visits of nodes of the target edge set's target node
+ * set are counted (not the seed itself on a homogeneous edge set); nodes the
+ * seed links to in the target edge set's forward index are dropped; the
+ * num_negatives_per_seed most visited (ties: smaller id first) fill the row
+ * of d_out (int64 [num_seeds, num_negatives_per_seed]), the rest are uniform
+ * draws over the target node set (never the seed of a homogeneous edge set).
+ * Draws come from Philox4x32-10 keyed by the sampler seed; call_index selects
+ * the stream. Errors: "Invalid target_edgeset_idx"; no forward index for the
+ * edge set; a target node set with no node to draw for the fallback slots.
+ * Asynchronous: seeds outside the root node set, a full visit table and
+ * exhausted fallback draws are latched in the workspace and reported by
+ * dgfx_random_walk_negatives_check (which synchronises `stream`).
+ * ------------------------------------------------------------------------ */
+int dgfx_random_walk_negatives_workspace_size(const dgfx_sampler* sampler,
+                                              int64_t num_seeds,
+                                              int32_t target_edgeset,
+                                              int32_t num_walks,
+                                              int32_t num_negatives_per_seed,
+                                              size_t* bytes);
+int dgfx_random_walk_negatives(dgfx_sampler* sampler, const int64_t* d_seeds,
+                               int64_t num_seeds, int32_t target_edgeset,
+                               int32_t num_walks, int32_t num_negatives_per_seed,
+                               uint64_t call_index, int64_t* d_out,
+                               void* d_workspace, size_t workspace_bytes,
+                               dgfx_stream stream);
+int dgfx_random_walk_negatives_check(const void* d_workspace, dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
  * Subgraph around a set of seeds. Replaces the numbering and edge set of
  * SubGraphExtractor (dgf/src/sampling/in_memory_sampler_ext.cc:600-772) as
  * the union of a merged batch of per-seed samples (dgfx_sample_out layout,

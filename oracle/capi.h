@@ -184,6 +184,24 @@ void* oracle_sampler_create_csr(int n_nodesets, const std::int64_t* num_nodes, i
   return h.release();
 }
 
+// Random-walk negatives for n seeds into out[n * k] (see
+// dgf_oracle::RandomWalkNegatives; kind 0 = the reference's generator, 1 =
+// the device's Philox stream for sampler_seed / call_index). Returns 0 or the
+// status code (message in oracle_last_error()).
+int oracle_random_walk_negatives(void* hv, const std::int64_t* seeds, std::int64_t n, int target_edgeset,
+                                 int num_walks, int k, int kind, std::uint64_t sampler_seed,
+                                 std::uint64_t call_index, int threads, std::int64_t* out) {
+  auto* h = static_cast<OracleHandle*>(hv);
+  dgf_oracle::Status st = dgf_oracle::RandomWalkNegatives(h->sampler, seeds, static_cast<std::size_t>(n),
+                                                          target_edgeset, num_walks, k, kind, sampler_seed,
+                                                          call_index, threads, out);
+  if (!st.ok()) {
+    g_oracle_error = st.msg;
+    return st.code;
+  }
+  return 0;
+}
+
 void oracle_sampler_free(void* h) { delete static_cast<OracleHandle*>(h); }
 
 // Samples n seeds; keeps the results in the handle. Returns 0 on success,

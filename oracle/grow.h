@@ -12,6 +12,8 @@
 //       dgf/src/sampling/in_memory_sampler_ext.cc:1020-1093
 //   * Sampler::Sample (argument checks, mt19937_64 seeding of the builder
 //     pool and of every seed)  dgf/src/sampling/in_memory_sampler_ext.cc:418-533
+//   * RandomWalkNegativeSamplerHelper / Sampler::RandomWalkNegativeSampling
+//       dgf/src/sampling/in_memory_sampler_ext.cc:774-948
 //
 // The driver is a template over the adjacency-index type so that the same
 // restatement runs on top of (a) the oracle's own restated AdjacencyIndex
@@ -347,5 +349,178 @@ class Sampler {
     return Status::Ok();
   }
 };
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as
+// easy as 1, 2, 3", SC'11; published round multipliers and Weyl key
+// increments) and the multiply-high reduction to [0, range) (Lemire 2019).
+// Used to replay the device's random stream draw for draw.
+struct Philox4 {
+  std::uint32_t v[4];
+};
+inline Philox4 Philox4x32_10(Philox4 c, std::uint32_t k0, std::uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    const std::uint64_t p0 = static_cast<std::uint64_t>(0xD2511F53u) * c.v[0];
+    const std::uint64_t p1 = static_cast<std::uint64_t>(0xCD9E8D57u) * c.v[2];
+    c = Philox4{{static_cast<std::uint32_t>(p1 >> 32) ^ c.v[1] ^ k0, static_cast<std::uint32_t>(p1),
+                 static_cast<std::uint32_t>(p0 >> 32) ^ c.v[3] ^ k1, static_cast<std::uint32_t>(p0)}};
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+inline std::uint64_t MulHiRange(std::uint64_t r, std::uint64_t range) {
+  return static_cast<std::uint64_t>((static_cast<unsigned __int128>(r) * range) >> 64);
+}
+
+// Random-walk negatives. kind 0 draws exactly as the reference does (one
+// std::mt19937_64 per seed seeded from the sampler's generator, in seed order;
+// uniform_int_distribution for the plan edge, the neighbour and the fallback
+// node). kind 1 replays the device's stream instead: Philox4x32-10 with key
+// (seed_lo ^ call_hi, seed_hi ^ 0x52574E53) and counter (walk, step, seed
+// slot, call_lo) per step, (attempt, 2^31 | slot j, seed slot, call_lo) per
+// fallback draw, at most 64 fallback attempts. Visit counts are kept in
+// node order and ranked by a stable sort on the count, so ties go to the
+// smaller node id; the reference's order among equal counts is its hash
+// map's iteration order.
+template <class Index>
+bool OracleHasEdge(const Index& idx, InputIdx src, InputIdx tgt) {
+  if (src + 1 >= idx.source_blocks.size()) return false;
+  if constexpr (requires { idx.HasEdge(src, tgt); }) {
+    return idx.HasEdge(src, tgt);  // the reference's own (ref build)
+  } else {
+    const auto b = idx.target_node_idxs.begin() + idx.source_blocks[src];
+    const auto e = idx.target_node_idxs.begin() + idx.source_blocks[src + 1];
+    return std::binary_search(b, e, tgt);
+  }
+}
+
+template <class Index>
+Status RandomWalkNegatives(Sampler<Index>& s, const std::int64_t* seeds, std::size_t n, int target_edgeset,
+                           int num_walks, int k, int kind, std::uint64_t sampler_seed, std::uint64_t call_index,
+                           int threads, std::int64_t* out) {
+  if (target_edgeset < 0 || target_edgeset >= static_cast<int>(s.edgesets.size())) {
+    return Status::Invalid("Invalid target_edgeset_idx");
+  }
+  const auto& es = s.edgesets[target_edgeset];
+  if (!es.fwd.has_value()) {
+    return Status::Invalid("Edgeset " + std::to_string(target_edgeset) +
+                           " does not have a forward index. Ensure it is traversed forward in the SamplingPlan.");
+  }
+  const int tns = es.dst_ns;
+  const std::size_t num_target = s.num_nodes[tns];
+  const bool homogeneous = es.src_ns == es.dst_ns;
+  if (n > 0 && k > 0 && (num_target < 1 || (homogeneous && num_target < 2))) {
+    return Status::Invalid("the target node set has no node to draw for the fallback slots");
+  }
+  const std::size_t root_nodes = s.num_nodes[s.plan.nodes[0].nodeset];
+  for (std::size_t i = 0; i < n; ++i) {
+    if (seeds[i] < 0 || static_cast<std::size_t>(seeds[i]) >= root_nodes) {
+      return Status::Invalid("seed at position " + std::to_string(i) + " is not a node of the plan's root node set");
+    }
+  }
+  std::vector<std::uint64_t> per_seed(n);
+  if (kind == 0) {
+    for (std::size_t i = 0; i < n; ++i) per_seed[i] = s.rng();
+  }
+  const std::uint32_t k0 = static_cast<std::uint32_t>(sampler_seed) ^ static_cast<std::uint32_t>(call_index >> 32);
+  const std::uint32_t k1 = static_cast<std::uint32_t>(sampler_seed >> 32) ^ 0x52574E53u;
+  const std::uint32_t call_lo = static_cast<std::uint32_t>(call_index);
+  std::vector<Status> status(n);
+
+  auto one = [&](std::size_t slot) {
+    const InputIdx seed = static_cast<InputIdx>(seeds[slot]);
+    std::int64_t* row = out + slot * static_cast<std::size_t>(k);
+    std::mt19937_64 rng(per_seed[slot]);
+    std::map<InputIdx, int> visits;
+    for (int w = 0; w < num_walks; ++w) {
+      InputIdx cur = seed;
+      int pn = 0;
+      for (std::uint32_t step = 0; !s.plan.nodes[pn].edges.empty(); ++step) {
+        const auto& node = s.plan.nodes[pn];
+        std::size_t ei, pick_r = 0;
+        Philox4 r{};
+        if (kind == 0) {
+          std::uniform_int_distribution<std::size_t> e_dist(0, node.edges.size() - 1);
+          ei = e_dist(rng);
+        } else {
+          r = Philox4x32_10(Philox4{{static_cast<std::uint32_t>(w), step, static_cast<std::uint32_t>(slot), call_lo}},
+                            k0, k1);
+          ei = MulHiRange(static_cast<std::uint64_t>(r.v[1]) << 32 | r.v[0], node.edges.size());
+        }
+        const PlanEdge& pe = s.plan.edges[node.edges[ei]];
+        const auto& ces = s.edgesets[pe.edgeset];
+        const std::optional<Index>& idx = pe.reversed ? ces.bwd : ces.fwd;
+        if (!idx.has_value()) {
+          status[slot] = Status::Invalid("Edgeset does not have the required index.");
+          return;
+        }
+        const std::size_t b = idx->source_blocks[cur], e = idx->source_blocks[cur + 1];
+        if (e == b) break;
+        if (kind == 0) {
+          std::uniform_int_distribution<std::size_t> n_dist(0, e - b - 1);
+          pick_r = n_dist(rng);
+        } else {
+          pick_r = MulHiRange(static_cast<std::uint64_t>(r.v[3]) << 32 | r.v[2], e - b);
+        }
+        cur = idx->target_node_idxs[b + pick_r];
+        pn = pe.child;
+        if (s.plan.nodes[pn].nodeset == tns) {
+          if (homogeneous && cur == seed) continue;
+          ++visits[cur];
+        }
+      }
+    }
+    std::vector<std::pair<InputIdx, int>> cand;
+    for (const auto& [node, count] : visits) {
+      if (!OracleHasEdge(*es.fwd, seed, node)) cand.emplace_back(node, count);
+    }
+    std::stable_sort(cand.begin(), cand.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
+    const int take = std::min<int>(static_cast<int>(cand.size()), k);
+    for (int j = 0; j < take; ++j) row[j] = static_cast<std::int64_t>(cand[j].first);
+    for (int j = take; j < k; ++j) {
+      if (kind == 0) {
+        std::uniform_int_distribution<InputIdx> t_dist(0, num_target - 1);
+        for (;;) {
+          const InputIdx c = t_dist(rng);
+          if (homogeneous && c == seed) continue;
+          row[j] = static_cast<std::int64_t>(c);
+          break;
+        }
+      } else {
+        row[j] = -1;
+        for (std::uint32_t a = 0; a < 64; ++a) {
+          const Philox4 r = Philox4x32_10(
+              Philox4{{a, 0x80000000u | static_cast<std::uint32_t>(j), static_cast<std::uint32_t>(slot), call_lo}}, k0,
+              k1);
+          const InputIdx c = MulHiRange(static_cast<std::uint64_t>(r.v[1]) << 32 | r.v[0], num_target);
+          if (homogeneous && c == seed) continue;
+          row[j] = static_cast<std::int64_t>(c);
+          break;
+        }
+      }
+    }
+  };
+
+  const int nt = std::max(1, threads);
+  std::atomic<std::size_t> next{0};
+  auto worker = [&]() {
+    for (;;) {
+      const std::size_t i = next.fetch_add(1);
+      if (i >= n) break;
+      one(i);
+    }
+  };
+  if (nt == 1) {
+    worker();
+  } else {
+    std::vector<std::thread> pool;
+    for (int t = 0; t < nt; ++t) pool.emplace_back(worker);
+    for (auto& t : pool) t.join();
+  }
+  for (const Status& st : status) {
+    if (!st.ok()) return st;
+  }
+  return Status::Ok();
+}
 
 }  // namespace dgf_oracle

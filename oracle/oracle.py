@@ -19,7 +19,8 @@ And a float64 numpy restatement of the aggregation math:
 And a numpy restatement of the edge-time propagation,
 dgf/src/transform/temporal.py:95-103, and a pure-Python restatement of
 SubGraphExtractor (in_memory_sampler_ext.cc:600-772) for small graphs in the
-deterministic modes.
+deterministic modes; the C++ libraries also restate the random-walk negative
+sampler (in_memory_sampler_ext.cc:774-948).
 """
 
 from __future__ import annotations
@@ -80,6 +81,10 @@ def _lib(ref: bool) -> ctypes.CDLL:
         ]
         lib.oracle_sample.restype = ctypes.c_int
         lib.oracle_sample.argtypes = [ctypes.c_void_p, _p64, _p64, _p64, ctypes.c_int64, ctypes.c_int]
+        lib.oracle_random_walk_negatives.restype = ctypes.c_int
+        lib.oracle_random_walk_negatives.argtypes = [ctypes.c_void_p, _p64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                                     ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64,
+                                                     ctypes.c_int, _p64]
         lib.oracle_result_counts.argtypes = [ctypes.c_void_p, _p64, _p64]
         lib.oracle_result_copy.argtypes = [ctypes.c_void_p, _p64, _p64, _p64]
         lib.oracle_index_build.restype = ctypes.c_void_p
@@ -321,6 +326,22 @@ class OracleSampler:
                 es[name] = np.stack([esrc[b : b + ec[i, e]], edst[b : b + ec[i, e]]])
                 b += ec[i, e]
             out.append((ns, es))
+        return out
+
+
+    def random_walk_negatives(self, seeds, target_edgeset: int, num_walks: int, k: int, kind: int = 0,
+                              sampler_seed: int = 0, call_index: int = 0, threads: int = 1) -> np.ndarray:
+        """RandomWalkNegativeSampling (in_memory_sampler_ext.cc:774-948) as
+        int64 [len(seeds), k]. kind 0 draws from the reference's generator
+        (this sampler's std::mt19937_64, one per seed); kind 1 replays the
+        device's Philox stream for (sampler_seed, call_index)."""
+        seeds = np.ascontiguousarray(np.asarray(seeds, np.int64).reshape(-1))
+        out = np.zeros((len(seeds), max(int(k), 0)), np.int64)
+        st = self.lib.oracle_random_walk_negatives(self.h, _p(seeds), len(seeds), int(target_edgeset), int(num_walks),
+                                                   int(k), int(kind), int(sampler_seed) & ((1 << 64) - 1),
+                                                   int(call_index) & ((1 << 64) - 1), int(threads), _p(out))
+        if st != 0:
+            raise OracleError(_err(self.lib))
         return out
 
 

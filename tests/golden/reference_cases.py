@@ -252,3 +252,22 @@ SUBGRAPH_LINE = ({"n1": 1, "n2": 1}, {"e11": ("n1", "n1", [[0], [0]]), "e12": ("
 # 2 hops, hop_width 20: sample(0) == subgraph([0]).
 EGO_EDGES = [[0, 0, 0, 1, 1, 1, 2, 2, 3, 4, 4, 4, 4, 5, 6, 6, 6, 7],
              [1, 4, 6, 0, 2, 3, 1, 4, 1, 0, 2, 5, 6, 4, 0, 4, 7, 6]]
+
+# ---------------------------------------------------------------------------
+# Random-walk negative sampling: in_memory_sampler_test.py:1171-1277 and
+# dgf/src/generate/edge_neighbor_generator_test.py:48-131, on the
+# recommender-like graph of dgf/src/util/gen_test_graph.py:2253-2329
+# (n1: 3 nodes, n2: 6 nodes, e2: n1 -> n2 with edges 0->0, 0->1, 1->1, 1->2).
+# Plans: "walk3" = n1 -e2-> n2 -e2(rev)-> n1 -e2-> n2 (all hop_width 1);
+# "walk2" = n1 -e2-> n2 -e2(rev)-> n1. Each case: (name, plan, seeds,
+# num_walks, k, {row: expected first entry}); every entry must be a node of
+# n2 (0..5).
+# ---------------------------------------------------------------------------
+RECOMMENDER_NODES = {"n1": 3, "n2": 6}
+RECOMMENDER_E2 = [[0, 0, 1, 1], [0, 1, 1, 2]]
+RW_NEGATIVE_CASES = [
+    ("random walk top-1 :1171-1225", "walk3", [0], 500, 3, {0: 2}),
+    ("fallback with 0 walks :1227-1277", "walk2", [0], 0, 3, {}),
+    ("generator seeds of edges 0 and 2 :85-119", "walk3", [0, 1], 500, 3, {0: 2, 1: 0}),
+    ("generator seed without edges :121-131", "walk3", [2], 500, 3, {}),
+]
