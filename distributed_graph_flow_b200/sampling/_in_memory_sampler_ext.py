@@ -109,13 +109,20 @@ def BuildAdjacencyIndex(
 ) -> AdjacencyIndex:
     """Same contract as the reference's BuildAdjacencyIndex (ext.cc:1020-1093)."""
     torch = _torch()
-    adj = np.asarray(py_adjacency)
-    if adj.ndim != 2 or adj.shape[0] != 2:
-        raise ValueError("adjacency must have shape [2, num_edges]")
-    adj = np.ascontiguousarray(adj.astype(np.int64, copy=False))
     dev = torch.device("cuda", torch.cuda.current_device())
-    src = torch.from_numpy(adj[0].copy()).to(dev, non_blocking=False)
-    dst = torch.from_numpy(adj[1].copy()).to(dev, non_blocking=False)
+    if isinstance(py_adjacency, torch.Tensor) and py_adjacency.is_cuda:
+        # Already in HBM (e.g. io.graph_in_memory.read_graph(device=...)).
+        if py_adjacency.dim() != 2 or py_adjacency.shape[0] != 2:
+            raise ValueError("adjacency must have shape [2, num_edges]")
+        src = py_adjacency[0].to(device=dev, dtype=torch.int64).contiguous()
+        dst = py_adjacency[1].to(device=dev, dtype=torch.int64).contiguous()
+    else:
+        adj = np.asarray(py_adjacency)
+        if adj.ndim != 2 or adj.shape[0] != 2:
+            raise ValueError("adjacency must have shape [2, num_edges]")
+        adj = np.ascontiguousarray(adj.astype(np.int64, copy=False))
+        src = torch.from_numpy(adj[0].copy()).to(dev, non_blocking=False)
+        dst = torch.from_numpy(adj[1].copy()).to(dev, non_blocking=False)
     ts = None
     if py_timestamps is not None:
         if populate_edge_idxs:

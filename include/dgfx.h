@@ -447,6 +447,41 @@ int dgfx_random_walk_negatives(dgfx_sampler* sampler, const int64_t* d_seeds,
 int dgfx_random_walk_negatives_check(const void* d_workspace, dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Raw node id -> node index. Replaces ByteIdToIdxMapper / PairMapping
+ * (dgf/src/io/io_ext.cc:26-170) and the integer-id dictionary of
+ * _read_node_set (dgf/src/io/graph_in_memory.py:80-125) used when a GF graph
+ * is loaded. Ids are read in place on the device:
+ *   DGFX_IDS_INT64  d_ids = int64[num_ids]
+ *   DGFX_IDS_FIXED  d_ids = bytes, num_ids rows of `width` bytes (numpy 'S')
+ *   DGFX_IDS_VAR    d_ids = bytes, d_offsets = int64[num_ids + 1] (Arrow binary)
+ * A byte id is its bytes without trailing zero bytes; a repeated id maps to
+ * its last position. The index borrows d_ids / d_offsets (keep them alive).
+ * Lookup writes the index of every query id (-1 when absent) and, if
+ * `mismatch` is non-null, synchronises and stores the largest position of an
+ * absent id (-1 if none). Integer ids only match integer ids. Lookups on one
+ * index are serialised by the caller.
+ * ------------------------------------------------------------------------ */
+enum { DGFX_IDS_INT64 = 0, DGFX_IDS_FIXED = 1, DGFX_IDS_VAR = 2 };
+typedef struct dgfx_id_index dgfx_id_index;
+int dgfx_id_index_create(int32_t kind, const void* d_ids, const int64_t* d_offsets,
+                         int64_t width, int64_t num_ids, dgfx_stream stream,
+                         dgfx_id_index** out);
+void dgfx_id_index_destroy(dgfx_id_index* index);
+int dgfx_id_index_lookup(const dgfx_id_index* index, int32_t kind, const void* d_ids,
+                         const int64_t* d_offsets, int64_t width, int64_t num_ids,
+                         int64_t* d_out, int64_t* mismatch, dgfx_stream stream);
+
+/* Keeps the pairs whose two indices are >= 0 (dangling-edge removal,
+ * graph_in_memory.py:185-198), in order: d_out_src / d_out_dst get the kept
+ * pairs, d_out_pos (nullable) their positions in the input; *num_kept is
+ * read back (synchronises `stream`). */
+int dgfx_compact_pairs_workspace_size(int64_t num_pairs, size_t* bytes);
+int dgfx_compact_pairs(const int64_t* d_src, const int64_t* d_dst, int64_t num_pairs,
+                       int64_t* d_out_src, int64_t* d_out_dst, int64_t* d_out_pos,
+                       int64_t* num_kept, void* d_workspace, size_t workspace_bytes,
+                       dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
  * Subgraph around a set of seeds. Replaces the numbering and edge set of
  * SubGraphExtractor (dgf/src/sampling/in_memory_sampler_ext.cc:600-772) as
  * the union of a merged batch of per-seed samples (dgfx_sample_out layout,

@@ -13,7 +13,11 @@
 
 #include <cstdint>
 #include <cstring>
+#include <atomic>
 #include <memory>
+#include <string_view>
+#include <thread>
+#include <unordered_map>
 #include <string>
 #include <vector>
 
@@ -200,6 +204,48 @@ int oracle_random_walk_negatives(void* hv, const std::int64_t* seeds, std::int64
     return st.code;
   }
   return 0;
+}
+
+// Raw id -> index (ByteIdToIdxMapper / PairMapping, dgf/src/io/io_ext.cc:
+// 26-170): index_ids are n fixed-width byte rows of width wi, queries m rows
+// of width wq; a byte id is its bytes without trailing zero bytes; a repeated
+// index id maps to its last position; unknown ids map to -1. The query loop
+// is split into blocks over `threads` threads like PairMapping; *mismatch is
+// the largest unknown position (-1 if none).
+void oracle_bytes_map(const char* index_ids, std::int64_t n, std::int64_t wi, const char* queries, std::int64_t m,
+                      std::int64_t wq, int threads, std::int64_t* out, std::int64_t* mismatch) {
+  auto view = [](const char* base, std::int64_t i, std::int64_t w) {
+    std::int64_t len = w;
+    const char* p = base + i * w;
+    while (len > 0 && p[len - 1] == 0) --len;
+    return std::string_view(p, static_cast<std::size_t>(len));
+  };
+  std::unordered_map<std::string_view, std::int64_t> index;
+  index.reserve(static_cast<std::size_t>(n) * 2);
+  for (std::int64_t i = 0; i < n; ++i) index[view(index_ids, i, wi)] = i;
+  std::atomic<std::int64_t> last{-1};
+  const int nt = std::max(1, threads);
+  std::vector<std::thread> pool;
+  for (int t = 0; t < nt; ++t) {
+    pool.emplace_back([&, t]() {
+      const std::int64_t lo = m * t / nt, hi = m * (t + 1) / nt;
+      std::int64_t local = -1;
+      for (std::int64_t i = lo; i < hi; ++i) {
+        auto it = index.find(view(queries, i, wq));
+        if (it == index.end()) {
+          out[i] = -1;
+          local = i;
+        } else {
+          out[i] = it->second;
+        }
+      }
+      std::int64_t cur = last.load();
+      while (local > cur && !last.compare_exchange_weak(cur, local)) {
+      }
+    });
+  }
+  for (auto& th : pool) th.join();
+  *mismatch = last.load();
 }
 
 void oracle_sampler_free(void* h) { delete static_cast<OracleHandle*>(h); }

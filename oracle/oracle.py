@@ -20,7 +20,8 @@ And a numpy restatement of the edge-time propagation,
 dgf/src/transform/temporal.py:95-103, and a pure-Python restatement of
 SubGraphExtractor (in_memory_sampler_ext.cc:600-772) for small graphs in the
 deterministic modes; the C++ libraries also restate the random-walk negative
-sampler (in_memory_sampler_ext.cc:774-948).
+sampler (in_memory_sampler_ext.cc:774-948) and the raw-id mapping of GF
+graph loading (dgf/src/io/io_ext.cc:26-170).
 """
 
 from __future__ import annotations
@@ -85,6 +86,8 @@ def _lib(ref: bool) -> ctypes.CDLL:
         lib.oracle_random_walk_negatives.argtypes = [ctypes.c_void_p, _p64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                                      ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64,
                                                      ctypes.c_int, _p64]
+        lib.oracle_bytes_map.argtypes = [ctypes.c_char_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_char_p,
+                                          ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _p64, _p64]
         lib.oracle_result_counts.argtypes = [ctypes.c_void_p, _p64, _p64]
         lib.oracle_result_copy.argtypes = [ctypes.c_void_p, _p64, _p64, _p64]
         lib.oracle_index_build.restype = ctypes.c_void_p
@@ -343,6 +346,49 @@ class OracleSampler:
         if st != 0:
             raise OracleError(_err(self.lib))
         return out
+
+
+# ---------------------------------------------------------------------------
+# Raw id -> index (dgf/src/io/io_ext.cc:26-170; integer ids:
+# dgf/src/io/graph_in_memory.py:111-125).
+# ---------------------------------------------------------------------------
+def _id_key(v):
+    if isinstance(v, (bytes, np.bytes_)):
+        return bytes(v).rstrip(b"\0")
+    return int(v)
+
+
+def id_map(index_ids, query_ids):
+    """(int64 indices, -1 for unknown ids; last unknown position or -1): a
+    dict from id to its last position, byte ids without trailing zeros."""
+    table = {}
+    for i, v in enumerate(np.asarray(index_ids).tolist()):
+        table[_id_key(v)] = i
+    q = np.asarray(query_ids).tolist()
+    out = np.empty(len(q), np.int64)
+    mismatch = -1
+    for i, v in enumerate(q):
+        r = table.get(_id_key(v))
+        if r is None:
+            out[i] = -1
+            mismatch = i
+        else:
+            out[i] = r
+    return out, mismatch
+
+
+def bytes_map(index_ids: np.ndarray, query_ids: np.ndarray, threads: int = 1):
+    """id_map for numpy byte arrays in C++ (unordered_map over string views,
+    the query loop split over `threads`, like PairMapping)."""
+    lib = _lib(False)
+    a = np.ascontiguousarray(index_ids)
+    b = np.ascontiguousarray(query_ids)
+    out = np.empty(len(b), np.int64)
+    mm = np.full(1, -1, np.int64)
+    lib.oracle_bytes_map(a.tobytes() if a.size else b"", len(a), max(1, a.dtype.itemsize),
+                         b.tobytes() if b.size else b"", len(b), max(1, b.dtype.itemsize), int(threads), _p(out),
+                         _p(mm))
+    return out, int(mm[0])
 
 
 # ---------------------------------------------------------------------------

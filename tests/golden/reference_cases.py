@@ -271,3 +271,35 @@ RW_NEGATIVE_CASES = [
     ("generator seeds of edges 0 and 2 :85-119", "walk3", [0, 1], 500, 3, {0: 2, 1: 0}),
     ("generator seed without edges :121-131", "walk3", [2], 500, 3, {}),
 ]
+
+# ---------------------------------------------------------------------------
+# Raw id -> index: dgf/src/io/io_cc_test.py:24-85. Each case: (name, index
+# ids, query ids, expected indices, expected last-mismatch position).
+# ---------------------------------------------------------------------------
+ID_MAP_CASES = [
+    ("with_all_matches", [b"X", b"Y"], [b"Y", b"X", b"Y"], [1, 0, 1], -1),
+    ("with_missing_match", [b"X", b"Y"], [b"Y", b"X", b"Z"], [1, 0, -1], 2),
+    ("empty_index", [], [], [], -1),
+    ("empty_value", [b"X", b""], [b"", b"X", b"Z"], [1, 0, -1], 2),
+]
+# PairMapping (:87-103): mappers over [X, Y] and [Z, X].
+PAIR_MAP_CASE = ([b"X", b"Y"], [b"Z", b"X"], [b"Y", b"X", b"_"], [b"Z", b"Z", b"X"],
+                 [[1, 0, -1], [0, 0, 1]], 2, -1)
+
+# ---------------------------------------------------------------------------
+# GF graph fixture: dgf/src/util/gen_test_graph.py:345-466 (generate_gf_graph,
+# edge_ids=True) and the in-memory graph it must load as (:1259-1330,
+# node_ids=True, edge_ids=True); checked by dgf/src/io/graph_in_memory_test.py:
+# 28-177. n1 ids are bytes (one shard), n2 ids int64 (two shards); e2's
+# targets are n2's integer ids; with dangling edges e2's second source is
+# b"missing" ("Node ID 'missing' not found in nodeset 'n1'", one e2 edge left
+# when removed).
+# ---------------------------------------------------------------------------
+GF_N1 = {"#id": [b"1", b"2"], "f1": [[b"blue"], [b"red"]], "f2": [[0.0, 1.0], [2.0, 3.0]]}
+GF_N2_SHARDS = [
+    {"#id": [1], "f3": [4], "f4": [10], "f5": [[11, 12]], "f6": [[[11, 12], [13, 14]]]},
+    {"#id": [2], "f3": [5], "f4": [11], "f5": [[12, 13, 14]], "f6": [[[15, 16], [17, 18], [19, 20]]]},
+]
+GF_E1 = {"#source": [b"1", b"1"], "#target": [b"1", b"2"], "#id": [b"a", b"b"]}
+GF_E2 = {"#source": [b"1", b"1"], "#target": [1, 2], "#id": [b"A", b"B"]}
+GF_ADJACENCY = {"e1": [[0, 0], [0, 1]], "e2": [[0, 0], [0, 1]]}
