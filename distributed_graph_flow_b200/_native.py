@@ -121,7 +121,8 @@ SIGNATURES = {
     "dgfx_random_walk_negatives_workspace_size": (_int, [_vp, _i64, _i32, _i32, _i32, ctypes.POINTER(_sz)]),
     "dgfx_random_walk_negatives": (_int, [_vp, _vp, _i64, _i32, _i32, _i32, _u64, _vp, _vp, _sz, _vp]),
     "dgfx_random_walk_negatives_check": (_int, [_vp, _vp]),
-    "dgfx_id_index_create": (_int, [_i32, _vp, _vp, _i64, _i64, _vp, ctypes.POINTER(_vp)]),
+    "dgfx_id_index_table_bytes": (_int, [_i64, ctypes.POINTER(_sz)]),
+    "dgfx_id_index_create": (_int, [_i32, _vp, _vp, _i64, _i64, _vp, _sz, _vp, ctypes.POINTER(_vp)]),
     "dgfx_id_index_destroy": (None, [_vp]),
     "dgfx_id_index_lookup": (_int, [_vp, _i32, _vp, _vp, _i64, _i64, _vp, ctypes.POINTER(_i64), _vp]),
     "dgfx_compact_pairs_workspace_size": (_int, [_i64, ctypes.POINTER(_sz)]),

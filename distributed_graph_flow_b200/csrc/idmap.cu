@@ -17,11 +17,12 @@
 // (CAS into an empty slot; a slot holding an equal id keeps the larger index
 // through atomicMax, since equal ids carry equal tags) and probed by one
 // thread per query, comparing tags first and the id bytes only on a tag
-// match. Hashes: FNV-1a 64 over the id bytes (Fowler, Noll, Vo), the
-// SplitMix64 finaliser for integer ids (Steele, Lea, Flood, "Fast splittable
-// pseudorandom number generators", OOPSLA 2014). Ids are read where they lie:
-// int64 arrays, fixed-width byte rows (numpy 'S' arrays) or Arrow binary
-// columns (int64 offsets + bytes). Dangling-edge removal is a stable
+// match. A byte id hashes as its little-endian 32-bit words (zero padded)
+// folded by multiply-xorshift, then the SplitMix64 finaliser (Steele, Lea,
+// Flood, "Fast splittable pseudorandom number generators", OOPSLA 2014),
+// which also hashes integer ids. Ids are read where they lie: int64 arrays,
+// fixed-width byte rows (numpy 'S' arrays; rows of a multiple of 4 bytes are
+// read a word at a time) or Arrow binary columns (int64 offsets + bytes). Dangling-edge removal is a stable
 // compaction (flag, scan, scatter) that also returns the kept edges'
 // positions so edge features can be filtered with them.
 #include <memory>
@@ -38,13 +39,29 @@ constexpr int kThreads = 256;
 
 struct KeysDev {
   int32_t kind;
+  int32_t words;           // fixed-width rows of a multiple of 4 bytes on a 4-byte boundary: read as 32-bit words
   int64_t width;           // DGFX_IDS_FIXED: bytes per id
   const int64_t* ints;     // DGFX_IDS_INT64
   const uint8_t* bytes;    // DGFX_IDS_FIXED / DGFX_IDS_VAR
   const int64_t* offsets;  // DGFX_IDS_VAR: [n + 1]
 };
 
-__device__ __forceinline__ void id_bytes(const KeysDev& k, int64_t i, const uint8_t** p, int64_t* len) {
+// Byte id i as (first byte, length without trailing zero bytes).
+__device__ __forceinline__ void id_span(const KeysDev& k, int64_t i, int64_t* start, int64_t* len) {
+  if (k.words) {
+    const uint32_t* row = reinterpret_cast<const uint32_t*>(k.bytes + i * k.width);
+    int64_t L = 0;
+    for (int64_t j = k.width / 4 - 1; j >= 0; --j) {
+      const uint32_t w = row[j];
+      if (w != 0) {
+        L = 4 * j + (39 - __clz(w)) / 8;  // bytes up to the highest non-zero one (little-endian)
+        break;
+      }
+    }
+    *start = i * k.width;
+    *len = L;
+    return;
+  }
   int64_t b, e;
   if (k.kind == DGFX_IDS_FIXED) {
     b = i * k.width;
@@ -54,8 +71,18 @@ __device__ __forceinline__ void id_bytes(const KeysDev& k, int64_t i, const uint
     e = k.offsets[i + 1];
   }
   while (e > b && k.bytes[e - 1] == 0) --e;  // trailing zero bytes are not part of the id
-  *p = k.bytes + b;
+  *start = b;
   *len = e - b;
+}
+
+// Little-endian 32-bit word j of an id (bytes past its length read as zero;
+// in a fixed-width row they are zero already).
+__device__ __forceinline__ uint32_t id_word(const KeysDev& k, int64_t start, int64_t len, int64_t j) {
+  if (k.words) return reinterpret_cast<const uint32_t*>(k.bytes + start)[j];
+  uint32_t w = 0;
+  const int64_t b = 4 * j;
+  for (int t = 0; t < 4 && b + t < len; ++t) w |= static_cast<uint32_t>(k.bytes[start + b + t]) << (8 * t);
+  return w;
 }
 
 __device__ __forceinline__ uint64_t mix64(uint64_t x) {
@@ -67,41 +94,59 @@ __device__ __forceinline__ uint64_t mix64(uint64_t x) {
   return x;
 }
 
-__device__ __forceinline__ uint64_t hash_bytes(const uint8_t* p, int64_t len) {
-  uint64_t h = 0xcbf29ce484222325ull;
-  for (int64_t j = 0; j < len; ++j) {
-    h ^= p[j];
-    h *= 0x100000001b3ull;
+// Hash of a byte id: its 32-bit words folded by multiply-xorshift, then the
+// SplitMix64 finaliser; identical for every storage layout of the same id.
+__device__ __forceinline__ uint64_t hash_span(const KeysDev& k, int64_t start, int64_t len) {
+  uint64_t h = 0x9E3779B97F4A7C15ull ^ static_cast<uint64_t>(len);
+  const int64_t nw = (len + 3) / 4;
+  for (int64_t j = 0; j < nw; ++j) {
+    h = (h ^ id_word(k, start, len, j)) * 0x9E3779B97F4A7C15ull;
+    h ^= h >> 29;
   }
-  return mix64(h);  // spread FNV's low bits over the slot index
+  return mix64(h);
 }
 
-__device__ __forceinline__ uint64_t hash_id(const KeysDev& k, int64_t i) {
-  if (k.kind == DGFX_IDS_INT64) return mix64(static_cast<uint64_t>(k.ints[i]));
-  const uint8_t* p;
-  int64_t len;
-  id_bytes(k, i, &p, &len);
-  return hash_bytes(p, len);
-}
-
-// Id a[i] == id b[j] (both of the same family: integers or bytes).
-__device__ __forceinline__ bool same_id(const KeysDev& a, int64_t i, const KeysDev& b, int64_t j) {
-  if (a.kind == DGFX_IDS_INT64) return a.ints[i] == b.ints[j];
-  const uint8_t *pa, *pb;
-  int64_t la, lb;
-  id_bytes(a, i, &pa, &la);
-  id_bytes(b, j, &pb, &lb);
+__device__ __forceinline__ bool same_span(const KeysDev& a, int64_t sa, int64_t la, const KeysDev& b, int64_t sb,
+                                          int64_t lb) {
   if (la != lb) return false;
-  for (int64_t t = 0; t < la; ++t) {
-    if (pa[t] != pb[t]) return false;
+  const int64_t nw = (la + 3) / 4;
+  for (int64_t j = 0; j < nw; ++j) {
+    if (id_word(a, sa, la, j) != id_word(b, sb, lb, j)) return false;
   }
   return true;
+}
+
+// An id in registers: its hash and, for byte ids, its span.
+struct IdRef {
+  uint64_t hash;
+  int64_t start, len, value;
+};
+
+__device__ __forceinline__ IdRef load_id(const KeysDev& k, int64_t i) {
+  IdRef r{};
+  if (k.kind == DGFX_IDS_INT64) {
+    r.value = k.ints[i];
+    r.hash = mix64(static_cast<uint64_t>(r.value));
+    return r;
+  }
+  id_span(k, i, &r.start, &r.len);
+  r.hash = hash_span(k, r.start, r.len);
+  return r;
+}
+
+// Index id `idx` equals the id `r` (read from layout `q`).
+__device__ __forceinline__ bool matches(const KeysDev& keys, int64_t idx, const KeysDev& q, const IdRef& r) {
+  if (keys.kind == DGFX_IDS_INT64) return keys.ints[idx] == r.value;
+  int64_t s, l;
+  id_span(keys, idx, &s, &l);
+  return same_span(keys, s, l, q, r.start, r.len);
 }
 
 __global__ void id_index_build_kernel(KeysDev keys, int64_t n, unsigned long long* table, uint64_t mask,
                                       unsigned long long* full) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
-    const uint64_t h = hash_id(keys, i);
+    const IdRef r = load_id(keys, i);
+    const uint64_t h = r.hash;
     const unsigned long long word = (static_cast<unsigned long long>(h >> 32) << 32) | static_cast<uint32_t>(i);
     uint64_t s = h & mask;
     bool placed = false;
@@ -115,7 +160,7 @@ __global__ void id_index_build_kernel(KeysDev keys, int64_t n, unsigned long lon
         }
         w = prev;
       }
-      if ((w >> 32) == (word >> 32) && same_id(keys, static_cast<uint32_t>(w), keys, i)) {
+      if ((w >> 32) == (word >> 32) && matches(keys, static_cast<uint32_t>(w), keys, r)) {
         atomicMax(&table[s], word);  // equal ids: the later position wins
         placed = true;
         break;
@@ -129,14 +174,15 @@ __global__ void id_index_build_kernel(KeysDev keys, int64_t n, unsigned long lon
 __global__ void id_index_lookup_kernel(KeysDev keys, const unsigned long long* table, uint64_t mask, KeysDev q,
                                        int64_t n, int64_t* out, unsigned long long* mismatch) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
-    const uint64_t h = hash_id(q, i);
+    const IdRef r = load_id(q, i);
+    const uint64_t h = r.hash;
     const uint32_t tag = static_cast<uint32_t>(h >> 32);
     uint64_t s = h & mask;
     int64_t found = -1;
     for (uint64_t probe = 0; probe <= mask; ++probe) {
       const unsigned long long w = table[s];
       if (w == kEmptyWord) break;
-      if (static_cast<uint32_t>(w >> 32) == tag && same_id(keys, static_cast<uint32_t>(w), q, i)) {
+      if (static_cast<uint32_t>(w >> 32) == tag && matches(keys, static_cast<uint32_t>(w), q, r)) {
         found = static_cast<uint32_t>(w);
         break;
       }
@@ -172,6 +218,7 @@ unsigned grid_for(int64_t n) {
 int make_keys(int32_t kind, const void* d_ids, const int64_t* d_offsets, int64_t width, int64_t n, KeysDev* k,
               const char* what) {
   k->kind = kind;
+  k->words = 0;
   k->width = width;
   k->ints = nullptr;
   k->bytes = nullptr;
@@ -186,6 +233,7 @@ int make_keys(int32_t kind, const void* d_ids, const int64_t* d_offsets, int64_t
     case DGFX_IDS_FIXED:
       if (width < 1) return fail(DGFX_ERR_INVALID_ARGUMENT, std::string(what) + ": id width must be >= 1");
       k->bytes = static_cast<const uint8_t*>(d_ids);
+      k->words = (width % 4 == 0 && reinterpret_cast<uintptr_t>(d_ids) % 4 == 0) ? 1 : 0;
       return DGFX_OK;
     case DGFX_IDS_VAR:
       if (d_offsets == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, std::string(what) + ": null offsets");
@@ -207,10 +255,26 @@ struct dgfx_id_index {
   int64_t n = 0;
   uint64_t mask = 0;
   unsigned long long* table = nullptr;  // [mask + 1] words, then 2 status words
+  bool owned = false;                   // allocated here (no caller table)
 };
 
+namespace {
+uint64_t table_capacity(int64_t num_ids) {
+  uint64_t cap = 1024;
+  while (cap < static_cast<uint64_t>(2 * num_ids)) cap <<= 1;
+  return cap;
+}
+}  // namespace
+
+extern "C" int dgfx_id_index_table_bytes(int64_t num_ids, size_t* bytes) {
+  if (bytes == nullptr || num_ids < 0) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_id_index_table_bytes: bad arguments");
+  *bytes = (table_capacity(num_ids) + 2) * sizeof(unsigned long long);
+  return DGFX_OK;
+}
+
 extern "C" int dgfx_id_index_create(int32_t kind, const void* d_ids, const int64_t* d_offsets, int64_t width,
-                                    int64_t num_ids, dgfx_stream stream_, dgfx_id_index** out) {
+                                    int64_t num_ids, void* d_table, size_t table_bytes, dgfx_stream stream_,
+                                    dgfx_id_index** out) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (out == nullptr || num_ids < 0) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_id_index_create: bad arguments");
   *out = nullptr;
@@ -220,10 +284,18 @@ extern "C" int dgfx_id_index_create(int32_t kind, const void* d_ids, const int64
   auto ix = std::make_unique<dgfx_id_index>();
   DGFX_TRY(make_keys(kind, d_ids, d_offsets, width, num_ids, &ix->keys, "dgfx_id_index_create"));
   ix->n = num_ids;
-  uint64_t cap = 1024;
-  while (cap < static_cast<uint64_t>(2 * num_ids)) cap <<= 1;
+  const uint64_t cap = table_capacity(num_ids);
   ix->mask = cap - 1;
-  DGFX_CUDA_TRY(cudaMalloc(&ix->table, (cap + 2) * sizeof(unsigned long long)));
+  const size_t need = (cap + 2) * sizeof(unsigned long long);
+  if (d_table != nullptr) {
+    if (table_bytes < need || reinterpret_cast<uintptr_t>(d_table) % 8 != 0) {
+      return fail(DGFX_ERR_WORKSPACE, "dgfx_id_index_create: table memory too small or not 8-byte aligned");
+    }
+    ix->table = static_cast<unsigned long long*>(d_table);
+  } else {
+    DGFX_CUDA_TRY(cudaMalloc(&ix->table, need));
+    ix->owned = true;
+  }
   DGFX_CUDA_TRY(cudaMemsetAsync(ix->table, 0xFF, cap * sizeof(unsigned long long), stream));
   DGFX_CUDA_TRY(cudaMemsetAsync(ix->table + cap, 0, 2 * sizeof(unsigned long long), stream));
   if (num_ids > 0) {
@@ -235,7 +307,7 @@ extern "C" int dgfx_id_index_create(int32_t kind, const void* d_ids, const int64
   DGFX_CUDA_TRY(cudaMemcpyAsync(&full, ix->table + cap, sizeof(full), cudaMemcpyDeviceToHost, stream));
   DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
   if (full != 0) {
-    cudaFree(ix->table);
+    if (ix->owned) cudaFree(ix->table);
     ix->table = nullptr;
     return fail(DGFX_ERR_INTERNAL, "dgfx_id_index_create: id table full");
   }
@@ -245,7 +317,7 @@ extern "C" int dgfx_id_index_create(int32_t kind, const void* d_ids, const int64
 
 extern "C" void dgfx_id_index_destroy(dgfx_id_index* ix) {
   if (ix == nullptr) return;
-  if (ix->table != nullptr) cudaFree(ix->table);
+  if (ix->owned && ix->table != nullptr) cudaFree(ix->table);
   delete ix;
 }
 

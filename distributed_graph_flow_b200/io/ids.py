@@ -105,9 +105,13 @@ class IdIndex:
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         with torch.cuda.device(self.device):
             self._ids = _DeviceIds(ids, self.device)
+            need = ctypes.c_size_t()
+            _native.check(_native.lib().dgfx_id_index_table_bytes(self._ids.n, ctypes.byref(need)))
+            # The table comes from torch's caching allocator (no cudaMalloc per index).
+            self._table = torch.empty(need.value, dtype=torch.uint8, device=self.device)
             h = ctypes.c_void_p()
-            _native.check(_native.lib().dgfx_id_index_create(*self._ids.args(), _native.stream_handle(),
-                                                             ctypes.byref(h)))
+            _native.check(_native.lib().dgfx_id_index_create(*self._ids.args(), _native.ptr(self._table),
+                                                             need.value, _native.stream_handle(), ctypes.byref(h)))
         self._h = h.value
         self.num_ids = self._ids.n
         self.integer = self._ids.kind == IDS_INT64

@@ -463,9 +463,13 @@ int dgfx_random_walk_negatives_check(const void* d_workspace, dgfx_stream stream
  * ------------------------------------------------------------------------ */
 enum { DGFX_IDS_INT64 = 0, DGFX_IDS_FIXED = 1, DGFX_IDS_VAR = 2 };
 typedef struct dgfx_id_index dgfx_id_index;
+/* Table memory: d_table (8-byte aligned, dgfx_id_index_table_bytes) is
+ * borrowed for the index's lifetime; with d_table NULL the index allocates
+ * its own. Creation synchronises `stream`. */
+int dgfx_id_index_table_bytes(int64_t num_ids, size_t* bytes);
 int dgfx_id_index_create(int32_t kind, const void* d_ids, const int64_t* d_offsets,
-                         int64_t width, int64_t num_ids, dgfx_stream stream,
-                         dgfx_id_index** out);
+                         int64_t width, int64_t num_ids, void* d_table,
+                         size_t table_bytes, dgfx_stream stream, dgfx_id_index** out);
 void dgfx_id_index_destroy(dgfx_id_index* index);
 int dgfx_id_index_lookup(const dgfx_id_index* index, int32_t kind, const void* d_ids,
                          const int64_t* d_offsets, int64_t width, int64_t num_ids,
