@@ -133,13 +133,6 @@ __host__ __device__ inline size_t counter_bytes(int threads) {
   return static_cast<size_t>(threads / 32) * 256 * 4 + 256 * 4;
 }
 
-__device__ __forceinline__ uint64_t draw64(const Params& p, int32_t q, int32_t e, uint32_t m, uint32_t slot,
-                                           uint2 call) {
-  U4 c{static_cast<uint32_t>(q), static_cast<uint32_t>(e) | ((m >> 1) << 16), slot, call.x};
-  const U4 r = philox4x32_10(c, p.key0 ^ call.y, p.key1);
-  return (m & 1u) ? (static_cast<uint64_t>(r.w) << 32 | r.z) : (static_cast<uint64_t>(r.y) << 32 | r.x);
-}
-
 // One expansion task, first half: choose up to k neighbours of node v over
 // plan edge e and record their CSR positions (int64, -1 = empty) in the
 // child slots base + j * stride (j < k) of the pick array `at`. The column
@@ -194,8 +187,15 @@ __device__ void expand_task(const Params& p, long long* at, int32_t q, int32_t e
         // Floyd: for j = nv-cnt .. nv-1 pick t in [0, j]; take t unless
         // already taken, else take j. Chosen offsets go to the child slots.
         int32_t taken = 0;
+        U4 block{};  // draws m and m + 1 are the two halves of one Philox block
         for (int64_t j = nv - cnt; j < nv; ++j) {
-          const uint64_t r = draw64(p, q, e, static_cast<uint32_t>(taken), slot, call);
+          if ((taken & 1) == 0) {
+            const U4 c{static_cast<uint32_t>(q), static_cast<uint32_t>(e) | ((static_cast<uint32_t>(taken) >> 1) << 16),
+                       slot, call.x};
+            block = philox4x32_10(c, p.key0 ^ call.y, p.key1);
+          }
+          const uint64_t r = (taken & 1) ? (static_cast<uint64_t>(block.w) << 32 | block.z)
+                                         : (static_cast<uint64_t>(block.y) << 32 | block.x);
           int64_t t = static_cast<int64_t>(bounded64(r, static_cast<uint64_t>(j + 1)));
           for (int32_t i = 0; i < taken; ++i) {
             if (at[base + i * stride] == t) {
