@@ -369,8 +369,9 @@ int sm_count() {
 // One warp per segment over its items in CSR order (perm[j] = item of slot j,
 // nullptr = identity); lane l owns the 16-byte slices v = l + 32 i of the
 // H x D message row, each inside one head. Online softmax: per slice a running
-// (max, sum, weighted sum) rescaled when the max grows, so every message row
-// is read once and no [E, H] weight array is materialised.
+// (max, sum, weighted sum), rescaled once per group of four rows to the
+// group's new max, so every message row is read once and no [E, H] weight
+// array is materialised.
 template <class MT>
 __device__ __forceinline__ void unpack16(const uint4& x, float* f);
 template <>
@@ -409,6 +410,28 @@ struct SoftmaxState {
     s = s * sc + p;
 #pragma unroll
     for (int k = 0; k < EPV; ++k) acc[k] = acc[k] * sc + p * x[k];
+    m = mn;
+  }
+  // U rows at once: one rescale to the group's new max, then U plain
+  // accumulations (rows past the segment carry l = -inf, x = 0).
+  template <int U>
+  __device__ __forceinline__ void add_group(const float* l, const float (*x)[EPV]) {
+    float mg = l[0];
+#pragma unroll
+    for (int u = 1; u < U; ++u) mg = fmaxf(mg, l[u]);
+    const float mn = fmaxf(m, mg);
+    if (mn == -INFINITY) return;  // every logit so far is -inf
+    const float sc = expf(m - mn);
+    s *= sc;
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) acc[k] *= sc;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float p = expf(l[u] - mn);
+      s += p;
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) acc[k] = fmaf(p, x[u][k], acc[k]);
+    }
     m = mn;
   }
   __device__ __forceinline__ void merge(float m2, float s2, const float* acc2) {
@@ -468,16 +491,16 @@ __global__ void __launch_bounds__(256) segment_softmax_kernel(
         }
       }
 #pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        if (j0 + u < hi) {
+      for (int i = 0; i < VPL; ++i) {
+        if (lane + 32 * i < vpr) {
+          float f[kU][EPV];
+          float lg[kU];
 #pragma unroll
-          for (int i = 0; i < VPL; ++i) {
-            if (lane + 32 * i < vpr) {
-              float f[EPV];
-              unpack16<MT>(x[u][i], f);
-              st[i].add(l[u][i], f);
-            }
+          for (int u = 0; u < kU; ++u) {
+            unpack16<MT>(x[u][i], f[u]);
+            lg[u] = l[u][i];
           }
+          st[i].template add_group<kU>(lg, f);
         }
       }
     }
