@@ -450,7 +450,7 @@ struct SoftmaxState {
 // its output; chunks of a split segment write their states (per slice: max,
 // sum, EPV weighted sums) for segment_softmax_fixup_kernel.
 template <class MT, class OT, int VPL>
-__global__ void __launch_bounds__(256) segment_softmax_kernel(
+__global__ void __launch_bounds__(256, (VPL == 1 && sizeof(MT) == 2) ? 5 : 1) segment_softmax_kernel(
     const int64_t* __restrict__ rowptr, const int64_t* __restrict__ task_off, const int64_t* __restrict__ split_off,
     const int32_t* __restrict__ task_row, const int64_t* __restrict__ num_tasks, const uint32_t* __restrict__ perm,
     const float* __restrict__ logits, int heads, const uint4* __restrict__ msg, int64_t vpr, int head_dim,
