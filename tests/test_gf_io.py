@@ -283,3 +283,43 @@ def test_gpu_read_graph_device_into_sampler(cuda, tmp_path):
     for x, y in zip(a, b):
         np.testing.assert_array_equal(x.node_sets["u"].features["#idx"], y.node_sets["u"].features["#idx"])
         np.testing.assert_array_equal(x.edge_sets["f"].adjacency, y.edge_sets["f"].adjacency)
+
+
+def test_parquet_columns_to_numpy():
+    """Column conversions of dgf/src/io/parquet.py:63-135: binary -> 'S<max>'
+    (zero padded, chunked and sliced), string -> bytes, fixed-size lists ->
+    [n, k] (nested), variable lists -> object arrays, numbers as they are."""
+    import pyarrow as pa
+
+    from distributed_graph_flow_b200.io import parquet as P
+
+    col = pa.chunked_array([pa.array([b"1", b"22", b""]), pa.array([b"abc", b"z"]).slice(1)])
+    out = P.column_to_numpy(col)
+    assert out.dtype == np.dtype("S2") and out.tolist() == [b"1", b"22", b"", b"z"]  # the slice drops "abc"
+    assert P.column_to_numpy(pa.chunked_array([pa.array([b""])])).dtype == np.dtype("S1")
+    assert P.column_to_numpy(pa.chunked_array([pa.array(["ab", "c"])])).tolist() == [b"ab", b"c"]
+    fixed = P.column_to_numpy(pa.chunked_array([pa.array([[[1, 2], [3, 4]]], type=pa.list_(pa.list_(pa.int64(), 2), 2))]))
+    assert fixed.shape == (1, 2, 2) and fixed.tolist() == [[[1, 2], [3, 4]]]
+    var = P.column_to_numpy(pa.chunked_array([pa.array([[1], [2, 3]]), pa.array([[4, 5, 6]])]))
+    assert var.dtype == object and [v.tolist() for v in var] == [[1], [2, 3], [4, 5, 6]]
+    f = P.column_to_numpy(pa.chunked_array([pa.array([1.5, 2.5], type=pa.float32())]))
+    assert f.dtype == np.float32 and f.tolist() == [1.5, 2.5]
+    assert P.sharded_filename("e1", 3, 12) == "e1-00003-of-00012.parquet"
+    assert [P.estimate_num_shards(n) for n in (0, 1, 1000, 1001, 10**9)] == [0, 1, 1, 2, 100]
+
+
+def test_oracle_id_maps_agree():
+    """The Python and C++ restatements of the id map agree on random ids with
+    repeats, trailing zeros, different widths and unknown ids."""
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(4)
+    index = np.array([b"k%d" % v for v in rng.integers(0, 5000, 4000)] + [b"t\0", b""], dtype="S10")
+    query = np.concatenate([index[rng.integers(0, len(index), 9000)].astype("S14"),
+                            np.array([b"miss%d" % i for i in range(50)], dtype="S14")])
+    rng.shuffle(query)
+    a, ma = O.id_map(index, query)
+    for th in (1, 4):
+        b, mb = O.bytes_map(index, query, threads=th)
+        np.testing.assert_array_equal(a, b)
+        assert ma == mb
