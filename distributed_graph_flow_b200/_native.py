@@ -127,6 +127,8 @@ SIGNATURES = {
     "dgfx_id_index_lookup": (_int, [_vp, _i32, _vp, _vp, _i64, _i64, _vp, ctypes.POINTER(_i64), _vp]),
     "dgfx_compact_pairs_workspace_size": (_int, [_i64, ctypes.POINTER(_sz)]),
     "dgfx_compact_pairs": (_int, [_vp, _vp, _i64, _vp, _vp, _vp, ctypes.POINTER(_i64), _vp, _sz, _vp]),
+    "dgfx_timeseries_windows": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "dgfx_gather_segments": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp]),
     "dgfx_subgraph_union_workspace_size": (_int, [_i64, _i64, ctypes.POINTER(_sz)]),
     "dgfx_subgraph_union": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _i64, _i64, _vp, _vp,
                                    _vp, _vp, _vp, _vp, _sz, _vp]),

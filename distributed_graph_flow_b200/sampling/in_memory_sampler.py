@@ -14,6 +14,10 @@ from feature tables uploaded to HBM once. ``sample_batch`` is the zero-copy
 path for a GNN on the same device: the merged batch and its features stay in
 HBM.
 
+With ``slice_timeseries_by_seed`` and seed timestamps, every sampled node's
+``is_timeseries`` features are cut to its seed's past on the device
+(``sampling.temporal``).
+
 Extension beyond the reference: ``sampling_mode=MODE_MOST_RECENT`` (newest-k
 temporal neighbours).
 """
@@ -30,6 +34,8 @@ from distributed_graph_flow_b200.data import in_memory_graph as in_memory_graph_
 from distributed_graph_flow_b200.data import schema as schema_lib
 from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext
 from distributed_graph_flow_b200.sampling import config as config_lib
+from distributed_graph_flow_b200.sampling import temporal as sampling_temporal
+from distributed_graph_flow_b200.util import temporal as temporal_util
 
 MODE_RANDOM = _native.MODE_RANDOM
 MODE_FIRST = _native.MODE_FIRST
@@ -132,6 +138,8 @@ class Sampler:
         self._max_timeseries_len = max_timeseries_len
         self._has_temporal_edgesets = has_temporal_edgesets
         self._store: Optional[DeviceFeatureStore] = None
+        self._ts_cache = None
+        self._slicers: Dict[str, "sampling_temporal.TimeseriesSlicer"] = {}
 
     def set_return_options(self, return_features: bool, return_node_idxs: bool):
         self._return_features = return_features
@@ -181,18 +189,52 @@ class Sampler:
         host = _in_memory_sampler_ext.batch_to_host(merged)
         graphs = _in_memory_sampler_ext.export_graphs(merged, host)
         self._finalize(merged, host, graphs)
-        if ts is not None and self._slice_timeseries_by_seed and self._return_features:
-            self._check_timeseries(ts)
+        if self._slice_timeseries_by_seed and self._return_features:
+            self._slice_timeseries(merged, host, graphs, ts)
         return graphs[0] if single else graphs
 
-    def _check_timeseries(self, ts):
+    def _timeseries_cache(self):
+        if self._ts_cache is None and self._schema is not None:
+            self._ts_cache = temporal_util.extract_timeseries_schema_cache(self._schema)
+        return self._ts_cache
+
+    def _slice_timeseries(self, merged, host, graphs, ts):
+        """Causal slicing of every sampled node's timeseries features by its
+        seed's timestamp (in_memory_sampler.py:270-310), on the device
+        (sampling.temporal.TimeseriesSlicer over the whole merged batch)."""
+        cache = self._timeseries_cache()
+        if ts is None:
+            if cache is not None and cache.has_timeseries:
+                raise ValueError(
+                    "`seed_timestamps` must be provided when `slice_timeseries_by_seed=True` and the schema contains"
+                    " `is_timeseries=True` features."
+                )
+            return
         if self._schema is None:
             raise ValueError(
                 "schema must be provided when `slice_timeseries_by_seed=True` and `seed_timestamps` are passed."
             )
-        for ns in self._schema.node_sets.values():
-            if any(f.is_timeseries for f in ns.features.values()):
-                raise NotImplementedError("causal slicing of is_timeseries features is not supported by this sampler")
+        node_ids_host, node_off = host[0], host[1]
+        B = merged.B
+        for s, ns_name in enumerate(merged.nodeset_names):
+            specs = cache.node_sets.get(ns_name)
+            if not specs or ns_name not in self._full_graph.node_sets:
+                continue
+            slicer = self._slicers.get(ns_name)
+            if slicer is None:
+                slicer = sampling_temporal.TimeseriesSlicer(self._full_graph.node_sets[ns_name].features, specs,
+                                                            self._cc_sampler._device)
+                self._slicers[ns_name] = slicer
+            if not slicer.groups:
+                continue
+            a = int(node_off[s * B])
+            counts = np.diff(node_off[s * B:(s + 1) * B + 1])
+            cutoffs = np.repeat(np.asarray(ts, np.int64), counts)
+            sliced = slicer.slice(node_ids_host[a:int(node_off[(s + 1) * B])], cutoffs, self._max_timeseries_len)
+            for i, g in enumerate(graphs):
+                lo, hi = int(node_off[s * B + i]) - a, int(node_off[s * B + i + 1]) - a
+                for fname, col in sliced.items():
+                    g.node_sets[ns_name].features[fname] = col[lo:hi]
 
     def _finalize(self, merged, host, graphs):
         """Adds features (gathered on device over the merged batch) and drops

@@ -486,6 +486,28 @@ int dgfx_compact_pairs(const int64_t* d_src, const int64_t* d_dst, int64_t num_p
                        dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Causal windows of per-node time series. Replaces the per-node loop of
+ * filter_timeseries_by_timestamp (dgf/src/sampling/temporal.py:24-130).
+ * Node r's timestamp series is d_times[d_row_offsets[r] .. d_row_offsets[r+1])
+ * (sorted). For query i (node d_rows[i], cutoff d_cutoffs[i]) the window is
+ * the entries with time <= cutoff, keeping the last max_len of them
+ * (max_len < 0: all): d_rel_start[i] = its first entry relative to the row,
+ * d_len[i] = its length. d_workspace: 8 bytes. Synchronises `stream`; a row
+ * id outside [0, num_rows) is DGFX_ERR_INVALID_ARGUMENT.
+ * dgfx_gather_segments copies segment i, d_len[i] elements of elem_bytes
+ * starting at element d_start[i] of d_values, to element d_out_offsets[i] of
+ * d_out (packed ragged output).
+ * ------------------------------------------------------------------------ */
+int dgfx_timeseries_windows(const int64_t* d_row_offsets, const int64_t* d_times,
+                            int64_t num_rows, const int64_t* d_rows,
+                            const int64_t* d_cutoffs, int64_t n, int64_t max_len,
+                            int64_t* d_rel_start, int64_t* d_len, void* d_workspace,
+                            dgfx_stream stream);
+int dgfx_gather_segments(const void* d_values, int64_t elem_bytes, const int64_t* d_start,
+                         const int64_t* d_len, const int64_t* d_out_offsets, int64_t n,
+                         void* d_out, dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
  * Subgraph around a set of seeds. Replaces the numbering and edge set of
  * SubGraphExtractor (dgf/src/sampling/in_memory_sampler_ext.cc:600-772) as
  * the union of a merged batch of per-seed samples (dgfx_sample_out layout,

@@ -21,7 +21,8 @@ dgf/src/transform/temporal.py:95-103, and a pure-Python restatement of
 SubGraphExtractor (in_memory_sampler_ext.cc:600-772) for small graphs in the
 deterministic modes; the C++ libraries also restate the random-walk negative
 sampler (in_memory_sampler_ext.cc:774-948) and the raw-id mapping of GF
-graph loading (dgf/src/io/io_ext.cc:26-170).
+graph loading (dgf/src/io/io_ext.cc:26-170), and a numpy restatement of the
+causal timeseries slicing (dgf/src/sampling/temporal.py:24-63).
 """
 
 from __future__ import annotations
@@ -389,6 +390,33 @@ def bytes_map(index_ids: np.ndarray, query_ids: np.ndarray, threads: int = 1):
                          b.tobytes() if b.size else b"", len(b), max(1, b.dtype.itemsize), int(threads), _p(out),
                          _p(mm))
     return out, int(mm[0])
+
+
+# ---------------------------------------------------------------------------
+# Causal timeseries slicing (dgf/src/sampling/temporal.py:24-63).
+# ---------------------------------------------------------------------------
+def timeseries_window(times, values, cutoff: int, max_len: Optional[int]):
+    """One entity's window of one feature: entries with time <= cutoff
+    (np.searchsorted side="right"), the last max_len of them."""
+    end = int(np.searchsorted(np.asarray(times), cutoff, side="right"))
+    start = max(0, end - max_len) if max_len is not None else 0
+    return np.asarray(values)[slice(start, end)]
+
+
+def filter_timeseries(features: dict, groups, cutoffs, max_len: Optional[int]) -> dict:
+    """{feature: object array} for entities 0..n-1 with per-entity cutoffs;
+    groups = [(timestamp feature or None, [feature names])]."""
+    out = {}
+    for ts_name, names in groups:
+        if ts_name is None:
+            continue
+        times = features[ts_name]
+        for f in names:
+            col = np.empty(len(cutoffs), dtype=object)
+            for i, c in enumerate(cutoffs):
+                col[i] = timeseries_window(times[i], features[f][i], int(c), max_len)
+            out[f] = col
+    return out
 
 
 # ---------------------------------------------------------------------------

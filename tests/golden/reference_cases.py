@@ -303,3 +303,33 @@ GF_N2_SHARDS = [
 GF_E1 = {"#source": [b"1", b"1"], "#target": [b"1", b"2"], "#id": [b"a", b"b"]}
 GF_E2 = {"#source": [b"1", b"1"], "#target": [1, 2], "#id": [b"A", b"B"]}
 GF_ADJACENCY = {"e1": [[0, 0], [0, 1]], "e2": [[0, 0], [0, 1]]}
+
+# ---------------------------------------------------------------------------
+# Causal timeseries slicing: dgf/src/sampling/temporal_test.py:67-298 and
+# in_memory_sampler_test.py:1279-1460. Each case: (name, {feature: rows},
+# groups [(timestamp feature, [features])], target, max_len, expected
+# {feature: rows}).
+# ---------------------------------------------------------------------------
+TS_FILTER_CASES = [
+    ("scalar target 28, max 2 :67-131",
+     {"time": [[10, 20, 30, 40, 50], [5, 15, 25, 35]], "signal": [[1.0, 2.0, 3.0, 4.0, 5.0], [0.5, 1.5, 2.5, 3.5]]},
+     [("time", ["time", "signal"])], 28, 2,
+     {"time": [[10, 20], [15, 25]], "signal": [[1.0, 2.0], [1.5, 2.5]]}),
+    ("group without timestamps left alone :133-183",
+     {"time": [[10, 20, 30, 40]], "signal": [[1.0, 2.0, 3.0, 4.0]], "waveform": [[0.1, 0.2, 0.3, 0.4]]},
+     [("time", ["time", "signal"]), (None, ["waveform"])], 25, None,
+     {"time": [[10, 20]], "signal": [[1.0, 2.0]], "waveform": [[0.1, 0.2, 0.3, 0.4]]}),
+    ("edge set target 20 :185-240",
+     {"timestamps": [[10, 20, 30, 40]], "edge_sig": [[1.0, 2.0, 3.0, 4.0]]},
+     [("timestamps", ["timestamps", "edge_sig"])], 20, None,
+     {"timestamps": [[10, 20]], "edge_sig": [[1.0, 2.0]]}),
+    ("cache and filter target 30 :262-294",
+     {"time": [[10, 20, 30, 40, 50]], "signal": [[1.0, 2.0, 3.0, 4.0, 5.0]]},
+     [("time", ["time", "signal"])], 30, None,
+     {"time": [[10, 20, 30]], "signal": [[1.0, 2.0, 3.0]]}),
+]
+# Sampler level (in_memory_sampler_test.py:1279-1400): alerts (#creation_time
+# 30, 60) <- hardware (one node, time 10..70, signal 1..7), one hop reversed,
+# temporal sampling, max_timeseries_len 3, seeds [0, 1] at [30, 60].
+TS_SAMPLER_TIME = [10, 20, 30, 40, 50, 60, 70]
+TS_SAMPLER_EXPECTED = [([10, 20, 30], [1.0, 2.0, 3.0]), ([40, 50, 60], [4.0, 5.0, 6.0])]
