@@ -323,3 +323,36 @@ def test_oracle_id_maps_agree():
         b, mb = O.bytes_map(index, query, threads=th)
         np.testing.assert_array_equal(a, b)
         assert ma == mb
+
+
+def test_parquet_write_read_round_trip(tmp_path):
+    """write_numpy_dict then the reader's column conversion give back every
+    feature kind of the GF fixture (scalars, fixed and variable lists, bytes),
+    split over several shards."""
+    from distributed_graph_flow_b200.io import parquet as P
+
+    exp = _expected_graph()
+    for name, ns in exp.node_sets.items():
+        P.write_numpy_dict(ns.features, name, str(tmp_path), _schema().node_sets[name].features, num_shards=2)
+        table = P.read_tables(P.list_shards(str(tmp_path / name)))
+        got, count = P.table_to_numpy_dict(table)
+        assert count == ns.num_nodes
+        for k, v in ns.features.items():
+            _assert_values(got[k], v, f"{name}.{k}")
+
+
+def test_fix_schema_suspicious_shapes():
+    from distributed_graph_flow_b200.data import schema as S
+    from distributed_graph_flow_b200.io import graph_in_memory as gim
+
+    F = S.FeatureSchema
+    s = S.GraphSchema(node_sets={"n": S.NodeSchema({"#id": F(S.FeatureFormat.BYTES, shape=(None, 1)),
+                                                   "x": F(S.FeatureFormat.FLOAT_32, shape=(None, 4))})},
+                      edge_sets={})
+    gim.fix_schema(s)
+    f = s.node_sets["n"].features
+    assert f["#id"].shape == () and f["x"].shape == (4,)
+    assert f["#id"].semantic == S.FeatureSemantic.PRIMARY_ID
+    with pytest.raises(ValueError, match="no feature look like a primary key"):
+        gim.fix_schema(S.GraphSchema(node_sets={"m": S.NodeSchema({"y": F(S.FeatureFormat.INTEGER_64)})},
+                                     edge_sets={}))
