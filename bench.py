@@ -141,25 +141,35 @@ class ClockSampler:
                 "source": "nvml" if self._nvml is not None else "nvidia-smi"}
 
 
+TIMING = {}
+
+
 def timed(fn, steps, sync_fn, name="timed", finish=None):
-    """Device time (ms per call) of `steps` calls bracketed by syncs, inside
-    an NVTX range (so profilers can be restricted to the timed region).
-    `finish` joins side streams into the timing stream before the end event."""
+    """Device time of `steps` calls bracketed by syncs, inside an NVTX range
+    (so profilers can be restricted to the timed region). An event is
+    recorded on the launching stream before every call and after the last
+    one; the result is the MEDIAN of the per-call intervals in ms (the mean
+    over the whole region is kept in TIMING[name]). `finish` joins side
+    streams into the timing stream before the end event, so the last
+    interval includes their drain."""
     import torch
 
     sync_fn()
-    s = torch.cuda.Event(enable_timing=True)
-    e = torch.cuda.Event(enable_timing=True)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     torch.cuda.nvtx.range_push(name)
-    s.record()
     for i in range(steps):
+        ev[i].record()
         fn(i)
     if finish is not None:
         finish()
-    e.record()
+    ev[steps].record()
     sync_fn()
     torch.cuda.nvtx.range_pop()
-    return s.elapsed_time(e) / steps
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    total = ev[0].elapsed_time(ev[steps])
+    TIMING[name] = {"median_ms": statistics.median(per), "mean_ms": total / steps, "steps": steps,
+                    "min_ms": min(per), "max_ms": max(per)}
+    return statistics.median(per)
 
 
 def count_dgfx_launches(fn):
@@ -313,9 +323,12 @@ def bench_large(args, rank, world, dev):
                                      "gbs": gather_bytes / ms_gather / 1e6}
     dom = max(kernels, key=lambda k: kernels[k]["ms"])
     traffic = ncu_traffic().get(dom, {}).get("bytes_per_launch")
-    roof = {"kernel": dom, "bound": "hbm", "achieved": round(kernels[dom]["gbs"], 1), "peak": hbm,
-            "peak_kind": peak_kind, "unit": "GB/s", "frac": round(kernels[dom]["gbs"] / hbm, 4),
-            "traffic": traffic}
+    roof = {"kernel": dom, "bound": "latency" if dom == "sampler" else "hbm",
+            "achieved": round(kernels[dom]["gbs"], 1), "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": round(kernels[dom]["gbs"] / hbm, 4), "traffic": traffic}
+    if dom == "sampler":
+        roof["note"] = ("dependent random row / column loads per hop: bound by memory latency, reported against "
+                        "the measured HBM copy bandwidth")
 
     # End to end through the public API with host buffers.
     if args.minimal:
@@ -336,15 +349,12 @@ def bench_large(args, rank, world, dev):
         "vs_baseline": None,
         "dtype": "int64 ids / bf16 features",
         "data": "synthetic (seeded power-law graph with the sizes of the 1.6B-edge graph; N(0,1) bf16 features)",
-        "config": {"workload": "large sharded sampling: 111,059,956 nodes, 1,615,685,872 edges, Zipf(2.0), "
-                               "fanout [15,10,5], 8192 seeds/GPU, bf16 128-d features node-range partitioned",
-                   "seeds_per_gpu": B_SEEDS, "fanout": FANOUT, "nodes_per_step_rank0": total_nodes,
-                   "edges_per_step_rank0": total_edges, "l2": "inputs larger than L2 (7.4 GB CSR, 28 GB features)",
-                   "parallelism": f"seed-sharded dp{world}, topology replicated, features node-range partitioned",
-                   "pipelined": bool(args.overlap and world >= 1),
-                   "step": "sample a batch + gather every sampled node's features (gather of step i overlaps "
-                           "sampling of step i+1 on a second stream)" if args.overlap else
-                           "sample a batch + gather every sampled node's features"},
+        "config": large_config(args, world),
+        "workload_stats": {"nodes_per_step_rank0": total_nodes, "edges_per_step_rank0": total_edges,
+                           "pipelined": bool(args.overlap),
+                           "pipelining": "the feature gather of step i overlaps the sampling of step i+1 on a "
+                                         "second stream" if args.overlap else "none",
+                           "timing": TIMING.get("step")},
         "clocks": clk,
         "roofline": roof,
         "kernels": kernels,
@@ -354,15 +364,28 @@ def bench_large(args, rank, world, dev):
     }
     cache_info = getattr(sharded.features, "cache_info", None)
     if cache_info is not None:
-        res["config"]["halo_cache"] = dict(cache_info, what="replicated read-only copy of the most-referenced "
-                                                            "feature rows (by in-degree); ownership stays "
-                                                            "node-range partitioned")
-    res["config"]["halo"] = {"p2p": "peer loads over NVLink (one gather kernel)",
-                             "exchange": "bulk peer exchange (bucket by owner, owner-local gather, sequential "
-                                         "NVLink pulls; NCCL one-word barriers)" if world > 1 else
-                                         "local gather (one rank)",
-                             "nccl": "NCCL all-to-all halo exchange"}[args.halo]
+        res["workload_stats"]["halo_cache"] = dict(cache_info)
     return res, (spec, index, table, cc, plan, seeds, W, sharded)
+
+
+def large_config(args, world):
+    """The headline workload's configuration (identical in both arms)."""
+    cfg = {"workload": "large sharded sampling: 111,059,956 nodes, 1,615,685,872 edges, Zipf(2.0), "
+                       "fanout [15,10,5], 8192 seeds/GPU, bf16 128-d features node-range partitioned",
+           "seeds_per_gpu": B_SEEDS, "fanout": FANOUT, "feature_dim": FEAT_DIM,
+           "l2": "inputs larger than L2 (7.4 GB CSR, 28 GB features)",
+           "parallelism": f"seed-sharded dp{world}, topology replicated, features node-range partitioned",
+           "step": "sample a batch of 8192 seeds + gather every sampled node's features"}
+    if args.scale != 1.0:
+        cfg["scale"] = args.scale
+    if world > 1:
+        cfg["halo"] = {"p2p": "peer loads over NVLink (one gather kernel)",
+                       "exchange": "bulk peer exchange (bucket by owner, owner-local gather, NVLink pushes, "
+                                   "device barrier)",
+                       "nccl": "NCCL all-to-all halo exchange"}[args.halo]
+        if args.halo == "exchange":
+            cfg["halo_cache_fraction"] = args.halo_cache
+    return cfg
 
 
 def ctypes_stats(cc):
@@ -455,16 +478,22 @@ def cpu_sampler_from_index(index, num_nodes, plan, temporal=False, fill_threads=
     return s, ("reference" if ref else "port")
 
 
-def cpu_large_baseline(index, table_host, num_nodes, plan, seeds, budget_s=15.0, threads=None):
+def cpu_large_baseline(index, table_host, num_nodes, plan, seeds, budget_s=15.0, threads=None, parity=None):
     """Samples (topology via the reference's compiled samplers when built,
     else the restatement) + numpy feature gather per sample, like
-    add_features_to_samples. Returns (subgraphs/s, cores, kind, sample desc)."""
+    add_features_to_samples. Returns (subgraphs/s, cores, kind, sample desc,
+    parity). With parity = (device FIRST-mode sampler, device seeds), one
+    FIRST-mode batch (oldest-first) of the device is first compared with the
+    oracle's over the same index, outside the timing."""
     threads = threads or host_cores()
     need = (index.rowptr.numel() + index.col.numel()) * 8 * 1.6 / 1e9 + 4
     if host_mem_gb() < need:
         raise RuntimeError(f"CPU baseline infeasible at this size: needs ~{need:.0f} GB host memory, "
                            f"{host_mem_gb():.0f} GB available")
     s, kind = cpu_sampler_from_index(index, num_nodes, plan)
+    par = None
+    if parity is not None:
+        par = first_mode_parity(s, parity[0], parity[1], None)
     done = 0
     t_sample = t_feat = 0.0
     t_start = time.perf_counter()
@@ -485,7 +514,29 @@ def cpu_large_baseline(index, table_host, num_nodes, plan, seeds, budget_s=15.0,
         done += len(batch)
     rate = done / (t_sample + t_feat)
     return rate, threads, kind, {"seeds": done, "batches": i, "sample_s": round(t_sample, 3),
-                                 "feature_gather_s": round(t_feat, 3), "features": table_host is not None}
+                                 "feature_gather_s": round(t_feat, 3), "features": table_host is not None}, par
+
+
+def first_mode_parity(oracle_sampler, device_first, seeds_dev, seed_ts_dev):
+    """One FIRST-mode batch (oldest-first under a cutoff; the reference's
+    debug_sampling) of the device sampler against the oracle's over the same
+    index: True when node ids, local edges and offsets are identical. The
+    oracle handle is returned to random mode afterwards."""
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+    from oracle import oracle as O
+
+    oracle_sampler.set_mode(O.MODE_FIRST)
+    try:
+        got = ext.batch_to_host(device_first.sample_merged(seeds_dev, seed_ts_dev))
+        device_first.check()
+        exp = oracle_sampler.sample_merged(seeds_dev.cpu().numpy(),
+                                           None if seed_ts_dev is None else seed_ts_dev.cpu().numpy(),
+                                           threads=host_cores())
+        same = all(np.array_equal(a, b) for a, b in zip(got, exp))
+        return {"first_mode_batch_bit_exact": bool(same), "seeds": int(seeds_dev.numel()),
+                "nodes": int(got[1][-1]), "edges": int(got[3][-1])}
+    finally:
+        oracle_sampler.set_mode(O.MODE_RANDOM)
 
 
 def host_mem_gb():
@@ -541,23 +592,31 @@ def bench_spmm(dev, steps, scale=1.0):
                      "peak_kind": peak_kind, "frac": round(gbs / hbm, 4),
                      "traffic": ncu_traffic().get(f"spmm_{name}", {}).get("bytes_per_launch")}
         del x, y
-    # CPU baseline: scipy CSR @ dense on a bounded row sample (fp32).
+    # CPU baseline: torch-CPU sparse CSR @ dense (fp32) on all host cores
+    # over a bounded row sample (jax is not installed, so jax.ops.segment_sum
+    # on CPU cannot run; torch's CSR SpMM stands in for it).
     try:
-        import scipy.sparse as sp
-
-        rows = 200_000
-        rp = rowptr[: rows + 1].cpu().numpy()
-        c = col[: rp[-1]].cpu().numpy()
-        v = val[: rp[-1]].cpu().numpy()
-        xh = synth.normal_features(0, spec.num_nodes, F, 5, torch.float32, dev).cpu().numpy()
-        a = sp.csr_matrix((v, c, rp), shape=(rows, spec.num_nodes))
-        t0 = time.perf_counter()
-        _ = a @ xh
-        dt = time.perf_counter() - t0
-        alg = 8 * (rows + 1) + len(c) * 8 + len(c) * F * 4 + rows * F * 4
-        out["cpu_baseline"] = {"value": round(alg / dt / 1e9, 2), "unit": "GB/s (same byte count)", "cores": 1,
-                               "kind": "scipy CSR @ dense (jax is not installed; scipy stands in)",
-                               "sample": f"first {rows} rows, fp32"}
+        th = host_cores()
+        torch.set_num_threads(th)
+        rows = 400_000
+        rp = rowptr[: rows + 1].cpu()
+        nnz_s = int(rp[-1])
+        c = col[:nnz_s].cpu().long()
+        v = val[:nnz_s].cpu()
+        xh = synth.normal_features(0, spec.num_nodes, F, 5, torch.float32, dev).cpu()
+        a = torch.sparse_csr_tensor(rp, c, v, size=(rows, spec.num_nodes))
+        _ = torch.sparse.mm(a, xh)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 8.0:
+            _ = torch.sparse.mm(a, xh)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        alg = 8 * (rows + 1) + nnz_s * 8 + nnz_s * F * 4 + rows * F * 4
+        out["cpu_baseline"] = {"value": round(alg / dt / 1e9, 2), "unit": "GB/s (same byte count)", "cores": th,
+                               "kind": "port (torch-CPU CSR SpMM stands in for jax.ops.segment_sum on CPU)",
+                               "sample": f"first {rows} rows ({nnz_s} nnz), fp32, {reps} reps, "
+                                         f"{dt * 1e3:.1f} ms each"}
+        out["speedup_vs_cpu_fp32"] = round(out["fp32"]["achieved_gbs"] / out["cpu_baseline"]["value"], 1)
     except Exception as exc:  # noqa: BLE001
         out["cpu_baseline"] = {"unavailable": str(exc)}
     return out
@@ -1044,53 +1103,99 @@ def bench_hetero(dev, steps, scale=1.0):
 # ---------------------------------------------------------------------------
 # Reference arm: the reference's CPU sampler on the host cores.
 # ---------------------------------------------------------------------------
+def _chain_plan(nodeset, edgeset, widths):
+    """A forward chain plan (root -hop_width[0]-> ... ) as plain objects with
+    the SamplingPlan field names, so the reference arm imports nothing from
+    the library."""
+    from types import SimpleNamespace
+
+    node = SimpleNamespace(nodeset=nodeset, children=[])
+    for w in reversed(widths):
+        node = SimpleNamespace(nodeset=nodeset, children=[
+            SimpleNamespace(edgeset=edgeset, reversed=False, hop_width=int(w), node=node)])
+    return SimpleNamespace(root=node, with_replacement=False)
+
+
+# The large workload's generator parameters (the same GraphSpec as
+# distributed_graph_flow_b200.synth.LARGE_SHARDED), repeated here so the
+# reference arm does not import the library.
+LARGE_NODES, LARGE_EDGES, LARGE_ALPHA, LARGE_MAX_DEG, LARGE_SEED = 111_059_956, 1_615_685_872, 2.0, 20_000, 4
+
+
 def reference_arm(args, rank, world):
+    """The reference's own CPU sampler on the host cores, on rank 0 only.
+
+    Nothing here touches the GPU or loads the library: the graph, the seeds
+    and the feature table come from the host restatement of the seeded
+    generators (oracle/synth_cpu.h; the same graph, seeds and features as
+    the device arm), the adjacency index is built by the reference's own
+    AdjacencyIndex::CreateFromEdgeList (oracle/_ref, compiled from the
+    reference's unmodified in_memory_sampler.cc; one call per source range
+    on all host cores, concatenated), and each step samples one batch of
+    8192 seeds with the reference's per-node samplers under the restated
+    SampleBuilder / Sampler::Sample driver, then gathers every sampled
+    node's feature row with numpy per sample (add_features_to_samples).
+    Setup is untimed; W warm-up and K timed steps follow."""
     if rank != 0:
         return None
-    import torch
+    from oracle import oracle as O
 
-    from distributed_graph_flow_b200 import synth
-
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
-    spec = large_spec(args.scale)
-    need_gb = 14 + 30
+    cores = host_cores()
+    ref = O.available(ref=True)
+    scale = args.scale
+    n = max(1000, int(LARGE_NODES * scale)) if scale != 1.0 else LARGE_NODES
+    E = int(LARGE_EDGES * scale) if scale != 1.0 else LARGE_EDGES
     avail = host_mem_gb()
-    from distributed_graph_flow_b200.sampling import config as cfg
+    # Index (8 B per edge + 8 B per node) + build transients (~16 B per edge)
+    # + the bf16 feature table.
+    need_gb = (24 * E + 8 * n) / 1e9 + n * FEAT_DIM * 2 / 1e9 + 8
+    base = {"impl": "reference", "metric": "sampled subgraphs/sec", "unit": "subgraphs/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int64 ids / bf16 features",
+            "data": "synthetic (the device arm's seeded graph, seeds and features, generated on the host)",
+            "config": large_config(args, world)}
+    if avail < need_gb:
+        return dict(base, unavailable=f"host memory: the reference index and feature table need ~{need_gb:.0f} GB, "
+                                      f"{avail:.0f} GB available")
+    plan = _chain_plan("paper", "cites", FANOUT)
+    t0 = time.perf_counter()
+    s = O.OracleSampler.from_synth(n, E, LARGE_ALPHA, LARGE_MAX_DEG, LARGE_SEED, plan, mode=O.MODE_RANDOM,
+                                   num_threads=cores, seed=99, ref=ref, build_threads=cores)
+    t_index = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    table = O.synth_normal_features(0, n, FEAT_DIM, LARGE_SEED + 100, bf16=True, threads=cores)
+    t_feat = time.perf_counter() - t0
+    W, K = args.warmup, args.steps
+    seeds = O.synth_uniform_int((W + K) * B_SEEDS, 0, n, 77, 5, threads=cores).reshape(W + K, B_SEEDS)
 
-    plan = cfg.explicit_plan("paper", "cites", FANOUT)
-    # Inputs (untimed): the same seeded graph, built on the device and copied
-    # to the host in CreateFromEdgeList order.
-    index, _, _ = synth.build_graph(spec, dev)
-    table_host = None
-    if avail > need_gb + 20:
-        table_host = synth.normal_features(0, spec.num_nodes, FEAT_DIM, spec.seed + 100, torch.bfloat16, dev).cpu().view(
-            torch.int16).numpy()
-    seeds = synth.uniform_int((args.warmup + args.steps) * B_SEEDS, 0, spec.num_nodes, 77, 5, dev).view(
-        -1, B_SEEDS).cpu().numpy()
-    budget = max(20.0, 12.0 * args.steps)
-    rate, cores, kind, sample = cpu_large_baseline(index, table_host, spec.num_nodes, plan, seeds, budget_s=budget)
-    res = {
-        "impl": "reference",
-        "metric": "sampled subgraphs/sec",
-        "value": round(rate, 1),
-        "unit": "subgraphs/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "int64 ids / bf16 features",
-        "data": "synthetic (same seeded graph as the dgfx arm)",
-        "config": {"workload": "large sharded sampling: 111,059,956 nodes, 1,615,685,872 edges, Zipf(2.0), "
-                               "fanout [15,10,5], 8192 seeds/GPU, bf16 128-d features node-range partitioned",
-                   "host_mem_available_gb": round(avail, 1)},
-        "cpu_baseline": {"value": round(rate, 1), "unit": "subgraphs/s", "cores": cores, "kind": kind,
-                         "sample": json.dumps(sample)},
-        "e2e": {"value": round(rate, 1), "unit": "subgraphs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    return res
+    def step(batch):
+        nc, _, nodes, _, _ = s.sample_raw(batch, threads=cores)
+        off = 0
+        for c in nc[:, 0]:
+            _ = table[nodes[off:off + c]]
+            off += c
+
+    for i in range(W):
+        step(seeds[i])
+    per = []
+    for i in range(K):
+        t1 = time.perf_counter()
+        step(seeds[W + i])
+        per.append(time.perf_counter() - t1)
+    ms = statistics.median(per) * 1e3
+    rate = B_SEEDS / (ms / 1e3)
+    return dict(base, value=round(rate, 1), ms_per_step=round(ms, 3),
+                cpu_baseline={"value": round(rate, 1), "unit": "subgraphs/s", "cores": cores,
+                              "kind": "reference" if ref else "port",
+                              "sample": f"{K} timed batches of {B_SEEDS} seeds (median), after {W} warm-up; "
+                                        f"topology by the reference's compiled samplers on {cores} threads + "
+                                        f"numpy feature gather per sample"},
+                e2e={"value": round(rate, 1), "unit": "subgraphs/s", "h2d_bytes_per_step": 0,
+                     "d2h_bytes_per_step": 0},
+                setup={"index_build_s": round(t_index, 1), "feature_table_s": round(t_feat, 1),
+                       "index": "reference AdjacencyIndex::CreateFromEdgeList per source range" if ref else
+                                "restated CreateFromEdgeList per source range",
+                       "host_mem_available_gb": round(avail, 1)})
 
 
 def main():
@@ -1120,13 +1225,14 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
-    import torch
-
     if args.impl == "reference":
         # Rank 0 alone times the reference's CPU sampler; other ranks exit.
+        # No GPU, torch or library code runs in this arm.
         if rank == 0:
             print(json.dumps(reference_arm(args, rank, world)), flush=True)
         return
+
+    import torch
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -1150,10 +1256,18 @@ def main():
             if host_mem_gb() > 80:
                 table_host = table.cpu().view(torch.int16).numpy()
             try:
-                rate, cores, kind, sample = cpu_large_baseline(index, table_host, spec.num_nodes, plan,
-                                                               seeds.cpu().numpy(), budget_s=15.0)
+                from distributed_graph_flow_b200 import _native
+                from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+
+                first = ext.create_device_sampler(plan, ["paper"], [spec.num_nodes], ["cites"], [index], [None],
+                                                  _native.MODE_FIRST, seed=1234)
+                rate, cores, kind, sample, par = cpu_large_baseline(index, table_host, spec.num_nodes, plan,
+                                                                    seeds.cpu().numpy(), budget_s=15.0,
+                                                                    parity=(first, seeds[W]))
+                del first
                 res["cpu_baseline"] = {"value": round(rate, 1), "unit": "subgraphs/s", "cores": cores, "kind": kind,
                                        "sample": json.dumps(sample)}
+                res["parity"] = {"large_sharded": par}
             except Exception as exc:  # noqa: BLE001
                 res["cpu_baseline"] = {"unavailable": str(exc)}
             del table_host

@@ -133,7 +133,7 @@ SIGNATURES = {
     "dgfx_subgraph_union": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _i64, _i64, _vp, _vp,
                                    _vp, _vp, _vp, _vp, _sz, _vp]),
     "dgfx_merge_edgeset": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
-    "dgfx_synth_graph_workspace_size": (_int, [_i64, ctypes.POINTER(_sz)]),
+    "dgfx_synth_graph_workspace_size": (_int, [_i64, _i64, ctypes.POINTER(_sz)]),
     "dgfx_synth_graph": (_int, [_i64, _i64, ctypes.c_double, _i64, _u64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "dgfx_synth_bipartite": (_int, [_i64, _i64, _i64, ctypes.c_double, _i64, _u64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "dgfx_synth_uniform_int": (_int, [_i64, _i64, _i64, _u64, ctypes.c_uint32, _vp, _vp]),

@@ -2,7 +2,10 @@
 // datasets), generated on the device so billion-edge inputs take seconds.
 //
 // Graph: out-degrees follow a discrete power law P(d) ~ d^-alpha (inverse
-// transform of a Pareto draw, floor(u^(-1/(alpha-1))), capped), rescaled
+// transform of a Pareto draw, floor(u^(-1/(alpha-1))), capped: the largest
+// k <= max_degree with k^-(alpha-1) >= u, found by binary search in a table
+// of those thresholds computed once on the host, so a host restatement of
+// the generator gives the same degrees bit for bit), rescaled
 // exactly to num_edges by row pointers rowptr[v] = floor(cum_v * E / S) over
 // the raw degree prefix sums cum (S = total raw degree). Targets follow a
 // power-law popularity: rank r = floor(N * u^3) mapped through the affine
@@ -16,7 +19,9 @@
 // rows.
 #include <cuda_bf16.h>
 
+#include <cmath>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "primitives.cuh"
@@ -30,15 +35,20 @@ __device__ __forceinline__ double u01(uint32_t hi, uint32_t lo) {
   return static_cast<double>(x) * (1.0 / 9007199254740992.0);
 }
 
-__global__ void raw_degree_kernel(int64_t n, double inv_am1, int64_t max_deg, uint32_t k0, uint32_t k1,
+// thr[k - 1] = k^-(alpha - 1) for k = 1 .. max_deg (thr[0] = 1 >= u).
+__global__ void raw_degree_kernel(int64_t n, const double* __restrict__ thr, int64_t max_deg, uint32_t k0, uint32_t k1,
                                   int64_t* __restrict__ deg) {
   for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < n;
        v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const U4 r = philox4x32_10(U4{static_cast<uint32_t>(v), static_cast<uint32_t>(v >> 32), 0x5eedu, 1u}, k0, k1);
     const double u = 1.0 - u01(r.x, r.y);  // (0, 1]
-    double d = floor(pow(u, -inv_am1));
-    if (!(d < static_cast<double>(max_deg))) d = static_cast<double>(max_deg);
-    deg[v] = d < 1.0 ? 1 : static_cast<int64_t>(d);
+    int64_t lo = 1, hi = max_deg;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi + 1) >> 1;
+      if (__ldg(thr + mid - 1) >= u) lo = mid;
+      else hi = mid - 1;
+    }
+    deg[v] = lo;
   }
 }
 
@@ -129,9 +139,12 @@ uint64_t gcd64(uint64_t a, uint64_t b) {
 
 using namespace dgfx;
 
-extern "C" int dgfx_synth_graph_workspace_size(int64_t num_nodes, size_t* bytes) {
-  if (bytes == nullptr || num_nodes < 1) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_synth_graph_workspace_size");
-  *bytes = align_up(sizeof(int64_t) * (num_nodes + 1), 256) + 256 + scan_workspace_bytes(num_nodes + 1) + 1024;
+extern "C" int dgfx_synth_graph_workspace_size(int64_t num_nodes, int64_t max_degree, size_t* bytes) {
+  if (bytes == nullptr || num_nodes < 1 || max_degree < 1) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_synth_graph_workspace_size");
+  }
+  *bytes = align_up(sizeof(int64_t) * (num_nodes + 1), 256) + 256 + scan_workspace_bytes(num_nodes + 1) +
+           align_up(sizeof(double) * static_cast<size_t>(max_degree), 256) + 1024;
   return DGFX_OK;
 }
 
@@ -143,12 +156,19 @@ int synth_graph(int64_t num_src, int64_t num_dst, int64_t num_edges, double alph
     return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_synth_graph: bad arguments");
   }
   size_t need = 0;
-  DGFX_TRY(dgfx_synth_graph_workspace_size(num_src, &need));
+  DGFX_TRY(dgfx_synth_graph_workspace_size(num_src, max_degree, &need));
   if (d_workspace == nullptr || workspace_bytes < need) return fail(DGFX_ERR_WORKSPACE, "dgfx_synth_graph: workspace");
   Arena arena(d_workspace, workspace_bytes);
   int64_t* deg = arena.take<int64_t>(static_cast<size_t>(num_src + 1));
+  double* thr = arena.take<double>(static_cast<size_t>(max_degree));
+  {
+    std::vector<double> h(static_cast<size_t>(max_degree));
+    for (int64_t k = 1; k <= max_degree; ++k) h[k - 1] = std::pow(static_cast<double>(k), -(alpha - 1.0));
+    // Pageable source: the copy has been staged when the call returns.
+    DGFX_CUDA_TRY(cudaMemcpyAsync(thr, h.data(), h.size() * sizeof(double), cudaMemcpyHostToDevice, stream));
+  }
   const uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
-  raw_degree_kernel<<<blocks_for(num_src), 256, 0, stream>>>(num_src, 1.0 / (alpha - 1.0), max_degree, k0, k1, deg);
+  raw_degree_kernel<<<blocks_for(num_src), 256, 0, stream>>>(num_src, thr, max_degree, k0, k1, deg);
   DGFX_CUDA_TRY(cudaGetLastError());
   int64_t* total = arena.take<int64_t>(1);
   DGFX_TRY(exclusive_scan<int64_t>(deg, d_rowptr, num_src, true, arena, stream));

@@ -42,7 +42,7 @@ def rowptr_and_edges(spec: GraphSpec, device, with_edges: bool = True, stream=No
     torch = _native.require_cuda()
     lib = _native.lib()
     need = ctypes.c_size_t()
-    _native.check(lib.dgfx_synth_graph_workspace_size(spec.num_nodes, ctypes.byref(need)))
+    _native.check(lib.dgfx_synth_graph_workspace_size(spec.num_nodes, spec.max_degree, ctypes.byref(need)))
     ws = torch.empty(need.value, dtype=torch.uint8, device=device)
     rowptr = torch.empty(spec.num_nodes + 1, dtype=torch.int64, device=device)
     src = dst = None
@@ -159,7 +159,7 @@ def build_hetero_graph(spec: HeteroSpec, device) -> HeteroGraph:
         s_ns, t_ns, ne = spec.edge_sets[name]
         n_s, n_t = spec.node_sets[s_ns], spec.node_sets[t_ns]
         need = ctypes.c_size_t()
-        _native.check(lib.dgfx_synth_graph_workspace_size(n_s, ctypes.byref(need)))
+        _native.check(lib.dgfx_synth_graph_workspace_size(n_s, spec.max_degree, ctypes.byref(need)))
         ws = torch.empty(need.value, dtype=torch.uint8, device=device)
         rowptr = torch.empty(n_s + 1, dtype=torch.int64, device=device)
         src = torch.empty(ne, dtype=torch.int64, device=device)

@@ -564,12 +564,12 @@ int dgfx_merge_edgeset(const int64_t* d_node_offsets,
  * list src/dst int64[num_edges]. Pure function of its arguments.
  * dgfx_synth_bipartite: the same with sources [0, num_src) and targets
  * drawn from [0, num_dst) (an edge type between two node sets; workspace as
- * dgfx_synth_graph_workspace_size(num_src)).
+ * dgfx_synth_graph_workspace_size(num_src, max_degree)).
  * dgfx_synth_uniform_int: out[i] uniform in [lo, hi) (Philox stream id).
  * dgfx_synth_normal_features: rows [node_begin, node_begin + count) of a
  * N(0,1) [*, dim] matrix keyed by node id (partition independent).
  * ------------------------------------------------------------------------ */
-int dgfx_synth_graph_workspace_size(int64_t num_nodes, size_t* bytes);
+int dgfx_synth_graph_workspace_size(int64_t num_nodes, int64_t max_degree, size_t* bytes);
 int dgfx_synth_graph(int64_t num_nodes, int64_t num_edges, double alpha,
                      int64_t max_degree, uint64_t seed, int64_t* d_rowptr,
                      int64_t* d_src, int64_t* d_dst, void* d_workspace,

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "grow.h"
+#include "synth_cpu.h"
 
 namespace {
 thread_local std::string g_oracle_error;
@@ -186,6 +187,141 @@ void* oracle_sampler_create_csr(int n_nodesets, const std::int64_t* num_nodes, i
   if (seed >= 0) s.rng.seed(static_cast<std::uint64_t>(seed));
   else s.rng.seed(std::random_device()());
   return h.release();
+}
+
+// A sampler over one homogeneous synthetic edge set (synth_cpu.h: the
+// library's power-law generator restated on the host, optional uniform
+// integer edge timestamps), indexed by OracleCreate — on the reference
+// build, the reference's own AdjacencyIndex::CreateFromEdgeList — with no
+// GPU involved. The edge list is cut into contiguous source-node ranges and
+// each range is indexed by its own CreateFromEdgeList call (sources
+// renumbered from the range start) on build_threads host threads; because
+// the index sorts by source first, concatenating the ranges' rows gives the
+// index one call over the whole list would build. Returns nullptr on error.
+void* oracle_sampler_create_synth(std::int64_t num_nodes, std::int64_t num_edges, double alpha,
+                                  std::int64_t max_degree, std::uint64_t graph_seed, int has_ts, std::int64_t ts_lo,
+                                  std::int64_t ts_hi, std::uint64_t ts_seed, std::uint32_t ts_stream,
+                                  int n_plan_nodes, const int* node_first_edge, const int* node_num_edges,
+                                  int n_plan_edges, const int* edge_hop_width, const int* edge_child,
+                                  int with_replacement, int mode, int num_threads, std::int64_t seed,
+                                  int build_threads) {
+  auto h = std::make_unique<OracleHandle>();
+  auto& s = h->sampler;
+  s.plan.with_replacement = with_replacement != 0;
+  for (int i = 0; i < n_plan_nodes; ++i) {
+    dgf_oracle::PlanNode n;
+    n.nodeset = 0;
+    for (int j = 0; j < node_num_edges[i]; ++j) n.edges.push_back(node_first_edge[i] + j);
+    s.plan.nodes.push_back(n);
+  }
+  for (int i = 0; i < n_plan_edges; ++i) s.plan.edges.push_back({0, false, edge_hop_width[i], edge_child[i]});
+  s.num_nodes.assign(1, num_nodes);
+  s.mode = mode;
+  s.has_temporal = has_ts != 0;
+  s.num_threads = num_threads;
+  s.num_steps = s.plan.nodes.size();
+  s.edgesets.assign(1, {});
+  auto& es = s.edgesets[0];
+  es.need_fwd = true;
+  es.src_ns = es.dst_ns = 0;
+
+  const int nt = std::max(1, build_threads);
+  std::vector<std::int64_t> rowptr(static_cast<std::size_t>(num_nodes) + 1);
+  dgf_synth::graph_rowptr(num_nodes, num_edges, alpha, max_degree, graph_seed, rowptr.data(), nt);
+  std::uint64_t pa = 0, pb = 0;
+  dgf_synth::target_permutation(static_cast<std::uint64_t>(num_nodes), graph_seed, &pa, &pb);
+  const std::uint32_t k0 = static_cast<std::uint32_t>(graph_seed), k1 = static_cast<std::uint32_t>(graph_seed >> 32);
+  // Source ranges of about equal edge counts (4 per thread for balance).
+  const int nchunks = 4 * nt;
+  std::vector<std::int64_t> cut(nchunks + 1, num_nodes);
+  cut[0] = 0;
+  for (int c = 1; c < nchunks; ++c) {
+    const std::int64_t want = num_edges / nchunks * c;
+    cut[c] = std::upper_bound(rowptr.begin(), rowptr.end() - 1, want) - rowptr.begin() - 1;
+    cut[c] = std::max(cut[c], cut[c - 1]);
+  }
+  std::vector<OracleIndex> parts(nchunks);
+  std::vector<dgf_oracle::Status> errs(nchunks);
+  std::atomic<int> next{0};
+  std::vector<std::thread> pool;
+  for (int t = 0; t < nt; ++t) {
+    pool.emplace_back([&]() {
+      for (int c = next++; c < nchunks; c = next++) {
+        const std::int64_t lo = cut[c], hi = cut[c + 1];
+        const std::int64_t e0 = rowptr[lo], e1 = rowptr[hi];
+        std::vector<dgf_oracle::InputIdx> src(static_cast<std::size_t>(e1 - e0)), dst(src.size());
+        std::vector<std::int64_t> ts;
+        for (std::int64_t v = lo; v < hi; ++v) {
+          for (std::int64_t j = rowptr[v]; j < rowptr[v + 1]; ++j) {
+            src[j - e0] = static_cast<dgf_oracle::InputIdx>(v - lo);
+            dst[j - e0] = static_cast<dgf_oracle::InputIdx>(dgf_synth::edge_target(j, num_nodes, pa, pb, k0, k1));
+          }
+        }
+        if (has_ts) {
+          // Edge j's timestamp is element j of the uniform stream.
+          ts.resize(src.size());
+          const std::uint32_t t0 = static_cast<std::uint32_t>(ts_seed), t1 = static_cast<std::uint32_t>(ts_seed >> 32);
+          const std::uint64_t range = static_cast<std::uint64_t>(ts_hi - ts_lo);
+          for (std::int64_t j = e0; j < e1; ++j) {
+            const dgf_synth::U4 r = dgf_synth::philox4x32_10(
+                dgf_synth::U4{static_cast<std::uint32_t>(j), static_cast<std::uint32_t>(j >> 32), ts_stream, 3u}, t0, t1);
+            ts[j - e0] = ts_lo + static_cast<std::int64_t>(
+                                     dgf_synth::bounded64(static_cast<std::uint64_t>(r.y) << 32 | r.x, range));
+          }
+        }
+        errs[c] = OracleCreate(src, dst, has_ts ? ts.data() : nullptr, false, static_cast<std::size_t>(hi - lo),
+                               static_cast<std::size_t>(num_nodes), &parts[c]);
+      }
+    });
+  }
+  for (auto& th : pool) th.join();
+  for (const auto& st : errs) {
+    if (!st.ok()) {
+      g_oracle_error = st.msg;
+      return nullptr;
+    }
+  }
+  OracleIndex idx;
+  idx.source_blocks.resize(static_cast<std::size_t>(num_nodes) + 1);
+  idx.target_node_idxs.resize(static_cast<std::size_t>(num_edges));
+  if (has_ts) idx.timestamps.resize(static_cast<std::size_t>(num_edges));
+  pool.clear();
+  for (int t = 0; t < nt; ++t) {
+    pool.emplace_back([&, t]() {
+      for (int c = t; c < nchunks; c += nt) {
+        const std::int64_t lo = cut[c], hi = cut[c + 1], e0 = rowptr[lo];
+        const OracleIndex& p = parts[c];
+        for (std::int64_t i = 0; i < hi - lo; ++i) idx.source_blocks[lo + i] = e0 + p.source_blocks[i];
+        std::copy(p.target_node_idxs.begin(), p.target_node_idxs.end(), idx.target_node_idxs.begin() + e0);
+        if (has_ts) std::copy(p.timestamps.begin(), p.timestamps.end(), idx.timestamps.begin() + e0);
+        parts[c] = OracleIndex();
+      }
+    });
+  }
+  for (auto& th : pool) th.join();
+  idx.source_blocks[num_nodes] = static_cast<dgf_oracle::InputIdx>(num_edges);
+  es.fwd = std::move(idx);
+  if (seed >= 0) s.rng.seed(static_cast<std::uint64_t>(seed));
+  else s.rng.seed(std::random_device()());
+  return h.release();
+}
+
+// Switches the sampling mode of a sampler handle (kRandom / kFirst /
+// kMostRecent), so one index serves a deterministic parity batch and the
+// timed random-mode baseline.
+void oracle_sampler_set_mode(void* hv, int mode) { static_cast<OracleHandle*>(hv)->sampler.mode = mode; }
+
+// CSR arrays of the sampler's forward index of edge set e (rowptr int64[n+1],
+// col int64[E], ts int64[E] if temporal); sizes via oracle_index_sizes on
+// the sampler's index. Returns 0, or -1 if the edge set has no forward index.
+int oracle_sampler_fwd_csr(void* hv, int e, std::int64_t* rowptr, std::int64_t* col, std::int64_t* ts) {
+  auto* h = static_cast<OracleHandle*>(hv);
+  if (e < 0 || e >= static_cast<int>(h->sampler.edgesets.size()) || !h->sampler.edgesets[e].fwd) return -1;
+  const OracleIndex& x = *h->sampler.edgesets[e].fwd;
+  if (rowptr) for (std::size_t i = 0; i < x.source_blocks.size(); ++i) rowptr[i] = static_cast<std::int64_t>(x.source_blocks[i]);
+  if (col) for (std::size_t i = 0; i < x.target_node_idxs.size(); ++i) col[i] = static_cast<std::int64_t>(x.target_node_idxs[i]);
+  if (ts) for (std::size_t i = 0; i < x.timestamps.size(); ++i) ts[i] = x.timestamps[i];
+  return 0;
 }
 
 // Random-walk negatives for n seeds into out[n * k] (see
@@ -368,6 +504,27 @@ std::int64_t oracle_index_sample(void* hv, int kind, std::int64_t source,
   const std::int64_t n = std::min<std::int64_t>(cap, static_cast<std::int64_t>(res.size()));
   for (std::int64_t i = 0; i < n; ++i) out[i] = static_cast<std::int64_t>(res[i]);
   return static_cast<std::int64_t>(res.size());
+}
+
+// CPU restatement of the synthetic generators (synth_cpu.h).
+void oracle_synth_rowptr(std::int64_t n_src, std::int64_t num_edges, double alpha, std::int64_t max_degree,
+                         std::uint64_t seed, std::int64_t* rowptr, int threads) {
+  dgf_synth::graph_rowptr(n_src, num_edges, alpha, max_degree, seed, rowptr, threads);
+}
+
+void oracle_synth_edges(const std::int64_t* rowptr, std::int64_t n_src, std::int64_t n_dst, std::uint64_t seed,
+                        std::int64_t* src, std::int64_t* dst, int threads) {
+  dgf_synth::graph_edges(rowptr, n_src, n_dst, seed, src, dst, threads);
+}
+
+void oracle_synth_uniform_int(std::int64_t n, std::int64_t lo, std::int64_t hi, std::uint64_t seed,
+                              std::uint32_t stream, std::int64_t* out, int threads) {
+  dgf_synth::uniform_int(n, lo, hi, seed, stream, out, threads);
+}
+
+void oracle_synth_normal_features(std::int64_t node_begin, std::int64_t count, std::int64_t dim, std::uint64_t seed,
+                                  int bf16, void* out, int threads) {
+  dgf_synth::normal_features(node_begin, count, dim, seed, bf16, out, threads);
 }
 
 }  // extern "C"

@@ -102,6 +102,19 @@ def _lib(ref: bool) -> ctypes.CDLL:
         lib.oracle_index_sample.restype = ctypes.c_int64
         lib.oracle_index_sample.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
                                             ctypes.c_int64, ctypes.c_int64, ctypes.c_uint64, _p64, ctypes.c_int64]
+        _i64, _u64, _u32, _dbl = ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_double
+        lib.oracle_synth_rowptr.argtypes = [_i64, _i64, _dbl, _i64, _u64, _p64, ctypes.c_int]
+        lib.oracle_synth_edges.argtypes = [_p64, _i64, _i64, _u64, _p64, _p64, ctypes.c_int]
+        lib.oracle_synth_uniform_int.argtypes = [_i64, _i64, _i64, _u64, _u32, _p64, ctypes.c_int]
+        lib.oracle_synth_normal_features.argtypes = [_i64, _i64, _i64, _u64, ctypes.c_int, ctypes.c_void_p,
+                                                     ctypes.c_int]
+        lib.oracle_sampler_create_synth.restype = ctypes.c_void_p
+        lib.oracle_sampler_create_synth.argtypes = [
+            _i64, _i64, _dbl, _i64, _u64, ctypes.c_int, _i64, _i64, _u64, _u32, ctypes.c_int, _pi, _pi, ctypes.c_int,
+            _pi, _pi, ctypes.c_int, ctypes.c_int, ctypes.c_int, _i64, ctypes.c_int]
+        lib.oracle_sampler_set_mode.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        lib.oracle_sampler_fwd_csr.restype = ctypes.c_int
+        lib.oracle_sampler_fwd_csr.argtypes = [ctypes.c_void_p, ctypes.c_int, _p64, _p64, _p64]
         _libs[key] = lib
     return _libs[key]
 
@@ -238,6 +251,48 @@ class OracleSampler:
             raise OracleError(_err(self.lib))
 
     @classmethod
+    def from_synth(cls, num_nodes, num_edges, alpha, max_degree, graph_seed, plan, ts_range=None, ts_seed=0,
+                   ts_stream=11, mode=MODE_RANDOM, num_threads=0, seed=0, ref=False, build_threads=8):
+        """Sampler over the library's synthetic power-law graph (one node set,
+        one edge set, optional uniform integer edge times drawn from stream
+        `ts_stream` of `ts_seed`), generated on the host by the generator's
+        restatement and indexed by CreateFromEdgeList (the reference's own
+        with ref=True) in source ranges on build_threads threads."""
+        self = cls.__new__(cls)
+        self.lib = _lib(ref)
+        self.nodesets = [plan.root.nodeset]
+        self.edgesets = [plan.root.children[0].edgeset]
+        node_ns, first, num, e_es, e_rev, e_hw, e_child = _flatten_plan(plan, {self.nodesets[0]: 0},
+                                                                        {self.edgesets[0]: 0})
+        if any(e_rev) or any(e != 0 for e in e_es):
+            raise OracleError("from_synth: plans over one forward edge set only")
+        lo, hi = ts_range if ts_range is not None else (0, 1)
+        self._keep = []
+        self.h = self.lib.oracle_sampler_create_synth(
+            int(num_nodes), int(num_edges), float(alpha), int(max_degree), int(graph_seed), int(ts_range is not None),
+            int(lo), int(hi), int(ts_seed), int(ts_stream), len(node_ns), _ints(first), _ints(num), len(e_es),
+            _ints(e_hw), _ints(e_child), int(bool(plan.with_replacement)), int(mode), int(num_threads), int(seed),
+            int(build_threads))
+        if not self.h:
+            raise OracleError(_err(self.lib))
+        self._synth = (int(num_nodes), int(num_edges), ts_range is not None)
+        return self
+
+    def set_mode(self, mode: int) -> None:
+        self.lib.oracle_sampler_set_mode(self.h, int(mode))
+
+    def forward_csr(self):
+        """(rowptr, col, ts or None) of the forward index of a from_synth
+        sampler, as int64 arrays."""
+        n, e, has_ts = self._synth
+        rp = np.empty(n + 1, np.int64)
+        col = np.empty(e, np.int64)
+        ts = np.empty(e, np.int64) if has_ts else None
+        if self.lib.oracle_sampler_fwd_csr(self.h, 0, _p(rp), _p(col), _p(ts)) != 0:
+            raise OracleError("no forward index")
+        return rp, col, ts
+
+    @classmethod
     def from_csr(cls, num_nodes, nodesets, edgesets, csr_fwd, plan, mode=MODE_RANDOM, num_threads=0, seed=0,
                  temporal=False, ref=False, fill_threads=8, csr_bwd=None):
         """Sampler over prebuilt CSR arrays {edgeset: (rowptr int64, col
@@ -315,6 +370,12 @@ class OracleSampler:
         self.lib.oracle_result_copy(self.h, _p(nodes), _p(esrc), _p(edst))
         return nc, ec, nodes, esrc, edst
 
+    def sample_merged(self, seeds, seed_ts=None, masks=None, threads: int = 1):
+        """The batch in the device's merged layout: (node_ids, node_offsets,
+        edges [2, E] of local ids, edge_offsets), node-set major then sample,
+        offsets with a trailing total."""
+        return merged_layout(*self.sample_raw(seeds, seed_ts, masks, threads))
+
     def sample(self, seeds, seed_ts=None, masks=None, threads: int = 1):
         """Per seed: ({nodeset: ids}, {edgeset: [2, E] adjacency})."""
         nc, ec, nodes, esrc, edst = self.sample_raw(seeds, seed_ts, masks, threads)
@@ -353,6 +414,36 @@ class OracleSampler:
 # Raw id -> index (dgf/src/io/io_ext.cc:26-170; integer ids:
 # dgf/src/io/graph_in_memory.py:111-125).
 # ---------------------------------------------------------------------------
+def merged_layout(nc, ec, nodes, esrc, edst):
+    """sample_raw's output (sample-major; node sets / edge sets in order
+    within a sample) rearranged node-set (edge-set) major, then by sample."""
+    B, NS = nc.shape
+    ES = ec.shape[1]
+    n_start = np.concatenate([[0], np.cumsum(nc.sum(1))])
+    e_start = np.concatenate([[0], np.cumsum(ec.sum(1))])
+    n_in = np.concatenate([np.zeros((B, 1), np.int64), np.cumsum(nc, 1)], 1)
+    e_in = np.concatenate([np.zeros((B, 1), np.int64), np.cumsum(ec, 1)], 1)
+    node_off = np.concatenate([[0], np.cumsum(nc.T.ravel())]).astype(np.int64)
+    edge_off = np.concatenate([[0], np.cumsum(ec.T.ravel())]).astype(np.int64)
+    if NS == 1 and ES <= 1:
+        return nodes, node_off, np.stack([esrc, edst]), edge_off
+    node_parts, src_parts, dst_parts = [], [], []
+    for s in range(NS):
+        for i in range(B):
+            a = n_start[i] + n_in[i, s]
+            node_parts.append(nodes[a:a + nc[i, s]])
+    for e in range(ES):
+        for i in range(B):
+            a = e_start[i] + e_in[i, e]
+            src_parts.append(esrc[a:a + ec[i, e]])
+            dst_parts.append(edst[a:a + ec[i, e]])
+
+    def cat(parts):
+        return np.concatenate(parts) if parts else np.zeros(0, np.int64)
+
+    return cat(node_parts), node_off, np.stack([cat(src_parts), cat(dst_parts)]), edge_off
+
+
 def _id_key(v):
     if isinstance(v, (bytes, np.bytes_)):
         return bytes(v).rstrip(b"\0")
@@ -376,6 +467,38 @@ def id_map(index_ids, query_ids):
         else:
             out[i] = r
     return out, mismatch
+
+
+def synth_graph(num_src: int, num_dst: int, num_edges: int, alpha: float, max_degree: int, seed: int,
+                with_edges: bool = True, threads: int = 8):
+    """Host restatement of the library's power-law graph generator
+    (synth_cpu.h): rowptr int64[num_src + 1] and the source-major edge list
+    (src, dst) int64[num_edges] (None unless with_edges)."""
+    lib = _lib(False)
+    rp = np.empty(num_src + 1, np.int64)
+    lib.oracle_synth_rowptr(num_src, num_edges, float(alpha), max_degree, seed, _p(rp), threads)
+    if not with_edges:
+        return rp, None, None
+    src = np.empty(num_edges, np.int64)
+    dst = np.empty(num_edges, np.int64)
+    lib.oracle_synth_edges(_p(rp), num_src, num_dst, seed, _p(src), _p(dst), threads)
+    return rp, src, dst
+
+
+def synth_uniform_int(n: int, lo: int, hi: int, seed: int, stream_id: int, threads: int = 8) -> np.ndarray:
+    out = np.empty(n, np.int64)
+    _lib(False).oracle_synth_uniform_int(n, lo, hi, seed, stream_id, _p(out), threads)
+    return out
+
+
+def synth_normal_features(node_begin: int, count: int, dim: int, seed: int, bf16: bool, threads: int = 8,
+                          out: Optional[np.ndarray] = None) -> np.ndarray:
+    """N(0, 1) rows; bf16=True returns the bf16 bit patterns as uint16."""
+    if out is None:
+        out = np.empty((count, dim), np.uint16 if bf16 else np.float32)
+    _lib(False).oracle_synth_normal_features(node_begin, count, dim, seed, int(bool(bf16)),
+                                             out.ctypes.data_as(ctypes.c_void_p), threads)
+    return out
 
 
 def bytes_map(index_ids: np.ndarray, query_ids: np.ndarray, threads: int = 1):

@@ -326,3 +326,120 @@ def test_large_tree_global_memory_path(sampling):
                                 debug_sampling=True)
     assert s._cc_sampler.tree_size > 8192
     _compare(sampling, graph, schema, conf, sampling.MODE_FIRST, False, np.arange(20))
+
+
+def _chain_graph(n_hop2, masked_row=False):
+    """Node 0 -> node 1 (its only neighbour), node 1 -> nodes 2 .. n_hop2 + 1:
+    every sample of seed 0 expands node 1 at the second hop."""
+    from distributed_graph_flow_b200.data import in_memory_graph as img
+    from distributed_graph_flow_b200.data import schema as sch
+
+    src = np.concatenate([[0], np.ones(n_hop2, np.int64)])
+    dst = np.concatenate([[1], np.arange(2, n_hop2 + 2)])
+    graph = img.InMemoryGraph(node_sets={"v": img.InMemoryNodeSet(num_nodes=n_hop2 + 2)},
+                              edge_sets={"e": img.InMemoryEdgeSet(adjacency=np.stack([src, dst]).astype(np.int64))})
+    schema = sch.GraphSchema(node_sets={"v": sch.NodeSchema()}, edge_sets={"e": sch.EdgeSchema("v", "v")})
+    return graph, schema
+
+
+def _chi2_p(obs, expected):
+    from scipy import stats
+
+    return stats.chi2.sf(((obs - expected) ** 2 / expected).sum(), len(obs) - 1)
+
+
+@pytest.mark.parametrize("with_replacement", [False, True])
+def test_random_mode_second_hop_chi_square(sampling, with_replacement):
+    """Second-hop draws: node 1 (reached from every seed) picks k of its n
+    neighbours uniformly; inclusion frequency k / n each. With replacement
+    the picked nodes are new local nodes but the draws are the same."""
+    n_nb, k, trials = 19, 4, 4000
+    graph, schema = _chain_graph(n_nb)
+    plan = sampling.explicit_plan("v", "e", [3, k])
+    plan.with_replacement = with_replacement
+    s = sampling.create_sampler(graph, plan, schema, return_features=False, return_node_idxs=True, batch_size=1000,
+                                seed=21)
+    counts = np.zeros(n_nb + 2)
+    for _ in range(trials // 1000):
+        for g in s.sample(np.zeros(1000, np.int64)):
+            ids = g.node_sets["v"].features["#idx"]
+            assert ids[0] == 0 and ids[1] == 1
+            hop2 = ids[2:]
+            assert len(hop2) == k and len(np.unique(hop2)) == k
+            counts[hop2] += 1
+    assert counts[:2].sum() == 0
+    p = _chi2_p(counts[2:], np.full(n_nb, trials * k / n_nb))
+    assert p > 1e-4, f"p={p:.2e} counts={counts[2:]}"
+
+
+def test_random_mode_masked_chi_square(sampling):
+    """A masked edge is never drawn; the other n - 1 neighbours are drawn
+    with frequency k / (n - 1) each."""
+    from distributed_graph_flow_b200.data import in_memory_graph as img
+    from distributed_graph_flow_b200.data import schema as sch
+
+    n_nb, k, trials, masked = 17, 5, 4000, 6
+    src = np.zeros(n_nb, np.int64)
+    dst = np.arange(1, n_nb + 1)
+    graph = img.InMemoryGraph(node_sets={"v": img.InMemoryNodeSet(num_nodes=n_nb + 1)},
+                              edge_sets={"e": img.InMemoryEdgeSet(adjacency=np.stack([src, dst]))})
+    schema = sch.GraphSchema(node_sets={"v": sch.NodeSchema()}, edge_sets={"e": sch.EdgeSchema("v", "v")})
+    plan = sampling.explicit_plan("v", "e", [k])
+    s = sampling.create_sampler(graph, plan, schema, return_features=False, return_node_idxs=True, batch_size=trials,
+                                seed=3, edgeset_to_mask="e")
+    counts = np.zeros(n_nb + 1)
+    for g in s.sample(np.zeros(trials, np.int64), masked_edge_idxs=np.full(trials, masked)):
+        ids = g.node_sets["v"].features["#idx"][1:]
+        assert len(ids) == k
+        counts[ids] += 1
+    assert counts[dst[masked]] == 0
+    keep = np.ones(n_nb + 1, bool)
+    keep[0] = keep[dst[masked]] = False
+    p = _chi2_p(counts[keep], np.full(n_nb - 1, trials * k / (n_nb - 1)))
+    assert p > 1e-4, f"p={p:.2e}"
+
+
+def test_is_deterministic(sampling):
+    """Fixed sampler seed: every new sampler draws the same random-mode
+    samples (in_memory_sampler_test.py:578-612); another seed draws others."""
+    graph, schema = toy_graph()
+    for batch_size in [1, 2]:
+        for seed_idxs in [[0, 1], [1]]:
+            for num_hops in [0, 1, 2]:
+                for hop_width in [1, 2]:
+                    truth = None
+                    for _ in range(20):
+                        plan = sampling.simple_sampling_config_to_sampling_plan(
+                            sampling.SimpleSamplingConfig(seed_nodeset="n1", num_hops=num_hops, hop_width=hop_width),
+                            schema)
+                        s = sampling.create_sampler(graph, plan, schema, return_node_idxs=True, batch_size=batch_size,
+                                                    seed=1234)
+                        got = _graph_arrays_list(s.sample(seed_idxs))
+                        if truth is None:
+                            truth = got
+                        else:
+                            assert _same(truth, got)
+    # Larger graph, random mode with draws: same seed same stream; other seed differs.
+    graph, schema = random_hetero_graph(11, temporal=False)
+    plan = sampling.simple_sampling_config_to_sampling_plan(
+        sampling.SimpleSamplingConfig(seed_nodeset="a", num_hops=2, hop_width=2), schema)
+    seeds = np.arange(40)
+    runs = [_graph_arrays_list(sampling.create_sampler(graph, plan, schema, return_node_idxs=True, batch_size=40,
+                                                       seed=sd).sample(seeds)) for sd in (1234, 1234, 99)]
+    assert _same(runs[0], runs[1])
+    assert not _same(runs[0], runs[2])
+
+
+def _graph_arrays_list(graphs):
+    return [_graph_arrays(g) for g in graphs]
+
+
+def _same(a, b):
+    if len(a) != len(b):
+        return False
+    for (na, ea), (nb, eb) in zip(a, b):
+        if na.keys() != nb.keys() or ea.keys() != eb.keys():
+            return False
+        if any(not np.array_equal(na[k], nb[k]) for k in na) or any(not np.array_equal(ea[k], eb[k]) for k in ea):
+            return False
+    return True
