@@ -133,6 +133,14 @@ SIGNATURES = {
     "dgfx_subgraph_union": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _i64, _i64, _vp, _vp,
                                    _vp, _vp, _vp, _vp, _sz, _vp]),
     "dgfx_merge_edgeset": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "dgfx_sampler_set_kernel": (_int, [_vp, _i32]),
+    "dgfx_csr_add_diagonal": (_int, [_vp, _vp, _i64, ctypes.c_float, _i32, _vp, _vp, _vp, _vp]),
+    "dgfx_csr_row_ids": (_int, [_vp, _i64, _vp, _vp]),
+    "dgfx_segment_counts": (_int, [_vp, _i64, _i64, _vp, _vp]),
+    "dgfx_gather_rows_scaled": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "dgfx_batch_csr": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp]),
+    "dgfx_sampler_kernel_info": (_int, [_vp, _p_i32]),
+    "dgfx_sampler_kernel_stats": (_int, [_vp, _vp, _p_i64]),
     "dgfx_synth_graph_workspace_size": (_int, [_i64, _i64, ctypes.POINTER(_sz)]),
     "dgfx_synth_graph": (_int, [_i64, _i64, ctypes.c_double, _i64, _u64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "dgfx_synth_bipartite": (_int, [_i64, _i64, _i64, ctypes.c_double, _i64, _u64, _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -177,3 +177,136 @@ def sage_mean_linear_relu(rowptr, col, x, weight, bias=None, agg=None, workspace
         agg = torch.empty((n_rows, int(x.shape[1])), dtype=torch.bfloat16, device=x.device)
     csr_spmm(rowptr, col, x, normalize=True, out=agg, workspace=workspace, stream=stream)
     return dense_concat(x[:n_rows], agg, weight, bias, relu=True, out=out, stream=stream)
+
+
+# ---------------------------------------------------------------------------
+# Propagation matrices of the reference's sparse GNN layers, CSR transpose,
+# segment-sum gradient, mean aggregation over a sampled batch.
+# ---------------------------------------------------------------------------
+def _symmetric_structure(src, dst, num_nodes: int, stream=None):
+    """CSR (rowptr int64, col int32) of A + A^T for an edge list on one node
+    set: every edge contributes (dst, src) and (src, dst); duplicates and
+    self loops are kept (the sum of COO matrices keeps them too). Rows are
+    sorted by column."""
+    torch = _native.require_cuda()
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+
+    s = src.to(torch.int64).contiguous()
+    d = dst.to(torch.int64).contiguous()
+    rows = torch.cat([d, s])
+    cols = torch.cat([s, d])
+    idx = ext.build_adjacency_index_device(rows, cols, None, num_nodes, num_nodes, False, False, stream=stream)
+    return idx.rowptr, idx.col
+
+
+def _add_diagonal(rowptr, col, num_nodes: int, diag: float, normalize: bool, stream=None):
+    torch = _native.require_cuda()
+    nnz = int(col.numel()) + num_nodes
+    out_rowptr = torch.empty(num_nodes + 1, dtype=torch.int64, device=rowptr.device)
+    out_col = torch.empty(max(nnz, 1), dtype=torch.int32, device=rowptr.device)[:nnz]
+    out_val = torch.empty(max(nnz, 1), dtype=torch.float32, device=rowptr.device)[:nnz]
+    _native.check(_native.lib().dgfx_csr_add_diagonal(
+        _native.ptr(rowptr), _native.ptr(col), num_nodes, float(diag), int(bool(normalize)), _native.ptr(out_rowptr),
+        _native.ptr(out_col), _native.ptr(out_val), _native.stream_handle(stream)))
+    return out_rowptr, out_col, out_val
+
+
+def gcn_matrix(src, dst, num_nodes: int, stream=None):
+    """D^-1/2 (A + A^T + I) D^-1/2 as CSR (rowptr int64, col int32, val
+    float32), D = row sums: the reference's GCN propagation matrix
+    ``(adj + adj.transpose()).add_eye().normalize_symmetric()``
+    (homo_gnn_sparse_deferred.py:293). Symmetric, so it is its own
+    transpose."""
+    rowptr, col = _symmetric_structure(src, dst, num_nodes, stream)
+    return _add_diagonal(rowptr, col, num_nodes, 1.0, True, stream)
+
+
+def gin_matrix(src, dst, num_nodes: int, epsilon: float = 0.0, stream=None):
+    """A + A^T + (1 + epsilon) I as CSR (rowptr, col, val): the reference's
+    GIN propagation matrix ``(adj + adj.transpose()).add_eye(1 +
+    epsilon)`` (homo_gnn_sparse_deferred.py:526)."""
+    rowptr, col = _symmetric_structure(src, dst, num_nodes, stream)
+    return _add_diagonal(rowptr, col, num_nodes, 1.0 + float(epsilon), False, stream)
+
+
+def csr_row_ids(rowptr, stream=None):
+    """int64 row of every CSR entry."""
+    torch = _native.require_cuda()
+    R = int(rowptr.numel()) - 1
+    nnz = int(rowptr[-1].item()) if R >= 0 else 0
+    rows = torch.empty(max(nnz, 1), dtype=torch.int64, device=rowptr.device)[:nnz]
+    _native.check(_native.lib().dgfx_csr_row_ids(_native.ptr(rowptr), R, _native.ptr(rows),
+                                                 _native.stream_handle(stream)))
+    return rows
+
+
+def csr_transpose(rowptr, col, val, num_cols: int, stream=None):
+    """Transpose of a CSR matrix [R, num_cols] -> [num_cols, R] (rowptr,
+    col int32, val float32 or None); entries of a transposed row are in
+    original row order."""
+    torch = _native.require_cuda()
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+
+    R = int(rowptr.numel()) - 1
+    nnz = int(col.numel())
+    rows = torch.empty(max(nnz, 1), dtype=torch.int64, device=rowptr.device)[:nnz]
+    _native.check(_native.lib().dgfx_csr_row_ids(_native.ptr(rowptr), R, _native.ptr(rows),
+                                                 _native.stream_handle(stream)))
+    idx = ext.build_adjacency_index_device(rows, col.to(torch.int64), None, R, int(num_cols), True, val is not None,
+                                           stream=stream)
+    val_t = None
+    if val is not None:
+        val_t = torch.empty_like(val)
+        val_t[idx.edge_pos] = val
+    return idx.rowptr, idx.col, val_t
+
+
+def segment_counts(segment_ids, num_segments: int, stream=None):
+    torch = _native.require_cuda()
+    ids = segment_ids.to(torch.int64).contiguous()
+    cnt = torch.empty(max(1, num_segments), dtype=torch.int32, device=ids.device)[:num_segments]
+    _native.check(_native.lib().dgfx_segment_counts(_native.ptr(ids), int(ids.numel()), int(num_segments),
+                                                    _native.ptr(cnt), _native.stream_handle(stream)))
+    return cnt
+
+
+def gather_rows_scaled(src, segment_ids, num_segments: int, counts=None, stream=None):
+    """out[i] = src[ids[i]] / max(counts[ids[i]], 1) (no division if counts is
+    None); zero rows for ids outside [0, num_segments)."""
+    torch = _native.require_cuda()
+    ids = segment_ids.to(torch.int64).contiguous()
+    src = src.contiguous()
+    F = int(src.numel() // max(1, src.shape[0])) if src.dim() > 1 else 1
+    out = torch.empty((int(ids.numel()),) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
+    _native.check(_native.lib().dgfx_gather_rows_scaled(
+        _native.ptr(src), _dtype_code(src.dtype), _native.ptr(ids), int(ids.numel()), int(num_segments), F,
+        _native.ptr(counts), _native.ptr(out), _native.stream_handle(stream)))
+    return out
+
+
+def batch_csr(batch, stream=None):
+    """CSR over the batch nodes of a merged sampled batch (one node set, one
+    edge set): rowptr int64 [capacity + 1] (rows past the batch's node count
+    empty), col int32 [edge capacity], col = batch index of the sampled
+    neighbour. No host synchronisation."""
+    torch = _native.require_cuda()
+    cap = int(batch.node_ids.numel())
+    ecap = int(batch.edge_src.numel())
+    rowptr = torch.empty(cap + 1, dtype=torch.int64, device=batch.node_ids.device)
+    col = torch.empty(max(ecap, 1), dtype=torch.int32, device=batch.node_ids.device)[:ecap]
+    _native.check(_native.lib().dgfx_batch_csr(
+        _native.ptr(batch.node_offsets), _native.ptr(batch.edge_offsets), _native.ptr(batch.edge_src),
+        _native.ptr(batch.edge_dst), int(batch.B), cap, _native.ptr(rowptr), _native.ptr(col),
+        _native.stream_handle(stream)))
+    return rowptr, col
+
+
+def batch_mean_aggregate(batch, features, out=None, workspace=None, csr=None, stream=None):
+    """Mean aggregation over a merged sampled batch (jax.ops.segment_sum
+    mean pooling of hetero_gnn.py:282-294, messages = the features of the
+    sampled neighbours flowing to the node that sampled them): out[v] =
+    mean of features[u] over the batch edges v -> u, zero rows for nodes
+    without sampled neighbours. features [capacity, F] in batch order
+    (the rows gathered for batch.node_ids)."""
+    rowptr, col = csr if csr is not None else batch_csr(batch, stream)
+    return csr_spmm(rowptr, col, features, normalize=True, out=out, workspace=workspace, stream=stream)

@@ -32,7 +32,7 @@ NVCC_FLAGS = ARCH + [
     f"-I{INCLUDE}",
 ]
 SOURCES = ["capi.cu", "primitives.cu", "csr_build.cu", "sampler.cu", "aggregate.cu", "halo.cu", "peer.cu", "synth.cu",
-           "transform.cu", "dense.cu", "subgraph.cu", "negatives.cu", "idmap.cu", "timeseries.cu"]
+           "transform.cu", "dense.cu", "subgraph.cu", "negatives.cu", "idmap.cu", "timeseries.cu", "sparse_ops.cu"]
 
 
 def nvcc() -> str:

@@ -71,6 +71,13 @@ struct EdgeDev {
   int32_t stride;   // Z(child)
   int32_t edgeset;
   int32_t reversed;
+  int32_t rel_off;  // first child slot relative to the parent's position
+  int32_t child;    // plan node the edge leads to
+};
+
+// Plan node as the warp sampler walks it.
+struct PlanNodeDev {
+  int32_t first_edge, num_edges, nodeset, in_edge;  // in_edge: the plan edge into this node (-1 at the root)
 };
 
 struct Params {
@@ -103,6 +110,18 @@ struct Params {
   int32_t pbits;               // bits of a local id (local ids < T <= 2^pbits)
   int32_t keybits;             // bits of an edge sort key (edgeset | src | dst)
   uint32_t ns_key_base[kMaxNodesets];  // node set offsets of the 32-bit dedup keys
+  // Warp sampler (one warp per seed over occupied positions only).
+  const PlanNodeDev* pnodes;
+  int32_t warp_cap;            // entries per warp in shared memory (power of two)
+  int32_t max_edges_per_node;  // tasks per entry and level
+  int32_t warp_bytes;          // shared memory per warp
+  unsigned int* overflow_count;  // [0] seeds for the padded kernel, [1] next seed of the warp kernel
+  int32_t* overflow_list;        // seeds with more entries than any warp slot holds
+  // Global-memory slots (capacity big_cap >= T entries) for seeds that
+  // outgrow the warp's shared arrays; a lock word per slot.
+  char* big_slots;
+  unsigned int* big_locks;
+  int32_t big_cap, big_bytes, num_big_slots;
 };
 
 // Per-CTA working arrays (shared or global memory). The dedup table packs
@@ -400,7 +419,7 @@ __device__ unsigned long long* block_radix_sort(unsigned long long* a, unsigned 
   return a;
 }
 
-__global__ void __launch_bounds__(256) sample_kernel(Params p) {
+__device__ __forceinline__ void sample_one(const Params& p, const int64_t sample) {
   extern __shared__ __align__(16) char smem_dyn[];
   __shared__ uint64_t scan_tmp[33];
   __shared__ int32_t ns_count[kMaxNodesets];
@@ -410,7 +429,6 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   __shared__ int32_t wtot[8];
   __shared__ int lbits_s;
 
-  const int64_t sample = blockIdx.x;
   const int T = p.T;
   int32_t* cnt = reinterpret_cast<int32_t*>(smem_dyn);
   int32_t* dbase = cnt + (blockDim.x >> 5) * 256;
@@ -673,6 +691,577 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
   if (threadIdx.x < 3) atomicAdd(&p.status[3 + threadIdx.x], static_cast<unsigned long long>(stats[threadIdx.x]));
 }
 
+// Padded sampler: one CTA per seed. Without an overflow list it samples seed
+// blockIdx.x; with one (after the warp sampler) its CTAs take the listed
+// seeds in turn.
+__global__ void __launch_bounds__(256) sample_kernel(Params p) {
+  if (p.overflow_list == nullptr) {
+    sample_one(p, blockIdx.x);
+    return;
+  }
+  const unsigned int n = *p.overflow_count;
+  for (unsigned int i = blockIdx.x; i < n; i += gridDim.x) {
+    sample_one(p, p.overflow_list[i]);
+    __syncthreads();  // the next seed re-initialises the CTA's shared state
+  }
+}
+
+// ===========================================================================
+// Warp sampler: one warp per seed over the occupied tree positions only.
+//
+// The padded tree has T positions, but on power-law graphs only a few
+// percent of them are occupied (rows shorter than the hop width, empty
+// rows). The warp sampler keeps one compact entry per occupied position
+// (node id, padded position, parent entry, plan node) in shared memory,
+// level by level, so every phase costs the entries a seed really has:
+//   1. expansion: the tasks (entry, plan edge) of a level go to the lanes in
+//      chunks of four rounds: the lanes load the row bounds of all four
+//      rounds at once, find temporal cutoffs with an 8-pivot search per lane
+//      (ceil(log9(d)) dependent loads), draw the picks (same Philox counters
+//      as the padded sampler: tree position, plan edge, seed slot, call),
+//      and a warp scan gives each task its place among the next level's
+//      entries, which stay in position order; then the lanes load the picked
+//      columns, four in flight each;
+//   2. numbering: an entry's rank in depth-first order is its index in its
+//      level plus, for every other level, the number of entries there with a
+//      smaller position (binary searches over the position-sorted levels);
+//      a hash table keeps each node's smallest rank (atomicMin) and a walk
+//      over the entries in rank order numbers first discoveries per node set
+//      (__match_any_sync), exactly the reference's first-discovery order;
+//   3. edges: one key (edgeset | src | dst) per non-root entry, a warp
+//      bitonic sort, deduplication by a ballot scan.
+// Results go to the same per-seed scratch slices as the padded sampler's,
+// so the compaction is shared and both samplers give identical batches. A
+// seed whose tree outgrows warp_cap entries is listed for the padded sampler
+// (it starts again there with the same random stream).
+// ===========================================================================
+constexpr int kWarpCapMax = 256;
+constexpr int kWarpsPerCta = 4;
+constexpr int kMaxWarpDepth = 30;
+
+__host__ __device__ inline int warp_region_bytes(int cap, int ns, int es, int depth) {
+  const int b = 24 * cap + 4 * (ns + es + depth + 2);
+  return (b + 15) & ~15;
+}
+
+// upper_bound(ts[0, n), cut): entries with ts <= cut. Eight pivots per round,
+// all loads of a round in flight; rows of <= 8 entries take one round.
+__device__ __forceinline__ int64_t upper_bound_9ary(const int64_t* __restrict__ ts, int64_t n, int64_t cut,
+                                                    unsigned int* probes) {
+  int64_t lo = 0, hi = n;
+  while (hi - lo > 8) {
+    const int64_t len = hi - lo;
+    int64_t v[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) v[g] = __ldg(ts + lo + ((g + 1) * len) / 9);
+    int c = 0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) c += v[g] <= cut ? 1 : 0;  // pivots <= cut form a prefix
+    const int64_t base = lo;
+    if (c > 0) lo = base + (c * len) / 9 + 1;
+    if (c < 8) hi = base + ((c + 1) * len) / 9;
+    *probes += 8;
+  }
+  const int64_t len = hi - lo;
+  int64_t v[8];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) v[g] = g < len ? __ldg(ts + lo + g) : 0;
+  int c = 0;
+#pragma unroll
+  for (int g = 0; g < 8; ++g) c += (g < len && v[g] <= cut) ? 1 : 0;
+  *probes += static_cast<unsigned int>(len);
+  return lo + c;
+}
+
+// Philox block of draw pair m >> 1 of one expansion task (the padded
+// sampler's counters: tree position, plan edge | block index, seed slot,
+// call index).
+__device__ __forceinline__ U4 task_block(uint32_t key0, uint32_t key1, int32_t q, int32_t e, int32_t m, uint32_t slot,
+                                         uint2 call) {
+  const U4 c{static_cast<uint32_t>(q), static_cast<uint32_t>(e) | ((static_cast<uint32_t>(m) >> 1) << 16), slot, call.x};
+  return philox4x32_10(c, key0 ^ call.y, key1);
+}
+
+// Picks of one task into at[0, cnt): CSR positions in adjacency order
+// (random: Floyd's k-subset of the valid row; FIRST / MOST_RECENT: the first
+// / last cnt valid entries). Random draws from rows of at most 64 valid
+// entries keep the chosen set as a 64-bit mask (O(1) duplicate test; the
+// set bits come out in adjacency order); longer rows use the shared array.
+__device__ __forceinline__ void warp_picks(uint32_t key0, uint32_t key1, long long* at, int32_t cnt, int64_t rb,
+                                           int64_t nv, int64_t moff, int mode, int32_t q, int32_t e, uint32_t slot,
+                                           uint2 call) {
+  if (mode == DGFX_MODE_RANDOM && cnt < nv) {
+    const bool small = nv <= 64;
+    unsigned long long chosen = 0;
+    U4 block{};
+    for (int32_t m = 0; m < cnt; ++m) {
+      if ((m & 1) == 0) block = task_block(key0, key1, q, e, m, slot, call);
+      const uint64_t r = (m & 1) ? (static_cast<uint64_t>(block.w) << 32 | block.z)
+                                 : (static_cast<uint64_t>(block.y) << 32 | block.x);
+      const int64_t j = nv - cnt + m;
+      int64_t t = static_cast<int64_t>(bounded64(r, static_cast<uint64_t>(j + 1)));
+      if (small) {
+        if ((chosen >> t) & 1ull) t = j;
+        chosen |= 1ull << t;
+      } else {
+        for (int32_t i = 0; i < m; ++i) {
+          if (at[i] == t) {
+            t = j;
+            break;
+          }
+        }
+        at[m] = t;
+      }
+    }
+    if (small) {
+      for (int32_t i = 0; i < cnt; ++i) {
+        long long off = __ffsll(static_cast<long long>(chosen)) - 1;
+        chosen &= chosen - 1;
+        if (moff >= 0 && off >= moff) ++off;
+        at[i] = rb + off;
+      }
+      return;
+    }
+    for (int32_t i = 1; i < cnt; ++i) {  // adjacency order
+      const long long x = at[i];
+      int32_t j = i - 1;
+      while (j >= 0 && at[j] > x) {
+        at[j + 1] = at[j];
+        --j;
+      }
+      at[j + 1] = x;
+    }
+    for (int32_t i = 0; i < cnt; ++i) {
+      long long off = at[i];
+      if (moff >= 0 && off >= moff) ++off;
+      at[i] = rb + off;
+    }
+    return;
+  }
+  const int64_t first = (mode == DGFX_MODE_MOST_RECENT) ? nv - cnt : 0;
+  for (int32_t i = 0; i < cnt; ++i) {
+    int64_t off = first + i;
+    if (moff >= 0 && off >= moff) ++off;
+    at[i] = rb + off;
+  }
+}
+
+// Per-warp shared arrays (capacity C entries).
+struct WarpArrays {
+  long long* at;     // [C] CSR positions of picks; then the dedup table; then edge keys
+  int32_t* node;     // [C] node ids; with pos, the sorted edge keys at the end
+  int32_t* pos;      // [C] padded positions; then dedup slots
+  int32_t* meta;     // [C] parent entry << 8 | plan node
+  uint16_t* order;   // [C] entry of each depth-first rank
+  uint16_t* local;   // [C] rank, then local id
+  int32_t* ns_cnt;   // [NS]
+  int32_t* es_cnt;   // [ES]
+  int32_t* lv;       // [depth + 2] level boundaries
+};
+
+// A word of the dedup table: the shared-memory variant reads it plainly;
+// the global-memory variant (big slots) reads it at L2 with an atomic, since
+// the table is written by atomics there and a plain load could return a
+// stale L1 line.
+template <bool kGlobal>
+__device__ __forceinline__ unsigned long long tab_read(unsigned long long* a) {
+  if constexpr (kGlobal) return atomicAdd(a, 0ull);
+  else return *a;
+}
+
+// Samples one seed with arrays of capacity C; returns false (nothing
+// written) if the tree has more than C occupied positions.
+template <bool kGlobal>
+__device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArrays& w, const int C, const int64_t sample,
+                                                uint2 call) {
+  constexpr unsigned FULL = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  const int NS = p.num_nodesets, ES = p.num_edgesets, D = p.depth;
+  long long* at = w.at;
+  int32_t* node = w.node;
+  int32_t* pos = w.pos;
+  int32_t* meta = w.meta;
+  uint16_t* order = w.order;
+  uint16_t* local = w.local;
+  int32_t* ns_cnt = w.ns_cnt;
+  int32_t* es_cnt = w.es_cnt;
+  int32_t* lv = w.lv;
+
+  const uint32_t slot = static_cast<uint32_t>(sample);
+  const bool has_ts = p.seed_ts != nullptr;
+  const int64_t sts = has_ts ? p.seed_ts[sample] : 0;
+  const int64_t mask = p.masks != nullptr ? p.masks[sample] : -1;
+  const int64_t seed = p.seeds[sample];
+  const bool ok = !(p.root_has_children && (seed < 0 || seed >= p.root_num_src));
+  if (!ok && lane == 0) atomicMin(&p.status[0], static_cast<unsigned long long>(sample));
+  for (int i = lane; i < NS; i += 32) ns_cnt[i] = 0;
+  for (int i = lane; i < ES; i += 32) es_cnt[i] = 0;
+  if (lane == 0) {
+    node[0] = static_cast<int32_t>(seed);
+    pos[0] = 0;
+    meta[0] = 0;  // plan node 0, no parent
+    lv[0] = 0;
+    lv[1] = ok ? 1 : 0;
+  }
+  __syncwarp();
+  unsigned int st_rows = 0, st_picks = 0, st_probes = 0;
+
+  // 1. Expansion, level by level; tasks in chunks of two rounds.
+  bool overflow = false;
+  const int maxm = p.max_edges_per_node;
+  for (int d = 0; d < D; ++d) {
+    const int l0 = lv[d], l1 = lv[d + 1];
+    int fill = l1;
+    const int ntask = (l1 - l0) * maxm;
+    for (int t0 = 0; t0 < ntask; t0 += 32) {
+      const int t = t0 + lane;
+      int32_t cnt = 0, pe = -1, q = 0, ent = 0;
+      int64_t rb = 0, nv = 0, moff = -1;
+      int md = p.mode;
+      if (t < ntask) {
+        const int e = l0 + t / maxm, j = t - (t / maxm) * maxm;
+        const PlanNodeDev P = p.pnodes[meta[e] & 0xFF];
+        if (j < P.num_edges) {
+          pe = P.first_edge + j;
+          ent = e;
+          q = pos[e];
+          const EdgeDev& E = p.edges[pe];
+          const int32_t v = node[e];
+          rb = __ldg(E.rowptr + v);
+          int64_t n = __ldg(E.rowptr + v + 1) - rb;
+          const bool temporal = has_ts && E.ts != nullptr;
+          if (!has_ts && E.ts != nullptr) {
+            // SampleRandomUniform / SampleFirst on a temporal index fail
+            // (in_memory_sampler.cc:26-30, 168-172).
+            atomicOr(&p.status[1], 1ull);
+            n = 0;
+          }
+          if (temporal && n > 0) n = upper_bound_9ary(E.ts + rb, n, sts, &st_probes);
+          if (!temporal && mask >= 0 && E.edgeset == p.mask_edgeset && E.edge_pos != nullptr && mask < E.num_edges) {
+            const int64_t ps = E.edge_pos[mask];
+            if (ps >= rb && ps < rb + n) moff = ps - rb;
+          }
+          nv = n - (moff >= 0 ? 1 : 0);
+          cnt = static_cast<int32_t>(nv < E.k ? nv : E.k);
+          md = (p.mode == DGFX_MODE_MOST_RECENT && !temporal) ? DGFX_MODE_RANDOM : p.mode;
+          ++st_rows;
+          st_picks += static_cast<unsigned int>(cnt);
+        }
+      }
+      const int32_t inc = warp_inclusive_scan(cnt);
+      const int32_t tot = __shfl_sync(FULL, inc, 31);
+      if (fill + tot > C) {
+        overflow = true;
+        break;
+      }
+      if (cnt > 0) {
+        const int32_t out = fill + inc - cnt;
+        warp_picks(p.key0, p.key1, at + out, cnt, rb, nv, moff, md, q, pe, slot, call);
+        const EdgeDev& E = p.edges[pe];
+        const int32_t base = q + E.rel_off;
+        const int32_t mt = (ent << 8) | E.child;
+        for (int32_t i = 0; i < cnt; ++i) {
+          pos[out + i] = base + i * E.stride;
+          meta[out + i] = mt;
+        }
+      }
+      fill += tot;
+    }
+    if (overflow) break;
+    __syncwarp();
+    // Columns of the new entries, four loads in flight per lane.
+    for (int i0 = l1 + lane; i0 < fill; i0 += 32 * 4) {
+      int32_t v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + 32 * u;
+        v[u] = -1;
+        if (i < fill) v[u] = __ldg(p.edges[p.pnodes[meta[i] & 0xFF].in_edge].col + at[i]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (i0 + 32 * u < fill) node[i0 + 32 * u] = v[u];
+      }
+    }
+    if (lane == 0) lv[d + 2] = fill;
+    __syncwarp();
+  }
+  if (overflow) {  // redone with larger arrays (its work is counted there)
+    __syncwarp();
+    return false;
+  }
+  st_rows = warp_reduce_sum(st_rows);
+  st_picks = warp_reduce_sum(st_picks);
+  st_probes = warp_reduce_sum(st_probes);
+  if (lane == 0) {
+    atomicAdd(&p.status[3], static_cast<unsigned long long>(st_rows));
+    atomicAdd(&p.status[4], static_cast<unsigned long long>(st_picks));
+    atomicAdd(&p.status[5], static_cast<unsigned long long>(st_probes));
+  }
+  const int n = lv[D + 1];
+
+  // 2. Numbering. Rank in depth-first order = number of entries with a
+  //    smaller position: all pairs (broadcast loads) for small trees,
+  //    binary searches over the position-sorted levels otherwise.
+  if (n <= 64) {
+    const int32_t p0 = lane < n ? pos[lane] : 0x7FFFFFFF;
+    const int32_t p1 = lane + 32 < n ? pos[lane + 32] : 0x7FFFFFFF;
+    int r0 = 0, r1 = 0;
+    for (int j = 0; j < n; ++j) {
+      const int32_t pj = pos[j];
+      r0 += pj < p0 ? 1 : 0;
+      r1 += pj < p1 ? 1 : 0;
+    }
+    if (lane < n) {
+      local[lane] = static_cast<uint16_t>(r0);
+      order[r0] = static_cast<uint16_t>(lane);
+    }
+    if (lane + 32 < n) {
+      local[lane + 32] = static_cast<uint16_t>(r1);
+      order[r1] = static_cast<uint16_t>(lane + 32);
+    }
+  } else {
+    for (int i = lane; i < n; i += 32) {
+      const int32_t pq = pos[i];
+      int d = 0;
+      while (i >= lv[d + 1]) ++d;
+      int r = i - lv[d];
+      for (int d2 = 0; d2 <= D; ++d2) {
+        if (d2 == d) continue;
+        int lo = lv[d2], hi = lv[d2 + 1];
+        const int b0 = lo;
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (pos[mid] < pq) lo = mid + 1;
+          else hi = mid;
+        }
+        r += lo - b0;
+      }
+      local[i] = static_cast<uint16_t>(r);
+      order[r] = static_cast<uint16_t>(i);
+    }
+  }
+  __syncwarp();
+  unsigned long long* tab = reinterpret_cast<unsigned long long*>(at);
+  if (!p.with_replacement) {
+    int H = 2;
+    while (H < 2 * n && H < C) H <<= 1;
+    const int log2H = 31 - __clz(H);
+    for (int i = lane; i < H; i += 32) {
+      if constexpr (kGlobal) atomicExch(&tab[i], kEmptyKey);
+      else tab[i] = kEmptyKey;
+    }
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const int ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
+      const uint32_t key = p.ns_key_base[ns] + static_cast<uint32_t>(node[i]);
+      const unsigned long long entry = (static_cast<unsigned long long>(key) << 32) | local[i];
+      uint32_t h = (key * 0x9E3779B1u) >> (32 - log2H);
+      int where = -1;
+      for (int probe = 0; probe < H; ++probe) {
+        const unsigned long long prev = atomicCAS(&tab[h], kEmptyKey, entry);
+        if (prev == kEmptyKey) {
+          where = static_cast<int>(h);
+          break;
+        }
+        if (static_cast<uint32_t>(prev >> 32) == key) {
+          atomicMin(&tab[h], entry);
+          where = static_cast<int>(h);
+          break;
+        }
+        h = (h + 1) & static_cast<uint32_t>(H - 1);
+      }
+      if (where < 0) atomicOr(&p.status[2], 1ull);  // cannot happen: H > n
+      pos[i] = where;  // positions are not needed any more
+    }
+    __syncwarp();
+  }
+  // First discoveries in rank order, numbered per node set; with
+  // replacement every entry is a new node.
+  for (int r0 = 0; r0 < n; r0 += 32) {
+    const int r = r0 + lane;
+    int ns = -1, i = -1;
+    if (r < n) {
+      i = order[r];
+      const bool first = p.with_replacement ||
+                         (pos[i] >= 0 && static_cast<uint32_t>(tab_read<kGlobal>(&tab[pos[i]])) == static_cast<uint32_t>(r));
+      if (first) ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
+    }
+    const uint32_t peers = __match_any_sync(FULL, ns);
+    int base = 0;
+    if (ns >= 0) base = ns_cnt[ns];
+    __syncwarp();
+    if (ns >= 0) {
+      const uint32_t l = static_cast<uint32_t>(base) + __popc(peers & lt);
+      if (p.with_replacement) local[i] = static_cast<uint16_t>(l);
+      else tab[pos[i]] = (tab_read<kGlobal>(&tab[pos[i]]) & 0xFFFFFFFF00000000ull) | (0x80000000u | l);
+      if ((peers & lt) == 0) ns_cnt[ns] = base + __popc(peers);
+    }
+    __syncwarp();
+  }
+  if (!p.with_replacement) {
+    for (int i = lane; i < n; i += 32) {
+      local[i] = pos[i] >= 0 ? static_cast<uint16_t>(static_cast<uint32_t>(tab_read<kGlobal>(&tab[pos[i]])) & 0x7FFFFFFFu) : 0;
+    }
+  }
+  __syncwarp();
+  // Nodes per node set in local-id order (every occurrence of a node writes
+  // the same value).
+  int most = 1;
+  for (int g = 0; g < NS; ++g) most = max(most, ns_cnt[g]);
+  const int lb = max(1, 32 - __clz(most - 1));
+  int32_t* out_nodes = p.scratch_nodes + sample * static_cast<int64_t>(p.T);
+  for (int i = lane; i < n; i += 32) {
+    const int ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
+    int b = 0;
+    for (int g = 0; g < ns; ++g) b += ns_cnt[g];
+    out_nodes[b + local[i]] = node[i];
+  }
+  __syncwarp();
+
+  // 3. Edges: a 32-bit key (edgeset | src | dst; local ids < 4096) per
+  //    non-root entry, sort (ranks by broadcast loads for up to 64 keys, else
+  //    a bitonic sort), deduplicate.
+  const int nk = n > 0 ? n - 1 : 0;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(at);
+  auto edge_key = [&](int c) -> uint32_t {
+    const int par = meta[c] >> 8;
+    const EdgeDev& E = p.edges[p.pnodes[meta[c] & 0xFF].in_edge];
+    const uint32_t a = local[par], b = local[c];
+    const uint32_t src = E.reversed ? b : a, dst = E.reversed ? a : b;
+    return (static_cast<uint32_t>(E.edgeset) << (2 * lb)) | (src << lb) | dst;
+  };
+  const uint32_t* ek;
+  if (nk <= 64) {
+    const uint32_t k0 = lane < nk ? edge_key(lane + 1) : ~0u;
+    const uint32_t k1 = lane + 32 < nk ? edge_key(lane + 33) : ~0u;
+    if (lane < nk) keys[lane] = k0;
+    if (lane + 32 < nk) keys[lane + 32] = k1;
+    __syncwarp();
+    int r0 = 0, r1 = 0;
+    for (int j = 0; j < nk; ++j) {
+      const uint32_t kj = keys[j];
+      r0 += (kj < k0 || (kj == k0 && j < lane)) ? 1 : 0;
+      r1 += (kj < k1 || (kj == k1 && j < lane + 32)) ? 1 : 0;
+    }
+    uint32_t* sorted = reinterpret_cast<uint32_t*>(node);
+    if (lane < nk) sorted[r0] = k0;
+    if (lane + 32 < nk) sorted[r1] = k1;
+    ek = sorted;
+  } else {
+    int P = 1;
+    while (P < nk) P <<= 1;
+    for (int i = lane; i < P; i += 32) keys[i] = i < nk ? edge_key(i + 1) : ~0u;
+    __syncwarp();
+    for (int k = 2; k <= P; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = lane; i < P; i += 32) {
+          const int ixj = i ^ j;
+          if (ixj > i) {
+            const uint32_t a = keys[i], b = keys[ixj];
+            if ((a > b) == ((i & k) == 0)) {
+              keys[i] = b;
+              keys[ixj] = a;
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+    ek = keys;
+  }
+  __syncwarp();
+  uint64_t* out_edges = p.scratch_edges + sample * static_cast<int64_t>(p.T);
+  const uint32_t lmask = (1u << lb) - 1;
+  int wbase = 0;
+  for (int i0 = 0; i0 < nk; i0 += 32) {
+    const int i = i0 + lane;
+    const uint32_t k = i < nk ? ek[i] : ~0u;
+    const bool fresh = i < nk && (i == 0 || ek[i - 1] != k);
+    const uint32_t m = __ballot_sync(FULL, fresh);
+    if (fresh) {
+      const unsigned long long es = k >> (2 * lb);
+      out_edges[wbase + __popc(m & lt)] = (es << 48) | (static_cast<unsigned long long>((k >> lb) & lmask) << 24) |
+                                          (k & lmask);
+      atomicAdd(&es_cnt[static_cast<int>(es)], 1);
+    }
+    wbase += __popc(m);
+  }
+  __syncwarp();
+  for (int g = lane; g < NS; g += 32) p.node_cnt[g * p.B + sample] = ns_cnt[g];
+  for (int g = lane; g < ES; g += 32) p.edge_cnt[g * p.B + sample] = es_cnt[g];
+  __syncwarp();
+  return true;
+}
+
+__device__ __forceinline__ WarpArrays carve_warp(char* base, int C, int32_t* counters, int NS, int ES) {
+  WarpArrays w;
+  w.at = reinterpret_cast<long long*>(base);
+  w.node = reinterpret_cast<int32_t*>(base + 8 * static_cast<size_t>(C));
+  w.pos = w.node + C;
+  w.meta = w.pos + C;
+  w.order = reinterpret_cast<uint16_t*>(w.meta + C);
+  w.local = w.order + C;
+  w.ns_cnt = counters;
+  w.es_cnt = counters + NS;
+  w.lv = counters + NS + ES;
+  return w;
+}
+
+// Persistent warps: each takes the next seed from a counter in turn, so a
+// warp whose seed has a large tree does not hold back the others.
+__global__ void __launch_bounds__(kWarpsPerCta * 32, 8) warp_sample_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(16) char smem_warp[];
+  const int lane = threadIdx.x & 31;
+  const int C = p.warp_cap;
+  const int NS = p.num_nodesets, ES = p.num_edgesets;
+  char* wb = smem_warp + static_cast<size_t>(threadIdx.x >> 5) * p.warp_bytes;
+  int32_t* counters = reinterpret_cast<int32_t*>(wb + 24 * static_cast<size_t>(C));  // always in shared memory
+  const WarpArrays w = carve_warp(wb, C, counters, NS, ES);
+  uint2 call;
+  {
+    const unsigned long long cidx =
+        p.call_dev != nullptr ? *p.call_dev : ((static_cast<unsigned long long>(p.call_hi) << 32) | p.call_lo);
+    call = make_uint2(static_cast<uint32_t>(cidx), static_cast<uint32_t>(cidx >> 32));
+  }
+  for (;;) {
+    unsigned int s = 0;
+    if (lane == 0) s = atomicAdd(p.overflow_count + 1, 1u);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    if (static_cast<int64_t>(s) >= p.B) break;
+    if (warp_sample_one<false>(p, w, C, static_cast<int64_t>(s), call)) continue;
+    // The tree outgrew the shared arrays: take a free global slot (each
+    // lock is tried once) and sample again there, else list the seed for
+    // the padded sampler.
+    int slot = -1;
+    if (lane == 0) {
+      for (int k = 0; k < p.num_big_slots; ++k) {
+        const int i = static_cast<int>((s + static_cast<unsigned int>(k)) % static_cast<unsigned int>(p.num_big_slots));
+        if (atomicCAS(&p.big_locks[i], 0u, 1u) == 0u) {
+          slot = i;
+          break;
+        }
+      }
+    }
+    slot = __shfl_sync(0xffffffffu, slot, 0);
+    if (slot >= 0) {
+      const WarpArrays g = carve_warp(p.big_slots + static_cast<size_t>(slot) * p.big_bytes, p.big_cap, counters, NS, ES);
+      warp_sample_one<true>(p, g, p.big_cap, static_cast<int64_t>(s), call);
+      __threadfence();  // the slot's writes are visible before it is released
+      __syncwarp();
+      if (lane == 0) {
+        atomicExch(&p.big_locks[slot], 0u);
+        atomicAdd(&p.status[7], 1ull);
+      }
+    } else if (lane == 0) {
+      p.overflow_list[atomicAdd(p.overflow_count, 1u)] = static_cast<int32_t>(s);
+      atomicAdd(&p.status[8], 1ull);
+    }
+    __syncwarp();
+  }
+}
+
 // Largest row length of an index (the cap on useful slots per plan edge).
 __global__ void max_degree_kernel(const int64_t* __restrict__ rowptr, int64_t n, unsigned long long* out) {
   unsigned long long m = 0;
@@ -740,6 +1329,14 @@ struct dgfx_sampler {
   int32_t with_replacement = 0, mode = 0, mask_edgeset = -1;
   uint64_t seed = 0;
   bool use_smem = true;
+  // Warp sampler (0 capacity: not eligible; kernel_kind 1 forces the padded
+  // sampler).
+  int32_t warp_cap = 0, max_edges_per_node = 1, warp_bytes = 0;
+  int32_t kernel_kind = 0;
+  int32_t padded_blocks = 0;  // CTAs of the padded sampler when it serves overflow seeds
+  int32_t warp_blocks = 0;    // resident CTAs of the (persistent) warp sampler
+  int32_t big_cap = 0;        // entries of a global slot (0: none; overflow seeds go to the padded sampler)
+  PlanNodeDev* d_pnodes = nullptr;
   int threads = 256;
   size_t smem_bytes = 0;
   int32_t pbits = 1, keybits = 2;
@@ -775,6 +1372,11 @@ struct SampleBufs {
   int32_t* node_cnt;
   int32_t* edge_cnt;
   char* global_work;
+  unsigned int* overflow_count;
+  int32_t* overflow_list;
+  int32_t num_big_slots;
+  unsigned int* big_locks;
+  char* big_slots;
 };
 
 void carve_sample(Arena& a, const dgfx_sampler* s, int64_t B, SampleBufs* b) {
@@ -783,6 +1385,11 @@ void carve_sample(Arena& a, const dgfx_sampler* s, int64_t B, SampleBufs* b) {
   b->node_cnt = a.take<int32_t>(static_cast<size_t>(B * s->num_nodesets));
   b->edge_cnt = a.take<int32_t>(static_cast<size_t>(B * s->num_edgesets));
   b->global_work = s->use_smem ? nullptr : a.take<char>(static_cast<size_t>(B) * work_bytes(s->T, s->H));
+  b->overflow_count = a.take<unsigned int>(2);  // [0] overflowed seeds, [1] next seed of the warp sampler
+  b->overflow_list = a.take<int32_t>(static_cast<size_t>(std::max<int64_t>(B, 1)));
+  b->num_big_slots = s->big_cap > 0 ? static_cast<int32_t>(std::min<int64_t>(256, std::max<int64_t>(1, B / 16))) : 0;
+  b->big_locks = a.take<unsigned int>(static_cast<size_t>(std::max(1, b->num_big_slots)));
+  b->big_slots = a.take<char>(static_cast<size_t>(b->num_big_slots) * 24 * static_cast<size_t>(s->big_cap));
 }
 
 size_t sample_ws_bytes(const dgfx_sampler* s, int64_t B) {
@@ -944,7 +1551,22 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
     E.stride = static_cast<int32_t>(Z[edge_child[j]]);
     E.edgeset = edge_edgeset[j];
     E.reversed = edge_reversed[j] != 0;
+    E.child = edge_child[j];
   }
+  // Warp sampler tables: per plan node its edges, node set and incoming
+  // edge; per plan edge the first child slot relative to the parent.
+  std::vector<PlanNodeDev> pnodes(num_plan_nodes);
+  for (int pn = 0; pn < num_plan_nodes; ++pn) {
+    pnodes[pn] = PlanNodeDev{node_first_edge[pn], node_num_edges[pn], node_nodeset[pn], -1};
+    int64_t off = 1;
+    for (int c = 0; c < node_num_edges[pn]; ++c) {
+      const int j = node_first_edge[pn] + c;
+      s->h_edges[j].rel_off = static_cast<int32_t>(off);
+      off += static_cast<int64_t>(slots[j]) * Z[edge_child[j]];
+      s->max_edges_per_node = std::max(s->max_edges_per_node, node_num_edges[pn]);
+    }
+  }
+  for (int j = 0; j < num_plan_edges; ++j) pnodes[edge_child[j]].in_edge = j;
   // Dedup keys: node ids of all node sets laid end to end in 32 bits.
   {
     uint64_t acc = 0;
@@ -967,8 +1589,12 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
   const size_t b_children = align_up(sizeof(int32_t) * std::max<size_t>(1, children.size()), 256);
   const size_t b_clevel = align_up(sizeof(int32_t) * clevel.size(), 256);
   const size_t b_status = 256;
+  const size_t b_pnodes = align_up(sizeof(PlanNodeDev) * pnodes.size(), 256);
   char* d = nullptr;
-  DGFX_CUDA_TRY(cudaMalloc(&d, b_edges + b_tasks + b_level + b_pos + b_children + b_clevel + b_status));
+  DGFX_CUDA_TRY(cudaMalloc(&d, b_edges + b_tasks + b_level + b_pos + b_children + b_clevel + b_status + b_pnodes));
+  s->d_pnodes = reinterpret_cast<PlanNodeDev*>(d + b_edges + b_tasks + b_level + b_pos + b_children + b_clevel +
+                                               b_status);
+  DGFX_CUDA_TRY(cudaMemcpy(s->d_pnodes, pnodes.data(), sizeof(PlanNodeDev) * pnodes.size(), cudaMemcpyHostToDevice));
   s->d_tables = d;
   s->d_edges = reinterpret_cast<EdgeDev*>(d);
   s->d_tasks = reinterpret_cast<int4*>(d + b_edges);
@@ -988,8 +1614,10 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
     DGFX_CUDA_TRY(cudaMemcpy(s->d_children, children.data(), sizeof(int32_t) * children.size(), cudaMemcpyHostToDevice));
   }
   DGFX_CUDA_TRY(cudaMemcpy(s->d_clevel, clevel.data(), sizeof(int32_t) * clevel.size(), cudaMemcpyHostToDevice));
-  // Status: first bad seed, ts missing, table overflow, 3 stats, device call index.
-  const unsigned long long init[7] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
+  // Status: first bad seed, ts missing, table overflow, 3 stats, device call
+  // index, seeds finished in a global slot, seeds finished by the padded
+  // sampler.
+  const unsigned long long init[9] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
   DGFX_CUDA_TRY(cudaMemcpy(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice));
 
   // The plan as random walks see it (plan nodes, plan edges with their CSR,
@@ -1040,6 +1668,43 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
     DGFX_CUDA_TRY(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(s->smem_bytes)));
   }
+  // Warp sampler: capacity = the tree size rounded up to a power of two,
+  // at most kWarpCapMax entries (larger trees go to the padded sampler when
+  // they outgrow it). Plan node ids and parent entries are packed in 8 and
+  // 24 bits.
+  if (num_plan_nodes <= 256 && s->depth <= kMaxWarpDepth) {
+    int cap = 2;
+    while (cap < T && cap < kWarpCapMax) cap <<= 1;
+    const int bytes = warp_region_bytes(cap, num_nodesets, num_edgesets, s->depth);
+    if (bytes * kWarpsPerCta <= 200 * 1024) {
+      s->warp_cap = cap;
+      s->warp_bytes = bytes;
+      // Global slots for larger trees: local ids and entries stay below 4096
+      // (16-bit ranks, 32-bit edge keys).
+      if (T > cap && T <= 4096) {
+        int big = cap;
+        while (big < T) big <<= 1;
+        s->big_cap = big;
+      }
+      if (bytes * kWarpsPerCta > 48 * 1024) {
+        DGFX_CUDA_TRY(cudaFuncSetAttribute(warp_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           bytes * kWarpsPerCta));
+      }
+    }
+  }
+  {
+    int dev = 0, sms = 148, per_sm = 1;
+    DGFX_CUDA_TRY(cudaGetDevice(&dev));
+    DGFX_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    DGFX_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sample_kernel, s->threads, s->smem_bytes));
+    s->padded_blocks = std::max(1, sms * std::max(1, per_sm));
+    if (s->warp_cap > 0) {
+      int wper = 1;
+      DGFX_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&wper, warp_sample_kernel, kWarpsPerCta * 32,
+                                                                 static_cast<size_t>(s->warp_bytes) * kWarpsPerCta));
+      s->warp_blocks = std::max(1, sms * std::max(1, wper));
+    }
+  }
   *out = s.release();
   return DGFX_OK;
 }
@@ -1049,6 +1714,29 @@ extern "C" void dgfx_sampler_destroy(dgfx_sampler* s) {
   if (s->d_tables != nullptr) cudaFree(s->d_tables);
   if (s->walk.d_nodes != nullptr) cudaFree(s->walk.d_nodes);
   delete s;
+}
+
+extern "C" int dgfx_sampler_set_kernel(dgfx_sampler* s, int32_t kind) {
+  if (s == nullptr || kind < 0 || kind > 1) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_set_kernel: bad arguments");
+  s->kernel_kind = kind;
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_sampler_kernel_info(const dgfx_sampler* s, int32_t* warp_capacity) {
+  if (s == nullptr || warp_capacity == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_kernel_info: null");
+  *warp_capacity = s->kernel_kind == 0 ? s->warp_cap : 0;
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_sampler_kernel_stats(dgfx_sampler* s, dgfx_stream stream_, int64_t* out2) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (s == nullptr || out2 == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_kernel_stats: null argument");
+  unsigned long long st[2];
+  DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status + 7, sizeof(st), cudaMemcpyDeviceToHost, stream));
+  DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
+  out2[0] = static_cast<int64_t>(st[0]);
+  out2[1] = static_cast<int64_t>(st[1]);
+  return DGFX_OK;
 }
 
 extern "C" int dgfx_sampler_tree_size(const dgfx_sampler* s, int64_t* positions) {
@@ -1092,6 +1780,7 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   // Status words 0..5 (memsets, so the call can be captured in a CUDA graph).
   DGFX_CUDA_TRY(cudaMemsetAsync(s->d_status, 0xFF, sizeof(unsigned long long), stream));
   DGFX_CUDA_TRY(cudaMemsetAsync(s->d_status + 1, 0, 5 * sizeof(unsigned long long), stream));
+  DGFX_CUDA_TRY(cudaMemsetAsync(s->d_status + 7, 0, 2 * sizeof(unsigned long long), stream));
   s->last_B = B;
   s->last_seeds = d_seeds;
   Arena arena(d_workspace, workspace_bytes);
@@ -1140,9 +1829,37 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   p.pbits = s->pbits;
   p.keybits = s->keybits;
   for (int i = 0; i < kMaxNodesets; ++i) p.ns_key_base[i] = s->ns_key_base[i];
+  p.pnodes = s->d_pnodes;
+  p.warp_cap = s->warp_cap;
+  p.max_edges_per_node = s->max_edges_per_node;
+  p.warp_bytes = s->warp_bytes;
+  p.overflow_count = b.overflow_count;
+  p.overflow_list = nullptr;
   const size_t smem = s->smem_bytes;
-  sample_kernel<<<static_cast<unsigned>(B), s->threads, smem, stream>>>(p);
-  DGFX_CUDA_TRY(cudaGetLastError());
+  if (s->warp_cap > 0 && s->kernel_kind == 0) {
+    DGFX_CUDA_TRY(cudaMemsetAsync(b.overflow_count, 0, 2 * sizeof(unsigned int), stream));
+    if (b.num_big_slots > 0) {
+      DGFX_CUDA_TRY(cudaMemsetAsync(b.big_locks, 0, sizeof(unsigned int) * b.num_big_slots, stream));
+    }
+    p.overflow_list = b.overflow_list;
+    p.big_slots = b.big_slots;
+    p.big_locks = b.big_locks;
+    p.num_big_slots = b.num_big_slots;
+    p.big_cap = s->big_cap;
+    p.big_bytes = 24 * s->big_cap;
+    const int64_t blocks = std::min<int64_t>(ceil_div(B, kWarpsPerCta), s->warp_blocks);
+    warp_sample_kernel<<<static_cast<unsigned>(blocks), kWarpsPerCta * 32,
+                         static_cast<size_t>(s->warp_bytes) * kWarpsPerCta, stream>>>(p);
+    DGFX_CUDA_TRY(cudaGetLastError());
+    if (s->T > s->warp_cap) {  // seeds whose trees outgrew the warp's capacity
+      const int64_t pb = std::min<int64_t>(B, s->padded_blocks);
+      sample_kernel<<<static_cast<unsigned>(pb), s->threads, smem, stream>>>(p);
+      DGFX_CUDA_TRY(cudaGetLastError());
+    }
+  } else {
+    sample_kernel<<<static_cast<unsigned>(B), s->threads, smem, stream>>>(p);
+    DGFX_CUDA_TRY(cudaGetLastError());
+  }
   const size_t mark = arena.used;
   DGFX_TRY(exclusive_scan<int32_t>(b.node_cnt, out->node_offsets, B * s->num_nodesets, true, arena, stream));
   arena.used = mark;

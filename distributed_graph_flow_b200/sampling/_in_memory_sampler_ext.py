@@ -256,6 +256,25 @@ class Sampler:
         _native.check(_native.lib().dgfx_sampler_tree_size(self._handle, ctypes.byref(v)))
         return v.value
 
+    def set_kernel(self, kind: int) -> None:
+        """0 (default): warp sampler with padded fallback for large trees;
+        1: padded sampler for every seed. Both give identical batches."""
+        _native.check(_native.lib().dgfx_sampler_set_kernel(self._handle, int(kind)))
+
+    @property
+    def warp_capacity(self) -> int:
+        """Per-seed entry capacity of the warp sampler (0: not used)."""
+        v = ctypes.c_int32()
+        _native.check(_native.lib().dgfx_sampler_kernel_info(self._handle, ctypes.byref(v)))
+        return v.value
+
+    def kernel_stats(self, stream=None):
+        """(seeds finished in a global slot, seeds finished by the padded
+        sampler) of the last call."""
+        out = (ctypes.c_int64 * 2)()
+        _native.check(_native.lib().dgfx_sampler_kernel_stats(self._handle, _native.stream_handle(stream), out))
+        return int(out[0]), int(out[1])
+
     # -- sampling --------------------------------------------------------
     def _workspace(self, nbytes: int):
         """Scratch reused across calls (calls on one sampler are serialised

@@ -123,6 +123,22 @@ int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_nodeset,
                         dgfx_sampler** out);
 void dgfx_sampler_destroy(dgfx_sampler* sampler);
 
+/* Kernel choice of dgfx_sampler_sample (no counterpart in the reference,
+ * whose sampler is host code). kind 0 (default): the warp sampler (one warp
+ * per seed over the occupied tree positions, in shared memory) when the
+ * plan allows it, with seeds whose trees outgrow its capacity finished by
+ * the padded sampler; kind 1: the padded sampler (one CTA per seed over all
+ * tree positions) for every seed. Both give identical batches in every mode
+ * (same random stream). dgfx_sampler_kernel_info reports the warp
+ * sampler's per-seed entry capacity, 0 when it is not used. */
+int dgfx_sampler_set_kernel(dgfx_sampler* sampler, int32_t kind);
+int dgfx_sampler_kernel_info(const dgfx_sampler* sampler, int32_t* warp_capacity);
+/* Of the last dgfx_sampler_sample's seeds (synchronises `stream`):
+ * out2[0] = seeds the warp sampler finished in a global-memory slot (trees
+ * larger than its shared arrays), out2[1] = seeds finished by the padded
+ * sampler (trees larger than any slot, or every slot busy). */
+int dgfx_sampler_kernel_stats(dgfx_sampler* sampler, dgfx_stream stream, int64_t* out2);
+
 /* Positions of the padded per-seed expansion tree (an upper bound on the
  * nodes of one sample). */
 int dgfx_sampler_tree_size(const dgfx_sampler* sampler, int64_t* positions);
@@ -554,6 +570,45 @@ int dgfx_merge_edgeset(const int64_t* d_node_offsets,
                        int64_t num_out, int64_t sentinel_src,
                        int64_t sentinel_dst, int64_t* d_out_src,
                        int64_t* d_out_dst, dgfx_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Sparse-matrix helpers around dgfx_spmm_csr.
+ * dgfx_csr_add_diagonal: from the structure CSR of S = A + A^T (implicit
+ * values 1; built by dgfx_csr_build over the concatenated edge list) writes
+ * M = S + diag * I with one diagonal entry appended per row (out_rowptr
+ * [n + 1], out_col / out_val [nnz + n]); normalize_symmetric != 0 scales
+ * entry (r, c) by 1 / sqrt(d_r d_c), d = row sums of M. Replaces the
+ * propagation matrices the reference builds with sparse_deferred:
+ * GCN (adj + adj.T).add_eye().normalize_symmetric()
+ * (dgf/src/learning/jax/layers/homo_gnn_sparse_deferred.py:293) and GIN
+ * (adj + adj.T).add_eye(1 + eps) (:526).
+ * dgfx_csr_row_ids: out[j] = row of CSR entry j (to transpose a CSR for the
+ * SpMM's backward pass: rows of the transpose = columns of the matrix).
+ * dgfx_segment_counts: counts[s] = items with id s (ids outside [0, n_seg)
+ * are skipped), the degrees of jax.ops.segment_sum's mean pooling
+ * (dgf/src/learning/jax/layers/hetero_gnn.py:288-293).
+ * dgfx_gather_rows_scaled: out[i, :] = src[ids[i], :] (/ max(counts[ids[i]],
+ * 1) if counts != NULL), zero rows for ids outside [0, num_segments): the
+ * gradient of segment_sum / segment mean with respect to its data.
+ * dgfx_batch_csr: the merged batch of a one-node-set, one-edge-set sampler
+ * (dgfx_sampler_sample) as a CSR over batch nodes: row = batch index of an
+ * edge's source, column (int32) = batch index of its target; rows past the
+ * batch's node count up to node_capacity are empty (rowptr has
+ * node_capacity + 1 entries), so no host synchronisation is needed. With
+ * dgfx_spmm_csr(normalize=1) it is the mean aggregation of hetero_gnn.py:
+ * 282-294 over the sampled subgraph, messages flowing from the sampled
+ * neighbours to the node that sampled them.
+ * ------------------------------------------------------------------------ */
+int dgfx_csr_add_diagonal(const int64_t* d_rowptr, const int32_t* d_col, int64_t num_rows, float diag,
+                          int32_t normalize_symmetric, int64_t* d_out_rowptr, int32_t* d_out_col, float* d_out_val,
+                          dgfx_stream stream);
+int dgfx_csr_row_ids(const int64_t* d_rowptr, int64_t num_rows, int64_t* d_out, dgfx_stream stream);
+int dgfx_segment_counts(const int64_t* d_ids, int64_t n, int64_t num_segments, int32_t* d_counts, dgfx_stream stream);
+int dgfx_gather_rows_scaled(const void* d_src, int dtype, const int64_t* d_ids, int64_t n, int64_t num_segments,
+                            int64_t feat, const int32_t* d_counts, void* d_out, dgfx_stream stream);
+int dgfx_batch_csr(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
+                   const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity, int64_t* d_rowptr,
+                   int32_t* d_col, dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
  * Seeded synthetic inputs (stand-ins for the benchmark datasets, the role of

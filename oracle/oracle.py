@@ -575,6 +575,81 @@ def csr_spmm(rowptr: np.ndarray, col: np.ndarray, x: np.ndarray, val: Optional[n
     return y
 
 
+def csr_spmm_grad_x(rowptr: np.ndarray, col: np.ndarray, dy: np.ndarray, num_x_rows: int,
+                    val: Optional[np.ndarray] = None, normalize: bool = False) -> np.ndarray:
+    """d loss / d X of Y = S A X for an upstream gradient dY: A^T S dY in
+    float64 (S = diag(1 / max(deg, 1)) when normalize)."""
+    import scipy.sparse as sp
+
+    rowptr = np.asarray(rowptr, np.int64)
+    n_rows = len(rowptr) - 1
+    v = np.ones(len(col), np.float64) if val is None else np.asarray(val, np.float64)
+    a = sp.csr_matrix((v, np.asarray(col, np.int64), rowptr), shape=(n_rows, num_x_rows))
+    g = np.asarray(dy, np.float64)
+    if normalize:
+        g = g / np.maximum(np.diff(rowptr).astype(np.float64), 1.0)[:, None]
+    return a.T @ g
+
+
+def segment_sum_grad(dy: np.ndarray, segment_ids: np.ndarray, num_segments: int, mean: bool = False) -> np.ndarray:
+    """d loss / d data of jax.ops.segment_sum(data, ids, n) [/ max(count, 1)]
+    (hetero_gnn.py:283-295): each item gets its segment's upstream gradient
+    (scaled by 1 / max(count, 1) for the mean), zero for ids out of range."""
+    ids = np.asarray(segment_ids, np.int64)
+    g = np.asarray(dy, np.float64)
+    ok = (ids >= 0) & (ids < num_segments)
+    out = np.zeros((len(ids),) + g.shape[1:], np.float64)
+    out[ok] = g[ids[ok]]
+    if mean:
+        cnt = np.bincount(ids[ok], minlength=num_segments).astype(np.float64)
+        out[ok] /= np.maximum(cnt[ids[ok]], 1.0).reshape((-1,) + (1,) * (g.ndim - 1))
+    return out
+
+
+def propagation_matrix(src: np.ndarray, dst: np.ndarray, num_nodes: int, diag: float,
+                       normalize_symmetric: bool) -> np.ndarray:
+    """Dense float64 (A + A^T + diag * I), optionally D^-1/2 (.) D^-1/2 with
+    D the row sums, for an edge list on one node set: the propagation
+    matrices of dgf/src/learning/jax/layers/homo_gnn_sparse_deferred.py:293
+    (GCN: ``(adj + adj.transpose()).add_eye().normalize_symmetric()``) and
+    :526 (GIN: ``(adj + adj.transpose()).add_eye(1 + epsilon)``). Their
+    arithmetic is the third-party sparse-deferred package (requirements.txt:
+    13, unpinned, not in the reference tree), restated from its published
+    semantics: a SparseMatrix is a COO sum (duplicate entries add),
+    transpose swaps the indices, add_eye(v) adds v on the diagonal, and
+    normalize_symmetric divides entry (i, j) by sqrt(rowsum_i) *
+    sqrt(colsum_j)."""
+    m = np.zeros((num_nodes, num_nodes), np.float64)
+    s = np.asarray(src, np.int64)
+    d = np.asarray(dst, np.int64)
+    np.add.at(m, (d, s), 1.0)
+    np.add.at(m, (s, d), 1.0)
+    m[np.arange(num_nodes), np.arange(num_nodes)] += diag
+    if normalize_symmetric:
+        r = np.sqrt(m.sum(1))
+        c = np.sqrt(m.sum(0))
+        m = m / r[:, None] / c[None, :]
+    return m
+
+
+def batch_mean_aggregate(node_offsets: np.ndarray, edge_offsets: np.ndarray, edges: np.ndarray,
+                         features: np.ndarray) -> np.ndarray:
+    """Mean aggregation over a merged sampled batch (one node set and edge
+    set), float64: out[v] = mean of features[u] over the batch edges v -> u
+    (jax.ops.segment_sum of the neighbours' features over the edge sources,
+    divided by max(count, 1); hetero_gnn.py:282-294 with the edge direction
+    reversed), zero for nodes without edges."""
+    n = int(node_offsets[-1])
+    B = len(node_offsets) - 1
+    samp = np.repeat(np.arange(B), np.diff(edge_offsets))
+    gsrc = node_offsets[:-1][samp] + edges[0]
+    gdst = node_offsets[:-1][samp] + edges[1]
+    out = np.zeros((n, features.shape[1]), np.float64)
+    np.add.at(out, gsrc, np.asarray(features[gdst], np.float64))
+    cnt = np.bincount(gsrc, minlength=n).astype(np.float64)
+    return out / np.maximum(cnt, 1.0)[:, None]
+
+
 # ---------------------------------------------------------------------------
 # Edge creation times (dgf/src/transform/temporal.py:95-103).
 # ---------------------------------------------------------------------------

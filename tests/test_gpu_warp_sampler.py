@@ -1,0 +1,136 @@
+"""The warp sampler (one warp per seed over occupied positions) against the
+padded sampler (one CTA per seed over every position) and the oracle.
+
+Both kernels draw from the same Philox counters, so their batches must be
+identical in every mode, random included: small heterogeneous graphs
+(temporal, masking, with replacement, several plans), trees larger than the
+warp's capacity (seeds handed to the padded sampler), and the power-law
+generator with the [15, 10, 5] plan. FIRST mode is also compared with the
+oracle where the warp path is taken."""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import random_hetero_graph
+
+pytestmark = pytest.mark.gpu
+
+
+def _pair(sampling, graph, schema, conf, mode, mask_es=None):
+    plan = sampling.simple_sampling_config_to_sampling_plan(sampling.SimpleSamplingConfig(**conf), schema)
+    a = sampling.create_sampler(graph, plan, schema, return_features=False, return_node_idxs=True, batch_size=64,
+                                sampling_mode=mode, seed=5, edgeset_to_mask=mask_es)
+    b = sampling.create_sampler(graph, plan, schema, return_features=False, return_node_idxs=True, batch_size=64,
+                                sampling_mode=mode, seed=5, edgeset_to_mask=mask_es)
+    b._cc_sampler.set_kernel(1)
+    return a, b
+
+
+def _same_batches(a, b, seeds, ts=None, masks=None, calls=2):
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+
+    dev = torch.device("cuda", 0)
+    sd = torch.as_tensor(np.asarray(seeds, np.int64), device=dev)
+    st = None if ts is None else torch.as_tensor(np.asarray(ts, np.int64), device=dev)
+    mk = None if masks is None else torch.as_tensor(np.asarray(masks, np.int64), device=dev)
+    for c in range(calls):
+        x = ext.batch_to_host(a._cc_sampler.sample_merged(sd, st, mk, call_index=c))
+        y = ext.batch_to_host(b._cc_sampler.sample_merged(sd, st, mk, call_index=c))
+        for u, v in zip(x, y):
+            np.testing.assert_array_equal(u, v)
+    a._cc_sampler.check()
+    b._cc_sampler.check()
+
+
+CONFS = [
+    dict(seed_nodeset="a", num_hops=2, hop_width=3),
+    dict(seed_nodeset="a", num_hops=3, hop_width=2, with_replacement=True),
+    dict(seed_nodeset="b", num_hops=2, hop_width=4, reverse=False),
+    dict(seed_nodeset="c", num_hops=3, hop_width=2),
+    dict(seed_nodeset="a", num_hops=2, hop_width=7),
+]
+
+
+@pytest.fixture(scope="module")
+def sampling(cuda):
+    from distributed_graph_flow_b200 import sampling
+
+    return sampling
+
+
+@pytest.mark.parametrize("conf", CONFS)
+@pytest.mark.parametrize("temporal", [False, True])
+@pytest.mark.parametrize("mode_name", ["MODE_RANDOM", "MODE_FIRST", "MODE_MOST_RECENT"])
+def test_warp_equals_padded(sampling, conf, temporal, mode_name):
+    if mode_name == "MODE_MOST_RECENT" and not temporal:
+        pytest.skip("newest-k needs timestamps")
+    graph, schema = random_hetero_graph(3, temporal=temporal)
+    conf = dict(conf, temporal_sampling=temporal)
+    a, b = _pair(sampling, graph, schema, conf, getattr(sampling, mode_name))
+    assert a._cc_sampler.warp_capacity > 0 and b._cc_sampler.warp_capacity == 0
+    rng = np.random.default_rng(4)
+    n = graph.node_sets[conf["seed_nodeset"]].num_nodes
+    seeds = np.concatenate([np.arange(n), rng.integers(0, n, 200)])
+    ts = rng.integers(-3, 55, len(seeds)) if temporal else None
+    _same_batches(a, b, seeds, ts)
+
+
+@pytest.mark.parametrize("mode_name", ["MODE_RANDOM", "MODE_FIRST"])
+def test_warp_equals_padded_masking(sampling, mode_name):
+    graph, schema = random_hetero_graph(6, temporal=False)
+    a, b = _pair(sampling, graph, schema, dict(seed_nodeset="a", num_hops=2, hop_width=3),
+                 getattr(sampling, mode_name), mask_es="ab")
+    rng = np.random.default_rng(2)
+    m = graph.edge_sets["ab"].adjacency.shape[1]
+    seeds = rng.integers(0, 40, 300)
+    masks = rng.integers(-1, m, 300)
+    _same_batches(a, b, seeds, None, masks)
+
+
+@pytest.mark.parametrize("mode_name", ["MODE_RANDOM", "MODE_FIRST"])
+def test_overflow_to_padded(sampling, mode_name):
+    """Trees beyond the warp capacity (256 entries) and beyond any global
+    slot (4096 entries) finish in the padded sampler; the batch is
+    unchanged."""
+    graph, schema = random_hetero_graph(8, temporal=False, sizes={"a": 60, "b": 30, "c": 9},
+                                        edges={"ab": ("a", "b", 3000), "aa": ("a", "a", 2000),
+                                               "bc": ("b", "c", 600), "ca": ("c", "a", 300)})
+    a, b = _pair(sampling, graph, schema, dict(seed_nodeset="a", num_hops=3, hop_width=6),
+                 getattr(sampling, mode_name))
+    assert a._cc_sampler.tree_size > 4096 and a._cc_sampler.warp_capacity == 256
+    seeds = np.arange(60)
+    _same_batches(a, b, seeds)
+    big, padded = a._cc_sampler.kernel_stats()
+    assert big == 0 and padded > 0  # no global slots for trees this large
+
+
+def test_large_generator_warp_equals_padded(cuda):
+    """The power-law generator at 0.5 % with the [15, 10, 5] plan, random and
+    FIRST modes, 4096 seeds (some outgrow the warp's shared arrays and finish
+    in global slots)."""
+    import dataclasses
+
+    from distributed_graph_flow_b200 import _native, synth
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+    from distributed_graph_flow_b200.sampling import config as cfg
+
+    dev = torch.device("cuda", 0)
+    s = synth.LARGE_SHARDED
+    spec = dataclasses.replace(s, num_nodes=int(s.num_nodes * 0.005), num_edges=int(s.num_edges * 0.005))
+    index, _, _ = synth.build_graph(spec, dev)
+    plan = cfg.explicit_plan("paper", "cites", [15, 10, 5])
+    seeds = synth.uniform_int(4096, 0, spec.num_nodes, 77, 5, dev)
+    for mode in (_native.MODE_RANDOM, _native.MODE_FIRST):
+        a = ext.create_device_sampler(plan, ["paper"], [spec.num_nodes], ["cites"], [index], [None], mode, seed=9)
+        b = ext.create_device_sampler(plan, ["paper"], [spec.num_nodes], ["cites"], [index], [None], mode, seed=9)
+        b.set_kernel(1)
+        for c in range(2):
+            x = ext.batch_to_host(a.sample_merged(seeds, call_index=c))
+            big, padded = a.kernel_stats()
+            assert big > 0 and padded == 0  # trees of 257..916 entries finish in global slots
+            y = ext.batch_to_host(b.sample_merged(seeds, call_index=c))
+            for u, v in zip(x, y):
+                np.testing.assert_array_equal(u, v)
+        a.check()
+        b.check()
