@@ -626,14 +626,17 @@ def bench_spmm(dev, steps, scale=1.0):
 # Temporal 169K-node sampler.
 # ---------------------------------------------------------------------------
 def bench_temporal(dev, steps, scale=1.0, streams=8):
-    """Temporal 169K-node sampler + fp32 feature gather, batches of 1024
-    seeds. Reported: eager launches on one stream; one CUDA graph per batch
-    on one stream (per-batch latency); and the headline throughput with
-    `streams` batches in flight (one captured step, sampler handle and
-    stream each)."""
+    """Temporal 169K-node sampler, batches of 1024 seeds, each step = sample
+    (cutoff = seed timestamp) + gather the fp32 features of the sampled
+    nodes + mean aggregation over the sampled subgraph (every node's mean of
+    the features of the neighbours it sampled; jax.ops.segment_sum mean
+    pooling of hetero_gnn.py:282-294). Reported: one batch per step on one
+    stream (eager launches, and one CUDA graph per batch: the per-batch
+    latency a training loop sees, the headline here) and `streams`
+    independent batches forked inside one graph (throughput)."""
     import torch
 
-    from distributed_graph_flow_b200 import _native, synth
+    from distributed_graph_flow_b200 import _native, aggregation, synth
     from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
     from distributed_graph_flow_b200.sampling import config as cfg
 
@@ -649,7 +652,13 @@ def bench_temporal(dev, steps, scale=1.0, streams=8):
     nb = 8 + steps
     seeds = synth.uniform_int(nb * B, 0, spec.num_nodes, 21, 9, dev).view(nb, B)
     sts = node_ts[seeds]
-    feats = torch.empty((B * cc.tree_size, FEAT_DIM), dtype=torch.float32, device=dev)
+    cap = B * cc.tree_size
+    ecap = B * (cc.tree_size - 1)
+    feats = torch.empty((cap, FEAT_DIM), dtype=torch.float32, device=dev)
+    aggs = torch.empty((cap, FEAT_DIM), dtype=torch.float32, device=dev)
+    rowptr = torch.empty(cap + 1, dtype=torch.int64, device=dev)
+    col = torch.empty(ecap, dtype=torch.int32, device=dev)
+    ws = aggregation.spmm_workspace(cap, ecap, FEAT_DIM, dev)
 
     def step(i):
         m = cc.sample_merged(seeds[i], sts[i], None, call_index=i, check=False)
@@ -657,6 +666,11 @@ def bench_temporal(dev, steps, scale=1.0, streams=8):
         _native.check(_native.lib().dgfx_gather_rows_ranged(
             _native.ptr(table), spec.num_nodes, FEAT_DIM * 4, _native.ptr(m.node_ids), _native.elem_ptr(off, 0),
             _native.elem_ptr(off, -1), int(m.node_ids.numel()), _native.ptr(feats), _native.stream_handle()))
+        _native.check(_native.lib().dgfx_batch_csr(
+            _native.ptr(off), _native.ptr(m.edge_offsets), _native.ptr(m.edge_src), _native.ptr(m.edge_dst), B, cap,
+            _native.ptr(rowptr), _native.ptr(col), _native.stream_handle()))
+        aggregation.batch_mean_aggregate(m, feats, out=aggs, workspace=ws, csr=(rowptr, col))
+        return m
 
     for i in range(5):
         step(i)
@@ -666,56 +680,100 @@ def bench_temporal(dev, steps, scale=1.0, streams=8):
     samplers = [ext.create_device_sampler(plan, ["v"], [spec.num_nodes], ["e"], [index], [None],
                                           _native.MODE_RANDOM, seed=3 + k, has_temporal=True)
                 for k in range(streams)]
-    one = ext.CapturedSampleStep(samplers[0], B, True, table)
+    one = ext.CapturedSampleStep(samplers[0], B, True, table, aggregate=True)
     for i in range(4):
         one.run(seeds[i], sts[i])
     ms_graph = timed(lambda i: one.run(seeds[8 + i], sts[8 + i]), steps, torch.cuda.synchronize,
                      "temporal_graph", finish=one.wait)
     del one
-    multi = ext.CapturedSampleStep(samplers, B, True, table)
+    multi = ext.CapturedSampleStep(samplers, B, True, table, aggregate=True)
     reps = steps // streams
     for i in range(4):
         multi.run(seeds[i * streams:(i + 1) * streams], sts[i * streams:(i + 1) * streams])
-    ms = timed(lambda i: multi.run(seeds[8 + i * streams:8 + (i + 1) * streams],
-                                   sts[8 + i * streams:8 + (i + 1) * streams]),
-               reps, torch.cuda.synchronize, "temporal", finish=multi.wait) / streams
+    ms_multi = timed(lambda i: multi.run(seeds[8 + i * streams:8 + (i + 1) * streams],
+                                         sts[8 + i * streams:8 + (i + 1) * streams]),
+                     reps, torch.cuda.synchronize, "temporal", finish=multi.wait) / streams
     for smp in samplers:
         smp.check()
+    del multi
     out = {"workload": "temporal 169,343 nodes / 1,166,243 edges, Zipf(2.1), ts in [0,50), fanout [10,5], "
-                       "1024 seeds per batch, cutoff = seed ts, fp32 128-d features",
-           "value": round(B / (ms / 1e3), 1), "unit": "subgraphs/s", "ms_per_batch": round(ms, 4),
-           "mode": f"{streams} independent batches of 1024 seeds per CUDA-graph replay (sample + gather each, "
-                   f"forked onto {streams} streams inside the graph, one sampler handle per batch)",
-           "single_stream_graph": {"value": round(B / (ms_graph / 1e3), 1), "ms_per_batch": round(ms_graph, 4)},
-           "eager": {"value": round(B / (ms_eager / 1e3), 1), "ms_per_batch": round(ms_eager, 4)}}
-    # CPU baseline on the same graph and seeds.
+                       "1024 seeds per batch, cutoff = seed ts, fp32 128-d features, then mean aggregation over the "
+                       "sampled subgraph",
+           "step": "sample + feature gather + mean aggregation (batch CSR + row-normalised SpMM), one batch",
+           "value": round(B / (ms_graph / 1e3), 1), "unit": "subgraphs/s", "ms_per_batch": round(ms_graph, 4),
+           "mode": "one batch of 1024 seeds per CUDA-graph replay on one stream",
+           "eager": {"value": round(B / (ms_eager / 1e3), 1), "ms_per_batch": round(ms_eager, 4)},
+           f"{streams}_batches_per_replay": {"value": round(B / (ms_multi / 1e3), 1),
+                                             "ms_per_batch": round(ms_multi, 4),
+                                             "mode": f"{streams} independent batches forked onto {streams} streams "
+                                                     "inside one CUDA graph"}}
+    # CPU baseline on the same graph and seeds (+ the FIRST-mode parity batch).
     try:
         from oracle import oracle as O
 
         s, kind = cpu_sampler_from_index(index, spec.num_nodes, plan, temporal=True)
+        first = ext.create_device_sampler(plan, ["v"], [spec.num_nodes], ["e"], [index], [None], _native.MODE_FIRST,
+                                          seed=3, has_temporal=True)
+        par = first_mode_parity(s, first, seeds[0], sts[0])
+        # The aggregation of that batch against the float64 restatement.
+        m = first.sample_merged(seeds[0], sts[0])
+        f0 = aggregation.gather_rows(table, m.node_ids)
+        a0 = aggregation.batch_mean_aggregate(m, f0)
+        nodes_h, off_h, edges_h, eoff_h = ext.batch_to_host(m)
+        n0 = int(off_h[-1])
+        fh = table.cpu().numpy()[nodes_h]
+        exp = O.batch_mean_aggregate(off_h, eoff_h, edges_h, fh)
+        mag = O.batch_mean_aggregate(off_h, eoff_h, edges_h, np.abs(fh))
+        err = np.abs(a0[:n0].cpu().numpy() - exp)
+        par["mean_aggregation_within_1e-5"] = bool(np.all(err <= 1e-5 * np.maximum(mag, 1e-30) + 1e-30))
+        del first
         th = host_cores()
         host_tab = table.cpu().numpy()
         seeds_h = seeds.cpu().numpy()
         sts_h = sts.cpu().numpy()
-        done, t_tot = 0, 0.0
+        done, t_tot, t_agg = 0, 0.0, 0.0
         i = 0
         while t_tot < 10.0 and i < nb:
             t0 = time.perf_counter()
-            nc, ec, nodes, _, _ = s.sample_raw(seeds_h[i], sts_h[i], threads=th)
-            off = 0
-            for c in nc[:, 0]:
-                _ = host_tab[nodes[off:off + c]]
+            nc, ec, nodes, esrc, edst = s.sample_raw(seeds_h[i], sts_h[i], threads=th)
+            rows, off = [], 0
+            for c in nc[:, 0]:  # add_features_to_samples: one gather per sample
+                rows.append(host_tab[nodes[off:off + c]])
                 off += c
-            t_tot += time.perf_counter() - t0
+            t1 = time.perf_counter()
+            cpu_mean_aggregate(nc[:, 0], ec[:, 0], esrc, edst, np.concatenate(rows))
+            t2 = time.perf_counter()
+            t_tot += t2 - t0
+            t_agg += t2 - t1
             done += B
             i += 1
             if i == nb:
                 i = 0
         out["cpu_baseline"] = {"value": round(done / t_tot, 1), "unit": "subgraphs/s", "cores": th, "kind": kind,
-                               "sample": f"{done} seeds, topology + numpy feature gather"}
+                               "sample": f"{done} seeds: topology ({kind} sampler, {th} threads) + numpy feature "
+                                         f"gather per sample + numpy mean aggregation over the merged batch "
+                                         f"({t_agg:.2f} s of {t_tot:.2f} s)"}
         out["speedup_vs_cpu"] = round(out["value"] / out["cpu_baseline"]["value"], 1)
+        out["parity"] = par
     except Exception as exc:  # noqa: BLE001
         out["cpu_baseline"] = {"unavailable": str(exc)}
+    return out
+
+
+def cpu_mean_aggregate(node_counts, edge_counts, esrc, edst, feats):
+    """Mean of the sampled neighbours' features for every node of a merged
+    batch on the host (numpy; sources are sorted within a sample, so batch
+    sources are sorted and np.add.reduceat sums each node's run)."""
+    n_off = np.concatenate([[0], np.cumsum(node_counts)])
+    samp = np.repeat(np.arange(len(edge_counts)), edge_counts)
+    gsrc = n_off[:-1][samp] + esrc
+    gdst = n_off[:-1][samp] + edst
+    out = np.zeros_like(feats)
+    if len(gsrc):
+        starts = np.flatnonzero(np.concatenate([[True], gsrc[1:] != gsrc[:-1]]))
+        sums = np.add.reduceat(feats[gdst], starts, axis=0)
+        cnt = np.diff(np.concatenate([starts, [len(gsrc)]]))
+        out[gsrc[starts]] = sums / cnt[:, None]
     return out
 
 

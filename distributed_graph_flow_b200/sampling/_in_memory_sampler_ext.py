@@ -494,11 +494,15 @@ class CapturedSampleStep:
     until the next ``run``: a list of K (MergedBatch, feature rows) pairs, or
     one pair for a single sampler. Each sampler handle belongs to this step
     (handles serialise their calls). ``table`` is a [num_rows, F] feature
-    matrix of node set ``feature_nodeset``."""
+    matrix of node set ``feature_nodeset``. With ``aggregate`` (one node set
+    and edge set) every node's mean over the features of the neighbours it
+    sampled follows the gather (aggregation.batch_mean_aggregate) and the
+    results are (MergedBatch, feature rows, aggregates) triples."""
 
     def __init__(self, samplers, batch_size: int, with_timestamps: bool, table=None, feature_nodeset: int = 0,
-                 stream=None):
+                 stream=None, aggregate: bool = False):
         torch = _torch()
+        from distributed_graph_flow_b200 import aggregation
         self.single = not isinstance(samplers, (list, tuple))
         self.samplers = [samplers] if self.single else list(samplers)
         K = len(self.samplers)
@@ -510,10 +514,21 @@ class CapturedSampleStep:
         self.seed_ts = torch.zeros((K, self.B), dtype=torch.int64, device=dev) if with_timestamps else None
         ns = int(feature_nodeset)
         self.features = [None] * K
+        self.aggregates = [None] * K
+        if aggregate and (table is None or any(len(smp._nodeset_index) != 1 or len(smp._edgeset_index) != 1
+                                               for smp in self.samplers)):
+            raise ValueError("aggregate needs a feature table and samplers over one node set and one edge set")
+        agg_bufs = [None] * K
         if table is not None:
             for k, smp in enumerate(self.samplers):
                 cap = self.B * smp.tree_size
                 self.features[k] = torch.empty((cap, int(table.shape[1])), dtype=table.dtype, device=dev)
+                if aggregate:
+                    ecap = self.B * max(1, smp.tree_size - 1)
+                    self.aggregates[k] = torch.empty((cap, int(table.shape[1])), dtype=table.dtype, device=dev)
+                    agg_bufs[k] = (torch.empty(cap + 1, dtype=torch.int64, device=dev),
+                                   torch.empty(ecap, dtype=torch.int32, device=dev),
+                                   aggregation.spmm_workspace(cap, ecap, int(table.shape[1]), dev))
 
         def body(k):
             smp = self.samplers[k]
@@ -526,6 +541,14 @@ class CapturedSampleStep:
                     _native.ptr(batch.node_ids), _native.elem_ptr(off, ns * self.B),
                     _native.elem_ptr(off, (ns + 1) * self.B), int(batch.node_ids.numel()),
                     _native.ptr(self.features[k]), _native.stream_handle()))
+                if aggregate:  # mean over each node's sampled neighbours
+                    rowptr, col, ws = agg_bufs[k]
+                    _native.check(_native.lib().dgfx_batch_csr(
+                        _native.ptr(off), _native.ptr(batch.edge_offsets), _native.ptr(batch.edge_src),
+                        _native.ptr(batch.edge_dst), self.B, int(batch.node_ids.numel()), _native.ptr(rowptr),
+                        _native.ptr(col), _native.stream_handle()))
+                    aggregation.csr_spmm(rowptr, col[:int(batch.edge_src.numel())], self.features[k], normalize=True,
+                                         out=self.aggregates[k], workspace=ws)
             return batch
 
         for k in range(K):  # allocates each sampler's workspace outside the capture
@@ -553,7 +576,10 @@ class CapturedSampleStep:
             if self.seed_ts is not None:
                 self.seed_ts.copy_(seed_ts.view(self.seed_ts.shape), non_blocking=True)
             self.graph.replay()
-        out = list(zip(self.batches, self.features))
+        if self.aggregates[0] is not None:
+            out = list(zip(self.batches, self.features, self.aggregates))
+        else:
+            out = list(zip(self.batches, self.features))
         return out[0] if self.single else out
 
     def wait(self):

@@ -16,6 +16,8 @@ reference's layers need gradients:
   matrices are built from the graph): a val that requires grad is rejected.
 * ``dgfx::segment_sum(data, segment_ids, num_segments, mean)`` — gradient:
   d data[i] = dY[ids[i]] (/ max(count, 1) for the mean), a row gather.
+  The two gradients are operators of their own (``dgfx::csr_spmm_grad_x``,
+  ``dgfx::segment_sum_grad``), so backward graphs trace with fake tensors.
 * ``dgfx::segment_softmax(logits, messages, segment_ids, num_segments)`` and
   ``dgfx::sage_mean_linear_relu(rowptr, col, x, weight, bias)`` — forward
   (inference) operators with fake implementations.
@@ -61,19 +63,30 @@ def _csr_spmm_setup(ctx, inputs, output):
     ctx.x_dtype = x.dtype
 
 
+@torch.library.custom_op(f"{_LIB}::csr_spmm_grad_x", mutates_args=())
+def csr_spmm_grad_x(rowptr: torch.Tensor, col: torch.Tensor, val: Optional[torch.Tensor], grad: torch.Tensor,
+                    normalize: bool, num_x_rows: int) -> torch.Tensor:
+    """A^T S dY: the transposed CSR (device build) times dY."""
+    v = val
+    if normalize:
+        # Entry (r, c) of S A is val_rc / max(deg_r, 1).
+        deg = (rowptr[1:] - rowptr[:-1]).clamp_min(1).to(torch.float32)
+        scale = (1.0 / deg)[aggregation.csr_row_ids(rowptr)]
+        v = scale if val is None else val * scale
+    rp_t, col_t, val_t = aggregation.csr_transpose(rowptr, col, v, int(num_x_rows))
+    return aggregation.csr_spmm(rp_t, col_t, grad.contiguous(), val=val_t, normalize=False, num_rows=int(num_x_rows))
+
+
+@csr_spmm_grad_x.register_fake
+def _csr_spmm_grad_x_fake(rowptr, col, val, grad, normalize, num_x_rows):
+    return grad.new_empty((num_x_rows, grad.shape[1]))
+
+
 def _csr_spmm_backward(ctx, grad):
     rowptr, col, val = ctx.saved_tensors
     dx = None
     if ctx.needs_input_grad[3]:
-        v = val
-        if ctx.normalize:
-            # Entry (r, c) of S A is val_rc / max(deg_r, 1).
-            deg = (rowptr[1:] - rowptr[:-1]).clamp_min(1).to(torch.float32)
-            scale = (1.0 / deg)[aggregation.csr_row_ids(rowptr)]
-            v = scale if val is None else val * scale
-        rp_t, col_t, val_t = aggregation.csr_transpose(rowptr, col, v if v is not None else None, ctx.num_x_rows)
-        dx = aggregation.csr_spmm(rp_t, col_t, grad.contiguous().to(ctx.x_dtype), val=val_t, normalize=False,
-                                  num_rows=ctx.num_x_rows)
+        dx = torch.ops.dgfx.csr_spmm_grad_x(rowptr, col, val, grad.to(ctx.x_dtype), ctx.normalize, ctx.num_x_rows)
     return None, None, None, dx, None, None
 
 
@@ -101,12 +114,23 @@ def _segment_sum_setup(ctx, inputs, output):
     ctx.data_dtype = data.dtype
 
 
+@torch.library.custom_op(f"{_LIB}::segment_sum_grad", mutates_args=())
+def segment_sum_grad(grad: torch.Tensor, segment_ids: torch.Tensor, num_segments: int, mean: bool) -> torch.Tensor:
+    """d data[i] = dY[ids[i]] (/ max(count, 1) for the mean)."""
+    counts = aggregation.segment_counts(segment_ids, int(num_segments)) if mean else None
+    return aggregation.gather_rows_scaled(grad.contiguous(), segment_ids, int(num_segments), counts)
+
+
+@segment_sum_grad.register_fake
+def _segment_sum_grad_fake(grad, segment_ids, num_segments, mean):
+    return grad.new_empty((segment_ids.shape[0], grad.shape[1]))
+
+
 def _segment_sum_backward(ctx, grad):
     (ids,) = ctx.saved_tensors
     d = None
     if ctx.needs_input_grad[0]:
-        counts = aggregation.segment_counts(ids, ctx.num_segments) if ctx.mean else None
-        d = aggregation.gather_rows_scaled(grad.contiguous().to(ctx.data_dtype), ids, ctx.num_segments, counts)
+        d = torch.ops.dgfx.segment_sum_grad(grad.to(ctx.data_dtype), ids, ctx.num_segments, ctx.mean)
     return d, None, None, None
 
 
