@@ -365,7 +365,78 @@ def bench_large(args, rank, world, dev):
     cache_info = getattr(sharded.features, "cache_info", None)
     if cache_info is not None:
         res["workload_stats"]["halo_cache"] = dict(cache_info)
+    if world > 1 and isinstance(sharded.features, driver.PeerFeatures):
+        res["multi_gpu"] = multi_gpu_checks(args, sharded, spec, seeds, W, K, rank, world, dev, sync)
     return res, (spec, index, table, cc, plan, seeds, W, sharded)
+
+
+def multi_gpu_checks(args, sharded, spec, seeds, W, K, rank, world, dev, sync):
+    """N > 1, outside the timed region (every rank takes the same collective
+    steps): (1) the feature rows one step gathered across the ranks equal
+    the rows regenerated from the seeded generator, bit for bit, on every
+    rank; (2) per-stage times of the bulk exchange (partition, barrier,
+    serve, barrier, scatter; medians over K steps, max over ranks); (3) the
+    same K steps with the replicated row cache switched off (pure node-range
+    partitioning)."""
+    import torch
+    import torch.distributed as dist
+
+    from distributed_graph_flow_b200 import _native, driver, synth
+
+    feats_obj = sharded.features
+    out = {}
+    # (1) correctness of the gathered halo rows.
+    merged, feats, _ = sharded.step(seeds[W])
+    torch.cuda.synchronize()
+    n = int(merged.node_offsets[-1].item())
+    ids = merged.node_ids[:n]
+    exp = synth.normal_rows(ids, FEAT_DIM, spec.seed + 100, torch.bfloat16)
+    owner = torch.div(ids, feats_obj.rows_per_rank, rounding_mode="floor")
+    remote = owner != rank
+    bad = (feats[:n].view(torch.int16) != exp.view(torch.int16)).any(dim=1)
+    t = torch.tensor([int(bad.sum().item()), n, int(remote.sum().item())], dtype=torch.int64, device=dev)
+    dist.all_reduce(t)
+    out["halo_rows_checked"] = int(t[1].item())
+    out["halo_rows_remote"] = int(t[2].item())
+    out["halo_rows_mismatched"] = int(t[0].item())
+    out["halo_rows_bit_exact"] = bool(t[0].item() == 0)
+    # (2) per-stage times of the exchange.
+    if feats_obj._ex is not None:
+        names = ["partition", "barrier_1", "serve", "barrier_2", "scatter"]
+        per = {k: [] for k in names}
+        cap = int(merged.node_ids.numel())
+        buf = torch.empty((cap, feats_obj.dim), dtype=feats_obj.dtype, device=dev)
+        for i in range(K):
+            m = sharded.cc.sample_merged(seeds[W + i], call_index=20_000 + i * world + rank, check=False)
+            ev = []
+            feats_obj.gather_range(m.node_ids, _native.elem_ptr(m.node_offsets, 0),
+                                   _native.elem_ptr(m.node_offsets, -1), cap, buf, stage_events=ev)
+            torch.cuda.synchronize()
+            for j, k in enumerate(names):
+                per[k].append(ev[j].elapsed_time(ev[j + 1]))
+        feats_obj.check()
+        med = torch.tensor([statistics.median(per[k]) for k in names], dtype=torch.float64, device=dev)
+        dist.all_reduce(med, op=dist.ReduceOp.MAX)
+        out["exchange_stage_ms"] = {k: round(float(v), 4) for k, v in zip(names, med.tolist())}
+        out["exchange_stage_note"] = "median over steps of each stage alone (not overlapped), max over ranks"
+    # (3) the replicated row cache off.
+    if feats_obj._replica is not None:
+        saved = (feats_obj._replica, feats_obj._hot_slot)
+        feats_obj._replica, feats_obj._hot_slot = None, None
+        step = sharded.step_overlapped if args.overlap else sharded.step
+        for i in range(2):
+            step(seeds[i])
+        sharded.drain()
+        ms = timed(lambda i: step(seeds[W + i]), K, sync, "step_no_cache", finish=sharded.drain)
+        feats_obj.check()
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        feats_obj._replica, feats_obj._hot_slot = saved
+        out["no_halo_cache"] = {"value": round(B_SEEDS * world / (float(t.item()) / 1e3), 1), "unit": "subgraphs/s",
+                                "ms_per_step": round(float(t.item()), 4),
+                                "what": "same steps with the replicated row cache off (pure node-range "
+                                        "partitioning: every remote row crosses NVLink)"}
+    return out
 
 
 def large_config(args, world):
@@ -653,12 +724,8 @@ def bench_temporal(dev, steps, scale=1.0, streams=8):
     seeds = synth.uniform_int(nb * B, 0, spec.num_nodes, 21, 9, dev).view(nb, B)
     sts = node_ts[seeds]
     cap = B * cc.tree_size
-    ecap = B * (cc.tree_size - 1)
     feats = torch.empty((cap, FEAT_DIM), dtype=torch.float32, device=dev)
     aggs = torch.empty((cap, FEAT_DIM), dtype=torch.float32, device=dev)
-    rowptr = torch.empty(cap + 1, dtype=torch.int64, device=dev)
-    col = torch.empty(ecap, dtype=torch.int32, device=dev)
-    ws = aggregation.spmm_workspace(cap, ecap, FEAT_DIM, dev)
 
     def step(i):
         m = cc.sample_merged(seeds[i], sts[i], None, call_index=i, check=False)
@@ -666,10 +733,7 @@ def bench_temporal(dev, steps, scale=1.0, streams=8):
         _native.check(_native.lib().dgfx_gather_rows_ranged(
             _native.ptr(table), spec.num_nodes, FEAT_DIM * 4, _native.ptr(m.node_ids), _native.elem_ptr(off, 0),
             _native.elem_ptr(off, -1), int(m.node_ids.numel()), _native.ptr(feats), _native.stream_handle()))
-        _native.check(_native.lib().dgfx_batch_csr(
-            _native.ptr(off), _native.ptr(m.edge_offsets), _native.ptr(m.edge_src), _native.ptr(m.edge_dst), B, cap,
-            _native.ptr(rowptr), _native.ptr(col), _native.stream_handle()))
-        aggregation.batch_mean_aggregate(m, feats, out=aggs, workspace=ws, csr=(rowptr, col))
+        aggregation.batch_mean_aggregate(m, feats, out=aggs)
         return m
 
     for i in range(5):
@@ -699,7 +763,7 @@ def bench_temporal(dev, steps, scale=1.0, streams=8):
     out = {"workload": "temporal 169,343 nodes / 1,166,243 edges, Zipf(2.1), ts in [0,50), fanout [10,5], "
                        "1024 seeds per batch, cutoff = seed ts, fp32 128-d features, then mean aggregation over the "
                        "sampled subgraph",
-           "step": "sample + feature gather + mean aggregation (batch CSR + row-normalised SpMM), one batch",
+           "step": "sample + feature gather + mean aggregation over the sampled subgraph (one kernel), one batch",
            "value": round(B / (ms_graph / 1e3), 1), "unit": "subgraphs/s", "ms_per_batch": round(ms_graph, 4),
            "mode": "one batch of 1024 seeds per CUDA-graph replay on one stream",
            "eager": {"value": round(B / (ms_eager / 1e3), 1), "ms_per_batch": round(ms_eager, 4)},

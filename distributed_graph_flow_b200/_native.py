@@ -139,6 +139,7 @@ SIGNATURES = {
     "dgfx_segment_counts": (_int, [_vp, _i64, _i64, _vp, _vp]),
     "dgfx_gather_rows_scaled": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "dgfx_batch_csr": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp]),
+    "dgfx_batch_mean": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _int, _i64, _vp, _vp]),
     "dgfx_sampler_kernel_info": (_int, [_vp, _p_i32]),
     "dgfx_sampler_kernel_stats": (_int, [_vp, _vp, _p_i64]),
     "dgfx_synth_graph_workspace_size": (_int, [_i64, _i64, ctypes.POINTER(_sz)]),
@@ -146,6 +147,7 @@ SIGNATURES = {
     "dgfx_synth_bipartite": (_int, [_i64, _i64, _i64, ctypes.c_double, _i64, _u64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "dgfx_synth_uniform_int": (_int, [_i64, _i64, _i64, _u64, ctypes.c_uint32, _vp, _vp]),
     "dgfx_synth_normal_features": (_int, [_i64, _i64, _i64, _u64, _int, _vp, _vp]),
+    "dgfx_synth_normal_rows": (_int, [_vp, _i64, _i64, _u64, _int, _vp, _vp]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

@@ -301,12 +301,22 @@ def batch_csr(batch, stream=None):
     return rowptr, col
 
 
-def batch_mean_aggregate(batch, features, out=None, workspace=None, csr=None, stream=None):
+def batch_mean_aggregate(batch, features, out=None, stream=None):
     """Mean aggregation over a merged sampled batch (jax.ops.segment_sum
     mean pooling of hetero_gnn.py:282-294, messages = the features of the
     sampled neighbours flowing to the node that sampled them): out[v] =
     mean of features[u] over the batch edges v -> u, zero rows for nodes
-    without sampled neighbours. features [capacity, F] in batch order
-    (the rows gathered for batch.node_ids)."""
-    rowptr, col = csr if csr is not None else batch_csr(batch, stream)
-    return csr_spmm(rowptr, col, features, normalize=True, out=out, workspace=workspace, stream=stream)
+    without sampled neighbours; rows past the batch's node count are left
+    as they are. features [capacity, F] in batch order (the rows gathered
+    for batch.node_ids). One kernel (dgfx_batch_mean); the same values as
+    csr_spmm(*batch_csr(batch), features, normalize=True)."""
+    torch = _native.require_cuda()
+    cap = int(batch.node_ids.numel())
+    F = int(features.numel() // max(1, features.shape[0]))
+    if out is None:
+        out = torch.empty_like(features)
+    _native.check(_native.lib().dgfx_batch_mean(
+        _native.ptr(batch.node_offsets), _native.ptr(batch.edge_offsets), _native.ptr(batch.edge_src),
+        _native.ptr(batch.edge_dst), int(batch.B), cap, _native.ptr(features), _dtype_code(features.dtype), F,
+        _native.ptr(out), _native.stream_handle(stream)))
+    return out

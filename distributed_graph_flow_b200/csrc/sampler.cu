@@ -117,11 +117,6 @@ struct Params {
   int32_t warp_bytes;          // shared memory per warp
   unsigned int* overflow_count;  // [0] seeds for the padded kernel, [1] next seed of the warp kernel
   int32_t* overflow_list;        // seeds with more entries than any warp slot holds
-  // Global-memory slots (capacity big_cap >= T entries) for seeds that
-  // outgrow the warp's shared arrays; a lock word per slot.
-  char* big_slots;
-  unsigned int* big_locks;
-  int32_t big_cap, big_bytes, num_big_slots;
 };
 
 // Per-CTA working arrays (shared or global memory). The dedup table packs
@@ -735,7 +730,7 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
 // seed whose tree outgrows warp_cap entries is listed for the padded sampler
 // (it starts again there with the same random stream).
 // ===========================================================================
-constexpr int kWarpCapMax = 256;
+constexpr int kWarpCapMax = 128;  // 4 entries per lane: ranks and edge sorts by one all-pairs pass
 constexpr int kWarpsPerCta = 4;
 constexpr int kMaxWarpDepth = 30;
 
@@ -782,67 +777,105 @@ __device__ __forceinline__ U4 task_block(uint32_t key0, uint32_t key1, int32_t q
   return philox4x32_10(c, key0 ^ call.y, key1);
 }
 
-// Picks of one task into at[0, cnt): CSR positions in adjacency order
-// (random: Floyd's k-subset of the valid row; FIRST / MOST_RECENT: the first
-// / last cnt valid entries). Random draws from rows of at most 64 valid
-// entries keep the chosen set as a 64-bit mask (O(1) duplicate test; the
-// set bits come out in adjacency order); longer rows use the shared array.
-__device__ __forceinline__ void warp_picks(uint32_t key0, uint32_t key1, long long* at, int32_t cnt, int64_t rb,
-                                           int64_t nv, int64_t moff, int mode, int32_t q, int32_t e, uint32_t slot,
-                                           uint2 call) {
-  if (mode == DGFX_MODE_RANDOM && cnt < nv) {
-    const bool small = nv <= 64;
-    unsigned long long chosen = 0;
-    U4 block{};
-    for (int32_t m = 0; m < cnt; ++m) {
-      if ((m & 1) == 0) block = task_block(key0, key1, q, e, m, slot, call);
-      const uint64_t r = (m & 1) ? (static_cast<uint64_t>(block.w) << 32 | block.z)
-                                 : (static_cast<uint64_t>(block.y) << 32 | block.x);
-      const int64_t j = nv - cnt + m;
-      int64_t t = static_cast<int64_t>(bounded64(r, static_cast<uint64_t>(j + 1)));
-      if (small) {
-        if ((chosen >> t) & 1ull) t = j;
-        chosen |= 1ull << t;
-      } else {
-        for (int32_t i = 0; i < m; ++i) {
-          if (at[i] == t) {
-            t = j;
-            break;
-          }
-        }
-        at[m] = t;
-      }
-    }
-    if (small) {
-      for (int32_t i = 0; i < cnt; ++i) {
-        long long off = __ffsll(static_cast<long long>(chosen)) - 1;
-        chosen &= chosen - 1;
-        if (moff >= 0 && off >= moff) ++off;
-        at[i] = rb + off;
-      }
-      return;
-    }
-    for (int32_t i = 1; i < cnt; ++i) {  // adjacency order
-      const long long x = at[i];
-      int32_t j = i - 1;
-      while (j >= 0 && at[j] > x) {
-        at[j + 1] = at[j];
-        --j;
-      }
-      at[j + 1] = x;
-    }
+// Picks of one round of tasks (one task per lane; all lanes call): into
+// at[0, cnt) of each lane's task, CSR positions in adjacency order. Random
+// mode: Floyd's k-subset of the valid row. The Philox blocks of the whole
+// round (counters: tree position, plan edge | block index, seed slot, call
+// index; two 64-bit draws per block, as in the padded sampler) are computed
+// lane-parallel into `stage` (stage_blocks blocks at a time), then each lane
+// runs its task's Floyd steps over its draws: rows of at most 64 valid
+// entries keep the chosen set as a 64-bit mask (O(1) duplicate test, the set
+// bits come out in adjacency order), longer rows use the task's own array.
+// FIRST / MOST_RECENT (and random with cnt == nv): the first / last cnt
+// valid entries.
+__device__ __forceinline__ void warp_round_picks(uint32_t key0, uint32_t key1, long long* at, int32_t cnt, int64_t rb,
+                                                 int64_t nv, int64_t moff, int mode, int32_t q, int32_t e,
+                                                 uint32_t slot, uint2 call, unsigned long long* stage,
+                                                 int stage_blocks) {
+  constexpr unsigned FULL = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const bool rnd = mode == DGFX_MODE_RANDOM && cnt > 0 && cnt < nv;
+  if (!rnd && cnt > 0) {
+    const int64_t first = (mode == DGFX_MODE_MOST_RECENT) ? nv - cnt : 0;
     for (int32_t i = 0; i < cnt; ++i) {
-      long long off = at[i];
+      int64_t off = first + i;
       if (moff >= 0 && off >= moff) ++off;
       at[i] = rb + off;
     }
+  }
+  const int nb = rnd ? (cnt + 1) >> 1 : 0;
+  const int incl = warp_inclusive_scan(nb);
+  const int total = __shfl_sync(FULL, incl, 31);
+  if (total == 0) return;
+  const int off = incl - nb;
+  const bool small = nv <= 64;
+  unsigned long long chosen = 0;
+  int32_t m = 0;
+  for (int base = 0; base < total; base += stage_blocks) {
+    const int end = min(total, base + stage_blocks);
+    for (int b0 = base; b0 < end; b0 += 32) {
+      const int b = b0 + lane;
+      // Owner of block b: the last lane whose first block is <= b.
+      int L = 0;
+#pragma unroll
+      for (int step = 16; step > 0; step >>= 1) {
+        const int oc = __shfl_sync(FULL, off, min(L + step, 31));
+        if (L + step <= 31 && oc <= b) L += step;
+      }
+      const int32_t qo = __shfl_sync(FULL, q, L);
+      const int32_t eo = __shfl_sync(FULL, e, L);
+      const int offo = __shfl_sync(FULL, off, L);
+      if (b < end) {
+        const U4 r = task_block(key0, key1, qo, eo, 2 * (b - offo), slot, call);
+        stage[2 * (b - base)] = static_cast<unsigned long long>(r.y) << 32 | r.x;
+        stage[2 * (b - base) + 1] = static_cast<unsigned long long>(r.w) << 32 | r.z;
+      }
+    }
+    __syncwarp();
+    if (rnd) {
+      for (; m < cnt && off + (m >> 1) < end; ++m) {
+        const uint64_t r = stage[2 * (off + (m >> 1) - base) + (m & 1)];
+        const int64_t j = nv - cnt + m;
+        int64_t t = static_cast<int64_t>(bounded64(r, static_cast<uint64_t>(j + 1)));
+        if (small) {
+          if ((chosen >> t) & 1ull) t = j;
+          chosen |= 1ull << t;
+        } else {
+          for (int32_t i = 0; i < m; ++i) {
+            if (at[i] == t) {
+              t = j;
+              break;
+            }
+          }
+          at[m] = t;
+        }
+      }
+    }
+    __syncwarp();
+  }
+  if (!rnd) return;
+  if (small) {
+    for (int32_t i = 0; i < cnt; ++i) {
+      long long o = __ffsll(static_cast<long long>(chosen)) - 1;
+      chosen &= chosen - 1;
+      if (moff >= 0 && o >= moff) ++o;
+      at[i] = rb + o;
+    }
     return;
   }
-  const int64_t first = (mode == DGFX_MODE_MOST_RECENT) ? nv - cnt : 0;
+  for (int32_t i = 1; i < cnt; ++i) {  // adjacency order
+    const long long x = at[i];
+    int32_t j = i - 1;
+    while (j >= 0 && at[j] > x) {
+      at[j + 1] = at[j];
+      --j;
+    }
+    at[j + 1] = x;
+  }
   for (int32_t i = 0; i < cnt; ++i) {
-    int64_t off = first + i;
-    if (moff >= 0 && off >= moff) ++off;
-    at[i] = rb + off;
+    long long o = at[i];
+    if (moff >= 0 && o >= moff) ++o;
+    at[i] = rb + o;
   }
 }
 
@@ -859,21 +892,13 @@ struct WarpArrays {
   int32_t* lv;       // [depth + 2] level boundaries
 };
 
-// A word of the dedup table: the shared-memory variant reads it plainly;
-// the global-memory variant (big slots) reads it at L2 with an atomic, since
-// the table is written by atomics there and a plain load could return a
-// stale L1 line.
-template <bool kGlobal>
-__device__ __forceinline__ unsigned long long tab_read(unsigned long long* a) {
-  if constexpr (kGlobal) return atomicAdd(a, 0ull);
-  else return *a;
-}
-
-// Samples one seed with arrays of capacity C; returns false (nothing
-// written) if the tree has more than C occupied positions.
-template <bool kGlobal>
-__device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArrays& w, const int C, const int64_t sample,
+// Samples one seed with arrays of capacity C = 32 * K (K entries per lane
+// in the all-pairs passes); returns false (nothing written) if the tree has
+// more than C occupied positions.
+template <int K>
+__device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArrays& w, const int64_t sample,
                                                 uint2 call) {
+  constexpr int C = 32 * K;
   constexpr unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const uint32_t lt = (1u << lane) - 1u;
@@ -955,9 +980,10 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
         overflow = true;
         break;
       }
+      const int32_t out = fill + inc - cnt;
+      warp_round_picks(p.key0, p.key1, at + out, cnt, rb, nv, moff, md, q, pe, slot, call,
+                       reinterpret_cast<unsigned long long*>(order), C / 4);
       if (cnt > 0) {
-        const int32_t out = fill + inc - cnt;
-        warp_picks(p.key0, p.key1, at + out, cnt, rb, nv, moff, md, q, pe, slot, call);
         const EdgeDev& E = p.edges[pe];
         const int32_t base = q + E.rel_off;
         const int32_t mt = (ent << 8) | E.child;
@@ -1002,44 +1028,26 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
   const int n = lv[D + 1];
 
   // 2. Numbering. Rank in depth-first order = number of entries with a
-  //    smaller position: all pairs (broadcast loads) for small trees,
-  //    binary searches over the position-sorted levels otherwise.
-  if (n <= 64) {
-    const int32_t p0 = lane < n ? pos[lane] : 0x7FFFFFFF;
-    const int32_t p1 = lane + 32 < n ? pos[lane + 32] : 0x7FFFFFFF;
-    int r0 = 0, r1 = 0;
+  //    smaller position (K entries per lane, all pairs by broadcast loads).
+  {
+    int32_t pk[K];
+    int rk[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      pk[k] = lane + 32 * k < n ? pos[lane + 32 * k] : 0x7FFFFFFF;
+      rk[k] = 0;
+    }
     for (int j = 0; j < n; ++j) {
       const int32_t pj = pos[j];
-      r0 += pj < p0 ? 1 : 0;
-      r1 += pj < p1 ? 1 : 0;
+#pragma unroll
+      for (int k = 0; k < K; ++k) rk[k] += pj < pk[k] ? 1 : 0;
     }
-    if (lane < n) {
-      local[lane] = static_cast<uint16_t>(r0);
-      order[r0] = static_cast<uint16_t>(lane);
-    }
-    if (lane + 32 < n) {
-      local[lane + 32] = static_cast<uint16_t>(r1);
-      order[r1] = static_cast<uint16_t>(lane + 32);
-    }
-  } else {
-    for (int i = lane; i < n; i += 32) {
-      const int32_t pq = pos[i];
-      int d = 0;
-      while (i >= lv[d + 1]) ++d;
-      int r = i - lv[d];
-      for (int d2 = 0; d2 <= D; ++d2) {
-        if (d2 == d) continue;
-        int lo = lv[d2], hi = lv[d2 + 1];
-        const int b0 = lo;
-        while (lo < hi) {
-          const int mid = (lo + hi) >> 1;
-          if (pos[mid] < pq) lo = mid + 1;
-          else hi = mid;
-        }
-        r += lo - b0;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (lane + 32 * k < n) {
+        local[lane + 32 * k] = static_cast<uint16_t>(rk[k]);
+        order[rk[k]] = static_cast<uint16_t>(lane + 32 * k);
       }
-      local[i] = static_cast<uint16_t>(r);
-      order[r] = static_cast<uint16_t>(i);
     }
   }
   __syncwarp();
@@ -1048,10 +1056,7 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     int H = 2;
     while (H < 2 * n && H < C) H <<= 1;
     const int log2H = 31 - __clz(H);
-    for (int i = lane; i < H; i += 32) {
-      if constexpr (kGlobal) atomicExch(&tab[i], kEmptyKey);
-      else tab[i] = kEmptyKey;
-    }
+    for (int i = lane; i < H; i += 32) tab[i] = kEmptyKey;
     __syncwarp();
     for (int i = lane; i < n; i += 32) {
       const int ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
@@ -1085,7 +1090,7 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     if (r < n) {
       i = order[r];
       const bool first = p.with_replacement ||
-                         (pos[i] >= 0 && static_cast<uint32_t>(tab_read<kGlobal>(&tab[pos[i]])) == static_cast<uint32_t>(r));
+                         (pos[i] >= 0 && static_cast<uint32_t>(tab[pos[i]]) == static_cast<uint32_t>(r));
       if (first) ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
     }
     const uint32_t peers = __match_any_sync(FULL, ns);
@@ -1095,14 +1100,14 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     if (ns >= 0) {
       const uint32_t l = static_cast<uint32_t>(base) + __popc(peers & lt);
       if (p.with_replacement) local[i] = static_cast<uint16_t>(l);
-      else tab[pos[i]] = (tab_read<kGlobal>(&tab[pos[i]]) & 0xFFFFFFFF00000000ull) | (0x80000000u | l);
+      else tab[pos[i]] = (tab[pos[i]] & 0xFFFFFFFF00000000ull) | (0x80000000u | l);
       if ((peers & lt) == 0) ns_cnt[ns] = base + __popc(peers);
     }
     __syncwarp();
   }
   if (!p.with_replacement) {
     for (int i = lane; i < n; i += 32) {
-      local[i] = pos[i] >= 0 ? static_cast<uint16_t>(static_cast<uint32_t>(tab_read<kGlobal>(&tab[pos[i]])) & 0x7FFFFFFFu) : 0;
+      local[i] = pos[i] >= 0 ? static_cast<uint16_t>(static_cast<uint32_t>(tab[pos[i]]) & 0x7FFFFFFFu) : 0;
     }
   }
   __syncwarp();
@@ -1120,9 +1125,8 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
   }
   __syncwarp();
 
-  // 3. Edges: a 32-bit key (edgeset | src | dst; local ids < 4096) per
-  //    non-root entry, sort (ranks by broadcast loads for up to 64 keys, else
-  //    a bitonic sort), deduplicate.
+  // 3. Edges: a 32-bit key (edgeset | src | dst) per non-root entry,
+  //    sorted by rank (all pairs by broadcast loads), deduplicated.
   const int nk = n > 0 ? n - 1 : 0;
   uint32_t* keys = reinterpret_cast<uint32_t*>(at);
   auto edge_key = [&](int c) -> uint32_t {
@@ -1132,45 +1136,28 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     const uint32_t src = E.reversed ? b : a, dst = E.reversed ? a : b;
     return (static_cast<uint32_t>(E.edgeset) << (2 * lb)) | (src << lb) | dst;
   };
-  const uint32_t* ek;
-  if (nk <= 64) {
-    const uint32_t k0 = lane < nk ? edge_key(lane + 1) : ~0u;
-    const uint32_t k1 = lane + 32 < nk ? edge_key(lane + 33) : ~0u;
-    if (lane < nk) keys[lane] = k0;
-    if (lane + 32 < nk) keys[lane + 32] = k1;
+  {
+    uint32_t kk[K];
+    int rk[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      kk[k] = lane + 32 * k < nk ? edge_key(lane + 32 * k + 1) : ~0u;
+      rk[k] = 0;
+      if (lane + 32 * k < nk) keys[lane + 32 * k] = kk[k];
+    }
     __syncwarp();
-    int r0 = 0, r1 = 0;
     for (int j = 0; j < nk; ++j) {
       const uint32_t kj = keys[j];
-      r0 += (kj < k0 || (kj == k0 && j < lane)) ? 1 : 0;
-      r1 += (kj < k1 || (kj == k1 && j < lane + 32)) ? 1 : 0;
+#pragma unroll
+      for (int k = 0; k < K; ++k) rk[k] += (kj < kk[k] || (kj == kk[k] && j < lane + 32 * k)) ? 1 : 0;
     }
     uint32_t* sorted = reinterpret_cast<uint32_t*>(node);
-    if (lane < nk) sorted[r0] = k0;
-    if (lane + 32 < nk) sorted[r1] = k1;
-    ek = sorted;
-  } else {
-    int P = 1;
-    while (P < nk) P <<= 1;
-    for (int i = lane; i < P; i += 32) keys[i] = i < nk ? edge_key(i + 1) : ~0u;
-    __syncwarp();
-    for (int k = 2; k <= P; k <<= 1) {
-      for (int j = k >> 1; j > 0; j >>= 1) {
-        for (int i = lane; i < P; i += 32) {
-          const int ixj = i ^ j;
-          if (ixj > i) {
-            const uint32_t a = keys[i], b = keys[ixj];
-            if ((a > b) == ((i & k) == 0)) {
-              keys[i] = b;
-              keys[ixj] = a;
-            }
-          }
-        }
-        __syncwarp();
-      }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (lane + 32 * k < nk) sorted[rk[k]] = kk[k];
     }
-    ek = keys;
   }
+  const uint32_t* ek = reinterpret_cast<const uint32_t*>(node);
   __syncwarp();
   uint64_t* out_edges = p.scratch_edges + sample * static_cast<int64_t>(p.T);
   const uint32_t lmask = (1u << lb) - 1;
@@ -1211,10 +1198,11 @@ __device__ __forceinline__ WarpArrays carve_warp(char* base, int C, int32_t* cou
 
 // Persistent warps: each takes the next seed from a counter in turn, so a
 // warp whose seed has a large tree does not hold back the others.
+template <int K>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, 8) warp_sample_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(16) char smem_warp[];
   const int lane = threadIdx.x & 31;
-  const int C = p.warp_cap;
+  constexpr int C = 32 * K;
   const int NS = p.num_nodesets, ES = p.num_edgesets;
   char* wb = smem_warp + static_cast<size_t>(threadIdx.x >> 5) * p.warp_bytes;
   int32_t* counters = reinterpret_cast<int32_t*>(wb + 24 * static_cast<size_t>(C));  // always in shared memory
@@ -1230,36 +1218,22 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 8) warp_sample_kernel(const
     if (lane == 0) s = atomicAdd(p.overflow_count + 1, 1u);
     s = __shfl_sync(0xffffffffu, s, 0);
     if (static_cast<int64_t>(s) >= p.B) break;
-    if (warp_sample_one<false>(p, w, C, static_cast<int64_t>(s), call)) continue;
-    // The tree outgrew the shared arrays: take a free global slot (each
-    // lock is tried once) and sample again there, else list the seed for
-    // the padded sampler.
-    int slot = -1;
-    if (lane == 0) {
-      for (int k = 0; k < p.num_big_slots; ++k) {
-        const int i = static_cast<int>((s + static_cast<unsigned int>(k)) % static_cast<unsigned int>(p.num_big_slots));
-        if (atomicCAS(&p.big_locks[i], 0u, 1u) == 0u) {
-          slot = i;
-          break;
-        }
-      }
+    if (warp_sample_one<K>(p, w, static_cast<int64_t>(s), call)) {
+      if (lane == 0) atomicAdd(&p.status[7], 1ull);
+      continue;
     }
-    slot = __shfl_sync(0xffffffffu, slot, 0);
-    if (slot >= 0) {
-      const WarpArrays g = carve_warp(p.big_slots + static_cast<size_t>(slot) * p.big_bytes, p.big_cap, counters, NS, ES);
-      warp_sample_one<true>(p, g, p.big_cap, static_cast<int64_t>(s), call);
-      __threadfence();  // the slot's writes are visible before it is released
-      __syncwarp();
-      if (lane == 0) {
-        atomicExch(&p.big_locks[slot], 0u);
-        atomicAdd(&p.status[7], 1ull);
-      }
-    } else if (lane == 0) {
+    // The tree outgrew the warp's arrays: the padded sampler redoes it.
+    if (lane == 0) {
       p.overflow_list[atomicAdd(p.overflow_count, 1u)] = static_cast<int32_t>(s);
       atomicAdd(&p.status[8], 1ull);
     }
     __syncwarp();
   }
+}
+
+using WarpKernel = void (*)(const Params);
+WarpKernel warp_kernel_for(int cap) {
+  return cap <= 32 ? warp_sample_kernel<1> : (cap <= 64 ? warp_sample_kernel<2> : warp_sample_kernel<4>);
 }
 
 // Largest row length of an index (the cap on useful slots per plan edge).
@@ -1335,7 +1309,6 @@ struct dgfx_sampler {
   int32_t kernel_kind = 0;
   int32_t padded_blocks = 0;  // CTAs of the padded sampler when it serves overflow seeds
   int32_t warp_blocks = 0;    // resident CTAs of the (persistent) warp sampler
-  int32_t big_cap = 0;        // entries of a global slot (0: none; overflow seeds go to the padded sampler)
   PlanNodeDev* d_pnodes = nullptr;
   int threads = 256;
   size_t smem_bytes = 0;
@@ -1374,9 +1347,6 @@ struct SampleBufs {
   char* global_work;
   unsigned int* overflow_count;
   int32_t* overflow_list;
-  int32_t num_big_slots;
-  unsigned int* big_locks;
-  char* big_slots;
 };
 
 void carve_sample(Arena& a, const dgfx_sampler* s, int64_t B, SampleBufs* b) {
@@ -1387,9 +1357,6 @@ void carve_sample(Arena& a, const dgfx_sampler* s, int64_t B, SampleBufs* b) {
   b->global_work = s->use_smem ? nullptr : a.take<char>(static_cast<size_t>(B) * work_bytes(s->T, s->H));
   b->overflow_count = a.take<unsigned int>(2);  // [0] overflowed seeds, [1] next seed of the warp sampler
   b->overflow_list = a.take<int32_t>(static_cast<size_t>(std::max<int64_t>(B, 1)));
-  b->num_big_slots = s->big_cap > 0 ? static_cast<int32_t>(std::min<int64_t>(256, std::max<int64_t>(1, B / 16))) : 0;
-  b->big_locks = a.take<unsigned int>(static_cast<size_t>(std::max(1, b->num_big_slots)));
-  b->big_slots = a.take<char>(static_cast<size_t>(b->num_big_slots) * 24 * static_cast<size_t>(s->big_cap));
 }
 
 size_t sample_ws_bytes(const dgfx_sampler* s, int64_t B) {
@@ -1615,7 +1582,7 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
   }
   DGFX_CUDA_TRY(cudaMemcpy(s->d_clevel, clevel.data(), sizeof(int32_t) * clevel.size(), cudaMemcpyHostToDevice));
   // Status: first bad seed, ts missing, table overflow, 3 stats, device call
-  // index, seeds finished in a global slot, seeds finished by the padded
+  // index, seeds finished by the warp sampler, seeds it handed to the padded
   // sampler.
   const unsigned long long init[9] = {~0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
   DGFX_CUDA_TRY(cudaMemcpy(s->d_status, init, sizeof(init), cudaMemcpyHostToDevice));
@@ -1673,22 +1640,15 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
   // they outgrow it). Plan node ids and parent entries are packed in 8 and
   // 24 bits.
   if (num_plan_nodes <= 256 && s->depth <= kMaxWarpDepth) {
-    int cap = 2;
+    int cap = 32;  // 32, 64 or 128 entries: 1, 2 or 4 per lane
     while (cap < T && cap < kWarpCapMax) cap <<= 1;
     const int bytes = warp_region_bytes(cap, num_nodesets, num_edgesets, s->depth);
     if (bytes * kWarpsPerCta <= 200 * 1024) {
       s->warp_cap = cap;
       s->warp_bytes = bytes;
-      // Global slots for larger trees: local ids and entries stay below 4096
-      // (16-bit ranks, 32-bit edge keys).
-      if (T > cap && T <= 4096) {
-        int big = cap;
-        while (big < T) big <<= 1;
-        s->big_cap = big;
-      }
       if (bytes * kWarpsPerCta > 48 * 1024) {
-        DGFX_CUDA_TRY(cudaFuncSetAttribute(warp_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           bytes * kWarpsPerCta));
+        DGFX_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(warp_kernel_for(cap)),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, bytes * kWarpsPerCta));
       }
     }
   }
@@ -1700,7 +1660,8 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
     s->padded_blocks = std::max(1, sms * std::max(1, per_sm));
     if (s->warp_cap > 0) {
       int wper = 1;
-      DGFX_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&wper, warp_sample_kernel, kWarpsPerCta * 32,
+      DGFX_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&wper, reinterpret_cast<const void*>(warp_kernel_for(s->warp_cap)),
+                                                                 kWarpsPerCta * 32,
                                                                  static_cast<size_t>(s->warp_bytes) * kWarpsPerCta));
       s->warp_blocks = std::max(1, sms * std::max(1, wper));
     }
@@ -1838,17 +1799,9 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   const size_t smem = s->smem_bytes;
   if (s->warp_cap > 0 && s->kernel_kind == 0) {
     DGFX_CUDA_TRY(cudaMemsetAsync(b.overflow_count, 0, 2 * sizeof(unsigned int), stream));
-    if (b.num_big_slots > 0) {
-      DGFX_CUDA_TRY(cudaMemsetAsync(b.big_locks, 0, sizeof(unsigned int) * b.num_big_slots, stream));
-    }
     p.overflow_list = b.overflow_list;
-    p.big_slots = b.big_slots;
-    p.big_locks = b.big_locks;
-    p.num_big_slots = b.num_big_slots;
-    p.big_cap = s->big_cap;
-    p.big_bytes = 24 * s->big_cap;
     const int64_t blocks = std::min<int64_t>(ceil_div(B, kWarpsPerCta), s->warp_blocks);
-    warp_sample_kernel<<<static_cast<unsigned>(blocks), kWarpsPerCta * 32,
+    warp_kernel_for(s->warp_cap)<<<static_cast<unsigned>(blocks), kWarpsPerCta * 32,
                          static_cast<size_t>(s->warp_bytes) * kWarpsPerCta, stream>>>(p);
     DGFX_CUDA_TRY(cudaGetLastError());
     if (s->T > s->warp_cap) {  // seeds whose trees outgrew the warp's capacity
@@ -1916,7 +1869,10 @@ extern "C" int dgfx_sampler_stats(dgfx_sampler* s, dgfx_stream stream_, int64_t*
 // kNoAllocScratchBytes (64 MiB) and every GPU that loads this library holds
 // it until the process exits. Its device address is looked up with
 // cudaGetSymbolAddress once per device, on the first call made with that
-// device current; make that first call before any stream capture.
+// device current; make that first call before any stream capture. The
+// address is kept for the life of the process, so a device reset
+// (cudaDeviceReset) invalidates it: the entry point must not be called
+// again after one in the same process.
 // All calls share the array and it keeps the previous call's contents; the
 // sampler writes every scratch word it later reads, so nothing needs
 // clearing. Calls whose executions overlap on the GPU (two streams, or two

@@ -138,10 +138,67 @@ __global__ void batch_csr_kernel(const int64_t* __restrict__ node_off, const int
   }
 }
 
+// Mean aggregation over a merged sampled batch in one pass: one warp per
+// sample; a sample's edges are sorted by local source, so node l's edges are
+// one run found by binary search. out[nb + l] = mean over that run of
+// feats[nb + dst], summed in edge order (fp32), zero rows for nodes without
+// edges. Rows past the batch's node count are not written.
+template <class T>
+__global__ void batch_mean_kernel(const int64_t* __restrict__ node_off, const int64_t* __restrict__ edge_off,
+                                  const int64_t* __restrict__ edge_src, const int64_t* __restrict__ edge_dst,
+                                  int64_t B, const T* __restrict__ feats, int64_t feat,
+                                  T* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t w0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  for (int64_t i = w0; i < B; i += warps) {
+    const int64_t nb = node_off[i], nn = node_off[i + 1] - nb;
+    const int64_t eb = edge_off[i], ne = edge_off[i + 1] - eb;
+    int64_t e = 0;  // edges are sorted by source: walk them once
+    for (int64_t l = 0; l < nn; ++l) {
+      int64_t lo = e, hi = ne;  // first edge with source > l
+      while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (edge_src[eb + mid] <= l) lo = mid + 1;
+        else hi = mid;
+      }
+      const int64_t cnt = lo - e;
+      const float inv = 1.0f / static_cast<float>(cnt > 1 ? cnt : 1);
+      for (int64_t f = lane; f < feat; f += 32) {
+        float acc = 0.0f;
+        for (int64_t k = e; k < lo; ++k) acc += to_f<T>(feats[(nb + edge_dst[eb + k]) * feat + f]);
+        out[(nb + l) * feat + f] = from_f<T>(acc * inv);
+      }
+      e = lo;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace dgfx
 
 using namespace dgfx;
+
+extern "C" int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
+                               const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity,
+                               const void* d_feats, int dtype, int64_t feat, void* d_out, dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (num_seeds < 0 || node_capacity < 0 || feat <= 0 || d_node_offsets == nullptr || d_edge_offsets == nullptr ||
+      (dtype != DGFX_F32 && dtype != DGFX_BF16)) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_batch_mean: bad arguments");
+  }
+  const unsigned g = grid_for_items(std::max<int64_t>(num_seeds * 32, 1), 256);
+  if (dtype == DGFX_F32) {
+    batch_mean_kernel<float><<<g, 256, 0, stream>>>(d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst, num_seeds,
+                                                    static_cast<const float*>(d_feats), feat, static_cast<float*>(d_out));
+  } else {
+    batch_mean_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst,
+                                                            num_seeds, static_cast<const __nv_bfloat16*>(d_feats),
+                                                            feat, static_cast<__nv_bfloat16*>(d_out));
+  }
+  DGFX_CUDA_TRY(cudaGetLastError());
+  return DGFX_OK;
+}
 
 extern "C" int dgfx_csr_add_diagonal(const int64_t* d_rowptr, const int32_t* d_col, int64_t num_rows, float diag,
                                      int32_t normalize_symmetric, int64_t* d_out_rowptr, int32_t* d_out_col,

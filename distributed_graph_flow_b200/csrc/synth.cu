@@ -120,6 +120,27 @@ __global__ void normal_features_kernel(int64_t node_begin, int64_t count, int64_
   }
 }
 
+// Rows of the same N(0, 1) table for an arbitrary list of node ids.
+template <class T>
+__global__ void normal_rows_kernel(const int64_t* __restrict__ ids, int64_t count, int64_t dim, uint32_t k0, uint32_t k1,
+                                   T* __restrict__ out) {
+  const int64_t pairs = (dim + 1) / 2;
+  const int64_t total = count * pairs;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / pairs, p = i - row * pairs;
+    const int64_t v = ids[row];
+    const U4 r = philox4x32_10(U4{static_cast<uint32_t>(v), static_cast<uint32_t>(v >> 32), static_cast<uint32_t>(p), 4u},
+                               k0, k1);
+    const double u1 = 1.0 - u01(r.x, r.y);
+    const double u2 = u01(r.z, r.w);
+    const double rad = sqrt(-2.0 * log(u1));
+    const double a = 6.283185307179586 * u2;
+    out[row * dim + 2 * p] = from_float<T>(static_cast<float>(rad * cos(a)));
+    if (2 * p + 1 < dim) out[row * dim + 2 * p + 1] = from_float<T>(static_cast<float>(rad * sin(a)));
+  }
+}
+
 unsigned blocks_for(int64_t n) {
   const int64_t b = ceil_div(std::max<int64_t>(n, 1), 256);
   return static_cast<unsigned>(std::min<int64_t>(b, 148 * 64));
@@ -229,6 +250,25 @@ extern "C" int dgfx_synth_normal_features(int64_t node_begin, int64_t count, int
   } else {
     normal_features_kernel<__nv_bfloat16><<<blocks_for(work), 256, 0, stream>>>(node_begin, count, dim, k0, k1,
                                                                                 static_cast<__nv_bfloat16*>(d_out));
+  }
+  DGFX_CUDA_TRY(cudaGetLastError());
+  return DGFX_OK;
+}
+
+extern "C" int dgfx_synth_normal_rows(const int64_t* d_ids, int64_t count, int64_t dim, uint64_t seed, int dtype,
+                                      void* d_out, dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (count < 0 || dim < 1 || (dtype != DGFX_F32 && dtype != DGFX_BF16)) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_synth_normal_rows: bad arguments");
+  }
+  if (count == 0) return DGFX_OK;
+  const uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+  const int64_t work = count * ((dim + 1) / 2);
+  if (dtype == DGFX_F32) {
+    normal_rows_kernel<float><<<blocks_for(work), 256, 0, stream>>>(d_ids, count, dim, k0, k1, static_cast<float*>(d_out));
+  } else {
+    normal_rows_kernel<__nv_bfloat16><<<blocks_for(work), 256, 0, stream>>>(d_ids, count, dim, k0, k1,
+                                                                            static_cast<__nv_bfloat16*>(d_out));
   }
   DGFX_CUDA_TRY(cudaGetLastError());
   return DGFX_OK;

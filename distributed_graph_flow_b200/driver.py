@@ -209,8 +209,11 @@ class PeerFeatures:
         torch.cuda.synchronize(self.device)
         return self
 
-    def gather_range(self, ids, begin_ptr: int, end_ptr: int, max_rows: int, out, stream=None):
-        """out[i] = feature row of ids[*begin + i] for i < min(*end - *begin, max_rows)."""
+    def gather_range(self, ids, begin_ptr: int, end_ptr: int, max_rows: int, out, stream=None, stage_events=None):
+        """out[i] = feature row of ids[*begin + i] for i < min(*end - *begin, max_rows).
+        With a list ``stage_events`` (bulk exchange), CUDA events recorded on
+        the stream after each stage (partition, barrier, serve, barrier,
+        scatter) are appended to it."""
         if self._ex is None:
             _native.check(_native.lib().dgfx_gather_rows_p2p(
                 _native.ptr(self._ptrs), self.world, self.rows_per_rank, self.num_nodes, self.row_bytes,
@@ -223,19 +226,31 @@ class PeerFeatures:
         sh = int(s.cuda_stream)
         lib = _native.lib()
         rep_rows = 0 if self._replica is None else int(self._replica.shape[0])
+        def mark():
+            if stage_events is not None:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record(s)
+                stage_events.append(e)
+
+        mark()
         _native.check(lib.dgfx_exchange_partition(
             self._ex.ptr, self.world, self.exchange_rows, self.rows_per_rank, self.num_nodes, self.row_bytes,
             _native.ptr(ids), begin_ptr, end_ptr, int(max_rows), _native.ptr(self._hot_slot),
             _native.ptr(self._req_pos), _native.ptr(out), sh))
+        mark()
         self._group_barrier(s)
+        mark()
         _native.check(lib.dgfx_exchange_serve(
             _native.ptr(self._ex_ptrs), self.world, self.rank, self.exchange_rows, self.rows_per_rank, self.row_bytes,
             self.buffer.ptr, self.local_rows, _native.ptr(self._replica), rep_rows, _native.ptr(self._req_pos),
             _native.ptr(out), sh))
+        mark()
         self._group_barrier(s)
+        mark()
         _native.check(lib.dgfx_exchange_scatter(
             _native.ptr(self._ex_ptrs), self.world, self.rank, self.exchange_rows, self.row_bytes,
             _native.ptr(self._req_pos), _native.ptr(out), sh))
+        mark()
         return out
 
     def replicate(self, hot_ids):

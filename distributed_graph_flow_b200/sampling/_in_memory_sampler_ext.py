@@ -269,7 +269,7 @@ class Sampler:
         return v.value
 
     def kernel_stats(self, stream=None):
-        """(seeds finished in a global slot, seeds finished by the padded
+        """(seeds finished by the warp sampler, seeds finished by the padded
         sampler) of the last call."""
         out = (ctypes.c_int64 * 2)()
         _native.check(_native.lib().dgfx_sampler_kernel_stats(self._handle, _native.stream_handle(stream), out))
@@ -518,17 +518,12 @@ class CapturedSampleStep:
         if aggregate and (table is None or any(len(smp._nodeset_index) != 1 or len(smp._edgeset_index) != 1
                                                for smp in self.samplers)):
             raise ValueError("aggregate needs a feature table and samplers over one node set and one edge set")
-        agg_bufs = [None] * K
         if table is not None:
             for k, smp in enumerate(self.samplers):
                 cap = self.B * smp.tree_size
                 self.features[k] = torch.empty((cap, int(table.shape[1])), dtype=table.dtype, device=dev)
                 if aggregate:
-                    ecap = self.B * max(1, smp.tree_size - 1)
                     self.aggregates[k] = torch.empty((cap, int(table.shape[1])), dtype=table.dtype, device=dev)
-                    agg_bufs[k] = (torch.empty(cap + 1, dtype=torch.int64, device=dev),
-                                   torch.empty(ecap, dtype=torch.int32, device=dev),
-                                   aggregation.spmm_workspace(cap, ecap, int(table.shape[1]), dev))
 
         def body(k):
             smp = self.samplers[k]
@@ -542,13 +537,7 @@ class CapturedSampleStep:
                     _native.elem_ptr(off, (ns + 1) * self.B), int(batch.node_ids.numel()),
                     _native.ptr(self.features[k]), _native.stream_handle()))
                 if aggregate:  # mean over each node's sampled neighbours
-                    rowptr, col, ws = agg_bufs[k]
-                    _native.check(_native.lib().dgfx_batch_csr(
-                        _native.ptr(off), _native.ptr(batch.edge_offsets), _native.ptr(batch.edge_src),
-                        _native.ptr(batch.edge_dst), self.B, int(batch.node_ids.numel()), _native.ptr(rowptr),
-                        _native.ptr(col), _native.stream_handle()))
-                    aggregation.csr_spmm(rowptr, col[:int(batch.edge_src.numel())], self.features[k], normalize=True,
-                                         out=self.aggregates[k], workspace=ws)
+                    aggregation.batch_mean_aggregate(batch, self.features[k], out=self.aggregates[k])
             return batch
 
         for k in range(K):  # allocates each sampler's workspace outside the capture

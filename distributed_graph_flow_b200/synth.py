@@ -77,6 +77,17 @@ def normal_features(node_begin: int, count: int, dim: int, seed: int, dtype, dev
     return out
 
 
+def normal_rows(ids, dim: int, seed: int, dtype, stream=None):
+    """Rows ``ids`` (int64 device tensor) of the normal_features table."""
+    torch = _native.require_cuda()
+    code = _native.BF16 if dtype == torch.bfloat16 else _native.F32
+    n = int(ids.numel())
+    out = torch.empty((max(n, 1), dim), dtype=dtype, device=ids.device)[:n]
+    _native.check(_native.lib().dgfx_synth_normal_rows(_native.ptr(ids.contiguous()), n, dim, seed, code,
+                                                       _native.ptr(out), _stream(stream)))
+    return out
+
+
 def build_graph(spec: GraphSpec, device, keep_edges: bool = False):
     """Generates the graph and builds its forward index in HBM.
 

@@ -125,18 +125,17 @@ void dgfx_sampler_destroy(dgfx_sampler* sampler);
 
 /* Kernel choice of dgfx_sampler_sample (no counterpart in the reference,
  * whose sampler is host code). kind 0 (default): the warp sampler (one warp
- * per seed over the occupied tree positions, in shared memory) when the
- * plan allows it, with seeds whose trees outgrow its capacity finished by
- * the padded sampler; kind 1: the padded sampler (one CTA per seed over all
- * tree positions) for every seed. Both give identical batches in every mode
- * (same random stream). dgfx_sampler_kernel_info reports the warp
- * sampler's per-seed entry capacity, 0 when it is not used. */
+ * per seed over the occupied tree positions, in shared memory, up to 64
+ * entries) when the plan allows it, with seeds whose trees outgrow it
+ * finished by the padded sampler; kind 1: the padded sampler (one CTA per
+ * seed over all tree positions) for every seed. Both give identical batches
+ * in every mode (same random stream). dgfx_sampler_kernel_info reports the
+ * warp sampler's per-seed entry capacity, 0 when it is not used. */
 int dgfx_sampler_set_kernel(dgfx_sampler* sampler, int32_t kind);
 int dgfx_sampler_kernel_info(const dgfx_sampler* sampler, int32_t* warp_capacity);
 /* Of the last dgfx_sampler_sample's seeds (synchronises `stream`):
- * out2[0] = seeds the warp sampler finished in a global-memory slot (trees
- * larger than its shared arrays), out2[1] = seeds finished by the padded
- * sampler (trees larger than any slot, or every slot busy). */
+ * out2[0] = seeds the warp sampler finished, out2[1] = seeds whose trees
+ * outgrew its capacity and were finished by the padded sampler. */
 int dgfx_sampler_kernel_stats(dgfx_sampler* sampler, dgfx_stream stream, int64_t* out2);
 
 /* Positions of the padded per-seed expansion tree (an upper bound on the
@@ -189,8 +188,11 @@ int dgfx_sampler_sample(dgfx_sampler* sampler, const int64_t* d_seeds,
  * loads the library until exit; a call whose dgfx_sampler_workspace_size
  * exceeds 64 MiB fails with DGFX_ERR_INVALID_ARGUMENT. The array's address
  * is looked up on the first call on each device (make that call before any
- * stream capture). Calls share the array: calls that overlap on the GPU
- * race. This entry point has no counterpart in the reference. */
+ * stream capture) and kept for the life of the process: a device reset
+ * invalidates it, so do not call this entry point again after
+ * cudaDeviceReset in the same process. Calls share the array: calls that
+ * overlap on the GPU race. This entry point has no counterpart in the
+ * reference. */
 int dgfx_sampler_sample_noalloc(dgfx_sampler* sampler, const int64_t* d_seeds,
                                 const int64_t* d_seed_ts,
                                 const int64_t* d_masked_edges,
@@ -609,6 +611,14 @@ int dgfx_gather_rows_scaled(const void* d_src, int dtype, const int64_t* d_ids, 
 int dgfx_batch_csr(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
                    const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity, int64_t* d_rowptr,
                    int32_t* d_col, dgfx_stream stream);
+/* dgfx_batch_mean: the same mean aggregation in one pass (one warp per
+ * sample): out[v] = mean of feats[u] over the batch edges v -> u (fp32 sums
+ * in edge order), zero rows for nodes without edges; rows past the batch's
+ * node count are not written. feats / out [node_capacity, feat] in batch
+ * order, fp32 or bf16. */
+int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
+                    const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity, const void* d_feats,
+                    int dtype, int64_t feat, void* d_out, dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
  * Seeded synthetic inputs (stand-ins for the benchmark datasets, the role of
@@ -640,6 +650,11 @@ int dgfx_synth_uniform_int(int64_t n, int64_t lo, int64_t hi, uint64_t seed,
 int dgfx_synth_normal_features(int64_t node_begin, int64_t count, int64_t dim,
                                uint64_t seed, int dtype, void* d_out,
                                dgfx_stream stream);
+/* dgfx_synth_normal_rows: the rows of the dgfx_synth_normal_features table
+ * for an arbitrary list of node ids (regenerates any rank's rows, e.g. to
+ * check rows gathered from peers). */
+int dgfx_synth_normal_rows(const int64_t* d_ids, int64_t count, int64_t dim, uint64_t seed, int dtype, void* d_out,
+                           dgfx_stream stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -149,15 +149,14 @@ def test_segment_softmax(cuda, dtype, sorted_ids, H, D):
     msgs = torch.randn((E, H, D), generator=g, device=dev).to(dt)
     got = aggregation.segment_softmax(logits, msgs, ids, nseg, indices_are_sorted=sorted_ids, out_dtype=torch.float32)
     ref = _softmax_reference(logits, msgs.float(), ids, nseg)
-    tol = 1e-5 if dtype == "float32" else 1e-2
-    # Relative to the row scale: sum of |w * m| over the segment.
+    # fp32 output: 1e-5 of the row scale (the bf16 messages are exact in the
+    # reference, which reads the same rounded values); bf16 output: 1e-2.
     err = (got.double() - ref).abs()
     scale = ref.abs().amax(dim=-1, keepdim=True).clamp(min=1e-3)
-    assert float((err / scale).max()) <= tol, float((err / scale).max())
-    # bf16 output rounds once more.
+    assert float((err / scale).max()) <= 1e-5, float((err / scale).max())
     got16 = aggregation.segment_softmax(logits, msgs, ids, nseg, indices_are_sorted=sorted_ids)
     assert got16.dtype == dt
-    assert float(((got16.double() - ref).abs() / scale).max()) <= (1e-5 if dtype == "float32" else 2e-2)
+    assert float(((got16.double() - ref).abs() / scale).max()) <= (1e-5 if dtype == "float32" else 1e-2)
 
 
 def test_segment_softmax_deterministic_and_empty(cuda):
