@@ -139,37 +139,96 @@ __global__ void batch_csr_kernel(const int64_t* __restrict__ node_off, const int
 }
 
 // Mean aggregation over a merged sampled batch in one pass: one warp per
-// sample; a sample's edges are sorted by local source, so node l's edges are
-// one run found by binary search. out[nb + l] = mean over that run of
-// feats[nb + dst], summed in edge order (fp32), zero rows for nodes without
-// edges. Rows past the batch's node count are not written.
+// batch node v. Its sample i comes from a binary search of the node
+// offsets, its edges (a sample's edges are sorted by local source) from a
+// binary search of the sample's sources; each lane owns 16-byte chunks of
+// the feature row and sums the neighbours' chunks in edge order (fp32), four
+// rows in flight. out[v] = that sum / max(count, 1). Rows past the batch's
+// node count are not written.
+template <class T>
+__device__ __forceinline__ void chunk_add(const uint4& r, float* acc);
+template <>
+__device__ __forceinline__ void chunk_add<float>(const uint4& r, float* acc) {
+  acc[0] += __uint_as_float(r.x);
+  acc[1] += __uint_as_float(r.y);
+  acc[2] += __uint_as_float(r.z);
+  acc[3] += __uint_as_float(r.w);
+}
+template <>
+__device__ __forceinline__ void chunk_add<__nv_bfloat16>(const uint4& r, float* acc) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = __bfloat1622float2(h[q]);
+    acc[2 * q] += f.x;
+    acc[2 * q + 1] += f.y;
+  }
+}
+template <class T>
+__device__ __forceinline__ uint4 chunk_pack(const float* acc, float scale);
+template <>
+__device__ __forceinline__ uint4 chunk_pack<float>(const float* acc, float scale) {
+  return make_uint4(__float_as_uint(acc[0] * scale), __float_as_uint(acc[1] * scale), __float_as_uint(acc[2] * scale),
+                    __float_as_uint(acc[3] * scale));
+}
+template <>
+__device__ __forceinline__ uint4 chunk_pack<__nv_bfloat16>(const float* acc, float scale) {
+  uint4 r;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(acc[2 * q] * scale, acc[2 * q + 1] * scale);
+  return r;
+}
+
 template <class T>
 __global__ void batch_mean_kernel(const int64_t* __restrict__ node_off, const int64_t* __restrict__ edge_off,
                                   const int64_t* __restrict__ edge_src, const int64_t* __restrict__ edge_dst,
-                                  int64_t B, const T* __restrict__ feats, int64_t feat,
-                                  T* __restrict__ out) {
+                                  int64_t B, int64_t node_cap, const uint4* __restrict__ feats, int64_t chunks,
+                                  uint4* __restrict__ out) {
+  constexpr int V = 16 / sizeof(T);
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  const int64_t w0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  for (int64_t i = w0; i < B; i += warps) {
-    const int64_t nb = node_off[i], nn = node_off[i + 1] - nb;
-    const int64_t eb = edge_off[i], ne = edge_off[i + 1] - eb;
-    int64_t e = 0;  // edges are sorted by source: walk them once
-    for (int64_t l = 0; l < nn; ++l) {
-      int64_t lo = e, hi = ne;  // first edge with source > l
-      while (lo < hi) {
-        const int64_t mid = (lo + hi) >> 1;
-        if (edge_src[eb + mid] <= l) lo = mid + 1;
-        else hi = mid;
+  const int64_t total = node_off[B];
+  for (int64_t v = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; v < total && v < node_cap;
+       v += warps) {
+    int64_t lo = 0, hi = B;  // sample i: node_off[i] <= v < node_off[i + 1]
+    while (hi - lo > 1) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (node_off[mid] <= v) lo = mid;
+      else hi = mid;
+    }
+    const int64_t nb = node_off[lo], l = v - nb;
+    const int64_t eb = edge_off[lo], ne = edge_off[lo + 1] - eb;
+    int64_t a = 0, b = ne;  // first edge with source >= l
+    while (a < b) {
+      const int64_t mid = (a + b) >> 1;
+      if (edge_src[eb + mid] < l) a = mid + 1;
+      else b = mid;
+    }
+    int64_t c = a, d = ne;  // first edge with source > l
+    while (c < d) {
+      const int64_t mid = (c + d) >> 1;
+      if (edge_src[eb + mid] <= l) c = mid + 1;
+      else d = mid;
+    }
+    const int64_t cnt = c - a;
+    const float scale = 1.0f / static_cast<float>(cnt > 1 ? cnt : 1);
+    for (int64_t ch = lane; ch < chunks; ch += 32) {
+      float acc[V];
+#pragma unroll
+      for (int q = 0; q < V; ++q) acc[q] = 0.0f;
+      for (int64_t k = a; k < c; k += 4) {
+        uint4 r[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (k + u < c) r[u] = __ldg(feats + (nb + edge_dst[eb + k + u]) * chunks + ch);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (k + u < c) chunk_add<T>(r[u], acc);
+        }
       }
-      const int64_t cnt = lo - e;
-      const float inv = 1.0f / static_cast<float>(cnt > 1 ? cnt : 1);
-      for (int64_t f = lane; f < feat; f += 32) {
-        float acc = 0.0f;
-        for (int64_t k = e; k < lo; ++k) acc += to_f<T>(feats[(nb + edge_dst[eb + k]) * feat + f]);
-        out[(nb + l) * feat + f] = from_f<T>(acc * inv);
-      }
-      e = lo;
+      out[v * chunks + ch] = chunk_pack<T>(acc, scale);
     }
   }
 }
@@ -187,14 +246,23 @@ extern "C" int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_e
       (dtype != DGFX_F32 && dtype != DGFX_BF16)) {
     return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_batch_mean: bad arguments");
   }
-  const unsigned g = grid_for_items(std::max<int64_t>(num_seeds * 32, 1), 256);
+  const int64_t row_bytes = feat * (dtype == DGFX_F32 ? 4 : 2);
+  if (row_bytes % 16 != 0 || reinterpret_cast<uintptr_t>(d_feats) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(d_out) % 16 != 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_batch_mean: rows must be a multiple of 16 bytes, 16-byte aligned");
+  }
+  if (num_seeds == 0 || node_capacity == 0) return DGFX_OK;
+  const int64_t chunks = row_bytes / 16;
+  const unsigned g = grid_for_items(node_capacity * 32, 256);
   if (dtype == DGFX_F32) {
     batch_mean_kernel<float><<<g, 256, 0, stream>>>(d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst, num_seeds,
-                                                    static_cast<const float*>(d_feats), feat, static_cast<float*>(d_out));
+                                                    node_capacity, static_cast<const uint4*>(d_feats), chunks,
+                                                    static_cast<uint4*>(d_out));
   } else {
     batch_mean_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst,
-                                                            num_seeds, static_cast<const __nv_bfloat16*>(d_feats),
-                                                            feat, static_cast<__nv_bfloat16*>(d_out));
+                                                            num_seeds, node_capacity,
+                                                            static_cast<const uint4*>(d_feats), chunks,
+                                                            static_cast<uint4*>(d_out));
   }
   DGFX_CUDA_TRY(cudaGetLastError());
   return DGFX_OK;

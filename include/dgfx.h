@@ -615,7 +615,7 @@ int dgfx_batch_csr(const int64_t* d_node_offsets, const int64_t* d_edge_offsets,
  * sample): out[v] = mean of feats[u] over the batch edges v -> u (fp32 sums
  * in edge order), zero rows for nodes without edges; rows past the batch's
  * node count are not written. feats / out [node_capacity, feat] in batch
- * order, fp32 or bf16. */
+ * order, fp32 or bf16, rows a multiple of 16 bytes and 16-byte aligned. */
 int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
                     const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity, const void* d_feats,
                     int dtype, int64_t feat, void* d_out, dgfx_stream stream);
