@@ -497,10 +497,13 @@ class CapturedSampleStep:
     matrix of node set ``feature_nodeset``. With ``aggregate`` (one node set
     and edge set) every node's mean over the features of the neighbours it
     sampled follows the gather (aggregation.batch_mean_aggregate) and the
-    results are (MergedBatch, feature rows, aggregates) triples."""
+    results are (MergedBatch, feature rows, aggregates) triples. With
+    ``serial`` the K batches run one after the other on one stream inside
+    the graph (a training loop's sequence of batches, without the host's
+    per-batch launch cost)."""
 
     def __init__(self, samplers, batch_size: int, with_timestamps: bool, table=None, feature_nodeset: int = 0,
-                 stream=None, aggregate: bool = False):
+                 stream=None, aggregate: bool = False, serial: bool = False):
         torch = _torch()
         from distributed_graph_flow_b200 import aggregation
         self.single = not isinstance(samplers, (list, tuple))
@@ -509,7 +512,10 @@ class CapturedSampleStep:
         dev = self.samplers[0]._device
         self.B = int(batch_size)
         self.stream = stream if stream is not None else torch.cuda.Stream(device=dev)
-        self.branches = [self.stream] + [torch.cuda.Stream(device=dev) for _ in range(K - 1)]
+        if serial:  # the K batches one after the other on one stream
+            self.branches = [self.stream] * K
+        else:
+            self.branches = [self.stream] + [torch.cuda.Stream(device=dev) for _ in range(K - 1)]
         self.seeds = torch.zeros((K, self.B), dtype=torch.int64, device=dev)
         self.seed_ts = torch.zeros((K, self.B), dtype=torch.int64, device=dev) if with_timestamps else None
         ns = int(feature_nodeset)
@@ -547,13 +553,15 @@ class CapturedSampleStep:
         self.graph = torch.cuda.CUDAGraph()
         self.batches = [None] * K
         with torch.cuda.graph(self.graph, stream=self.stream):
-            for k in range(1, K):  # fork
-                self.branches[k].wait_stream(self.stream)
+            if not serial:
+                for k in range(1, K):  # fork
+                    self.branches[k].wait_stream(self.stream)
             for k in range(K):
                 with torch.cuda.stream(self.branches[k]):
                     self.batches[k] = body(k)
-            for k in range(1, K):  # join
-                self.stream.wait_stream(self.branches[k])
+            if not serial:
+                for k in range(1, K):  # join
+                    self.stream.wait_stream(self.branches[k])
         torch.cuda.synchronize(dev)
 
     def run(self, seeds, seed_ts=None):
