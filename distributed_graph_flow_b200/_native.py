@@ -89,6 +89,7 @@ SIGNATURES = {
     "dgfx_sampler_output_capacity": (_int, [_vp, _i64, _p_i64, _p_i64]),
     "dgfx_sampler_sample": (_int, [_vp, _vp, _vp, _vp, _i64, _u64, ctypes.POINTER(SampleOut), _vp, _sz, _vp]),
     "dgfx_sampler_sample_noalloc": (_int, [_vp, _vp, _vp, _vp, _i64, _u64, ctypes.POINTER(SampleOut), _vp]),
+    "dgfx_sampler_sample_split": (_int, [_vp, _vp, _vp, _vp, _i64, _u64, ctypes.POINTER(SampleOut), _vp, _sz, _vp, _vp]),
     "dgfx_sampler_check": (_int, [_vp, _vp]),
     "dgfx_sampler_stats": (_int, [_vp, _vp, _p_i64]),
     "dgfx_gather_rows": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),

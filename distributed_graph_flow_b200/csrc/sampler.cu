@@ -1310,6 +1310,11 @@ struct dgfx_sampler {
   int32_t padded_blocks = 0;  // CTAs of the padded sampler when it serves overflow seeds
   int32_t warp_blocks = 0;    // resident CTAs of the (persistent) warp sampler
   PlanNodeDev* d_pnodes = nullptr;
+  // Split calls (dgfx_sampler_sample_split): the first kernel's completion
+  // and this handle's last tail, so the next call on this handle waits for
+  // the previous tail before it reuses the workspace.
+  cudaEvent_t ev_warp = nullptr, ev_tail = nullptr;
+  bool tail_pending = false;
   int threads = 256;
   size_t smem_bytes = 0;
   int32_t pbits = 1, keybits = 2;
@@ -1672,6 +1677,8 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
 
 extern "C" void dgfx_sampler_destroy(dgfx_sampler* s) {
   if (s == nullptr) return;
+  if (s->ev_warp != nullptr) cudaEventDestroy(s->ev_warp);
+  if (s->ev_tail != nullptr) cudaEventDestroy(s->ev_tail);
   if (s->d_tables != nullptr) cudaFree(s->d_tables);
   if (s->walk.d_nodes != nullptr) cudaFree(s->walk.d_nodes);
   delete s;
@@ -1695,6 +1702,10 @@ extern "C" int dgfx_sampler_kernel_stats(dgfx_sampler* s, dgfx_stream stream_, i
   unsigned long long st[2];
   DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status + 7, sizeof(st), cudaMemcpyDeviceToHost, stream));
   DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
+  if (s->tail_pending) {
+    DGFX_CUDA_TRY(cudaEventSynchronize(s->ev_tail));
+    s->tail_pending = false;
+  }
   out2[0] = static_cast<int64_t>(st[0]);
   out2[1] = static_cast<int64_t>(st[1]);
   return DGFX_OK;
@@ -1724,11 +1735,15 @@ extern "C" int dgfx_sampler_output_capacity(const dgfx_sampler* s, int64_t num_s
   return DGFX_OK;
 }
 
-extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_ts,
-                                   const int64_t* d_masked_edges, int64_t B, uint64_t call_index,
-                                   const dgfx_sample_out* out, void* d_workspace, size_t workspace_bytes,
-                                   dgfx_stream stream_) {
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+namespace {
+// One sampling call. Everything runs on `stream` when tail == stream. With a
+// separate tail stream, the first sampling kernel runs on `stream` and the
+// rest (the padded kernel for large trees, the offset scans, the
+// compaction) on `tail` after it; the batch is complete in `tail` order.
+int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_ts, const int64_t* d_masked_edges,
+                int64_t B, uint64_t call_index, const dgfx_sample_out* out, void* d_workspace, size_t workspace_bytes,
+                cudaStream_t stream, cudaStream_t tail) {
+  const bool split = tail != stream;
   if (s == nullptr || out == nullptr || B < 0) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_sample: bad arguments");
   if (B > 0 && d_seeds == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_sample: null seeds");
   if (B >= (int64_t(1) << 31)) return fail(DGFX_ERR_UNSUPPORTED, "dgfx_sampler_sample: more than 2^31 - 1 seeds");
@@ -1737,6 +1752,14 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   }
   if (d_workspace == nullptr || workspace_bytes < sample_ws_bytes(s, B)) {
     return fail(DGFX_ERR_WORKSPACE, "dgfx_sampler_sample: workspace too small");
+  }
+  if (split) {
+    if (s->ev_warp == nullptr) DGFX_CUDA_TRY(cudaEventCreateWithFlags(&s->ev_warp, cudaEventDisableTiming));
+    if (s->ev_tail == nullptr) DGFX_CUDA_TRY(cudaEventCreateWithFlags(&s->ev_tail, cudaEventDisableTiming));
+  }
+  if (s->tail_pending) {  // the last split call's tail must end before the workspace is reused
+    DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
+    s->tail_pending = split;
   }
   // Status words 0..5 (memsets, so the call can be captured in a CUDA graph).
   DGFX_CUDA_TRY(cudaMemsetAsync(s->d_status, 0xFF, sizeof(unsigned long long), stream));
@@ -1748,8 +1771,16 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
   SampleBufs b;
   carve_sample(arena, s, B, &b);
   if (B == 0) {
-    DGFX_CUDA_TRY(cudaMemsetAsync(out->node_offsets, 0, sizeof(int64_t), stream));
-    DGFX_CUDA_TRY(cudaMemsetAsync(out->edge_offsets, 0, sizeof(int64_t), stream));
+    if (split) {
+      DGFX_CUDA_TRY(cudaEventRecord(s->ev_warp, stream));
+      DGFX_CUDA_TRY(cudaStreamWaitEvent(tail, s->ev_warp, 0));
+    }
+    DGFX_CUDA_TRY(cudaMemsetAsync(out->node_offsets, 0, sizeof(int64_t), tail));
+    DGFX_CUDA_TRY(cudaMemsetAsync(out->edge_offsets, 0, sizeof(int64_t), tail));
+    if (split) {
+      DGFX_CUDA_TRY(cudaEventRecord(s->ev_tail, tail));
+      s->tail_pending = true;
+    }
     return DGFX_OK;
   }
   Params p{};
@@ -1804,25 +1835,58 @@ extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, cons
     warp_kernel_for(s->warp_cap)<<<static_cast<unsigned>(blocks), kWarpsPerCta * 32,
                          static_cast<size_t>(s->warp_bytes) * kWarpsPerCta, stream>>>(p);
     DGFX_CUDA_TRY(cudaGetLastError());
+    if (split) {
+      DGFX_CUDA_TRY(cudaEventRecord(s->ev_warp, stream));
+      DGFX_CUDA_TRY(cudaStreamWaitEvent(tail, s->ev_warp, 0));
+    }
     if (s->T > s->warp_cap) {  // seeds whose trees outgrew the warp's capacity
       const int64_t pb = std::min<int64_t>(B, s->padded_blocks);
-      sample_kernel<<<static_cast<unsigned>(pb), s->threads, smem, stream>>>(p);
+      sample_kernel<<<static_cast<unsigned>(pb), s->threads, smem, tail>>>(p);
       DGFX_CUDA_TRY(cudaGetLastError());
     }
   } else {
     sample_kernel<<<static_cast<unsigned>(B), s->threads, smem, stream>>>(p);
     DGFX_CUDA_TRY(cudaGetLastError());
+    if (split) {
+      DGFX_CUDA_TRY(cudaEventRecord(s->ev_warp, stream));
+      DGFX_CUDA_TRY(cudaStreamWaitEvent(tail, s->ev_warp, 0));
+    }
   }
   const size_t mark = arena.used;
-  DGFX_TRY(exclusive_scan<int32_t>(b.node_cnt, out->node_offsets, B * s->num_nodesets, true, arena, stream));
+  DGFX_TRY(exclusive_scan<int32_t>(b.node_cnt, out->node_offsets, B * s->num_nodesets, true, arena, tail));
   arena.used = mark;
-  DGFX_TRY(exclusive_scan<int32_t>(b.edge_cnt, out->edge_offsets, B * s->num_edgesets, true, arena, stream));
+  DGFX_TRY(exclusive_scan<int32_t>(b.edge_cnt, out->edge_offsets, B * s->num_edgesets, true, arena, tail));
   const int64_t threads = 256;
   const int64_t blocks = ceil_div(B * 32, threads);
-  compact_kernel<<<static_cast<unsigned>(blocks), static_cast<unsigned>(threads), 0, stream>>>(
+  compact_kernel<<<static_cast<unsigned>(blocks), static_cast<unsigned>(threads), 0, tail>>>(
       p, out->node_offsets, out->edge_offsets, s->root_ns, out->node_ids, out->edge_src, out->edge_dst);
   DGFX_CUDA_TRY(cudaGetLastError());
+  if (split) {
+    DGFX_CUDA_TRY(cudaEventRecord(s->ev_tail, tail));
+    s->tail_pending = true;
+  }
   return DGFX_OK;
+}
+}  // namespace
+
+extern "C" int dgfx_sampler_sample(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_ts,
+                                   const int64_t* d_masked_edges, int64_t B, uint64_t call_index,
+                                   const dgfx_sample_out* out, void* d_workspace, size_t workspace_bytes,
+                                   dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  return sample_impl(s, d_seeds, d_seed_ts, d_masked_edges, B, call_index, out, d_workspace, workspace_bytes, stream,
+                     stream);
+}
+
+extern "C" int dgfx_sampler_sample_split(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_ts,
+                                         const int64_t* d_masked_edges, int64_t B, uint64_t call_index,
+                                         const dgfx_sample_out* out, void* d_workspace, size_t workspace_bytes,
+                                         dgfx_stream stream_, dgfx_stream tail_stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  cudaStream_t tail = reinterpret_cast<cudaStream_t>(tail_stream_);
+  if (tail == stream) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_sample_split: tail stream == stream");
+  return sample_impl(s, d_seeds, d_seed_ts, d_masked_edges, B, call_index, out, d_workspace, workspace_bytes, stream,
+                     tail);
 }
 
 extern "C" int dgfx_sampler_check(dgfx_sampler* s, dgfx_stream stream_) {
@@ -1831,6 +1895,10 @@ extern "C" int dgfx_sampler_check(dgfx_sampler* s, dgfx_stream stream_) {
   unsigned long long st[3];
   DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
   DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
+  if (s->tail_pending) {
+    DGFX_CUDA_TRY(cudaEventSynchronize(s->ev_tail));
+    s->tail_pending = false;
+  }
   if (st[0] != ~0ull) {
     int64_t seed = 0;
     DGFX_CUDA_TRY(cudaMemcpy(&seed, s->last_seeds + st[0], sizeof(seed), cudaMemcpyDeviceToHost));
@@ -1853,6 +1921,10 @@ extern "C" int dgfx_sampler_stats(dgfx_sampler* s, dgfx_stream stream_, int64_t*
   unsigned long long st[6];
   DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
   DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
+  if (s->tail_pending) {
+    DGFX_CUDA_TRY(cudaEventSynchronize(s->ev_tail));
+    s->tail_pending = false;
+  }
   for (int i = 0; i < 3; ++i) out3[i] = static_cast<int64_t>(st[3 + i]);
   return DGFX_OK;
 }

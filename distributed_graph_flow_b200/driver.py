@@ -339,31 +339,47 @@ class ShardedSampler:
     returns (merged batch, features of every sampled node in merged order,
     number of sampled nodes)."""
 
-    def __init__(self, cc_sampler, features: Optional[HaloFeatures], rank: int, world: int):
+    def __init__(self, cc_sampler, features: Optional[HaloFeatures], rank: int, world: int, cc_alt=None):
         self.cc = cc_sampler
+        # A second sampler over the same index and plan (same seed): with it,
+        # step_overlapped alternates the two so that one call's tail overlaps
+        # the next call's first kernel (each sampler owns one workspace).
+        self.cc_alt = cc_alt
         self.features = features
         self.rank = rank
         self.world = world
         self._calls = 0
+        self.gather_stream = None
+        self.tail_stream = None
 
     def step_overlapped(self, seeds, seed_ts=None):
         """Like step(), but the feature gather runs on a second stream so it
         overlaps the sampling of the next call (the sampler is latency-bound,
-        the gather bandwidth-bound). Results are valid once the caller's
-        stream has waited on ``gather_stream`` (``drain()``)."""
+        the gather bandwidth-bound), and with ``cc_alt`` each sampling call
+        is split (the large-tree kernel, scans and compaction on a tail
+        stream) so that it overlaps the next call's first kernel. Results are
+        valid once the caller's stream has waited on ``gather_stream``
+        (``drain()``). Batches equal step()'s for the same call order."""
         torch = _native.require_cuda()
         if not isinstance(self.features, PeerFeatures):
             return self.step(seeds, seed_ts)
         dev = self.features.device
-        if getattr(self, "gather_stream", None) is None:
+        if self.gather_stream is None:
             # High priority: the gather's CTAs are scheduled ahead of the
             # queued sampler CTAs of the next call as SM slots free up.
             self.gather_stream = torch.cuda.Stream(device=dev, priority=-1)
+            self.tail_stream = torch.cuda.Stream(device=dev) if self.cc_alt is not None else None
         main = torch.cuda.current_stream(dev)
         call = self._calls * self.world + self.rank
+        cc = self.cc if self.cc_alt is None or self._calls % 2 == 0 else self.cc_alt
         self._calls += 1
-        merged = self.cc.sample_merged(seeds, seed_ts, None, call_index=call, check=False)
-        self.gather_stream.wait_stream(main)
+        if self.tail_stream is None:
+            merged = cc.sample_merged(seeds, seed_ts, None, call_index=call, check=False)
+            self.gather_stream.wait_stream(main)
+        else:
+            merged = cc.sample_merged(seeds, seed_ts, None, call_index=call, check=False,
+                                      tail_stream=self.tail_stream)
+            self.gather_stream.wait_stream(self.tail_stream)
         cap = int(merged.node_ids.numel())
         with torch.cuda.stream(self.gather_stream):
             feats = torch.empty((cap, self.features.dim), dtype=self.features.dtype, device=dev)
@@ -375,11 +391,14 @@ class ShardedSampler:
         return merged, feats, None
 
     def drain(self):
-        """Makes the current stream wait for every overlapped gather."""
+        """Makes the current stream wait for every overlapped gather (and
+        every split sampling tail)."""
         torch = _native.require_cuda()
-        gs = getattr(self, "gather_stream", None)
+        gs = self.gather_stream
         if gs is not None:
             torch.cuda.current_stream(gs.device).wait_stream(gs)
+            if self.tail_stream is not None:
+                torch.cuda.current_stream(gs.device).wait_stream(self.tail_stream)
 
     def step(self, seeds, seed_ts=None, stream=None):
         call = self._calls * self.world + self.rank  # distinct random stream per rank and call

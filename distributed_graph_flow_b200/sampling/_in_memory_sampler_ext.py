@@ -302,13 +302,17 @@ class Sampler:
                 raise ValueError("seed_node_idxs and masked_edge_idxs must have the same size")
 
     def sample_merged(self, seeds, seed_ts=None, masks=None, stream=None, call_index: Optional[int] = None,
-                      check: bool = True) -> MergedBatch:
+                      check: bool = True, tail_stream=None) -> MergedBatch:
         """Samples one subgraph per seed into a device-resident merged batch.
 
         seeds / seed_ts / masks are int64 device tensors. With check=False the
         call stays asynchronous (errors are latched; call ``check()``).
         call_index=_native.CALL_INDEX_DEVICE takes the random-stream index from
         a device counter that every call advances (for CUDA-graph capture).
+        With ``tail_stream`` (a torch stream other than ``stream``) the call
+        runs split (dgfx_sampler_sample_split): the batch is complete in
+        ``tail_stream`` order, and ``stream`` is free for the next batch once
+        the first sampling kernel ends.
         """
         torch = _torch()
         lib = _native.lib()
@@ -334,14 +338,26 @@ class Sampler:
             call_index = self._calls
             self._calls += 1
         sh = _native.stream_handle(stream)
-        _native.check(
-            lib.dgfx_sampler_sample(
-                self._handle, _native.ptr(seeds), _native.ptr(seed_ts), _native.ptr(masks), B, int(call_index),
-                ctypes.byref(out), _native.ptr(ws), need.value, sh,
+        if tail_stream is None:
+            _native.check(
+                lib.dgfx_sampler_sample(
+                    self._handle, _native.ptr(seeds), _native.ptr(seed_ts), _native.ptr(masks), B, int(call_index),
+                    ctypes.byref(out), _native.ptr(ws), need.value, sh,
+                )
             )
-        )
+        else:
+            _native.check(
+                lib.dgfx_sampler_sample_split(
+                    self._handle, _native.ptr(seeds), _native.ptr(seed_ts), _native.ptr(masks), B, int(call_index),
+                    ctypes.byref(out), _native.ptr(ws), need.value, sh, _native.stream_handle(tail_stream),
+                )
+            )
+            # Tensors the tail reads or writes stay allocated until it ends.
+            for t in (seeds, seed_ts, masks, node_ids, node_off, edge_src, edge_dst, edge_off):
+                if t is not None:
+                    t.record_stream(tail_stream)
         if check:
-            self.check(stream)
+            self.check(stream if tail_stream is None else tail_stream)
         return MergedBatch(B, self._nodeset_names, self._edgeset_names, node_ids, node_off, edge_src, edge_dst,
                            edge_off)
 

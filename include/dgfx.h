@@ -125,8 +125,8 @@ void dgfx_sampler_destroy(dgfx_sampler* sampler);
 
 /* Kernel choice of dgfx_sampler_sample (no counterpart in the reference,
  * whose sampler is host code). kind 0 (default): the warp sampler (one warp
- * per seed over the occupied tree positions, in shared memory, up to 64
- * entries) when the plan allows it, with seeds whose trees outgrow it
+ * per seed over the occupied tree positions, in shared memory, 32 to 128
+ * entries by the plan's tree size) when the plan allows it, with seeds whose trees outgrow it
  * finished by the padded sampler; kind 1: the padded sampler (one CTA per
  * seed over all tree positions) for every seed. Both give identical batches
  * in every mode (same random stream). dgfx_sampler_kernel_info reports the
@@ -198,6 +198,25 @@ int dgfx_sampler_sample_noalloc(dgfx_sampler* sampler, const int64_t* d_seeds,
                                 const int64_t* d_masked_edges,
                                 int64_t num_seeds, uint64_t call_index,
                                 const dgfx_sample_out* out, dgfx_stream stream);
+
+/* Same result as dgfx_sampler_sample, split over two streams so that
+ * back-to-back batches overlap: the first sampling kernel runs on `stream`;
+ * the kernel that finishes the seeds with large sampled trees, the offset
+ * scans and the compaction of `out` run on `tail_stream` after it. `out` is
+ * complete in `tail_stream` order; `stream` is free for the next batch as
+ * soon as the first kernel ends. The next call on the same sampler waits on
+ * its `stream` for this call's tail before it touches the workspace, so
+ * callers that want two batches in flight alternate two samplers (and two
+ * workspaces). dgfx_sampler_check / _stats / _kernel_stats also wait for the
+ * tail. `tail_stream` must differ from `stream`. Identical batches to
+ * dgfx_sampler_sample for the same call_index. No reference counterpart. */
+int dgfx_sampler_sample_split(dgfx_sampler* sampler, const int64_t* d_seeds,
+                              const int64_t* d_seed_ts,
+                              const int64_t* d_masked_edges,
+                              int64_t num_seeds, uint64_t call_index,
+                              const dgfx_sample_out* out, void* d_workspace,
+                              size_t workspace_bytes, dgfx_stream stream,
+                              dgfx_stream tail_stream);
 
 /* Synchronises `stream` and reports the latched status of the last
  * dgfx_sampler_sample (reference messages, e.g. "The source node idx 7 is out

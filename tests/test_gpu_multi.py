@@ -103,13 +103,25 @@ def _worker(rank, world, port, q):
             pe.gather_range(ids, _native.elem_ptr(bounds, 0), _native.elem_ptr(bounds, 1), 20_000, out)
             torch.cuda.synchronize()
             assert torch.equal(out[: len(sel)], exp), f"exchange gather rank {rank} ({barrier})"
-            ss3 = driver.ShardedSampler(cc, pe, rank, world)
+            # With the NCCL barrier: two sampler handles, split sampling
+            # calls, three steps in flight before the drain.
+            cc_alt = None
+            if barrier == "nccl":
+                cc_alt = ext.create_device_sampler(plan, ["v"], [spec.num_nodes], ["e"], [index], [None], 0, seed=5)
+            ss3 = driver.ShardedSampler(cc, pe, rank, world, cc_alt=cc_alt)
+            steps = []
             for _ in range(3):
-                merged, feats, _ = ss3.step_overlapped(seeds)
-                ss3.drain()
-                torch.cuda.synchronize()
+                steps.append(ss3.step_overlapped(seeds))
+                if cc_alt is None:
+                    ss3.drain()
+            ss3.drain()
+            torch.cuda.synchronize()
+            for merged, feats, _ in steps:
                 total = int(merged.node_offsets[-1].item())
                 assert torch.equal(feats[:total], full[merged.node_ids[:total]]), f"exchange step {rank} ({barrier})"
+            cc.check()
+            if cc_alt is not None:
+                cc_alt.check()
             pe.check()
             pe.close()
         q.put((rank, "ok"))
