@@ -157,18 +157,22 @@ def timed(fn, steps, sync_fn, name="timed", finish=None):
     sync_fn()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     torch.cuda.nvtx.range_push(name)
+    h0 = time.perf_counter()
     for i in range(steps):
         ev[i].record()
         fn(i)
     if finish is not None:
         finish()
     ev[steps].record()
+    host_ms = (time.perf_counter() - h0) * 1e3 / steps
     sync_fn()
     torch.cuda.nvtx.range_pop()
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
     total = ev[0].elapsed_time(ev[steps])
+    # host_issue_ms: host time per call to enqueue the work; when it is close
+    # to mean_ms the GPU waits on the host.
     TIMING[name] = {"median_ms": statistics.median(per), "mean_ms": total / steps, "steps": steps,
-                    "min_ms": min(per), "max_ms": max(per)}
+                    "min_ms": min(per), "max_ms": max(per), "host_issue_ms": host_ms}
     return statistics.median(per)
 
 
@@ -445,6 +449,8 @@ def multi_gpu_checks(args, sharded, spec, seeds, W, K, rank, world, dev, sync):
             step(seeds[i])
         sharded.drain()
         ms = timed(lambda i: step(seeds[W + i]), K, sync, "step_no_cache", finish=sharded.drain)
+        if args.overlap:
+            ms = TIMING["step_no_cache"]["mean_ms"]  # as the headline: whole timed region / K
         feats_obj.check()
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

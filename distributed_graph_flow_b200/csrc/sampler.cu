@@ -46,6 +46,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "common.cuh"
@@ -117,6 +118,12 @@ struct Params {
   int32_t warp_bytes;          // shared memory per warp
   unsigned int* overflow_count;  // [0] seeds for the padded kernel, [1] next seed of the warp kernel
   int32_t* overflow_list;        // seeds with more entries than any warp slot holds
+  // Large-tree warp tier: seeds that outgrew warp_cap, redone by one warp
+  // each with big_cap entries (runtime capacity) before the padded sampler.
+  int32_t big_cap;               // 0: no large-tree tier
+  int32_t big_bytes;             // shared memory of one large-tree warp
+  unsigned int* mid_count;       // [0] seeds listed for the large-tree tier, [1] next of them
+  int32_t* mid_list;
 };
 
 // Per-CTA working arrays (shared or global memory). The dedup table packs
@@ -709,26 +716,29 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
 // rows). The warp sampler keeps one compact entry per occupied position
 // (node id, padded position, parent entry, plan node) in shared memory,
 // level by level, so every phase costs the entries a seed really has:
-//   1. expansion: the tasks (entry, plan edge) of a level go to the lanes in
-//      chunks of four rounds: the lanes load the row bounds of all four
-//      rounds at once, find temporal cutoffs with an 8-pivot search per lane
-//      (ceil(log9(d)) dependent loads), draw the picks (same Philox counters
-//      as the padded sampler: tree position, plan edge, seed slot, call),
-//      and a warp scan gives each task its place among the next level's
-//      entries, which stay in position order; then the lanes load the picked
-//      columns, four in flight each;
-//   2. numbering: an entry's rank in depth-first order is its index in its
-//      level plus, for every other level, the number of entries there with a
-//      smaller position (binary searches over the position-sorted levels);
+//   1. expansion: the tasks (entry, plan edge) of a level go to the lanes,
+//      one round of 32 at a time: each lane loads its row bounds, finds a
+//      temporal cutoff with an 8-pivot search (ceil(log9(d)) dependent
+//      loads), and the round's Philox blocks (same counters as the padded
+//      sampler: tree position, plan edge, seed slot, call) are computed
+//      lane-parallel before each lane runs its task's Floyd steps (a 64-bit
+//      mask for rows of at most 64 valid entries); a warp scan gives each
+//      task its place among the next level's entries; then the lanes load
+//      the picked columns, four in flight each;
+//   2. numbering: an entry's rank in depth-first order is the number of
+//      entries with a smaller padded position (all pairs, broadcast loads);
 //      a hash table keeps each node's smallest rank (atomicMin) and a walk
 //      over the entries in rank order numbers first discoveries per node set
 //      (__match_any_sync), exactly the reference's first-discovery order;
-//   3. edges: one key (edgeset | src | dst) per non-root entry, a warp
-//      bitonic sort, deduplication by a ballot scan.
+//   3. edges: one 32-bit key (edgeset | src | dst) per non-root entry,
+//      ranked by all pairs (stable), deduplicated by a ballot scan.
 // Results go to the same per-seed scratch slices as the padded sampler's,
-// so the compaction is shared and both samplers give identical batches. A
-// seed whose tree outgrows warp_cap entries is listed for the padded sampler
-// (it starts again there with the same random stream).
+// so the compaction is shared and every tier gives identical batches. Tiers:
+// the warp sampler proper (4 warps per CTA, 32..128 entries) takes every
+// seed; a seed whose tree outgrows it is listed for the large-tree tier (one
+// warp per CTA, up to 1024 entries, all-pairs passes in chunks of 128), and
+// a seed beyond that for the padded sampler. Each starts the seed again with
+// the same random stream.
 // ===========================================================================
 constexpr int kWarpCapMax = 128;  // 4 entries per lane: ranks and edge sorts by one all-pairs pass
 constexpr int kWarpsPerCta = 4;
@@ -768,6 +778,8 @@ __device__ __forceinline__ int64_t upper_bound_9ary(const int64_t* __restrict__ 
   return lo + c;
 }
 
+constexpr int kRegPicks = 16;  // register-resident Floyd picks (power of two)
+
 // Philox block of draw pair m >> 1 of one expansion task (the padded
 // sampler's counters: tree position, plan edge | block index, seed slot,
 // call index).
@@ -788,6 +800,7 @@ __device__ __forceinline__ U4 task_block(uint32_t key0, uint32_t key1, int32_t q
 // bits come out in adjacency order), longer rows use the task's own array.
 // FIRST / MOST_RECENT (and random with cnt == nv): the first / last cnt
 // valid entries.
+template <bool kReg>
 __device__ __forceinline__ void warp_round_picks(uint32_t key0, uint32_t key1, long long* at, int32_t cnt, int64_t rb,
                                                  int64_t nv, int64_t moff, int mode, int32_t q, int32_t e,
                                                  uint32_t slot, uint2 call, unsigned long long* stage,
@@ -809,6 +822,14 @@ __device__ __forceinline__ void warp_round_picks(uint32_t key0, uint32_t key1, l
   if (total == 0) return;
   const int off = incl - nb;
   const bool small = nv <= 64;
+  // kReg: rows longer than 64 with at most kRegPicks picks keep the chosen
+  // offsets in registers (unrolled duplicate test, sorting network; more
+  // code, shorter dependent chains, for the latency-bound large-tree tier);
+  // otherwise the task's own array.
+  const bool reg = kReg && !small && cnt <= kRegPicks && nv <= 0x7FFFFFFF;
+  uint32_t ch[kRegPicks];
+#pragma unroll
+  for (int i = 0; i < kRegPicks; ++i) ch[i] = 0xFFFFFFFFu;  // never an offset (nv <= 2^31 - 1)
   unsigned long long chosen = 0;
   int32_t m = 0;
   for (int base = 0; base < total; base += stage_blocks) {
@@ -840,6 +861,13 @@ __device__ __forceinline__ void warp_round_picks(uint32_t key0, uint32_t key1, l
         if (small) {
           if ((chosen >> t) & 1ull) t = j;
           chosen |= 1ull << t;
+        } else if (reg) {
+          bool dup = false;
+#pragma unroll
+          for (int i = 0; i < kRegPicks; ++i) dup |= ch[i] == static_cast<uint32_t>(t);
+          if (dup) t = j;
+#pragma unroll
+          for (int i = 0; i < kRegPicks; ++i) ch[i] = i == m ? static_cast<uint32_t>(t) : ch[i];
         } else {
           for (int32_t i = 0; i < m; ++i) {
             if (at[i] == t) {
@@ -860,6 +888,33 @@ __device__ __forceinline__ void warp_round_picks(uint32_t key0, uint32_t key1, l
       chosen &= chosen - 1;
       if (moff >= 0 && o >= moff) ++o;
       at[i] = rb + o;
+    }
+    return;
+  }
+  if (reg) {  // adjacency order: bitonic network (unused slots sort last)
+#pragma unroll
+    for (int k = 2; k <= kRegPicks; k <<= 1) {
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+        for (int i = 0; i < kRegPicks; ++i) {
+          const int l = i ^ j;
+          if (l > i) {
+            const uint32_t a = ch[i], b = ch[l];
+            const bool swap = (a > b) == ((i & k) == 0);
+            ch[i] = swap ? b : a;
+            ch[l] = swap ? a : b;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kRegPicks; ++i) {
+      if (i < cnt) {
+        long long o = ch[i];
+        if (moff >= 0 && o >= moff) ++o;
+        at[i] = rb + o;
+      }
     }
     return;
   }
@@ -981,8 +1036,8 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
         break;
       }
       const int32_t out = fill + inc - cnt;
-      warp_round_picks(p.key0, p.key1, at + out, cnt, rb, nv, moff, md, q, pe, slot, call,
-                       reinterpret_cast<unsigned long long*>(order), C / 4);
+      warp_round_picks<false>(p.key0, p.key1, at + out, cnt, rb, nv, moff, md, q, pe, slot, call,
+                              reinterpret_cast<unsigned long long*>(order), C / 4);
       if (cnt > 0) {
         const EdgeDev& E = p.edges[pe];
         const int32_t base = q + E.rel_off;
@@ -1034,7 +1089,8 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     int rk[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      pk[k] = lane + 32 * k < n ? pos[lane + 32 * k] : 0x7FFFFFFF;
+      const int i = lane + 32 * k;
+      pk[k] = i < n ? pos[i] : 0x7FFFFFFF;
       rk[k] = 0;
     }
     for (int j = 0; j < n; ++j) {
@@ -1044,9 +1100,10 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     }
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      if (lane + 32 * k < n) {
-        local[lane + 32 * k] = static_cast<uint16_t>(rk[k]);
-        order[rk[k]] = static_cast<uint16_t>(lane + 32 * k);
+      const int i = lane + 32 * k;
+      if (i < n) {
+        local[i] = static_cast<uint16_t>(rk[k]);
+        order[rk[k]] = static_cast<uint16_t>(i);
       }
     }
   }
@@ -1197,7 +1254,9 @@ __device__ __forceinline__ WarpArrays carve_warp(char* base, int C, int32_t* cou
 }
 
 // Persistent warps: each takes the next seed from a counter in turn, so a
-// warp whose seed has a large tree does not hold back the others.
+// warp whose seed has a large tree does not hold back the others. A seed
+// that outgrows the capacity (32 K entries) is listed for the large-tree
+// tier (if the sampler has one) or the padded sampler.
 template <int K>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, 8) warp_sample_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(16) char smem_warp[];
@@ -1222,10 +1281,15 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 8) warp_sample_kernel(const
       if (lane == 0) atomicAdd(&p.status[7], 1ull);
       continue;
     }
-    // The tree outgrew the warp's arrays: the padded sampler redoes it.
+    // The tree outgrew the warp's arrays: a larger tier redoes it (with the
+    // same random stream).
     if (lane == 0) {
-      p.overflow_list[atomicAdd(p.overflow_count, 1u)] = static_cast<int32_t>(s);
-      atomicAdd(&p.status[8], 1ull);
+      if (p.big_cap > 0) {
+        p.mid_list[atomicAdd(p.mid_count, 1u)] = static_cast<int32_t>(s);
+      } else {
+        p.overflow_list[atomicAdd(p.overflow_count, 1u)] = static_cast<int32_t>(s);
+        atomicAdd(&p.status[8], 1ull);
+      }
     }
     __syncwarp();
   }
@@ -1234,6 +1298,411 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 8) warp_sample_kernel(const
 using WarpKernel = void (*)(const Params);
 WarpKernel warp_kernel_for(int cap) {
   return cap <= 32 ? warp_sample_kernel<1> : (cap <= 64 ? warp_sample_kernel<2> : warp_sample_kernel<4>);
+}
+// ===========================================================================
+// Large-tree tier: one CTA of kCtaWarps warps per seed over the occupied
+// positions, for the seeds whose trees outgrew the warp sampler. The same
+// compact entries and phases as warp_sample_one, with every per-entry loop
+// spread over the CTA's threads (the tier exists because a single warp's
+// per-seed latency, not throughput, bounds these seeds):
+//   - expansion: tasks in rounds of blockDim; a block scan places each task's
+//     picks among the next level's entries (position order, as in the warp
+//     sampler); each warp draws its tasks' Philox blocks into its own
+//     staging quarter;
+//   - numbering: the entries of a level are in position order (children are
+//     appended by parent, plan edge and pick, and a parent's subtree holds
+//     its children's positions), so an entry's depth-first rank is its index
+//     within its level plus one binary search per other level; the hash
+//     table keeps each node's smallest rank; first discoveries are numbered
+//     per node set over contiguous rank ranges, one per warp (counts per
+//     warp, prefix over warps, then a walk per warp);
+//   - edges: stable ranks of the 32-bit keys by all pairs, deduplication by
+//     block scans of the first-of-run flags.
+// Capacity C entries (power of two, at most kLargeCapMax: local ids in 10
+// bits keep an edge key within 32 bits).
+// ===========================================================================
+constexpr int kLargeCapMax = 1024;
+constexpr int kCtaWarps = 4;
+
+__host__ __device__ inline int cta_region_bytes(int cap, int ns, int es, int depth) {
+  const int b = 24 * cap + 4 * (ns + es + depth + 2 + kCtaWarps * ns + 2 * kCtaWarps + 40);
+  return (b + 15) & ~15;
+}
+
+// Exclusive scan of one int per thread over the CTA (kCtaWarps warps);
+// `wsum` holds kCtaWarps ints. Two barriers; call from every thread.
+__device__ __forceinline__ int cta_exclusive_scan(int v, int* wsum, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int inc = warp_inclusive_scan(v);
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  int base = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < kCtaWarps; ++w) {
+    const int x = wsum[w];
+    base += w < warp ? x : 0;
+    tot += x;
+  }
+  __syncthreads();
+  *total = tot;
+  return base + inc - v;
+}
+
+// Samples one seed; returns false (nothing written) if the tree has more
+// than C occupied positions. All threads of the CTA call it.
+__device__ __forceinline__ bool cta_sample_one(const Params& p, const WarpArrays& w, int32_t* wcnt, int32_t* wsum,
+                                            const int64_t sample, uint2 call, const int C) {
+  constexpr unsigned FULL = 0xffffffffu;
+  constexpr int NT = kCtaWarps * 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t lt = (1u << lane) - 1u;
+  const int NS = p.num_nodesets, ES = p.num_edgesets, D = p.depth;
+  long long* at = w.at;
+  int32_t* node = w.node;
+  int32_t* pos = w.pos;
+  int32_t* meta = w.meta;
+  uint16_t* order = w.order;
+  uint16_t* local = w.local;
+  int32_t* ns_cnt = w.ns_cnt;
+  int32_t* es_cnt = w.es_cnt;
+  int32_t* lv = w.lv;
+
+  const uint32_t slot = static_cast<uint32_t>(sample);
+  const bool has_ts = p.seed_ts != nullptr;
+  const int64_t sts = has_ts ? p.seed_ts[sample] : 0;
+  const int64_t mask = p.masks != nullptr ? p.masks[sample] : -1;
+  const int64_t seed = p.seeds[sample];
+  const bool ok = !(p.root_has_children && (seed < 0 || seed >= p.root_num_src));
+  for (int i = tid; i < NS; i += NT) ns_cnt[i] = 0;
+  for (int i = tid; i < ES; i += NT) es_cnt[i] = 0;
+  if (tid == 0) {
+    if (!ok) atomicMin(&p.status[0], static_cast<unsigned long long>(sample));
+    node[0] = static_cast<int32_t>(seed);
+    pos[0] = 0;
+    meta[0] = 0;
+    lv[0] = 0;
+    lv[1] = ok ? 1 : 0;
+  }
+  __syncthreads();
+  unsigned int st_rows = 0, st_picks = 0, st_probes = 0;
+  // Each warp's Philox staging: a quarter of the order + local arrays.
+  const int stage_blocks = C / (4 * kCtaWarps);
+  unsigned long long* stage = reinterpret_cast<unsigned long long*>(order) + 2 * stage_blocks * warp;
+
+  // 1. Expansion.
+  bool overflow = false;
+  const int maxm = p.max_edges_per_node;
+  for (int d = 0; d < D && !overflow; ++d) {
+    const int l0 = lv[d], l1 = lv[d + 1];
+    int fill = l1;
+    const int ntask = (l1 - l0) * maxm;
+    for (int t0 = 0; t0 < ntask; t0 += NT) {
+      const int t = t0 + tid;
+      int32_t cnt = 0, pe = -1, q = 0, ent = 0;
+      int64_t rb = 0, nv = 0, moff = -1;
+      int md = p.mode;
+      if (t < ntask) {
+        const int e = l0 + t / maxm, j = t - (t / maxm) * maxm;
+        const PlanNodeDev P = p.pnodes[meta[e] & 0xFF];
+        if (j < P.num_edges) {
+          pe = P.first_edge + j;
+          ent = e;
+          q = pos[e];
+          const EdgeDev& E = p.edges[pe];
+          const int32_t v = node[e];
+          rb = __ldg(E.rowptr + v);
+          int64_t n = __ldg(E.rowptr + v + 1) - rb;
+          const bool temporal = has_ts && E.ts != nullptr;
+          if (!has_ts && E.ts != nullptr) {
+            // SampleRandomUniform / SampleFirst on a temporal index fail
+            // (in_memory_sampler.cc:26-30, 168-172).
+            atomicOr(&p.status[1], 1ull);
+            n = 0;
+          }
+          if (temporal && n > 0) n = upper_bound_9ary(E.ts + rb, n, sts, &st_probes);
+          if (!temporal && mask >= 0 && E.edgeset == p.mask_edgeset && E.edge_pos != nullptr && mask < E.num_edges) {
+            const int64_t ps = E.edge_pos[mask];
+            if (ps >= rb && ps < rb + n) moff = ps - rb;
+          }
+          nv = n - (moff >= 0 ? 1 : 0);
+          cnt = static_cast<int32_t>(nv < E.k ? nv : E.k);
+          md = (p.mode == DGFX_MODE_MOST_RECENT && !temporal) ? DGFX_MODE_RANDOM : p.mode;
+          ++st_rows;
+          st_picks += static_cast<unsigned int>(cnt);
+        }
+      }
+      int tot = 0;
+      const int32_t out = fill + cta_exclusive_scan(cnt, wsum, &tot);
+      if (fill + tot > C) {  // uniform: every thread sees the same total
+        overflow = true;
+        break;
+      }
+      warp_round_picks<true>(p.key0, p.key1, at + out, cnt, rb, nv, moff, md, q, pe, slot, call, stage, stage_blocks);
+      if (cnt > 0) {
+        const EdgeDev& E = p.edges[pe];
+        const int32_t base = q + E.rel_off;
+        const int32_t mt = (ent << 8) | E.child;
+        for (int32_t i = 0; i < cnt; ++i) {
+          pos[out + i] = base + i * E.stride;
+          meta[out + i] = mt;
+        }
+      }
+      fill += tot;
+    }
+    if (overflow) break;
+    __syncthreads();
+    // Columns of the new entries, four loads in flight per thread.
+    for (int i0 = l1 + tid; i0 < fill; i0 += NT * 4) {
+      int32_t v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + NT * u;
+        v[u] = -1;
+        if (i < fill) v[u] = __ldg(p.edges[p.pnodes[meta[i] & 0xFF].in_edge].col + at[i]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (i0 + NT * u < fill) node[i0 + NT * u] = v[u];
+      }
+    }
+    if (tid == 0) lv[d + 2] = fill;
+    __syncthreads();
+  }
+  if (overflow) {  // redone by the padded sampler (its work is counted there)
+    __syncthreads();
+    return false;
+  }
+  st_rows = warp_reduce_sum(st_rows);
+  st_picks = warp_reduce_sum(st_picks);
+  st_probes = warp_reduce_sum(st_probes);
+  if (lane == 0) {
+    atomicAdd(&p.status[3], static_cast<unsigned long long>(st_rows));
+    atomicAdd(&p.status[4], static_cast<unsigned long long>(st_picks));
+    atomicAdd(&p.status[5], static_cast<unsigned long long>(st_probes));
+  }
+  const int n = lv[D + 1];
+
+  // 2. Numbering: depth-first rank by binary searches over the levels.
+  for (int i = tid; i < n; i += NT) {
+    const int32_t pi = pos[i];
+    int r = 0;
+    for (int L = 0; L <= D; ++L) {
+      const int lo = lv[L], hi = lv[L + 1];
+      if (i >= lo && i < hi) {
+        r += i - lo;
+        continue;
+      }
+      int a = lo, b = hi;  // first entry of level L at or after pi
+      while (a < b) {
+        const int m = (a + b) >> 1;
+        if (pos[m] < pi) a = m + 1;
+        else b = m;
+      }
+      r += a - lo;
+    }
+    local[i] = static_cast<uint16_t>(r);
+    order[r] = static_cast<uint16_t>(i);
+  }
+  __syncthreads();
+  unsigned long long* tab = reinterpret_cast<unsigned long long*>(at);
+  if (!p.with_replacement) {
+    int H = 2;
+    while (H < 2 * n && H < C) H <<= 1;
+    const int log2H = 31 - __clz(H);
+    for (int i = tid; i < H; i += NT) tab[i] = kEmptyKey;
+    __syncthreads();
+    for (int i = tid; i < n; i += NT) {
+      const int ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
+      const uint32_t key = p.ns_key_base[ns] + static_cast<uint32_t>(node[i]);
+      const unsigned long long entry = (static_cast<unsigned long long>(key) << 32) | local[i];
+      uint32_t h = (key * 0x9E3779B1u) >> (32 - log2H);
+      int where = -1;
+      for (int probe = 0; probe < H; ++probe) {
+        const unsigned long long prev = atomicCAS(&tab[h], kEmptyKey, entry);
+        if (prev == kEmptyKey) {
+          where = static_cast<int>(h);
+          break;
+        }
+        if (static_cast<uint32_t>(prev >> 32) == key) {
+          atomicMin(&tab[h], entry);
+          where = static_cast<int>(h);
+          break;
+        }
+        h = (h + 1) & static_cast<uint32_t>(H - 1);
+      }
+      if (where < 0) atomicOr(&p.status[2], 1ull);  // cannot happen: H > n
+      pos[i] = where;  // positions are not needed any more
+    }
+    __syncthreads();
+  }
+  // First discoveries in rank order, numbered per node set. Warp v walks
+  // ranks [v * span, (v + 1) * span): pass 1 counts per node set, the
+  // counts become per-warp starting offsets, pass 2 numbers.
+  const int span = ((n + kCtaWarps - 1) / kCtaWarps + 31) & ~31;
+  const int rlo = min(n, warp * span), rhi = min(n, rlo + span);
+  auto first_ns = [&](int r, int* ent) -> int {
+    *ent = -1;
+    if (r >= rhi) return -1;
+    const int i = order[r];
+    *ent = i;
+    const bool first = p.with_replacement ||
+                       (pos[i] >= 0 && static_cast<uint32_t>(tab[pos[i]]) == static_cast<uint32_t>(r));
+    return first ? (NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset) : -1;
+  };
+  for (int i = tid; i < kCtaWarps * NS; i += NT) wcnt[i] = 0;
+  __syncthreads();
+  for (int r0 = rlo; r0 < rhi; r0 += 32) {
+    int ent;
+    const int ns = first_ns(r0 + lane, &ent);
+    const uint32_t peers = __match_any_sync(FULL, ns);
+    if (ns >= 0 && (peers & lt) == 0) wcnt[warp * NS + ns] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  for (int g = tid; g < NS; g += NT) {
+    int32_t run = 0;
+    for (int v = 0; v < kCtaWarps; ++v) {
+      const int32_t c = wcnt[v * NS + g];
+      wcnt[v * NS + g] = run;
+      run += c;
+    }
+    ns_cnt[g] = run;
+  }
+  __syncthreads();
+  for (int r0 = rlo; r0 < rhi; r0 += 32) {
+    int i;
+    const int ns = first_ns(r0 + lane, &i);
+    const uint32_t peers = __match_any_sync(FULL, ns);
+    int base = 0;
+    if (ns >= 0) base = wcnt[warp * NS + ns];
+    __syncwarp();
+    if (ns >= 0) {
+      const uint32_t l = static_cast<uint32_t>(base) + __popc(peers & lt);
+      if (p.with_replacement) local[i] = static_cast<uint16_t>(l);
+      else tab[pos[i]] = (tab[pos[i]] & 0xFFFFFFFF00000000ull) | (0x80000000u | l);
+      if ((peers & lt) == 0) wcnt[warp * NS + ns] = base + __popc(peers);
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  if (!p.with_replacement) {
+    for (int i = tid; i < n; i += NT) {
+      local[i] = pos[i] >= 0 ? static_cast<uint16_t>(static_cast<uint32_t>(tab[pos[i]]) & 0x7FFFFFFFu) : 0;
+    }
+  }
+  __syncthreads();
+  int most = 1;
+  for (int g = 0; g < NS; ++g) most = max(most, ns_cnt[g]);
+  const int lb = max(1, 32 - __clz(most - 1));
+  int32_t* out_nodes = p.scratch_nodes + sample * static_cast<int64_t>(p.T);
+  for (int i = tid; i < n; i += NT) {
+    const int ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
+    int b = 0;
+    for (int g = 0; g < ns; ++g) b += ns_cnt[g];
+    out_nodes[b + local[i]] = node[i];
+  }
+
+  // 3. Edges: stable ranks of the 32-bit keys (all pairs, four keys per
+  //    thread per chunk), then deduplication.
+  const int nk = n > 0 ? n - 1 : 0;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(at);
+  for (int i = tid; i < nk; i += NT) {
+    const int c = i + 1;
+    const int par = meta[c] >> 8;
+    const EdgeDev& E = p.edges[p.pnodes[meta[c] & 0xFF].in_edge];
+    const uint32_t a = local[par], b = local[c];
+    const uint32_t src = E.reversed ? b : a, dst = E.reversed ? a : b;
+    keys[i] = (static_cast<uint32_t>(E.edgeset) << (2 * lb)) | (src << lb) | dst;
+  }
+  __syncthreads();
+  uint32_t* sorted = reinterpret_cast<uint32_t*>(node);
+  // KC keys per thread per chunk, the fewest that cover the keys in one
+  // chunk (up to 4), so no thread compares for empty slots.
+  auto rank_keys = [&](auto kc_tag) {
+    constexpr int KC = decltype(kc_tag)::value;
+    for (int c0 = 0; c0 < nk; c0 += NT * KC) {
+      uint32_t kk[KC];
+      int rk[KC];
+#pragma unroll
+      for (int k = 0; k < KC; ++k) {
+        const int i = c0 + tid + NT * k;
+        kk[k] = i < nk ? keys[i] : ~0u;
+        rk[k] = 0;
+      }
+      for (int j = 0; j < nk; ++j) {
+        const uint32_t kj = keys[j];
+#pragma unroll
+        for (int k = 0; k < KC; ++k) rk[k] += (kj < kk[k] || (kj == kk[k] && j < c0 + tid + NT * k)) ? 1 : 0;
+      }
+#pragma unroll
+      for (int k = 0; k < KC; ++k) {
+        if (c0 + tid + NT * k < nk) sorted[rk[k]] = kk[k];
+      }
+    }
+  };
+  if (nk <= NT) rank_keys(std::integral_constant<int, 1>{});
+  else if (nk <= 2 * NT) rank_keys(std::integral_constant<int, 2>{});
+  else rank_keys(std::integral_constant<int, 4>{});
+  __syncthreads();
+  uint64_t* out_edges = p.scratch_edges + sample * static_cast<int64_t>(p.T);
+  const uint32_t lmask = (1u << lb) - 1;
+  int obase = 0;
+  for (int i0 = 0; i0 < nk; i0 += NT) {
+    const int i = i0 + tid;
+    const uint32_t k = i < nk ? sorted[i] : ~0u;
+    const bool fresh = i < nk && (i == 0 || sorted[i - 1] != k);
+    int tot = 0;
+    const int o = obase + cta_exclusive_scan(fresh ? 1 : 0, wsum, &tot);
+    if (fresh) {
+      const unsigned long long es = k >> (2 * lb);
+      out_edges[o] = (es << 48) | (static_cast<unsigned long long>((k >> lb) & lmask) << 24) | (k & lmask);
+      atomicAdd(&es_cnt[static_cast<int>(es)], 1);
+    }
+    obase += tot;
+  }
+  __syncthreads();
+  for (int g = tid; g < NS; g += NT) p.node_cnt[g * p.B + sample] = ns_cnt[g];
+  for (int g = tid; g < ES; g += NT) p.edge_cnt[g * p.B + sample] = es_cnt[g];
+  __syncthreads();  // the next seed re-initialises the shared arrays
+  return true;
+}
+
+// Persistent CTAs over the seeds the warp sampler listed; seeds beyond the
+// capacity go to the padded sampler.
+__global__ void __launch_bounds__(kCtaWarps * 32, 9) large_tree_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(16) char smem_large[];
+  __shared__ unsigned int next_s;
+  const int C = p.big_cap;
+  const int NS = p.num_nodesets, ES = p.num_edgesets;
+  int32_t* counters = reinterpret_cast<int32_t*>(smem_large + 24 * static_cast<size_t>(C));
+  const WarpArrays w = carve_warp(smem_large, C, counters, NS, ES);
+  int32_t* wcnt = counters + NS + ES + p.depth + 2;  // [kCtaWarps][NS]
+  int32_t* wsum = wcnt + kCtaWarps * NS;             // [kCtaWarps]
+  uint2 call;
+  {
+    const unsigned long long cidx =
+        p.call_dev != nullptr ? *p.call_dev : ((static_cast<unsigned long long>(p.call_hi) << 32) | p.call_lo);
+    call = make_uint2(static_cast<uint32_t>(cidx), static_cast<uint32_t>(cidx >> 32));
+  }
+  const unsigned int listed = p.mid_count[0];  // written by the warp sampler's kernel
+  for (;;) {
+    if (threadIdx.x == 0) {
+      const unsigned int i = atomicAdd(p.mid_count + 1, 1u);
+      next_s = i < listed ? static_cast<unsigned int>(p.mid_list[i]) : 0xFFFFFFFFu;
+    }
+    __syncthreads();
+    const unsigned int s = next_s;
+    __syncthreads();  // next_s is rewritten at the next turn
+    if (s == 0xFFFFFFFFu || static_cast<int64_t>(s) >= p.B) break;
+    if (cta_sample_one(p, w, wcnt, wsum, static_cast<int64_t>(s), call, C)) {
+      if (threadIdx.x == 0) atomicAdd(&p.status[7], 1ull);
+      continue;
+    }
+    if (threadIdx.x == 0) {
+      p.overflow_list[atomicAdd(p.overflow_count, 1u)] = static_cast<int32_t>(s);
+      atomicAdd(&p.status[8], 1ull);
+    }
+  }
 }
 
 // Largest row length of an index (the cap on useful slots per plan edge).
@@ -1309,6 +1778,8 @@ struct dgfx_sampler {
   int32_t kernel_kind = 0;
   int32_t padded_blocks = 0;  // CTAs of the padded sampler when it serves overflow seeds
   int32_t warp_blocks = 0;    // resident CTAs of the (persistent) warp sampler
+  // Large-tree warp tier (0 capacity: none): seeds that outgrow warp_cap.
+  int32_t big_cap = 0, big_bytes = 0, big_blocks = 0;
   PlanNodeDev* d_pnodes = nullptr;
   // Split calls (dgfx_sampler_sample_split): the first kernel's completion
   // and this handle's last tail, so the next call on this handle waits for
@@ -1352,6 +1823,8 @@ struct SampleBufs {
   char* global_work;
   unsigned int* overflow_count;
   int32_t* overflow_list;
+  unsigned int* mid_count;
+  int32_t* mid_list;
 };
 
 void carve_sample(Arena& a, const dgfx_sampler* s, int64_t B, SampleBufs* b) {
@@ -1362,6 +1835,8 @@ void carve_sample(Arena& a, const dgfx_sampler* s, int64_t B, SampleBufs* b) {
   b->global_work = s->use_smem ? nullptr : a.take<char>(static_cast<size_t>(B) * work_bytes(s->T, s->H));
   b->overflow_count = a.take<unsigned int>(2);  // [0] overflowed seeds, [1] next seed of the warp sampler
   b->overflow_list = a.take<int32_t>(static_cast<size_t>(std::max<int64_t>(B, 1)));
+  b->mid_count = a.take<unsigned int>(2);  // [0] seeds listed for the large-tree tier, [1] next of them
+  b->mid_list = a.take<int32_t>(static_cast<size_t>(std::max<int64_t>(B, 1)));
 }
 
 size_t sample_ws_bytes(const dgfx_sampler* s, int64_t B) {
@@ -1656,6 +2131,20 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, bytes * kWarpsPerCta));
       }
     }
+    // Large-tree tier: the tree size rounded up to a power of two, at most
+    // kLargeCapMax entries (trees beyond it go to the padded sampler).
+    if (s->warp_cap > 0 && T > s->warp_cap) {
+      const int big = std::min(pow2_at_least(T), kLargeCapMax);
+      const int bb = cta_region_bytes(big, num_nodesets, num_edgesets, s->depth);
+      if (big > s->warp_cap && bb <= 200 * 1024) {
+        s->big_cap = big;
+        s->big_bytes = bb;
+        if (bb > 48 * 1024) {
+          DGFX_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(large_tree_kernel),
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, bb));
+        }
+      }
+    }
   }
   {
     int dev = 0, sms = 148, per_sm = 1;
@@ -1669,6 +2158,12 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
                                                                  kWarpsPerCta * 32,
                                                                  static_cast<size_t>(s->warp_bytes) * kWarpsPerCta));
       s->warp_blocks = std::max(1, sms * std::max(1, wper));
+    }
+    if (s->big_cap > 0) {
+      int bper = 1;
+      DGFX_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bper, reinterpret_cast<const void*>(large_tree_kernel),
+                                                                 kCtaWarps * 32, static_cast<size_t>(s->big_bytes)));
+      s->big_blocks = std::max(1, sms * std::max(1, bper));
     }
   }
   *out = s.release();
@@ -1685,14 +2180,15 @@ extern "C" void dgfx_sampler_destroy(dgfx_sampler* s) {
 }
 
 extern "C" int dgfx_sampler_set_kernel(dgfx_sampler* s, int32_t kind) {
-  if (s == nullptr || kind < 0 || kind > 1) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_set_kernel: bad arguments");
+  if (s == nullptr || kind < 0 || kind > 2) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_set_kernel: bad arguments");
   s->kernel_kind = kind;
   return DGFX_OK;
 }
 
-extern "C" int dgfx_sampler_kernel_info(const dgfx_sampler* s, int32_t* warp_capacity) {
+extern "C" int dgfx_sampler_kernel_info(const dgfx_sampler* s, int32_t* warp_capacity, int32_t* large_capacity) {
   if (s == nullptr || warp_capacity == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_kernel_info: null");
-  *warp_capacity = s->kernel_kind == 0 ? s->warp_cap : 0;
+  *warp_capacity = s->kernel_kind != 1 ? s->warp_cap : 0;
+  if (large_capacity != nullptr) *large_capacity = s->kernel_kind == 0 ? s->big_cap : 0;
   return DGFX_OK;
 }
 
@@ -1827,9 +2323,15 @@ int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_t
   p.warp_bytes = s->warp_bytes;
   p.overflow_count = b.overflow_count;
   p.overflow_list = nullptr;
+  const bool big = s->big_cap > 0 && s->kernel_kind == 0;
+  p.big_cap = big ? s->big_cap : 0;
+  p.big_bytes = s->big_bytes;
+  p.mid_count = b.mid_count;
+  p.mid_list = b.mid_list;
   const size_t smem = s->smem_bytes;
-  if (s->warp_cap > 0 && s->kernel_kind == 0) {
+  if (s->warp_cap > 0 && s->kernel_kind != 1) {
     DGFX_CUDA_TRY(cudaMemsetAsync(b.overflow_count, 0, 2 * sizeof(unsigned int), stream));
+    if (big) DGFX_CUDA_TRY(cudaMemsetAsync(b.mid_count, 0, 2 * sizeof(unsigned int), stream));
     p.overflow_list = b.overflow_list;
     const int64_t blocks = std::min<int64_t>(ceil_div(B, kWarpsPerCta), s->warp_blocks);
     warp_kernel_for(s->warp_cap)<<<static_cast<unsigned>(blocks), kWarpsPerCta * 32,
@@ -1839,7 +2341,12 @@ int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_t
       DGFX_CUDA_TRY(cudaEventRecord(s->ev_warp, stream));
       DGFX_CUDA_TRY(cudaStreamWaitEvent(tail, s->ev_warp, 0));
     }
-    if (s->T > s->warp_cap) {  // seeds whose trees outgrew the warp's capacity
+    if (big) {  // seeds whose trees outgrew warp_cap: one CTA each with big_cap entries
+      const int64_t bb = std::min<int64_t>(B, s->big_blocks);
+      large_tree_kernel<<<static_cast<unsigned>(bb), kCtaWarps * 32, static_cast<size_t>(s->big_bytes), tail>>>(p);
+      DGFX_CUDA_TRY(cudaGetLastError());
+    }
+    if (s->T > (big ? s->big_cap : s->warp_cap)) {  // trees beyond every warp tier's capacity
       const int64_t pb = std::min<int64_t>(B, s->padded_blocks);
       sample_kernel<<<static_cast<unsigned>(pb), s->threads, smem, tail>>>(p);
       DGFX_CUDA_TRY(cudaGetLastError());

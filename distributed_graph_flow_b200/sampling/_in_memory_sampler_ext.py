@@ -224,6 +224,7 @@ class Sampler:
     def __init__(self):
         self._handle = None
         self._buffers = {}
+        self._sizes = {}  # B -> (node capacity, edge capacity, workspace bytes)
         self._calls = 0
 
     def __del__(self):
@@ -257,19 +258,30 @@ class Sampler:
         return v.value
 
     def set_kernel(self, kind: int) -> None:
-        """0 (default): warp sampler with padded fallback for large trees;
-        1: padded sampler for every seed. Both give identical batches."""
+        """0 (default): warp sampler, large-tree warp tier for seeds that
+        outgrow it, padded sampler for trees beyond that; 1: padded sampler
+        for every seed; 2: warp sampler with the padded sampler behind it.
+        All give identical batches."""
         _native.check(_native.lib().dgfx_sampler_set_kernel(self._handle, int(kind)))
+        self._sizes.clear()  # the workspace size depends on the kernel
+
+    def _kernel_info(self):
+        v, big = ctypes.c_int32(), ctypes.c_int32()
+        _native.check(_native.lib().dgfx_sampler_kernel_info(self._handle, ctypes.byref(v), ctypes.byref(big)))
+        return v.value, big.value
 
     @property
     def warp_capacity(self) -> int:
         """Per-seed entry capacity of the warp sampler (0: not used)."""
-        v = ctypes.c_int32()
-        _native.check(_native.lib().dgfx_sampler_kernel_info(self._handle, ctypes.byref(v)))
-        return v.value
+        return self._kernel_info()[0]
+
+    @property
+    def large_tree_capacity(self) -> int:
+        """Per-seed entry capacity of the large-tree warp tier (0: not used)."""
+        return self._kernel_info()[1]
 
     def kernel_stats(self, stream=None):
-        """(seeds finished by the warp sampler, seeds finished by the padded
+        """(seeds finished by a warp tier, seeds finished by the padded
         sampler) of the last call."""
         out = (ctypes.c_int64 * 2)()
         _native.check(_native.lib().dgfx_sampler_kernel_stats(self._handle, _native.stream_handle(stream), out))
@@ -318,19 +330,24 @@ class Sampler:
         lib = _native.lib()
         B = int(seeds.numel())
         self._validate_args(B, seed_ts, masks)
-        max_nodes = ctypes.c_int64()
-        max_edges = ctypes.c_int64()
-        _native.check(lib.dgfx_sampler_output_capacity(self._handle, B, ctypes.byref(max_nodes), ctypes.byref(max_edges)))
-        need = ctypes.c_size_t()
-        _native.check(lib.dgfx_sampler_workspace_size(self._handle, B, ctypes.byref(need)))
+        sizes = self._sizes.get(B)
+        if sizes is None:  # output capacity and workspace depend on B only
+            max_nodes = ctypes.c_int64()
+            max_edges = ctypes.c_int64()
+            _native.check(lib.dgfx_sampler_output_capacity(self._handle, B, ctypes.byref(max_nodes),
+                                                           ctypes.byref(max_edges)))
+            need = ctypes.c_size_t()
+            _native.check(lib.dgfx_sampler_workspace_size(self._handle, B, ctypes.byref(need)))
+            sizes = self._sizes[B] = (max(1, max_nodes.value), max(1, max_edges.value), need.value)
+        cap_nodes, cap_edges, need_bytes = sizes
         NS, ES = len(self._nodeset_names), len(self._edgeset_names)
         dev = self._device
-        node_ids = torch.empty(max(1, max_nodes.value), dtype=torch.int64, device=dev)
+        node_ids = torch.empty(cap_nodes, dtype=torch.int64, device=dev)
         node_off = torch.empty(NS * B + 1, dtype=torch.int64, device=dev)
-        edge_src = torch.empty(max(1, max_edges.value), dtype=torch.int64, device=dev)
-        edge_dst = torch.empty(max(1, max_edges.value), dtype=torch.int64, device=dev)
+        edge_src = torch.empty(cap_edges, dtype=torch.int64, device=dev)
+        edge_dst = torch.empty(cap_edges, dtype=torch.int64, device=dev)
         edge_off = torch.empty(ES * B + 1, dtype=torch.int64, device=dev)
-        ws = self._workspace(need.value)
+        ws = self._workspace(need_bytes)
         out = _native.SampleOut(
             _native.ptr(node_ids), _native.ptr(node_off), _native.ptr(edge_src), _native.ptr(edge_dst), _native.ptr(edge_off)
         )
@@ -342,14 +359,14 @@ class Sampler:
             _native.check(
                 lib.dgfx_sampler_sample(
                     self._handle, _native.ptr(seeds), _native.ptr(seed_ts), _native.ptr(masks), B, int(call_index),
-                    ctypes.byref(out), _native.ptr(ws), need.value, sh,
+                    ctypes.byref(out), _native.ptr(ws), need_bytes, sh,
                 )
             )
         else:
             _native.check(
                 lib.dgfx_sampler_sample_split(
                     self._handle, _native.ptr(seeds), _native.ptr(seed_ts), _native.ptr(masks), B, int(call_index),
-                    ctypes.byref(out), _native.ptr(ws), need.value, sh, _native.stream_handle(tail_stream),
+                    ctypes.byref(out), _native.ptr(ws), need_bytes, sh, _native.stream_handle(tail_stream),
                 )
             )
             # Tensors the tail reads or writes stay allocated until it ends.

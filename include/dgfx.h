@@ -126,16 +126,21 @@ void dgfx_sampler_destroy(dgfx_sampler* sampler);
 /* Kernel choice of dgfx_sampler_sample (no counterpart in the reference,
  * whose sampler is host code). kind 0 (default): the warp sampler (one warp
  * per seed over the occupied tree positions, in shared memory, 32 to 128
- * entries by the plan's tree size) when the plan allows it, with seeds whose trees outgrow it
- * finished by the padded sampler; kind 1: the padded sampler (one CTA per
- * seed over all tree positions) for every seed. Both give identical batches
- * in every mode (same random stream). dgfx_sampler_kernel_info reports the
- * warp sampler's per-seed entry capacity, 0 when it is not used. */
+ * entries by the plan's tree size) when the plan allows it; seeds whose
+ * trees outgrow it are redone by the large-tree warp tier (one warp per
+ * seed, up to 1024 entries), and seeds beyond that by the padded sampler
+ * (one CTA per seed over all tree positions). kind 1: the padded sampler
+ * for every seed. kind 2: the warp sampler with the padded sampler behind
+ * it (no large-tree tier). All give identical batches in every mode (same
+ * random stream). dgfx_sampler_kernel_info reports the warp sampler's and
+ * the large-tree tier's per-seed entry capacities under the current kind
+ * (0 when not used; large_capacity may be NULL). */
 int dgfx_sampler_set_kernel(dgfx_sampler* sampler, int32_t kind);
-int dgfx_sampler_kernel_info(const dgfx_sampler* sampler, int32_t* warp_capacity);
+int dgfx_sampler_kernel_info(const dgfx_sampler* sampler, int32_t* warp_capacity,
+                             int32_t* large_capacity);
 /* Of the last dgfx_sampler_sample's seeds (synchronises `stream`):
- * out2[0] = seeds the warp sampler finished, out2[1] = seeds whose trees
- * outgrew its capacity and were finished by the padded sampler. */
+ * out2[0] = seeds a warp tier finished, out2[1] = seeds whose trees
+ * outgrew every warp tier and were finished by the padded sampler. */
 int dgfx_sampler_kernel_stats(dgfx_sampler* sampler, dgfx_stream stream, int64_t* out2);
 
 /* Positions of the padded per-seed expansion tree (an upper bound on the

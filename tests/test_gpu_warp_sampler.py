@@ -88,26 +88,68 @@ def test_warp_equals_padded_masking(sampling, mode_name):
     _same_batches(a, b, seeds, None, masks)
 
 
+def _tiers(sampling, graph, schema, conf, mode):
+    """Samplers of one plan under kernel kinds 0 (warp, large-tree tier,
+    padded), 1 (padded only) and 2 (warp, padded)."""
+    out = []
+    for kind in (0, 1, 2):
+        plan = sampling.simple_sampling_config_to_sampling_plan(sampling.SimpleSamplingConfig(**conf), schema)
+        x = sampling.create_sampler(graph, plan, schema, return_features=False, return_node_idxs=True,
+                                    batch_size=64, sampling_mode=mode, seed=5)
+        x._cc_sampler.set_kernel(kind)
+        out.append(x)
+    return out
+
+
 @pytest.mark.parametrize("mode_name", ["MODE_RANDOM", "MODE_FIRST"])
-def test_overflow_to_padded(sampling, mode_name):
-    """Trees beyond the warp capacity (128 entries) finish in the padded
-    sampler; the batch is unchanged."""
+def test_overflow_to_large_tree_tier(sampling, mode_name):
+    """A three-hop plan without reverse edges (985 tree positions) on a
+    dense graph: trees beyond the warp capacity (128 entries; 38 of the 60
+    seeds in FIRST mode) are redone by the large-tree warp tier (1024
+    entries) under kind 0 and by the padded sampler under kind 2; the
+    batches of kinds 0, 1 and 2 are identical."""
     graph, schema = random_hetero_graph(8, temporal=False, sizes={"a": 60, "b": 30, "c": 9},
                                         edges={"ab": ("a", "b", 3000), "aa": ("a", "a", 2000),
                                                "bc": ("b", "c", 600), "ca": ("c", "a", 300)})
-    a, b = _pair(sampling, graph, schema, dict(seed_nodeset="a", num_hops=3, hop_width=6),
-                 getattr(sampling, mode_name))
-    assert a._cc_sampler.tree_size > 128 and a._cc_sampler.warp_capacity == 128
+    a, b, c = _tiers(sampling, graph, schema, dict(seed_nodeset="a", num_hops=3, hop_width=6, reverse=False),
+                     getattr(sampling, mode_name))
+    assert a._cc_sampler.tree_size == 985 and a._cc_sampler.warp_capacity == 128
+    assert a._cc_sampler.large_tree_capacity == 1024 and c._cc_sampler.large_tree_capacity == 0
+    assert b._cc_sampler.warp_capacity == 0 and c._cc_sampler.warp_capacity == 128
     seeds = np.arange(60)
     _same_batches(a, b, seeds)
     warp, padded = a._cc_sampler.kernel_stats()
-    assert padded > 0 and warp + padded == len(seeds)
+    assert padded == 0 and warp == len(seeds)
+    _same_batches(c, b, seeds)
+    warp, padded = c._cc_sampler.kernel_stats()
+    assert warp > 0 and padded > 0 and warp + padded == len(seeds)
+
+
+@pytest.mark.parametrize("mode_name", ["MODE_RANDOM", "MODE_FIRST"])
+@pytest.mark.parametrize("replace", [False, True])
+def test_beyond_large_tree_tier(sampling, mode_name, replace):
+    """A three-hop plan with reverse edges (thousands of tree positions, far
+    beyond the large-tree tier's 1024 entries): in FIRST mode 3 of the 200 seeds fill at
+    most 128 entries, 137 at most 1024 and 60 more, so every tier runs; the
+    batch equals the padded sampler's."""
+    graph, schema = random_hetero_graph(9, temporal=False, sizes={"a": 200, "b": 90, "c": 30},
+                                        edges={"ab": ("a", "b", 800), "aa": ("a", "a", 600),
+                                               "bc": ("b", "c", 300), "ca": ("c", "a", 200)})
+    a, b, _ = _tiers(sampling, graph, schema, dict(seed_nodeset="a", num_hops=3, hop_width=6,
+                                                    with_replacement=replace), getattr(sampling, mode_name))
+    assert a._cc_sampler.tree_size > 1024 and a._cc_sampler.large_tree_capacity == 1024
+    seeds = np.concatenate([np.arange(200), np.arange(200)[::-1]])
+    _same_batches(a, b, seeds)
+    warp, padded = a._cc_sampler.kernel_stats()
+    assert warp > 0 and padded > 0 and warp + padded == len(seeds)
 
 
 def test_large_generator_warp_equals_padded(cuda):
     """The power-law generator at 0.5 % with the [15, 10, 5] plan, random and
-    FIRST modes, 4096 seeds (about a sixth outgrow the warp's 128 entries
-    and finish in the padded sampler)."""
+    FIRST modes, 4096 seeds: about a sixth outgrow the warp's 128 entries and
+    finish in the large-tree tier (1024 entries >= the 916-position tree), or
+    in the padded sampler with that tier off; all three kernel kinds give the
+    same batches."""
     import dataclasses
 
     from distributed_graph_flow_b200 import _native, synth
@@ -121,23 +163,31 @@ def test_large_generator_warp_equals_padded(cuda):
     plan = cfg.explicit_plan("paper", "cites", [15, 10, 5])
     seeds = synth.uniform_int(4096, 0, spec.num_nodes, 77, 5, dev)
     for mode in (_native.MODE_RANDOM, _native.MODE_FIRST):
-        a = ext.create_device_sampler(plan, ["paper"], [spec.num_nodes], ["cites"], [index], [None], mode, seed=9)
-        b = ext.create_device_sampler(plan, ["paper"], [spec.num_nodes], ["cites"], [index], [None], mode, seed=9)
+        a, b, c = (ext.create_device_sampler(plan, ["paper"], [spec.num_nodes], ["cites"], [index], [None], mode,
+                                             seed=9) for _ in range(3))
         b.set_kernel(1)
-        for c in range(2):
-            x = ext.batch_to_host(a.sample_merged(seeds, call_index=c))
+        c.set_kernel(2)
+        assert a.large_tree_capacity == 1024
+        for call in range(2):
+            x = ext.batch_to_host(a.sample_merged(seeds, call_index=call))
             warp, padded = a.kernel_stats()
+            assert warp == 4096 and padded == 0
+            z = ext.batch_to_host(c.sample_merged(seeds, call_index=call))
+            warp, padded = c.kernel_stats()
             assert warp > 0 and padded > 0 and warp + padded == 4096  # trees of 129..916 entries: padded sampler
-            y = ext.batch_to_host(b.sample_merged(seeds, call_index=c))
-            for u, v in zip(x, y):
+            y = ext.batch_to_host(b.sample_merged(seeds, call_index=call))
+            for u, v, w in zip(x, y, z):
                 np.testing.assert_array_equal(u, v)
+                np.testing.assert_array_equal(w, v)
         a.check()
         b.check()
+        c.check()
 
 
 def test_split_call_alternating_handles(cuda):
     """dgfx_sampler_sample_split: two samplers alternated, each call's tail
-    (large-tree kernel, scans, compaction) on a second stream, give the same
+    (large-tree tier or padded sampler, scans, compaction) on a second
+    stream, give the same
     batches as one sampler's plain calls with the same call indices, with
     several batches in flight; the outputs stay allocated until their tail
     ends (record_stream)."""
@@ -159,6 +209,7 @@ def test_split_call_alternating_handles(cuda):
                                          _native.MODE_RANDOM, seed=9)
 
     ref, a, b = make(), make(), make()
+    b.set_kernel(2)  # b's tails run the padded sampler, a's the large-tree tier
     tail = torch.cuda.Stream(device=dev)
     main = torch.cuda.current_stream(dev)
     got = []
@@ -170,6 +221,7 @@ def test_split_call_alternating_handles(cuda):
     b.check()
     warp, padded = b.kernel_stats()
     assert warp > 0 and padded > 0
+    assert a.kernel_stats() == (2048, 0)
     for i in range(6):
         x = ext.batch_to_host(got[i])
         y = ext.batch_to_host(ref.sample_merged(seeds[i], call_index=i))
