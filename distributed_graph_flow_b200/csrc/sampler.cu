@@ -731,17 +731,19 @@ __global__ void __launch_bounds__(256) sample_kernel(Params p) {
 //      over the entries in rank order numbers first discoveries per node set
 //      (__match_any_sync), exactly the reference's first-discovery order;
 //   3. edges: one 32-bit key (edgeset | src | dst) per non-root entry,
-//      ranked by all pairs (stable), deduplicated by a ballot scan.
+//      sorted by a bitonic network over registers and lane shuffles,
+//      deduplicated by a ballot scan.
 // Results go to the same per-seed scratch slices as the padded sampler's,
 // so the compaction is shared and every tier gives identical batches. Tiers:
 // the warp sampler proper (4 warps per CTA, 32..128 entries) takes every
 // seed; a seed whose tree outgrows it is listed for the large-tree tier (one
-// warp per CTA, up to 1024 entries, all-pairs passes in chunks of 128), and
-// a seed beyond that for the padded sampler. Each starts the seed again with
+// CTA of four warps per seed, up to 512 entries), and a seed beyond that for
+// the padded sampler. Each starts the seed again with
 // the same random stream.
 // ===========================================================================
 constexpr int kWarpCapMax = 128;  // 4 entries per lane: ranks and edge sorts by one all-pairs pass
 constexpr int kWarpsPerCta = 4;
+constexpr int kCtaWarps = 4;  // warps of one large-tree CTA
 constexpr int kMaxWarpDepth = 30;
 
 __host__ __device__ inline int warp_region_bytes(int cap, int ns, int es, int depth) {
@@ -947,6 +949,84 @@ struct WarpArrays {
   int32_t* lv;       // [depth + 2] level boundaries
 };
 
+// Bitonic sort (ascending) of G * R keys held R per thread in blocked order:
+// element e = t * R + r, t the thread's index in its group of G threads
+// (one warp, or with kCta a CTA of kCtaWarps warps whose cross-warp stages
+// exchange through `xchg`, G * R words of shared memory, between barriers).
+// Stages within a thread swap registers, stages across lanes use shuffles.
+template <int R, bool kCta>
+__device__ __forceinline__ void bitonic_sort_blocked(uint32_t (&v)[R], int t, uint32_t* xchg) {
+  constexpr int G = kCta ? kCtaWarps * 32 : 32;
+  constexpr int P = G * R;
+  const int lane = threadIdx.x & 31;
+  auto ce = [&](int a, int b, int k) {  // a < b, both in this thread
+    const bool up = ((t * R + a) & k) == 0;
+    const uint32_t x = v[a], y = v[b];
+    const bool swap = (x > y) == up;
+    v[a] = swap ? y : x;
+    v[b] = swap ? x : y;
+  };
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j < R) {
+        if constexpr (R >= 2) {
+          if (j == 1) {
+            ce(0, 1, k);
+            if constexpr (R == 4) ce(2, 3, k);
+          } else if constexpr (R == 4) {
+            ce(0, 2, k);
+            ce(1, 3, k);
+          }
+        }
+      } else if (j < 32 * R) {
+        const int d = j / R;  // lane distance
+        const bool lower = (lane & d) == 0;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const uint32_t o = __shfl_xor_sync(0xffffffffu, v[r], d);
+          const bool up = ((t * R + r) & k) == 0;
+          v[r] = (lower == up) ? min(v[r], o) : max(v[r], o);
+        }
+      } else if constexpr (kCta) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) xchg[t * R + r] = v[r];
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int e = t * R + r;
+          const uint32_t o = xchg[e ^ j];
+          const bool lower = (e & j) == 0;
+          const bool up = (e & k) == 0;
+          v[r] = (lower == up) ? min(v[r], o) : max(v[r], o);
+        }
+        __syncthreads();
+      }
+    }
+  }
+}
+
+// Deduplication table of the compact samplers: 32-bit words (rank << 16 |
+// entry), the smallest rank of each node kept by atomicMin; a slot's node is
+// read through the entry it holds. Empty slots hold ~0 (ranks stay below
+// 2^15). Returns the slot, or -1 if the table is full (cannot happen: H > n).
+constexpr uint32_t kEmptyWord = 0xFFFFFFFFu;
+__device__ __forceinline__ int dedup_insert(const Params& p, uint32_t* tab, int H, int log2H, uint32_t key,
+                                            uint32_t word, const int32_t* node, const int32_t* meta, int NS) {
+  uint32_t h = (key * 0x9E3779B1u) >> (32 - log2H);
+  for (int probe = 0; probe < H; ++probe) {
+    const uint32_t prev = atomicCAS(&tab[h], kEmptyWord, word);
+    if (prev == kEmptyWord) return static_cast<int>(h);
+    const int j = static_cast<int>(prev & 0xFFFFu);
+    const int nsj = NS == 1 ? 0 : p.pnodes[meta[j] & 0xFF].nodeset;
+    if (p.ns_key_base[nsj] + static_cast<uint32_t>(node[j]) == key) {
+      atomicMin(&tab[h], word);
+      return static_cast<int>(h);
+    }
+    h = (h + 1) & static_cast<uint32_t>(H - 1);
+  }
+  return -1;
+}
+
 // Samples one seed with arrays of capacity C = 32 * K (K entries per lane
 // in the all-pairs passes); returns false (nothing written) if the tree has
 // more than C occupied positions.
@@ -1083,12 +1163,14 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
   const int n = lv[D + 1];
 
   // 2. Numbering. Rank in depth-first order = number of entries with a
-  //    smaller position (K entries per lane, all pairs by broadcast loads).
-  {
-    int32_t pk[K];
-    int rk[K];
+  //    smaller position (all pairs by broadcast loads, KC = ceil(n / 32)
+  //    entries per lane rounded up to a power of two, at most K).
+  auto rank_positions = [&](auto kc_tag) {
+    constexpr int KC = decltype(kc_tag)::value;
+    int32_t pk[KC];
+    int rk[KC];
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
+    for (int k = 0; k < KC; ++k) {
       const int i = lane + 32 * k;
       pk[k] = i < n ? pos[i] : 0x7FFFFFFF;
       rk[k] = 0;
@@ -1096,45 +1178,34 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     for (int j = 0; j < n; ++j) {
       const int32_t pj = pos[j];
 #pragma unroll
-      for (int k = 0; k < K; ++k) rk[k] += pj < pk[k] ? 1 : 0;
+      for (int k = 0; k < KC; ++k) rk[k] += pj < pk[k] ? 1 : 0;
     }
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
+    for (int k = 0; k < KC; ++k) {
       const int i = lane + 32 * k;
       if (i < n) {
         local[i] = static_cast<uint16_t>(rk[k]);
         order[rk[k]] = static_cast<uint16_t>(i);
       }
     }
-  }
+  };
+  if (K == 1 || n <= 32) rank_positions(std::integral_constant<int, 1>{});
+  else if (K == 2 || n <= 64) rank_positions(std::integral_constant<int, (K < 2 ? K : 2)>{});
+  else rank_positions(std::integral_constant<int, K>{});
   __syncwarp();
-  unsigned long long* tab = reinterpret_cast<unsigned long long*>(at);
+  uint32_t* tab = reinterpret_cast<uint32_t*>(at);  // 2 C words
   if (!p.with_replacement) {
     int H = 2;
-    while (H < 2 * n && H < C) H <<= 1;
+    while (H < 2 * n && H < 2 * C) H <<= 1;
     const int log2H = 31 - __clz(H);
-    for (int i = lane; i < H; i += 32) tab[i] = kEmptyKey;
+    for (int i = lane; i < H; i += 32) tab[i] = kEmptyWord;
     __syncwarp();
     for (int i = lane; i < n; i += 32) {
       const int ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
       const uint32_t key = p.ns_key_base[ns] + static_cast<uint32_t>(node[i]);
-      const unsigned long long entry = (static_cast<unsigned long long>(key) << 32) | local[i];
-      uint32_t h = (key * 0x9E3779B1u) >> (32 - log2H);
-      int where = -1;
-      for (int probe = 0; probe < H; ++probe) {
-        const unsigned long long prev = atomicCAS(&tab[h], kEmptyKey, entry);
-        if (prev == kEmptyKey) {
-          where = static_cast<int>(h);
-          break;
-        }
-        if (static_cast<uint32_t>(prev >> 32) == key) {
-          atomicMin(&tab[h], entry);
-          where = static_cast<int>(h);
-          break;
-        }
-        h = (h + 1) & static_cast<uint32_t>(H - 1);
-      }
-      if (where < 0) atomicOr(&p.status[2], 1ull);  // cannot happen: H > n
+      const int where = dedup_insert(p, tab, H, log2H, key, (static_cast<uint32_t>(local[i]) << 16) | i, node,
+                                     meta, NS);
+      if (where < 0) atomicOr(&p.status[2], 1ull);
       pos[i] = where;  // positions are not needed any more
     }
     __syncwarp();
@@ -1146,8 +1217,7 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     int ns = -1, i = -1;
     if (r < n) {
       i = order[r];
-      const bool first = p.with_replacement ||
-                         (pos[i] >= 0 && static_cast<uint32_t>(tab[pos[i]]) == static_cast<uint32_t>(r));
+      const bool first = p.with_replacement || (pos[i] >= 0 && (tab[pos[i]] >> 16) == static_cast<uint32_t>(r));
       if (first) ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
     }
     const uint32_t peers = __match_any_sync(FULL, ns);
@@ -1157,14 +1227,14 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     if (ns >= 0) {
       const uint32_t l = static_cast<uint32_t>(base) + __popc(peers & lt);
       if (p.with_replacement) local[i] = static_cast<uint16_t>(l);
-      else tab[pos[i]] = (tab[pos[i]] & 0xFFFFFFFF00000000ull) | (0x80000000u | l);
+      else tab[pos[i]] = 0x80000000u | l;
       if ((peers & lt) == 0) ns_cnt[ns] = base + __popc(peers);
     }
     __syncwarp();
   }
   if (!p.with_replacement) {
     for (int i = lane; i < n; i += 32) {
-      local[i] = pos[i] >= 0 ? static_cast<uint16_t>(static_cast<uint32_t>(tab[pos[i]]) & 0x7FFFFFFFu) : 0;
+      local[i] = pos[i] >= 0 ? static_cast<uint16_t>(tab[pos[i]] & 0x7FFFFFFFu) : 0;
     }
   }
   __syncwarp();
@@ -1183,9 +1253,8 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
   __syncwarp();
 
   // 3. Edges: a 32-bit key (edgeset | src | dst) per non-root entry,
-  //    sorted by rank (all pairs by broadcast loads), deduplicated.
+  //    sorted, deduplicated.
   const int nk = n > 0 ? n - 1 : 0;
-  uint32_t* keys = reinterpret_cast<uint32_t*>(at);
   auto edge_key = [&](int c) -> uint32_t {
     const int par = meta[c] >> 8;
     const EdgeDev& E = p.edges[p.pnodes[meta[c] & 0xFF].in_edge];
@@ -1193,27 +1262,27 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     const uint32_t src = E.reversed ? b : a, dst = E.reversed ? a : b;
     return (static_cast<uint32_t>(E.edgeset) << (2 * lb)) | (src << lb) | dst;
   };
-  {
-    uint32_t kk[K];
-    int rk[K];
+  // Sorted by a register bitonic sort over 32 * KC keys (KC per lane,
+  // ~0 padding sorts last; equal keys are equal edges, so stability does
+  // not matter).
+  auto sort_keys = [&](auto kc_tag) {
+    constexpr int KC = decltype(kc_tag)::value;
+    uint32_t v[KC];
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      kk[k] = lane + 32 * k < nk ? edge_key(lane + 32 * k + 1) : ~0u;
-      rk[k] = 0;
-      if (lane + 32 * k < nk) keys[lane + 32 * k] = kk[k];
+    for (int r = 0; r < KC; ++r) {
+      const int e = lane * KC + r;
+      v[r] = e < nk ? edge_key(e + 1) : ~0u;
     }
-    __syncwarp();
-    for (int j = 0; j < nk; ++j) {
-      const uint32_t kj = keys[j];
-#pragma unroll
-      for (int k = 0; k < K; ++k) rk[k] += (kj < kk[k] || (kj == kk[k] && j < lane + 32 * k)) ? 1 : 0;
-    }
+    bitonic_sort_blocked<KC, false>(v, lane, nullptr);
     uint32_t* sorted = reinterpret_cast<uint32_t*>(node);
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      if (lane + 32 * k < nk) sorted[rk[k]] = kk[k];
+    for (int r = 0; r < KC; ++r) {
+      if (lane * KC + r < nk) sorted[lane * KC + r] = v[r];
     }
-  }
+  };
+  if (K == 1 || nk <= 32) sort_keys(std::integral_constant<int, 1>{});
+  else if (K == 2 || nk <= 64) sort_keys(std::integral_constant<int, (K < 2 ? K : 2)>{});
+  else sort_keys(std::integral_constant<int, K>{});
   const uint32_t* ek = reinterpret_cast<const uint32_t*>(node);
   __syncwarp();
   uint64_t* out_edges = p.scratch_edges + sample * static_cast<int64_t>(p.T);
@@ -1316,13 +1385,16 @@ WarpKernel warp_kernel_for(int cap) {
 //     table keeps each node's smallest rank; first discoveries are numbered
 //     per node set over contiguous rank ranges, one per warp (counts per
 //     warp, prefix over warps, then a walk per warp);
-//   - edges: stable ranks of the 32-bit keys by all pairs, deduplication by
-//     block scans of the first-of-run flags.
-// Capacity C entries (power of two, at most kLargeCapMax: local ids in 10
-// bits keep an edge key within 32 bits).
+//   - edges: a bitonic sort of the 32-bit keys (registers, shuffles, and
+//     shared memory for the cross-warp stages), deduplication by block scans
+//     of the first-of-run flags.
+// Capacity C entries (power of two, at most kLargeCapMax = 512: 12 KB of
+// shared memory per CTA, so that nine CTAs fit an SM by both registers and
+// shared memory and a batch's large trees (about a sixth of 8192 seeds on
+// power-law graphs) take one wave; local ids in 9 bits keep an edge key
+// within 32 bits).
 // ===========================================================================
-constexpr int kLargeCapMax = 1024;
-constexpr int kCtaWarps = 4;
+constexpr int kLargeCapMax = 512;
 
 __host__ __device__ inline int cta_region_bytes(int cap, int ns, int es, int depth) {
   const int b = 24 * cap + 4 * (ns + es + depth + 2 + kCtaWarps * ns + 2 * kCtaWarps + 40);
@@ -1504,33 +1576,19 @@ __device__ __forceinline__ bool cta_sample_one(const Params& p, const WarpArrays
     order[r] = static_cast<uint16_t>(i);
   }
   __syncthreads();
-  unsigned long long* tab = reinterpret_cast<unsigned long long*>(at);
+  uint32_t* tab = reinterpret_cast<uint32_t*>(at);  // 2 C words
   if (!p.with_replacement) {
     int H = 2;
-    while (H < 2 * n && H < C) H <<= 1;
+    while (H < 2 * n && H < 2 * C) H <<= 1;
     const int log2H = 31 - __clz(H);
-    for (int i = tid; i < H; i += NT) tab[i] = kEmptyKey;
+    for (int i = tid; i < H; i += NT) tab[i] = kEmptyWord;
     __syncthreads();
     for (int i = tid; i < n; i += NT) {
       const int ns = NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset;
       const uint32_t key = p.ns_key_base[ns] + static_cast<uint32_t>(node[i]);
-      const unsigned long long entry = (static_cast<unsigned long long>(key) << 32) | local[i];
-      uint32_t h = (key * 0x9E3779B1u) >> (32 - log2H);
-      int where = -1;
-      for (int probe = 0; probe < H; ++probe) {
-        const unsigned long long prev = atomicCAS(&tab[h], kEmptyKey, entry);
-        if (prev == kEmptyKey) {
-          where = static_cast<int>(h);
-          break;
-        }
-        if (static_cast<uint32_t>(prev >> 32) == key) {
-          atomicMin(&tab[h], entry);
-          where = static_cast<int>(h);
-          break;
-        }
-        h = (h + 1) & static_cast<uint32_t>(H - 1);
-      }
-      if (where < 0) atomicOr(&p.status[2], 1ull);  // cannot happen: H > n
+      const int where = dedup_insert(p, tab, H, log2H, key, (static_cast<uint32_t>(local[i]) << 16) | i, node,
+                                     meta, NS);
+      if (where < 0) atomicOr(&p.status[2], 1ull);
       pos[i] = where;  // positions are not needed any more
     }
     __syncthreads();
@@ -1545,8 +1603,7 @@ __device__ __forceinline__ bool cta_sample_one(const Params& p, const WarpArrays
     if (r >= rhi) return -1;
     const int i = order[r];
     *ent = i;
-    const bool first = p.with_replacement ||
-                       (pos[i] >= 0 && static_cast<uint32_t>(tab[pos[i]]) == static_cast<uint32_t>(r));
+    const bool first = p.with_replacement || (pos[i] >= 0 && (tab[pos[i]] >> 16) == static_cast<uint32_t>(r));
     return first ? (NS == 1 ? 0 : p.pnodes[meta[i] & 0xFF].nodeset) : -1;
   };
   for (int i = tid; i < kCtaWarps * NS; i += NT) wcnt[i] = 0;
@@ -1579,7 +1636,7 @@ __device__ __forceinline__ bool cta_sample_one(const Params& p, const WarpArrays
     if (ns >= 0) {
       const uint32_t l = static_cast<uint32_t>(base) + __popc(peers & lt);
       if (p.with_replacement) local[i] = static_cast<uint16_t>(l);
-      else tab[pos[i]] = (tab[pos[i]] & 0xFFFFFFFF00000000ull) | (0x80000000u | l);
+      else tab[pos[i]] = 0x80000000u | l;
       if ((peers & lt) == 0) wcnt[warp * NS + ns] = base + __popc(peers);
     }
     __syncwarp();
@@ -1587,7 +1644,7 @@ __device__ __forceinline__ bool cta_sample_one(const Params& p, const WarpArrays
   __syncthreads();
   if (!p.with_replacement) {
     for (int i = tid; i < n; i += NT) {
-      local[i] = pos[i] >= 0 ? static_cast<uint16_t>(static_cast<uint32_t>(tab[pos[i]]) & 0x7FFFFFFFu) : 0;
+      local[i] = pos[i] >= 0 ? static_cast<uint16_t>(tab[pos[i]] & 0x7FFFFFFFu) : 0;
     }
   }
   __syncthreads();
@@ -1602,47 +1659,37 @@ __device__ __forceinline__ bool cta_sample_one(const Params& p, const WarpArrays
     out_nodes[b + local[i]] = node[i];
   }
 
-  // 3. Edges: stable ranks of the 32-bit keys (all pairs, four keys per
-  //    thread per chunk), then deduplication.
+  // 3. Edges: the 32-bit keys sorted by a bitonic sort over the CTA
+  //    (registers, shuffles, and shared memory across warps), then
+  //    deduplication.
   const int nk = n > 0 ? n - 1 : 0;
-  uint32_t* keys = reinterpret_cast<uint32_t*>(at);
-  for (int i = tid; i < nk; i += NT) {
-    const int c = i + 1;
+  auto edge_key = [&](int c) -> uint32_t {
     const int par = meta[c] >> 8;
     const EdgeDev& E = p.edges[p.pnodes[meta[c] & 0xFF].in_edge];
     const uint32_t a = local[par], b = local[c];
     const uint32_t src = E.reversed ? b : a, dst = E.reversed ? a : b;
-    keys[i] = (static_cast<uint32_t>(E.edgeset) << (2 * lb)) | (src << lb) | dst;
-  }
-  __syncthreads();
+    return (static_cast<uint32_t>(E.edgeset) << (2 * lb)) | (src << lb) | dst;
+  };
   uint32_t* sorted = reinterpret_cast<uint32_t*>(node);
-  // KC keys per thread per chunk, the fewest that cover the keys in one
-  // chunk (up to 4), so no thread compares for empty slots.
-  auto rank_keys = [&](auto kc_tag) {
+  uint32_t* xchg = reinterpret_cast<uint32_t*>(at);  // 2 C words >= 128 * 4
+  auto sort_keys = [&](auto kc_tag) {
     constexpr int KC = decltype(kc_tag)::value;
-    for (int c0 = 0; c0 < nk; c0 += NT * KC) {
-      uint32_t kk[KC];
-      int rk[KC];
+    uint32_t v[KC];
 #pragma unroll
-      for (int k = 0; k < KC; ++k) {
-        const int i = c0 + tid + NT * k;
-        kk[k] = i < nk ? keys[i] : ~0u;
-        rk[k] = 0;
-      }
-      for (int j = 0; j < nk; ++j) {
-        const uint32_t kj = keys[j];
+    for (int r = 0; r < KC; ++r) {
+      const int e = tid * KC + r;
+      v[r] = e < nk ? edge_key(e + 1) : ~0u;
+    }
+    __syncthreads();  // xchg overlays the dedup table read above
+    bitonic_sort_blocked<KC, true>(v, tid, xchg);
 #pragma unroll
-        for (int k = 0; k < KC; ++k) rk[k] += (kj < kk[k] || (kj == kk[k] && j < c0 + tid + NT * k)) ? 1 : 0;
-      }
-#pragma unroll
-      for (int k = 0; k < KC; ++k) {
-        if (c0 + tid + NT * k < nk) sorted[rk[k]] = kk[k];
-      }
+    for (int r = 0; r < KC; ++r) {
+      if (tid * KC + r < nk) sorted[tid * KC + r] = v[r];
     }
   };
-  if (nk <= NT) rank_keys(std::integral_constant<int, 1>{});
-  else if (nk <= 2 * NT) rank_keys(std::integral_constant<int, 2>{});
-  else rank_keys(std::integral_constant<int, 4>{});
+  if (nk <= NT) sort_keys(std::integral_constant<int, 1>{});
+  else if (nk <= 2 * NT) sort_keys(std::integral_constant<int, 2>{});
+  else sort_keys(std::integral_constant<int, 4>{});
   __syncthreads();
   uint64_t* out_edges = p.scratch_edges + sample * static_cast<int64_t>(p.T);
   const uint32_t lmask = (1u << lb) - 1;
