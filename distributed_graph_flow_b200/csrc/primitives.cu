@@ -86,6 +86,49 @@ int exclusive_scan(const Tin* d_in, int64_t* d_out, int64_t n, bool write_total,
   return DGFX_OK;
 }
 
+// One CTA per array; thread t owns the contiguous elements [t * per,
+// (t + 1) * per).
+template <class Tin>
+__global__ void __launch_bounds__(kSmallScanThreads)
+small_scan_pair_kernel(const Tin* __restrict__ in0, int64_t* __restrict__ out0, int64_t n0,
+                       const Tin* __restrict__ in1, int64_t* __restrict__ out1, int64_t n1) {
+  __shared__ int64_t smem[33];
+  const Tin* in = blockIdx.x == 0 ? in0 : in1;
+  int64_t* out = blockIdx.x == 0 ? out0 : out1;
+  const int64_t n = blockIdx.x == 0 ? n0 : n1;
+  const int64_t per = (n + kSmallScanThreads - 1) / kSmallScanThreads;
+  const int64_t lo = min(n, static_cast<int64_t>(threadIdx.x) * per), hi = min(n, lo + per);
+  int64_t s = 0;
+  for (int64_t i = lo; i < hi; ++i) s += static_cast<int64_t>(in[i]);
+  int64_t total;
+  int64_t prefix = block_exclusive_scan<int64_t>(s, smem, &total);
+  for (int64_t i = lo; i < hi; ++i) {
+    const int64_t v = static_cast<int64_t>(in[i]);
+    out[i] = prefix;
+    prefix += v;
+  }
+  if (threadIdx.x == 0) out[n] = total;
+}
+
+template <class Tin>
+int exclusive_scan_pair(const Tin* d_in0, int64_t* d_out0, int64_t n0, const Tin* d_in1, int64_t* d_out1,
+                        int64_t n1, Arena& ws, cudaStream_t stream) {
+  if (n0 <= kSmallScanMax && n1 <= kSmallScanMax) {
+    if (!ws.dry) {
+      small_scan_pair_kernel<Tin><<<2, kSmallScanThreads, 0, stream>>>(d_in0, d_out0, n0, d_in1, d_out1, n1);
+      DGFX_CUDA_TRY(cudaGetLastError());
+    }
+    return DGFX_OK;
+  }
+  const size_t mark = ws.used;
+  DGFX_TRY(exclusive_scan<Tin>(d_in0, d_out0, n0, true, ws, stream));
+  ws.used = mark;
+  return exclusive_scan<Tin>(d_in1, d_out1, n1, true, ws, stream);
+}
+
+template int exclusive_scan_pair<int32_t>(const int32_t*, int64_t*, int64_t, const int32_t*, int64_t*, int64_t,
+                                          Arena&, cudaStream_t);
+
 template int exclusive_scan<int64_t>(const int64_t*, int64_t*, int64_t, bool, Arena&, cudaStream_t);
 template int exclusive_scan<int32_t>(const int32_t*, int64_t*, int64_t, bool, Arena&, cudaStream_t);
 template int exclusive_scan<uint32_t>(const uint32_t*, int64_t*, int64_t, bool, Arena&, cudaStream_t);

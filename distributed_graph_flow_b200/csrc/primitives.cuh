@@ -21,6 +21,14 @@ size_t scan_workspace_bytes(int64_t n);
 template <class Tin>
 int exclusive_scan(const Tin* d_in, int64_t* d_out, int64_t n, bool write_total,
                    Arena& ws, cudaStream_t stream);
+// Two independent exclusive scans with totals (out[n] written). Arrays of at
+// most kSmallScanMax elements take one launch of one CTA per array (a batch's
+// per-seed counts); longer ones the general scan.
+constexpr int kSmallScanThreads = 1024;
+constexpr int64_t kSmallScanMax = 32 * kSmallScanThreads;
+template <class Tin>
+int exclusive_scan_pair(const Tin* d_in0, int64_t* d_out0, int64_t n0, const Tin* d_in1, int64_t* d_out1,
+                        int64_t n1, Arena& ws, cudaStream_t stream);
 
 // ---- radix sort -----------------------------------------------------------
 // Stable sort of (key, value) pairs by key bits [begin_bit, end_bit).

@@ -1827,6 +1827,7 @@ struct dgfx_sampler {
   int32_t warp_blocks = 0;    // resident CTAs of the (persistent) warp sampler
   // Large-tree warp tier (0 capacity: none): seeds that outgrow warp_cap.
   int32_t big_cap = 0, big_bytes = 0, big_blocks = 0;
+  int32_t sms = 148;
   PlanNodeDev* d_pnodes = nullptr;
   // Split calls (dgfx_sampler_sample_split): the first kernel's completion
   // and this handle's last tail, so the next call on this handle waits for
@@ -2199,6 +2200,7 @@ extern "C" int dgfx_sampler_create(int32_t num_plan_nodes, const int32_t* node_n
     DGFX_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     DGFX_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sample_kernel, s->threads, s->smem_bytes));
     s->padded_blocks = std::max(1, sms * std::max(1, per_sm));
+    s->sms = sms;
     if (s->warp_cap > 0) {
       int wper = 1;
       DGFX_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&wper, reinterpret_cast<const void*>(warp_kernel_for(s->warp_cap)),
@@ -2394,7 +2396,9 @@ int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_t
       DGFX_CUDA_TRY(cudaGetLastError());
     }
     if (s->T > (big ? s->big_cap : s->warp_cap)) {  // trees beyond every warp tier's capacity
-      const int64_t pb = std::min<int64_t>(B, s->padded_blocks);
+      // Behind the large-tree tier only the rare trees of more than big_cap
+      // entries remain: one CTA per SM (persistent over the list).
+      const int64_t pb = std::min<int64_t>(B, big ? s->sms : s->padded_blocks);
       sample_kernel<<<static_cast<unsigned>(pb), s->threads, smem, tail>>>(p);
       DGFX_CUDA_TRY(cudaGetLastError());
     }
@@ -2406,10 +2410,8 @@ int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_t
       DGFX_CUDA_TRY(cudaStreamWaitEvent(tail, s->ev_warp, 0));
     }
   }
-  const size_t mark = arena.used;
-  DGFX_TRY(exclusive_scan<int32_t>(b.node_cnt, out->node_offsets, B * s->num_nodesets, true, arena, tail));
-  arena.used = mark;
-  DGFX_TRY(exclusive_scan<int32_t>(b.edge_cnt, out->edge_offsets, B * s->num_edgesets, true, arena, tail));
+  DGFX_TRY(exclusive_scan_pair<int32_t>(b.node_cnt, out->node_offsets, B * s->num_nodesets, b.edge_cnt,
+                                        out->edge_offsets, B * s->num_edgesets, arena, tail));
   const int64_t threads = 256;
   const int64_t blocks = ceil_div(B * 32, threads);
   compact_kernel<<<static_cast<unsigned>(blocks), static_cast<unsigned>(threads), 0, tail>>>(
