@@ -1163,35 +1163,40 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
   const int n = lv[D + 1];
 
   // 2. Numbering. Rank in depth-first order = number of entries with a
-  //    smaller position (all pairs by broadcast loads, KC = ceil(n / 32)
-  //    entries per lane rounded up to a power of two, at most K).
-  auto rank_positions = [&](auto kc_tag) {
-    constexpr int KC = decltype(kc_tag)::value;
-    int32_t pk[KC];
-    int rk[KC];
-#pragma unroll
-    for (int k = 0; k < KC; ++k) {
-      const int i = lane + 32 * k;
-      pk[k] = i < n ? pos[i] : 0x7FFFFFFF;
-      rk[k] = 0;
+  //    smaller position (up to 32 entries: all pairs by broadcast loads).
+  if (n <= 32) {
+    const int32_t pk = lane < n ? pos[lane] : 0x7FFFFFFF;
+    int rk = 0;
+    for (int j = 0; j < n; ++j) rk += pos[j] < pk ? 1 : 0;
+    if (lane < n) {
+      local[lane] = static_cast<uint16_t>(rk);
+      order[rk] = static_cast<uint16_t>(lane);
     }
-    for (int j = 0; j < n; ++j) {
-      const int32_t pj = pos[j];
-#pragma unroll
-      for (int k = 0; k < KC; ++k) rk[k] += pj < pk[k] ? 1 : 0;
-    }
-#pragma unroll
-    for (int k = 0; k < KC; ++k) {
-      const int i = lane + 32 * k;
-      if (i < n) {
-        local[i] = static_cast<uint16_t>(rk[k]);
-        order[rk[k]] = static_cast<uint16_t>(i);
+  } else {
+    // More entries: the entries of a level are in position order, so the
+    // rank is the index within the own level plus a binary search in each
+    // other level (fewer instructions than all pairs).
+    for (int i = lane; i < n; i += 32) {
+      const int32_t pi = pos[i];
+      int r = 0;
+      for (int L = 0; L <= D; ++L) {
+        const int lo = lv[L], hi = lv[L + 1];
+        if (i >= lo && i < hi) {
+          r += i - lo;
+          continue;
+        }
+        int a = lo, b = hi;
+        while (a < b) {
+          const int m = (a + b) >> 1;
+          if (pos[m] < pi) a = m + 1;
+          else b = m;
+        }
+        r += a - lo;
       }
+      local[i] = static_cast<uint16_t>(r);
+      order[r] = static_cast<uint16_t>(i);
     }
-  };
-  if (K == 1 || n <= 32) rank_positions(std::integral_constant<int, 1>{});
-  else if (K == 2 || n <= 64) rank_positions(std::integral_constant<int, (K < 2 ? K : 2)>{});
-  else rank_positions(std::integral_constant<int, K>{});
+  }
   __syncwarp();
   uint32_t* tab = reinterpret_cast<uint32_t*>(at);  // 2 C words
   if (!p.with_replacement) {
