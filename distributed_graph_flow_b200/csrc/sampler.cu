@@ -1267,9 +1267,10 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     const uint32_t src = E.reversed ? b : a, dst = E.reversed ? a : b;
     return (static_cast<uint32_t>(E.edgeset) << (2 * lb)) | (src << lb) | dst;
   };
-  // Sorted by a register bitonic sort over 32 * KC keys (KC per lane,
-  // ~0 padding sorts last; equal keys are equal edges, so stability does
-  // not matter).
+  // Sorted by a register bitonic sort over 32 * KC keys (KC per lane: 1
+  // for up to 32 keys, else K; two variants keep the hot code small; ~0
+  // padding sorts last; equal keys are equal edges, so stability does not
+  // matter).
   auto sort_keys = [&](auto kc_tag) {
     constexpr int KC = decltype(kc_tag)::value;
     uint32_t v[KC];
@@ -1286,7 +1287,6 @@ __device__ __forceinline__ bool warp_sample_one(const Params& p, const WarpArray
     }
   };
   if (K == 1 || nk <= 32) sort_keys(std::integral_constant<int, 1>{});
-  else if (K == 2 || nk <= 64) sort_keys(std::integral_constant<int, (K < 2 ? K : 2)>{});
   else sort_keys(std::integral_constant<int, K>{});
   const uint32_t* ek = reinterpret_cast<const uint32_t*>(node);
   __syncwarp();
