@@ -96,16 +96,22 @@ small_scan_pair_kernel(const Tin* __restrict__ in0, int64_t* __restrict__ out0, 
   const Tin* in = blockIdx.x == 0 ? in0 : in1;
   int64_t* out = blockIdx.x == 0 ? out0 : out1;
   const int64_t n = blockIdx.x == 0 ? n0 : n1;
-  const int64_t per = (n + kSmallScanThreads - 1) / kSmallScanThreads;
-  const int64_t lo = min(n, static_cast<int64_t>(threadIdx.x) * per), hi = min(n, lo + per);
+  constexpr int kMaxPer = static_cast<int>(kSmallScanMax / kSmallScanThreads);
+  const int per = static_cast<int>((n + kSmallScanThreads - 1) / kSmallScanThreads);
+  const int64_t lo = static_cast<int64_t>(threadIdx.x) * per;
+  Tin v[kMaxPer];  // all loads issued before the scan, kept in registers
   int64_t s = 0;
-  for (int64_t i = lo; i < hi; ++i) s += static_cast<int64_t>(in[i]);
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    v[i] = (i < per && lo + i < n) ? in[lo + i] : Tin(0);
+    s += static_cast<int64_t>(v[i]);
+  }
   int64_t total;
   int64_t prefix = block_exclusive_scan<int64_t>(s, smem, &total);
-  for (int64_t i = lo; i < hi; ++i) {
-    const int64_t v = static_cast<int64_t>(in[i]);
-    out[i] = prefix;
-    prefix += v;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    if (i < per && lo + i < n) out[lo + i] = prefix;
+    prefix += static_cast<int64_t>(v[i]);
   }
   if (threadIdx.x == 0) out[n] = total;
 }

@@ -25,7 +25,7 @@ int exclusive_scan(const Tin* d_in, int64_t* d_out, int64_t n, bool write_total,
 // most kSmallScanMax elements take one launch of one CTA per array (a batch's
 // per-seed counts); longer ones the general scan.
 constexpr int kSmallScanThreads = 1024;
-constexpr int64_t kSmallScanMax = 32 * kSmallScanThreads;
+constexpr int64_t kSmallScanMax = 16 * kSmallScanThreads;
 template <class Tin>
 int exclusive_scan_pair(const Tin* d_in0, int64_t* d_out0, int64_t n0, const Tin* d_in1, int64_t* d_out1,
                         int64_t n1, Arena& ws, cudaStream_t stream);

@@ -1773,6 +1773,20 @@ __global__ void max_degree_kernel(const int64_t* __restrict__ rowptr, int64_t n,
 }
 
 // Merged batch from the per-seed scratch: one warp per seed.
+// Start of a call: status word 0 (first bad seed slot) to ~0, words 1..5
+// (flags, work counters) and 7..8 (seeds per tier) to 0; word 6 (the device
+// call index) is kept. The tiers' seed counters to 0.
+__global__ void reset_kernel(unsigned long long* status, unsigned int* overflow_count, unsigned int* mid_count) {
+  const int i = threadIdx.x;
+  if (i == 0) status[0] = ~0ull;
+  if (i >= 1 && i <= 5) status[i] = 0;
+  if (i == 7 || i == 8) status[i] = 0;
+  if (i < 2) {
+    overflow_count[i] = 0;
+    mid_count[i] = 0;
+  }
+}
+
 __global__ void compact_kernel(Params p, const int64_t* __restrict__ node_off, const int64_t* __restrict__ edge_off,
                                int root_ns, int64_t* __restrict__ node_ids, int64_t* __restrict__ edge_src,
                                int64_t* __restrict__ edge_dst) {
@@ -1784,6 +1798,23 @@ __global__ void compact_kernel(Params p, const int64_t* __restrict__ node_off, c
   const int64_t i = warp;
   const int32_t* src_nodes = p.scratch_nodes + i * static_cast<int64_t>(p.T);
   const uint64_t* src_edges = p.scratch_edges + i * static_cast<int64_t>(p.T);
+  if (p.num_nodesets == 1 && p.num_edgesets == 1) {
+    // One node set and one edge set: all four offsets, then the node and
+    // edge chunks, loaded before any store (one dependent round trip each).
+    const int64_t no = node_off[i], nc = node_off[i + 1] - no;
+    const int64_t eo = edge_off[i], ec = edge_off[i + 1] - eo;
+    const int64_t seed = p.seeds[i];
+    for (int64_t j = lane; j < nc || j < ec; j += 32) {
+      const int64_t v = j < nc ? static_cast<int64_t>(src_nodes[j]) : 0;
+      const uint64_t k = j < ec ? src_edges[j] : 0;
+      if (j < nc) node_ids[no + j] = (root_ns == 0 && j == 0) ? seed : v;
+      if (j < ec) {
+        edge_src[eo + j] = static_cast<int64_t>((k >> 24) & 0xFFFFFFull);
+        edge_dst[eo + j] = static_cast<int64_t>(k & 0xFFFFFFull);
+      }
+    }
+    return;
+  }
   int64_t acc = 0;
   for (int s = 0; s < p.num_nodesets; ++s) {
     const int64_t o = node_off[s * p.B + i];
@@ -2311,15 +2342,15 @@ int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_t
     DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
     s->tail_pending = split;
   }
-  // Status words 0..5 (memsets, so the call can be captured in a CUDA graph).
-  DGFX_CUDA_TRY(cudaMemsetAsync(s->d_status, 0xFF, sizeof(unsigned long long), stream));
-  DGFX_CUDA_TRY(cudaMemsetAsync(s->d_status + 1, 0, 5 * sizeof(unsigned long long), stream));
-  DGFX_CUDA_TRY(cudaMemsetAsync(s->d_status + 7, 0, 2 * sizeof(unsigned long long), stream));
   s->last_B = B;
   s->last_seeds = d_seeds;
   Arena arena(d_workspace, workspace_bytes);
   SampleBufs b;
   carve_sample(arena, s, B, &b);
+  // Status words and the tiers' seed counters in one launch (kernels only,
+  // so the call can be captured in a CUDA graph).
+  reset_kernel<<<1, 32, 0, stream>>>(s->d_status, b.overflow_count, b.mid_count);
+  DGFX_CUDA_TRY(cudaGetLastError());
   if (B == 0) {
     if (split) {
       DGFX_CUDA_TRY(cudaEventRecord(s->ev_warp, stream));
@@ -2384,8 +2415,6 @@ int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_t
   p.mid_list = b.mid_list;
   const size_t smem = s->smem_bytes;
   if (s->warp_cap > 0 && s->kernel_kind != 1) {
-    DGFX_CUDA_TRY(cudaMemsetAsync(b.overflow_count, 0, 2 * sizeof(unsigned int), stream));
-    if (big) DGFX_CUDA_TRY(cudaMemsetAsync(b.mid_count, 0, 2 * sizeof(unsigned int), stream));
     p.overflow_list = b.overflow_list;
     const int64_t blocks = std::min<int64_t>(ceil_div(B, kWarpsPerCta), s->warp_blocks);
     warp_kernel_for(s->warp_cap)<<<static_cast<unsigned>(blocks), kWarpsPerCta * 32,

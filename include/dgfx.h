@@ -127,8 +127,8 @@ void dgfx_sampler_destroy(dgfx_sampler* sampler);
  * whose sampler is host code). kind 0 (default): the warp sampler (one warp
  * per seed over the occupied tree positions, in shared memory, 32 to 128
  * entries by the plan's tree size) when the plan allows it; seeds whose
- * trees outgrow it are redone by the large-tree warp tier (one warp per
- * seed, up to 512 entries), and seeds beyond that by the padded sampler
+ * trees outgrow it are redone by the large-tree tier (one CTA of four warps
+ * per seed, up to 512 entries), and seeds beyond that by the padded sampler
  * (one CTA per seed over all tree positions). kind 1: the padded sampler
  * for every seed. kind 2: the warp sampler with the padded sampler behind
  * it (no large-tree tier). All give identical batches in every mode (same
