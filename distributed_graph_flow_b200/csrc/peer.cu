@@ -176,9 +176,8 @@ __global__ void __launch_bounds__(kPartThreads) exchange_partition_kernel(
   if (over) atomicOr(reinterpret_cast<unsigned*>(ex + kExStatusOff), 1u);
 }
 
-// Small CTAs (2 warps, <= 80 registers) so one fits on every SM beside a
-// resident sampler kernel when steps are pipelined; 8 loads in flight per
-// lane keep enough bytes moving per SM for NVLink.
+// Small CTAs (2 warps, <= 80 registers) that fit on an SM beside other
+// kernels when steps are pipelined; 8 loads in flight per lane.
 constexpr int kCopyThreads = 64;
 constexpr int kCopyUnroll = 8;
 constexpr int kChunk = 32;
@@ -376,8 +375,12 @@ int launch_exchange_copy(bool serve, const void* const* d_exchanges, int32_t wor
                          cudaStream_t stream) {
   const int64_t vpr = row_bytes / 16;
   const int64_t chunks = static_cast<int64_t>(world + 1) * ceil_div(std::max<int64_t>(slot_rows, 1), int64_t(kChunk));
+  // Up to 8 small CTAs (16 warps) per SM: on an idle GPU they keep enough
+  // rows in flight for the local gathers and the NVLink stores; beside a
+  // resident sampler kernel they start as its CTAs retire (the exchange
+  // runs on a high-priority stream).
   const int64_t blocks =
-      std::max<int64_t>(1, std::min<int64_t>(ceil_div(chunks, int64_t(kCopyThreads / 32)), int64_t(sm_count()) * 2));
+      std::max<int64_t>(1, std::min<int64_t>(ceil_div(chunks, int64_t(kCopyThreads / 32)), int64_t(sm_count()) * 8));
   const auto exs = reinterpret_cast<const char* const*>(d_exchanges);
   const int64_t rows_off = ex_rows_off(world, slot_rows);
   if (serve) {
