@@ -494,49 +494,34 @@ def ctypes_stats(cc):
 
 
 def bench_large_e2e(sharded, seeds_dev, W, K, dev, world, sync):
-    """Host seeds in, host topology + features out (pinned buffers), through
-    ShardedSampler.step; copies inside the timed region. The device-to-host
-    copies of step i run on a copy stream while step i + 1 samples (two sets
-    of pinned host buffers, used in turn)."""
+    """Host seeds in, host topology + features out, through the public
+    ShardedSampler.step_to_host: seeds copied in, the step sampled and
+    gathered, the batch's totals written by the GPU into pinned memory and
+    polled, then device-to-host copies of exactly the batch's sizes on a copy
+    stream (two sets of pinned host buffers, used in turn, so step i's copies
+    run while step i + 1 samples). All copies are inside the timed region."""
     import torch
+
+    from distributed_graph_flow_b200 import driver
 
     host_seeds = seeds_dev.cpu().pin_memory()
     cap_nodes = B_SEEDS * sharded.cc.tree_size
-
-    def host_set():
-        return (torch.empty(cap_nodes, dtype=torch.int64, pin_memory=True),
-                torch.empty(cap_nodes, dtype=torch.int64, pin_memory=True),
-                torch.empty(cap_nodes, dtype=torch.int64, pin_memory=True),
-                torch.empty((cap_nodes, FEAT_DIM), dtype=torch.bfloat16, pin_memory=True))
-
-    hosts = [host_set(), host_set()]
-    d_seeds = torch.empty(B_SEEDS, dtype=torch.int64, device=dev)
-    copy_stream = torch.cuda.Stream(device=dev)
+    hosts = [driver.HostBatch(cap_nodes, FEAT_DIM, torch.bfloat16) for _ in range(2)]
     moved = {"h2d": 0, "d2h": 0}
 
     def one(i):
-        h_nodes, h_src, h_dst, h_feat = hosts[i % 2]
-        d_seeds.copy_(host_seeds[W + i], non_blocking=True)
-        merged, feats, total = sharded.step(d_seeds)
-        counts = torch.stack([merged.node_offsets[-1], merged.edge_offsets[-1]]).cpu()  # waits for this step only
-        n, m = int(counts[0]), int(counts[1])
-        copy_stream.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(copy_stream):
-            parts = [(h_nodes, merged.node_ids, n), (h_src, merged.edge_src, m), (h_dst, merged.edge_dst, m)]
-            if feats is not None:
-                parts.append((h_feat, feats, n))
-            for host, dev_t, rows in parts:
-                host[:rows].copy_(dev_t[:rows], non_blocking=True)
-                dev_t.record_stream(copy_stream)
+        out = sharded.step_to_host(host_seeds[W + i], hosts[i % 2])
         moved["h2d"] += B_SEEDS * 8
-        moved["d2h"] += n * 8 + m * 16 + 16 + (n * FEAT_DIM * 2 if feats is not None else 0)
+        moved["d2h"] += 16 + out.n * 8 + out.m * 16 + (out.n * FEAT_DIM * 2 if sharded.features is not None else 0)
 
     for i in range(min(W, 2)):
         one(i)
+    for h in hosts:
+        h.wait()
     moved["h2d"] = moved["d2h"] = 0
     sync()
     t0 = time.perf_counter()
-    ms = timed(one, K, sync, "e2e", finish=lambda: torch.cuda.current_stream().wait_stream(copy_stream))
+    ms = timed(one, K, sync, "e2e", finish=sharded.drain_host)
     wall = (time.perf_counter() - t0) * 1e3 / K
     t = torch.tensor([max(ms, wall)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -546,7 +531,9 @@ def bench_large_e2e(sharded, seeds_dev, W, K, dev, world, sync):
     ms_max = float(t.item())
     return {"value": round(B_SEEDS * world / (ms_max / 1e3), 1), "unit": "subgraphs/s",
             "h2d_bytes_per_step": moved["h2d"] // K, "d2h_bytes_per_step": moved["d2h"] // K,
-            "ms_per_step": round(ms_max, 3)}
+            "ms_per_step": round(ms_max, 3),
+            "path": "ShardedSampler.step_to_host: totals published to pinned memory by the GPU and polled; "
+                    "copies of step i on a copy stream beside step i + 1"}
 
 
 # ---------------------------------------------------------------------------

@@ -236,7 +236,24 @@ __global__ void batch_mean_kernel(const int64_t* __restrict__ node_off, const in
 }  // namespace
 }  // namespace dgfx
 
+__global__ void publish_totals_kernel(const int64_t* __restrict__ a, const int64_t* __restrict__ b,
+                                      int64_t* out2) {
+  const int64_t x = *a, y = *b;
+  out2[1] = y;
+  out2[0] = x;
+}
+
 using namespace dgfx;
+
+extern "C" int dgfx_publish_totals(const int64_t* d_node_total, const int64_t* d_edge_total, int64_t* out2,
+                                   dgfx_stream stream_) {
+  if (d_node_total == nullptr || d_edge_total == nullptr || out2 == nullptr) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_publish_totals: null pointer");
+  }
+  publish_totals_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(d_node_total, d_edge_total, out2);
+  DGFX_CUDA_TRY(cudaGetLastError());
+  return DGFX_OK;
+}
 
 extern "C" int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
                                const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity,

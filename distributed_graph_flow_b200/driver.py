@@ -332,6 +332,32 @@ def hot_rows(index, count: int):
     return order[: max(0, min(int(count), num))].to(torch.int64).contiguous()
 
 
+class HostBatch:
+    """Pinned host buffers for one merged batch, filled by
+    ``ShardedSampler.step_to_host``: node ids, edge endpoints (local ids)
+    and the feature rows of every sampled node, sized for `node_capacity`
+    nodes and edges (the sampler's batch capacity). ``n`` / ``m`` are the
+    batch's node and edge counts; the arrays hold them once ``ready()``."""
+
+    def __init__(self, node_capacity: int, feat_dim: int, feat_dtype):
+        torch = _native.require_cuda()
+        cap = int(node_capacity)
+        self.node_ids = torch.empty(cap, dtype=torch.int64, pin_memory=True)
+        self.edge_src = torch.empty(cap, dtype=torch.int64, pin_memory=True)
+        self.edge_dst = torch.empty(cap, dtype=torch.int64, pin_memory=True)
+        self.features = torch.empty((cap, int(feat_dim)), dtype=feat_dtype, pin_memory=True)
+        self.totals = torch.full((2,), -1, dtype=torch.int64, pin_memory=True)  # written by the GPU
+        self.n = self.m = 0
+        self.done = None  # CUDA event recorded after the copies
+
+    def ready(self) -> bool:
+        return self.done is None or self.done.query()
+
+    def wait(self):
+        if self.done is not None:
+            self.done.synchronize()
+
+
 class ShardedSampler:
     """Per-rank sampler over the replicated topology plus halo features.
 
@@ -399,6 +425,62 @@ class ShardedSampler:
             torch.cuda.current_stream(gs.device).wait_stream(gs)
             if self.tail_stream is not None:
                 torch.cuda.current_stream(gs.device).wait_stream(self.tail_stream)
+
+    def step_to_host(self, host_seeds, out: HostBatch, timeout_s: float = 10.0) -> HostBatch:
+        """One step from host seeds (a pinned int64 tensor) to host results
+        in ``out``: seeds copied in, sampled and gathered as ``step``, then
+        the batch's node / edge totals are written by the GPU into
+        ``out.totals`` (pinned memory; ``dgfx_publish_totals``), which the
+        host polls (bounded by ``timeout_s``), so the copies of exactly the
+        batch's sizes are issued without a stream synchronisation and queue
+        behind the previous step's copies on a copy stream instead of
+        waiting for them. Returns ``out`` (its arrays valid once
+        ``out.ready()`` / after ``out.wait()``). Reusing a HostBatch waits
+        for its previous copies first; alternate two for overlap."""
+        import time
+
+        torch = _native.require_cuda()
+        dev = self.cc._device if hasattr(self.cc, "_device") else torch.device("cuda", torch.cuda.current_device())
+        if getattr(self, "_host_dev_seeds", None) is None or self._host_dev_seeds.numel() != host_seeds.numel():
+            self._host_dev_seeds = torch.empty(host_seeds.numel(), dtype=torch.int64, device=dev)
+            self._copy_stream = torch.cuda.Stream(device=dev)
+        out.wait()
+        tot = out.totals.numpy()
+        tot[:] = -1
+        seeds = self._host_dev_seeds
+        seeds.copy_(host_seeds, non_blocking=True)
+        merged, feats, _ = self.step(seeds)
+        main = torch.cuda.current_stream(dev)
+        _native.check(_native.lib().dgfx_publish_totals(
+            _native.elem_ptr(merged.node_offsets, -1), _native.elem_ptr(merged.edge_offsets, -1),
+            out.totals.data_ptr(), _native.stream_handle(main)))
+        t0 = time.perf_counter()
+        while tot[0] < 0 or tot[1] < 0:
+            if time.perf_counter() - t0 > timeout_s:
+                raise RuntimeError(f"step_to_host: the batch totals did not arrive within {timeout_s} s")
+        out.n, out.m = int(tot[0]), int(tot[1])
+        cs = self._copy_stream
+        cs.wait_stream(main)
+        if feats is not None and isinstance(self.features, PeerFeatures) and getattr(self, "gather_stream", None):
+            cs.wait_stream(self.gather_stream)
+        with torch.cuda.stream(cs):
+            parts = [(out.node_ids, merged.node_ids, out.n), (out.edge_src, merged.edge_src, out.m),
+                     (out.edge_dst, merged.edge_dst, out.m)]
+            if feats is not None:
+                parts.append((out.features, feats, out.n))
+            for host, dev_t, rows in parts:
+                host[:rows].copy_(dev_t[:rows], non_blocking=True)
+                dev_t.record_stream(cs)
+            out.done = torch.cuda.Event()
+            out.done.record(cs)
+        return out
+
+    def drain_host(self):
+        """Makes the current stream wait for every step_to_host copy."""
+        torch = _native.require_cuda()
+        cs = getattr(self, "_copy_stream", None)
+        if cs is not None:
+            torch.cuda.current_stream(cs.device).wait_stream(cs)
 
     def step(self, seeds, seed_ts=None, stream=None):
         call = self._calls * self.world + self.rank  # distinct random stream per rank and call

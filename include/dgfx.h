@@ -644,6 +644,17 @@ int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets
                     const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity, const void* d_feats,
                     int dtype, int64_t feat, void* d_out, dgfx_stream stream);
 
+/* Writes *d_node_total and *d_edge_total (for a merged batch: the last words
+ * of its node and edge offsets) to out2[0], out2[1] in stream order, from
+ * one thread on the GPU. out2 may be pinned host memory (a device address
+ * under unified addressing): a host that fills it with -1 and polls it
+ * learns a batch's sizes as soon as the batch is sampled, without a stream
+ * synchronisation or a copy that would queue behind earlier device-to-host
+ * copies, and can then issue the copies of exactly those sizes. No reference
+ * counterpart (the reference's batches live in host memory). */
+int dgfx_publish_totals(const int64_t* d_node_total, const int64_t* d_edge_total,
+                        int64_t* out2, dgfx_stream stream);
+
 /* ------------------------------------------------------------------------
  * Seeded synthetic inputs (stand-ins for the benchmark datasets, the role of
  * the reference's dgf/src/util/gen_test_graph.py generators at scale).

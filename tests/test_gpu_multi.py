@@ -303,3 +303,52 @@ def test_halo_exchange_two_gpus(cuda):
     for p in procs:
         p.join(timeout=120)
     assert res == {0: "ok", 1: "ok"}, res
+
+
+def test_step_to_host_single_rank(cuda):
+    """ShardedSampler.step_to_host (totals published by the GPU into pinned
+    memory and polled, copies of exactly the batch's sizes on a copy stream)
+    fills its host buffers with what step() returns on the device, over
+    alternating HostBatch objects and several steps in flight."""
+    from distributed_graph_flow_b200 import driver, synth
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+    from distributed_graph_flow_b200.sampling import config as cfg
+
+    dev = torch.device("cuda", 0)
+    spec = synth.GraphSpec(20_000, 200_000, 2.0, 1500, seed=5)
+    index, _, _ = synth.build_graph(spec, dev)
+    plan = cfg.explicit_plan("v", "e", [6, 4])
+    cc = ext.create_device_sampler(plan, ["v"], [spec.num_nodes], ["e"], [index], [None], 0, seed=3)
+    F = 64
+    pf = driver.PeerFeatures(spec.num_nodes, F, torch.bfloat16, spec.num_nodes, spec.num_nodes, 0, 1, dev)
+    synth.normal_features(0, spec.num_nodes, F, 4, torch.bfloat16, dev, out=pf.table)
+    pf.connect()
+    a = driver.ShardedSampler(cc, pf, 0, 1)
+    b = driver.ShardedSampler(cc, pf, 0, 1)
+    seeds = synth.uniform_int(4 * 512, 0, spec.num_nodes, 9, 5, dev).view(4, 512)
+    host_seeds = seeds.cpu().pin_memory()
+    hosts = [driver.HostBatch(512 * cc.tree_size, F, torch.bfloat16) for _ in range(2)]
+    got = []
+    for i in range(4):
+        out = a.step_to_host(host_seeds[i], hosts[i % 2])
+        if i >= 1:  # the previous batch of the other buffer set is complete once waited for
+            prev = hosts[(i - 1) % 2]
+            prev.wait()
+            got.append((prev.n, prev.m, prev.node_ids[:prev.n].clone(), prev.edge_src[:prev.m].clone(),
+                        prev.edge_dst[:prev.m].clone(), prev.features[:prev.n].clone()))
+    last = hosts[3 % 2]
+    last.wait()
+    got.append((last.n, last.m, last.node_ids[:last.n].clone(), last.edge_src[:last.m].clone(),
+                last.edge_dst[:last.m].clone(), last.features[:last.n].clone()))
+    for i in range(4):
+        merged, feats, _ = b.step(seeds[i])
+        torch.cuda.synchronize()
+        n = int(merged.node_offsets[-1].item())
+        m = int(merged.edge_offsets[-1].item())
+        gn, gm, nodes, src, dst, fh = got[i]
+        assert (gn, gm) == (n, m)
+        assert torch.equal(nodes, merged.node_ids[:n].cpu())
+        assert torch.equal(src, merged.edge_src[:m].cpu()) and torch.equal(dst, merged.edge_dst[:m].cpu())
+        assert torch.equal(fh, feats[:n].cpu())
+    cc.check()
+    pf.close()
