@@ -405,8 +405,8 @@ struct SoftmaxState {
   __device__ __forceinline__ void add(float l, const float* x) {
     const float mn = fmaxf(m, l);
     if (mn == -INFINITY) return;  // every logit so far is -inf
-    const float sc = expf(m - mn);
-    const float p = expf(l - mn);
+    const float sc = __expf(m - mn);
+    const float p = __expf(l - mn);
     s = s * sc + p;
 #pragma unroll
     for (int k = 0; k < EPV; ++k) acc[k] = acc[k] * sc + p * x[k];
@@ -421,13 +421,13 @@ struct SoftmaxState {
     for (int u = 1; u < U; ++u) mg = fmaxf(mg, l[u]);
     const float mn = fmaxf(m, mg);
     if (mn == -INFINITY) return;  // every logit so far is -inf
-    const float sc = expf(m - mn);
+    const float sc = __expf(m - mn);
     s *= sc;
 #pragma unroll
     for (int k = 0; k < EPV; ++k) acc[k] *= sc;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const float p = expf(l[u] - mn);
+      const float p = __expf(l[u] - mn);
       s += p;
 #pragma unroll
       for (int k = 0; k < EPV; ++k) acc[k] = fmaf(p, x[u][k], acc[k]);
@@ -437,7 +437,7 @@ struct SoftmaxState {
   __device__ __forceinline__ void merge(float m2, float s2, const float* acc2) {
     const float mn = fmaxf(m, m2);
     if (mn == -INFINITY) return;
-    const float a = expf(m - mn), b = expf(m2 - mn);
+    const float a = __expf(m - mn), b = __expf(m2 - mn);
     s = s * a + s2 * b;
 #pragma unroll
     for (int k = 0; k < EPV; ++k) acc[k] = acc[k] * a + acc2[k] * b;
