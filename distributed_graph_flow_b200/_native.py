@@ -118,6 +118,8 @@ SIGNATURES = {
     "dgfx_exchange_scatter": (_int, [_vp, _i32, _i32, _i64, _i64, _vp, _vp, _vp]),
     "dgfx_exchange_barrier": (_int, [_vp, _i32, _i32, ctypes.c_uint32, _u64, _vp]),
     "dgfx_exchange_check": (_int, [_vp, _i32, _vp]),
+    "dgfx_exchange_gather": (_int, [_vp, _vp, _i32, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _vp,
+                                    _i64, _vp, _i64, _vp, ctypes.c_uint32, _u64, _vp]),
     "dgfx_edge_timestamps": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp]),
     "dgfx_random_walk_negatives_workspace_size": (_int, [_vp, _i64, _i32, _i32, _i32, ctypes.POINTER(_sz)]),
     "dgfx_random_walk_negatives": (_int, [_vp, _vp, _i64, _i32, _i32, _i32, _u64, _vp, _vp, _sz, _vp]),

@@ -433,6 +433,24 @@ extern "C" int dgfx_exchange_barrier(const void* const* d_exchanges, int32_t wor
   return DGFX_OK;
 }
 
+extern "C" int dgfx_exchange_gather(const void* const* d_exchanges, void* d_exchange, int32_t world, int32_t rank,
+                                    int64_t slot_rows, int64_t rows_per_rank, int64_t num_nodes, int64_t row_bytes,
+                                    const int64_t* d_row_ids, const int64_t* d_begin, const int64_t* d_end,
+                                    int64_t max_rows, const int32_t* d_hot_slot, int32_t* d_req_pos,
+                                    const void* d_table, int64_t local_rows, const void* d_replica,
+                                    int64_t replica_rows, void* d_out, uint32_t epoch, uint64_t max_wait_ns,
+                                    dgfx_stream stream) {
+  DGFX_TRY(dgfx_exchange_partition(d_exchange, world, slot_rows, rows_per_rank, num_nodes, row_bytes, d_row_ids,
+                                   d_begin, d_end, max_rows, d_hot_slot, d_req_pos, d_out, stream));
+  DGFX_TRY(dgfx_exchange_barrier(d_exchanges, world, rank, epoch, max_wait_ns, stream));
+  DGFX_TRY(dgfx_exchange_serve(d_exchanges, world, rank, slot_rows, rows_per_rank, row_bytes, d_table, local_rows,
+                               d_replica, replica_rows, d_req_pos, d_out, stream));
+  uint32_t next = epoch + 1;
+  if (next > 0x7FFFFFFFu) next = 1;
+  DGFX_TRY(dgfx_exchange_barrier(d_exchanges, world, rank, next, max_wait_ns, stream));
+  return dgfx_exchange_scatter(d_exchanges, world, rank, slot_rows, row_bytes, d_req_pos, d_out, stream);
+}
+
 extern "C" int dgfx_exchange_check(const void* d_exchange, int32_t world, dgfx_stream stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (d_exchange == nullptr || world < 1 || world > kMaxWorld) {

@@ -342,11 +342,14 @@ class Sampler:
         cap_nodes, cap_edges, need_bytes = sizes
         NS, ES = len(self._nodeset_names), len(self._edgeset_names)
         dev = self._device
-        node_ids = torch.empty(cap_nodes, dtype=torch.int64, device=dev)
-        node_off = torch.empty(NS * B + 1, dtype=torch.int64, device=dev)
-        edge_src = torch.empty(cap_edges, dtype=torch.int64, device=dev)
-        edge_dst = torch.empty(cap_edges, dtype=torch.int64, device=dev)
-        edge_off = torch.empty(ES * B + 1, dtype=torch.int64, device=dev)
+        # One allocation for the five outputs (each starts on a 256-byte boundary).
+        lens = (cap_nodes, NS * B + 1, cap_edges, cap_edges, ES * B + 1)
+        starts, at = [], 0
+        for n in lens:
+            starts.append(at)
+            at += (n + 31) // 32 * 32
+        buf = torch.empty(at, dtype=torch.int64, device=dev)
+        node_ids, node_off, edge_src, edge_dst, edge_off = (buf[a:a + n] for a, n in zip(starts, lens))
         ws = self._workspace(need_bytes)
         out = _native.SampleOut(
             _native.ptr(node_ids), _native.ptr(node_off), _native.ptr(edge_src), _native.ptr(edge_dst), _native.ptr(edge_off)
@@ -370,7 +373,7 @@ class Sampler:
                 )
             )
             # Tensors the tail reads or writes stay allocated until it ends.
-            for t in (seeds, seed_ts, masks, node_ids, node_off, edge_src, edge_dst, edge_off):
+            for t in (seeds, seed_ts, masks, buf):
                 if t is not None:
                     t.record_stream(tail_stream)
         if check:

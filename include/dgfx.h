@@ -440,6 +440,21 @@ int dgfx_exchange_barrier(const void* const* d_exchanges, int32_t world,
                           dgfx_stream stream);
 int dgfx_exchange_check(const void* d_exchange, int32_t world,
                         dgfx_stream stream);
+/* The whole exchange of one gather in one call: partition, barrier with
+ * `epoch`, serve, barrier with the next epoch (epoch + 1, wrapping to 1
+ * after 2^31 - 1), scatter; the same launches as the five calls above, with
+ * no host code between them. The caller advances its epoch by two. No
+ * reference counterpart. */
+int dgfx_exchange_gather(const void* const* d_exchanges, void* d_exchange,
+                         int32_t world, int32_t rank, int64_t slot_rows,
+                         int64_t rows_per_rank, int64_t num_nodes,
+                         int64_t row_bytes, const int64_t* d_row_ids,
+                         const int64_t* d_begin, const int64_t* d_end,
+                         int64_t max_rows, const int32_t* d_hot_slot,
+                         int32_t* d_req_pos, const void* d_table,
+                         int64_t local_rows, const void* d_replica,
+                         int64_t replica_rows, void* d_out, uint32_t epoch,
+                         uint64_t max_wait_ns, dgfx_stream stream);
 
 /* ------------------------------------------------------------------------
  * Edge creation times from node creation times. Replaces the numpy body of

@@ -253,6 +253,55 @@ def test_exchange_emulated_ranks(cuda):
             _native.check(lib.dgfx_exchange_check(_native.ptr(bufs[0]), W, sh))  # flag cleared
 
 
+def test_exchange_gather_one_rank(cuda):
+    """dgfx_exchange_gather (partition, barrier, serve, barrier, scatter in one
+    call) with one rank, whose barrier passes at once: the rows equal the
+    table's in request order, with and without a replica table, on repeated
+    calls with advancing epochs."""
+    import ctypes
+
+    from distributed_graph_flow_b200 import _native, synth
+
+    lib = _native.lib()
+    dev = torch.device("cuda", 0)
+    sh = _native.stream_handle()
+    N, F = 9001, 64
+    row_bytes = F * 2
+    full = synth.normal_features(0, N, F, 6, torch.bfloat16, dev)
+    rng = np.random.default_rng(12)
+    n = 5000
+    ids = torch.from_numpy(rng.integers(-3, N + 3, n + 7)).to(dev)
+    bounds = torch.tensor([3, 3 + n], dtype=torch.int64, device=dev)
+    slot = n
+    need = ctypes.c_size_t()
+    _native.check(lib.dgfx_exchange_buffer_size(1, slot, row_bytes, ctypes.byref(need)))
+    buf = torch.zeros(need.value, dtype=torch.uint8, device=dev)
+    ptrs = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
+    pos = torch.empty(2 * slot, dtype=torch.int32, device=dev)
+    sel = ids[3:3 + n]
+    ok = (sel >= 0) & (sel < N)
+    exp = torch.zeros((n, F), dtype=torch.bfloat16, device=dev)
+    exp[ok] = full[sel[ok]]
+    hot_ids = torch.from_numpy(rng.choice(N, N // 4, replace=False)).to(dev)
+    hot = torch.full((N,), -1, dtype=torch.int32, device=dev)
+    hot[hot_ids] = torch.arange(len(hot_ids), dtype=torch.int32, device=dev)
+    replica = full[hot_ids].contiguous()
+    epoch = 1
+    for with_replica in (False, True, False):
+        out = torch.full((n + 2, F), 3.0, dtype=torch.bfloat16, device=dev)
+        _native.check(lib.dgfx_exchange_gather(
+            _native.ptr(ptrs), _native.ptr(buf), 1, 0, slot, N, N, row_bytes, _native.ptr(ids),
+            _native.elem_ptr(bounds, 0), _native.elem_ptr(bounds, 1), n,
+            _native.ptr(hot) if with_replica else None, _native.ptr(pos), _native.ptr(full), N,
+            _native.ptr(replica) if with_replica else None, int(replica.shape[0]) if with_replica else 0,
+            _native.ptr(out), epoch, 2_000_000_000, sh))
+        epoch += 2
+        torch.cuda.synchronize()
+        assert torch.equal(out[:n], exp), f"replica={with_replica}"
+        assert bool((out[n:] == 3.0).all())
+        _native.check(lib.dgfx_exchange_check(_native.ptr(buf), 1, sh))
+
+
 def test_exchange_barrier_single_gpu(cuda):
     """dgfx_exchange_barrier on one GPU: with one rank it passes at once; with
     two ranks whose peer flag already holds the epoch it passes; with a peer
