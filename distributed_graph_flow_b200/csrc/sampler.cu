@@ -1772,7 +1772,6 @@ __global__ void max_degree_kernel(const int64_t* __restrict__ rowptr, int64_t n,
   if ((threadIdx.x & 31) == 0) atomicMax(out, m);
 }
 
-// Merged batch from the per-seed scratch: one warp per seed.
 // Start of a call: status word 0 (first bad seed slot) to ~0, words 1..5
 // (flags, work counters) and 7..8 (seeds per tier) to 0; word 6 (the device
 // call index) is kept. The tiers' seed counters to 0.
@@ -1787,6 +1786,7 @@ __global__ void reset_kernel(unsigned long long* status, unsigned int* overflow_
   }
 }
 
+// Merged batch from the per-seed scratch: one warp per seed.
 __global__ void compact_kernel(Params p, const int64_t* __restrict__ node_off, const int64_t* __restrict__ edge_off,
                                int root_ns, int64_t* __restrict__ node_ids, int64_t* __restrict__ edge_src,
                                int64_t* __restrict__ edge_dst) {
@@ -2281,12 +2281,12 @@ extern "C" int dgfx_sampler_kernel_stats(dgfx_sampler* s, dgfx_stream stream_, i
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (s == nullptr || out2 == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_kernel_stats: null argument");
   unsigned long long st[2];
-  DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status + 7, sizeof(st), cudaMemcpyDeviceToHost, stream));
-  DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
-  if (s->tail_pending) {
-    DGFX_CUDA_TRY(cudaEventSynchronize(s->ev_tail));
+  if (s->tail_pending) {  // status words written by the last split call's tail
+    DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
     s->tail_pending = false;
   }
+  DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status + 7, sizeof(st), cudaMemcpyDeviceToHost, stream));
+  DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
   out2[0] = static_cast<int64_t>(st[0]);
   out2[1] = static_cast<int64_t>(st[1]);
   return DGFX_OK;
@@ -2483,12 +2483,12 @@ extern "C" int dgfx_sampler_check(dgfx_sampler* s, dgfx_stream stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (s == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_check: null sampler");
   unsigned long long st[3];
-  DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
-  DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
-  if (s->tail_pending) {
-    DGFX_CUDA_TRY(cudaEventSynchronize(s->ev_tail));
+  if (s->tail_pending) {  // status words written by the last split call's tail
+    DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
     s->tail_pending = false;
   }
+  DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
+  DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
   if (st[0] != ~0ull) {
     int64_t seed = 0;
     DGFX_CUDA_TRY(cudaMemcpy(&seed, s->last_seeds + st[0], sizeof(seed), cudaMemcpyDeviceToHost));
@@ -2509,12 +2509,12 @@ extern "C" int dgfx_sampler_stats(dgfx_sampler* s, dgfx_stream stream_, int64_t*
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (s == nullptr || out3 == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_stats: null argument");
   unsigned long long st[6];
-  DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
-  DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
-  if (s->tail_pending) {
-    DGFX_CUDA_TRY(cudaEventSynchronize(s->ev_tail));
+  if (s->tail_pending) {  // status words written by the last split call's tail
+    DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
     s->tail_pending = false;
   }
+  DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
+  DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
   for (int i = 0; i < 3; ++i) out3[i] = static_cast<int64_t>(st[3 + i]);
   return DGFX_OK;
 }

@@ -231,3 +231,30 @@ def test_split_call_alternating_handles(cuda):
     x = ext.batch_to_host(a.sample_merged(seeds[0], call_index=0))
     for u, v in zip(x, ext.batch_to_host(got[0])):
         np.testing.assert_array_equal(u, v)
+
+
+def test_split_call_status_after_tail(cuda):
+    """Status reads after a split call (check, kernel_stats) wait for the
+    call's tail on the stream they are given, so the large-tree tier's counts
+    are included without the caller joining the tail stream first."""
+    import dataclasses
+
+    from distributed_graph_flow_b200 import _native, synth
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+    from distributed_graph_flow_b200.sampling import config as cfg
+
+    dev = torch.device("cuda", 0)
+    s = synth.LARGE_SHARDED
+    spec = dataclasses.replace(s, num_nodes=int(s.num_nodes * 0.005), num_edges=int(s.num_edges * 0.005))
+    index, _, _ = synth.build_graph(spec, dev)
+    plan = cfg.explicit_plan("paper", "cites", [15, 10, 5])
+    seeds = synth.uniform_int(4096, 0, spec.num_nodes, 79, 5, dev)
+    a = ext.create_device_sampler(plan, ["paper"], [spec.num_nodes], ["cites"], [index], [None],
+                                  _native.MODE_RANDOM, seed=4)
+    tail = torch.cuda.Stream(device=dev)
+    for call in range(3):
+        a.sample_merged(seeds, call_index=call, check=False, tail_stream=tail)
+        warp, padded = a.kernel_stats()  # the current stream, not joined to the tail
+        assert warp + padded == 4096
+    a.sample_merged(seeds, call_index=5, check=False, tail_stream=tail)
+    a.check()
