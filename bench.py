@@ -38,6 +38,7 @@ sys.path.insert(0, str(ROOT))
 import numpy as np  # noqa: E402
 
 B_SEEDS = 8192
+GRAPH_STEPS = 4  # large sharded steps per CUDA-graph replay
 FANOUT = [15, 10, 5]
 FEAT_DIM = 128
 
@@ -258,6 +259,14 @@ def bench_large(args, rank, world, dev):
     spec, index, table, cc, sharded, plan = setup_large(rank, world, dev, args.scale, args.halo, args.halo_cache,
                                                         args.split)
     W, K = args.warmup, args.steps
+    from distributed_graph_flow_b200 import driver
+
+    # Steps per CUDA-graph replay: a divisor of K, so that exactly K steps are timed.
+    S = math.gcd(K, GRAPH_STEPS)
+    use_graph = args.graph and args.overlap and S > 1 and isinstance(sharded.features, driver.PeerFeatures)
+    if not use_graph:
+        S = 1
+    R = K // S
     seeds = synth.uniform_int((W + K) * B_SEEDS, 0, spec.num_nodes, 77 + rank, 5, dev).view(W + K, B_SEEDS)
 
     def barrier():
@@ -276,14 +285,25 @@ def bench_large(args, rank, world, dev):
         step(seeds[i])
     sharded.drain()
     cc.check()
+    if use_graph:
+        # S pipelined steps per CUDA-graph replay: the host issues one replay
+        # (and one seed copy) per S steps instead of ~10 launches per step.
+        captured = driver.CapturedSteps(sharded, B_SEEDS, steps=S)
+        for _ in range(max(3, -(-W // S))):  # warm-up replays
+            captured.replay(seeds[:S])
+        torch.cuda.synchronize()
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
     clocks.start()
-    ms = timed(lambda i: step(seeds[W + i]), K, sync, "step", finish=sharded.drain)
-    if args.overlap:
-        # Pipelined steps leave work on side streams, so per-step intervals on
-        # the launching stream alternate; the step time is the whole timed
-        # region (side streams drained into it) over K.
-        ms = TIMING["step"]["mean_ms"]
+    if use_graph:
+        timed(lambda r: captured.replay(seeds[W + r * S:W + (r + 1) * S]), R, sync, "step")
+        ms = TIMING["step"]["mean_ms"] / S  # whole timed region / K
+    else:
+        ms = timed(lambda i: step(seeds[W + i]), K, sync, "step", finish=sharded.drain)
+        if args.overlap:
+            # Pipelined steps leave work on side streams, so per-step intervals on
+            # the launching stream alternate; the step time is the whole timed
+            # region (side streams drained into it) over K.
+            ms = TIMING["step"]["mean_ms"]
     clk = clocks.stop()
     cc.check()
     if sharded.cc_alt is not None:
@@ -375,6 +395,8 @@ def bench_large(args, rank, world, dev):
                                                              "beside the first kernel of step i+1)"
                                                              if args.split else "")) if args.overlap else "none",
                            "step_time": "whole timed region / K" if args.overlap else "median per-step interval",
+                           "issue": (f"{S} steps per CUDA-graph replay (one replay and one seed copy per {S} steps)"
+                                     if use_graph else "every step's launches issued from the host"),
                            "timing": TIMING.get("step")},
         "clocks": clk,
         "roofline": roof,
@@ -1365,6 +1387,9 @@ def main():
                          "graph, of 180 GB)")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="run each step's feature gather on the sampling stream (no pipelining)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="large sharded steps: issue every step from the host instead of replaying "
+                         f"{GRAPH_STEPS} captured steps per CUDA graph")
     ap.add_argument("--no-split", dest="split", action="store_false",
                     help="overlapped steps: run each sampling call on one stream (no second sampler handle)")
     ap.add_argument("--minimal", action="store_true",

@@ -80,6 +80,8 @@ __global__ void __launch_bounds__(kGatherThreads, 32) gather_p2p_kernel(const ui
 //   [0, 8 * (world + 1))                 int64 request count per owner, then
 //                                        per local replica (slot `world`)
 //   [kExStatusOff, +4)                   uint32 status: 1 slot overflow, 2 barrier timeout
+//   [kExEpochOff, +4)                    uint32 this rank's barrier epoch when barriers take
+//                                        their epoch on the device (epoch argument 0)
 //   [kExFlagsOff, + 4 * world)           uint32 barrier arrival epoch per rank
 //   [kExIdsOff, + 8 * (world + 1) * S)   int64 request ids; slot o = ids owned by
 //                                        rank o, slot `world` = replica rows
@@ -91,6 +93,7 @@ __global__ void __launch_bounds__(kGatherThreads, 32) gather_p2p_kernel(const ui
 // ---------------------------------------------------------------------------
 constexpr int kMaxWorld = 16;
 constexpr int64_t kExStatusOff = 256;
+constexpr int64_t kExEpochOff = 264;  // uint32 device-side barrier epoch of this rank
 constexpr int64_t kExFlagsOff = 320;
 constexpr int64_t kExIdsOff = 512;
 
@@ -293,7 +296,19 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 __global__ void exchange_barrier_kernel(const char* const* __restrict__ exs, int32_t world, int32_t rank,
                                         uint32_t epoch, uint64_t max_wait_ns) {
+  __shared__ uint32_t s_epoch;
   const int t = threadIdx.x;
+  if (epoch == 0) {  // the epoch from this rank's device counter (every rank advances its own in step)
+    if (t == 0) {
+      uint32_t* c = reinterpret_cast<uint32_t*>(const_cast<char*>(exs[rank]) + kExEpochOff);
+      uint32_t e = *c + 1;
+      if (e > 0x7FFFFFFFu) e = 1;
+      *c = e;
+      s_epoch = e;
+    }
+    __syncthreads();
+    epoch = s_epoch;
+  }
   if (t >= world) return;
   __threadfence_system();
   uint32_t* remote = reinterpret_cast<uint32_t*>(const_cast<char*>(exs[t]) + kExFlagsOff) + rank;
@@ -445,7 +460,7 @@ extern "C" int dgfx_exchange_gather(const void* const* d_exchanges, void* d_exch
   DGFX_TRY(dgfx_exchange_barrier(d_exchanges, world, rank, epoch, max_wait_ns, stream));
   DGFX_TRY(dgfx_exchange_serve(d_exchanges, world, rank, slot_rows, rows_per_rank, row_bytes, d_table, local_rows,
                                d_replica, replica_rows, d_req_pos, d_out, stream));
-  uint32_t next = epoch + 1;
+  uint32_t next = epoch == 0 ? 0 : epoch + 1;  // 0: both barriers take the device epoch
   if (next > 0x7FFFFFFFu) next = 1;
   DGFX_TRY(dgfx_exchange_barrier(d_exchanges, world, rank, next, max_wait_ns, stream));
   return dgfx_exchange_scatter(d_exchanges, world, rank, slot_rows, row_bytes, d_req_pos, d_out, stream);

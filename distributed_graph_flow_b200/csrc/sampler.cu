@@ -1870,6 +1870,7 @@ struct dgfx_sampler {
   // the previous tail before it reuses the workspace.
   cudaEvent_t ev_warp = nullptr, ev_tail = nullptr;
   bool tail_pending = false;
+  unsigned long long tail_capture = 0;  // capture sequence that recorded ev_tail (0: recorded eagerly)
   int threads = 256;
   size_t smem_bytes = 0;
   int32_t pbits = 1, keybits = 2;
@@ -1892,6 +1893,15 @@ struct dgfx_sampler {
 const dgfx::WalkPlan* dgfx_sampler_walk_plan(const dgfx_sampler* s) { return s == nullptr ? nullptr : &s->walk; }
 
 namespace {
+
+// Host-side reads of the status words after a split call: `stream` waits
+// for the call's tail first (eagerly recorded tails only; a tail recorded
+// in a captured graph is ordered by that graph's replays on their stream).
+int wait_tail(dgfx_sampler* s, cudaStream_t stream) {
+  if (s->tail_pending && s->tail_capture == 0) DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
+  s->tail_pending = false;
+  return DGFX_OK;
+}
 
 int pow2_at_least(int64_t x) {
   int64_t p = 1;
@@ -2281,10 +2291,7 @@ extern "C" int dgfx_sampler_kernel_stats(dgfx_sampler* s, dgfx_stream stream_, i
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (s == nullptr || out2 == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_kernel_stats: null argument");
   unsigned long long st[2];
-  if (s->tail_pending) {  // status words written by the last split call's tail
-    DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
-    s->tail_pending = false;
-  }
+  DGFX_TRY(wait_tail(s, stream));
   DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status + 7, sizeof(st), cudaMemcpyDeviceToHost, stream));
   DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
   out2[0] = static_cast<int64_t>(st[0]);
@@ -2338,9 +2345,22 @@ int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_t
     if (s->ev_warp == nullptr) DGFX_CUDA_TRY(cudaEventCreateWithFlags(&s->ev_warp, cudaEventDisableTiming));
     if (s->ev_tail == nullptr) DGFX_CUDA_TRY(cudaEventCreateWithFlags(&s->ev_tail, cudaEventDisableTiming));
   }
+  cudaStreamCaptureStatus cst = cudaStreamCaptureStatusNone;
+  unsigned long long cid = 0;
+  DGFX_CUDA_TRY(cudaStreamGetCaptureInfo(stream, &cst, &cid));
+  const bool capturing = cst == cudaStreamCaptureStatusActive;
   if (s->tail_pending) {  // the last split call's tail must end before the workspace is reused
-    DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
-    s->tail_pending = split;
+    if (!capturing && s->tail_capture == 0) {
+      DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
+    } else if (capturing && s->tail_capture == cid) {
+      DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));  // recorded earlier in this capture
+    } else if (capturing) {
+      return fail(DGFX_ERR_FAILED_PRECONDITION,
+                  "dgfx_sampler_sample: a split call's tail is pending from outside this stream capture; "
+                  "call dgfx_sampler_check before capturing");
+    }
+    // else: recorded in a capture that has ended; its graph's replays are ordered on their stream.
+    s->tail_pending = false;
   }
   s->last_B = B;
   s->last_seeds = d_seeds;
@@ -2361,6 +2381,7 @@ int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_t
     if (split) {
       DGFX_CUDA_TRY(cudaEventRecord(s->ev_tail, tail));
       s->tail_pending = true;
+      s->tail_capture = capturing ? cid : 0;
     }
     return DGFX_OK;
   }
@@ -2454,6 +2475,7 @@ int sample_impl(dgfx_sampler* s, const int64_t* d_seeds, const int64_t* d_seed_t
   if (split) {
     DGFX_CUDA_TRY(cudaEventRecord(s->ev_tail, tail));
     s->tail_pending = true;
+    s->tail_capture = capturing ? cid : 0;
   }
   return DGFX_OK;
 }
@@ -2483,10 +2505,7 @@ extern "C" int dgfx_sampler_check(dgfx_sampler* s, dgfx_stream stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (s == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_check: null sampler");
   unsigned long long st[3];
-  if (s->tail_pending) {  // status words written by the last split call's tail
-    DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
-    s->tail_pending = false;
-  }
+  DGFX_TRY(wait_tail(s, stream));
   DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
   DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
   if (st[0] != ~0ull) {
@@ -2509,10 +2528,7 @@ extern "C" int dgfx_sampler_stats(dgfx_sampler* s, dgfx_stream stream_, int64_t*
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (s == nullptr || out3 == nullptr) return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_sampler_stats: null argument");
   unsigned long long st[6];
-  if (s->tail_pending) {  // status words written by the last split call's tail
-    DGFX_CUDA_TRY(cudaStreamWaitEvent(stream, s->ev_tail, 0));
-    s->tail_pending = false;
-  }
+  DGFX_TRY(wait_tail(s, stream));
   DGFX_CUDA_TRY(cudaMemcpyAsync(st, s->d_status, sizeof(st), cudaMemcpyDeviceToHost, stream));
   DGFX_CUDA_TRY(cudaStreamSynchronize(stream));
   for (int i = 0; i < 3; ++i) out3[i] = static_cast<int64_t>(st[3 + i]);

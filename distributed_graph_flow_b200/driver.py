@@ -226,9 +226,10 @@ class PeerFeatures:
         lib = _native.lib()
         rep_rows = 0 if self._replica is None else int(self._replica.shape[0])
         if stage_events is None and self.barrier == "device":
-            # One native call for the five launches (less host time per step).
-            epoch = (self._epoch % 0x7FFFFFFF) + 1
-            self._epoch = (epoch % 0x7FFFFFFF) + 1  # the call's second barrier used epoch + 1
+            # One native call for the five launches (less host time per step);
+            # barrier epochs from the device counter (epoch 0), as in
+            # _group_barrier, so the launches can be captured in a CUDA graph.
+            epoch = 0
             _native.check(lib.dgfx_exchange_gather(
                 _native.ptr(self._ex_ptrs), self._ex.ptr, self.world, self.rank, self.exchange_rows,
                 self.rows_per_rank, self.num_nodes, self.row_bytes, _native.ptr(ids), begin_ptr, end_ptr,
@@ -293,9 +294,10 @@ class PeerFeatures:
     def _group_barrier(self, s):
         """Stream-ordered barrier over the group (every rank calls it in the same order)."""
         if self.barrier == "device":
-            self._epoch = (self._epoch % 0x7FFFFFFF) + 1
+            # Epoch 0: the kernel advances this rank's device-side epoch, so
+            # a captured graph replays correctly (every barrier uses it).
             _native.check(_native.lib().dgfx_exchange_barrier(_native.ptr(self._ex_ptrs), self.world, self.rank,
-                                                              self._epoch, self.barrier_timeout_ns, int(s.cuda_stream)))
+                                                              0, self.barrier_timeout_ns, int(s.cuda_stream)))
         else:
             torch = _native.require_cuda()
             import torch.distributed as dist
@@ -341,6 +343,50 @@ def hot_rows(index, count: int):
     deg = torch.bincount(index.col, minlength=num)
     order = torch.sort(deg, descending=True, stable=True).indices
     return order[: max(0, min(int(count), num))].to(torch.int64).contiguous()
+
+
+class CapturedSteps:
+    """`steps` pipelined steps of a ShardedSampler (``step_overlapped``)
+    captured in one CUDA graph, for callers whose host would otherwise issue
+    the launches slower than the GPU runs them. The seeds of the steps live
+    in ``seeds`` ([steps, batch] int64 on the GPU; ``replay(block)`` copies a
+    block in first); each replay overwrites ``outputs`` (a list of (merged
+    batch, features, None) per step). Random streams come from the samplers'
+    device counters (every replay draws new ones); exchange barriers take
+    their epochs on the device, so at N > 1 every rank replays its own graph
+    in step. Needs the peer-feature store (``PeerFeatures``)."""
+
+    def __init__(self, sharded: "ShardedSampler", batch: int, steps: int = 4):
+        torch = _native.require_cuda()
+        if not isinstance(sharded.features, PeerFeatures):
+            raise ValueError("CapturedSteps needs PeerFeatures")
+        dev = sharded.features.device
+        self.sharded = sharded
+        self.steps = int(steps)
+        self.seeds = torch.zeros((self.steps, int(batch)), dtype=torch.int64, device=dev)
+        # Eager pass: streams, events, workspaces and size caches exist before capture.
+        for k in range(self.steps):
+            sharded.step_overlapped(self.seeds[k], call_index=_native.CALL_INDEX_DEVICE)
+        sharded.drain()
+        for h in (sharded.cc, sharded.cc_alt):
+            if h is not None:
+                h.check()  # synchronises and settles pending split tails
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream(device=dev)
+        cs.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.graph(self.graph, stream=cs):
+            self.outputs = [sharded.step_overlapped(self.seeds[k], call_index=_native.CALL_INDEX_DEVICE)
+                            for k in range(self.steps)]
+            sharded.drain()
+        torch.cuda.synchronize(dev)
+
+    def replay(self, seeds_block=None):
+        """Runs the captured steps (on the current stream) after copying
+        `seeds_block` ([steps, batch]) into ``seeds`` if given."""
+        if seeds_block is not None:
+            self.seeds.copy_(seeds_block, non_blocking=True)
+        self.graph.replay()
 
 
 class HostBatch:
@@ -389,14 +435,17 @@ class ShardedSampler:
         self.gather_stream = None
         self.tail_stream = None
 
-    def step_overlapped(self, seeds, seed_ts=None):
+    def step_overlapped(self, seeds, seed_ts=None, call_index=None):
         """Like step(), but the feature gather runs on a second stream so it
         overlaps the sampling of the next call (the sampler is latency-bound,
         the gather bandwidth-bound), and with ``cc_alt`` each sampling call
         is split (the large-tree kernel, scans and compaction on a tail
         stream) so that it overlaps the next call's first kernel. Results are
         valid once the caller's stream has waited on ``gather_stream``
-        (``drain()``). Batches equal step()'s for the same call order."""
+        (``drain()``). Batches equal step()'s for the same call order.
+        ``call_index=_native.CALL_INDEX_DEVICE`` draws the random stream
+        index from each sampler's device counter (for CUDA-graph capture,
+        ``CapturedSteps``)."""
         torch = _native.require_cuda()
         if not isinstance(self.features, PeerFeatures):
             return self.step(seeds, seed_ts)
@@ -407,7 +456,7 @@ class ShardedSampler:
             self.gather_stream = torch.cuda.Stream(device=dev, priority=-1)
             self.tail_stream = torch.cuda.Stream(device=dev) if self.cc_alt is not None else None
         main = torch.cuda.current_stream(dev)
-        call = self._calls * self.world + self.rank
+        call = self._calls * self.world + self.rank if call_index is None else call_index
         cc = self.cc if self.cc_alt is None or self._calls % 2 == 0 else self.cc_alt
         self._calls += 1
         if self.tail_stream is None:
@@ -423,8 +472,9 @@ class ShardedSampler:
             off = merged.node_offsets
             self.features.gather_range(merged.node_ids, _native.elem_ptr(off, 0), _native.elem_ptr(off, -1), cap,
                                        feats, stream=self.gather_stream)
-        for t in (merged.node_ids, merged.node_offsets):
-            t.record_stream(self.gather_stream)
+        if not torch.cuda.is_current_stream_capturing():
+            for t in (merged.node_ids, merged.node_offsets):
+                t.record_stream(self.gather_stream)
         return merged, feats, None
 
     def drain(self):

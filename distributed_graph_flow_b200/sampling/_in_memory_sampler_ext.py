@@ -372,10 +372,12 @@ class Sampler:
                     ctypes.byref(out), _native.ptr(ws), need_bytes, sh, _native.stream_handle(tail_stream),
                 )
             )
-            # Tensors the tail reads or writes stay allocated until it ends.
-            for t in (seeds, seed_ts, masks, buf):
-                if t is not None:
-                    t.record_stream(tail_stream)
+            # Tensors the tail reads or writes stay allocated until it ends
+            # (a captured graph keeps its own allocations).
+            if not torch.cuda.is_current_stream_capturing():
+                for t in (seeds, seed_ts, masks, buf):
+                    if t is not None:
+                        t.record_stream(tail_stream)
         if check:
             self.check(stream if tail_stream is None else tail_stream)
         return MergedBatch(B, self._nodeset_names, self._edgeset_names, node_ids, node_off, edge_src, edge_dst,

@@ -402,7 +402,10 @@ int dgfx_gather_rows_p2p(const void* const* d_tables, int32_t world,
  * dgfx_exchange_barrier: every rank publishes `epoch` (increasing per call,
  * same sequence on all ranks, starting at 1) in the other ranks' flags and
  * waits for theirs, at most max_wait_ns; a wait that runs out sets the
- * timeout flag instead of hanging.
+ * timeout flag instead of hanging. With epoch 0 the kernel takes the next
+ * epoch from a counter in this rank's exchange buffer, so the launches can
+ * be captured in a CUDA graph and replayed (every rank must then use epoch
+ * 0 for all its barriers, in the same sequence).
  * Local replica (optional): d_hot_slot int32[num_nodes] maps a node to its
  * row in this rank's d_replica table (a read-only copy of frequently
  * requested rows, replica_rows x row_bytes), -1 elsewhere. Requests for such
@@ -443,8 +446,9 @@ int dgfx_exchange_check(const void* d_exchange, int32_t world,
 /* The whole exchange of one gather in one call: partition, barrier with
  * `epoch`, serve, barrier with the next epoch (epoch + 1, wrapping to 1
  * after 2^31 - 1), scatter; the same launches as the five calls above, with
- * no host code between them. The caller advances its epoch by two. No
- * reference counterpart. */
+ * no host code between them. The caller advances its epoch by two; with
+ * epoch 0 both barriers take their epochs on the device (see
+ * dgfx_exchange_barrier). No reference counterpart. */
 int dgfx_exchange_gather(const void* const* d_exchanges, void* d_exchange,
                          int32_t world, int32_t rank, int64_t slot_rows,
                          int64_t rows_per_rank, int64_t num_nodes,

@@ -401,3 +401,59 @@ def test_step_to_host_single_rank(cuda):
         assert torch.equal(fh, feats[:n].cpu())
     cc.check()
     pf.close()
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_captured_steps_single_rank(cuda, mode):
+    """CapturedSteps (pipelined steps of two alternating samplers with split
+    calls, captured in one CUDA graph): every replayed step's features are the
+    table's rows of its sampled nodes; in FIRST mode (mode 1) each step's
+    batch equals an eager step() on the same seeds; in random mode (mode 0)
+    consecutive replays draw new random streams."""
+    from distributed_graph_flow_b200 import driver, synth
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+    from distributed_graph_flow_b200.sampling import config as cfg
+
+    dev = torch.device("cuda", 0)
+    spec = synth.GraphSpec(30_000, 400_000, 2.0, 3000, seed=6)
+    index, _, _ = synth.build_graph(spec, dev)
+    plan = cfg.explicit_plan("v", "e", [8, 4, 3])
+    mk = lambda sd: ext.create_device_sampler(plan, ["v"], [spec.num_nodes], ["e"], [index], [None], mode, seed=sd)
+    F = 64
+    pf = driver.PeerFeatures(spec.num_nodes, F, torch.bfloat16, spec.num_nodes, spec.num_nodes, 0, 1, dev)
+    synth.normal_features(0, spec.num_nodes, F, 4, torch.bfloat16, dev, out=pf.table)
+    pf.connect()
+    ss = driver.ShardedSampler(mk(3), pf, 0, 1, cc_alt=mk(4))
+    cap = driver.CapturedSteps(ss, 1024, steps=4)
+    blocks = synth.uniform_int(3 * 4 * 1024, 0, spec.num_nodes, 21, 5, dev).view(3, 4, 1024)
+    ref = driver.ShardedSampler(mk(3), pf, 0, 1)
+    prev = None
+    for r in range(3):
+        cap.replay(blocks[r])
+        torch.cuda.synchronize()
+        got = []
+        for k, (merged, feats, _) in enumerate(cap.outputs):
+            n = int(merged.node_offsets[-1].item())
+            m = int(merged.edge_offsets[-1].item())
+            nodes = merged.node_ids[:n]
+            assert torch.equal(feats[:n], pf.table[nodes]), f"replay {r} step {k}"
+            assert torch.equal(nodes[merged.node_offsets[:-1][merged.node_offsets[:-1] < n]],
+                               blocks[r, k][merged.node_offsets[:-1] < n])  # every sample starts with its seed
+            got.append((nodes.clone(), merged.edge_src[:m].clone(), merged.edge_dst[:m].clone()))
+            if mode == 1:
+                e_merged, _, _ = ref.step(blocks[r, k])
+                torch.cuda.synchronize()
+                en = int(e_merged.node_offsets[-1].item())
+                em = int(e_merged.edge_offsets[-1].item())
+                assert (en, em) == (n, m)
+                assert torch.equal(e_merged.node_ids[:en], nodes)
+                assert torch.equal(e_merged.edge_src[:em], merged.edge_src[:m])
+                assert torch.equal(e_merged.edge_dst[:em], merged.edge_dst[:m])
+        if mode == 0 and prev is not None:
+            # Same seeds as the previous replay? No: new seeds and new streams; at least
+            # one step's batch must differ from what the previous replay produced.
+            assert any(not torch.equal(a[0], b[0]) for a, b in zip(got, prev))
+        prev = got
+    ss.cc.check()
+    ss.cc_alt.check()
+    pf.close()
