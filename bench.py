@@ -38,7 +38,7 @@ sys.path.insert(0, str(ROOT))
 import numpy as np  # noqa: E402
 
 B_SEEDS = 8192
-GRAPH_STEPS = 4  # large sharded steps per CUDA-graph replay
+GRAPH_STEPS = 10  # at most this many large sharded steps per CUDA-graph replay
 FANOUT = [15, 10, 5]
 FEAT_DIM = 128
 
@@ -261,8 +261,10 @@ def bench_large(args, rank, world, dev):
     W, K = args.warmup, args.steps
     from distributed_graph_flow_b200 import driver
 
-    # Steps per CUDA-graph replay: a divisor of K, so that exactly K steps are timed.
-    S = math.gcd(K, GRAPH_STEPS)
+    # Steps per CUDA-graph replay: the largest divisor of K up to GRAPH_STEPS,
+    # so that exactly K steps are timed (a replay ends with its steps drained,
+    # so fewer, longer replays overlap more).
+    S = max(d for d in range(1, min(K, GRAPH_STEPS) + 1) if K % d == 0)
     use_graph = args.graph and args.overlap and S > 1 and isinstance(sharded.features, driver.PeerFeatures)
     if not use_graph:
         S = 1
@@ -1389,7 +1391,7 @@ def main():
                     help="run each step's feature gather on the sampling stream (no pipelining)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="large sharded steps: issue every step from the host instead of replaying "
-                         f"{GRAPH_STEPS} captured steps per CUDA graph")
+                         f"up to {GRAPH_STEPS} captured steps per CUDA graph")
     ap.add_argument("--no-split", dest="split", action="store_false",
                     help="overlapped steps: run each sampling call on one stream (no second sampler handle)")
     ap.add_argument("--minimal", action="store_true",
