@@ -158,7 +158,6 @@ class PeerFeatures:
             raise ValueError(f"barrier must be 'device' or 'nccl', got {barrier!r}")
         self.barrier = barrier
         self.barrier_timeout_ns = int(barrier_timeout_s * 1e9)
-        self._epoch = 0
         self.buffer = DeviceBuffer(max(1, local_rows) * self.row_bytes, device)
         self.table = self.buffer.tensor((local_rows, self.dim), dtype)
         self._peers = []
