@@ -85,9 +85,22 @@ def _infer_primary_key_or_none(name: str, schema) -> Optional[str]:
     return matching[0] if matching else None
 
 
-def fix_schema(schema: schema_lib.GraphSchema, fix_shape: bool = True) -> None:
-    """Sets missing primary keys (``#id``-like names) and drops the extra
-    leading None of [None, k] shapes when every feature of a set has one."""
+_TF_EXAMPLE_FORMATS = {schema_lib.FeatureFormat.INTEGER_32: schema_lib.FeatureFormat.INTEGER_64,
+                       schema_lib.FeatureFormat.BOOL: schema_lib.FeatureFormat.INTEGER_64,
+                       schema_lib.FeatureFormat.FLOAT_64: schema_lib.FeatureFormat.FLOAT_32}
+
+
+def fix_schema(schema: schema_lib.GraphSchema, create_pound_id_as_fall_back: bool = False, fix_shape: bool = True,
+               tf_example: bool = False) -> None:
+    """Repairs a schema in place (dgf/src/analyse/schema.py:168-265).
+
+    Sets missing primary keys (``#id``-like names) and drops the extra leading
+    None of [None, k] shapes when every feature of a set has one. With
+    ``create_pound_id_as_fall_back`` a node set with no key-like feature gets
+    a BYTES feature ``#id`` as its key (whether the data holds it is not
+    checked). With ``tf_example`` formats a TF Example cannot hold are
+    widened or narrowed to the ones it can: int32 and bool to int64, float64
+    to float32."""
 
     def suspicious(shape):
         return shape is not None and len(shape) == 2 and shape[0] is None and shape[1] is not None
@@ -97,17 +110,27 @@ def fix_schema(schema: schema_lib.GraphSchema, fix_shape: bool = True) -> None:
             for f in features.values():
                 f.shape = tuple() if f.shape[1] == 1 else tuple(f.shape[1:])
 
+    def fix_formats(features):
+        if tf_example:
+            for f in features.values():
+                f.format = _TF_EXAMPLE_FORMATS.get(f.format, f.format)
+
     for name, ns in schema.node_sets.items():
+        fix_formats(ns.features)
         fix_shapes(ns.features)
         if primary_feature_or_none(name, ns) is not None:
             continue
         pk = _infer_primary_key_or_none(name, ns)
+        if pk is None and create_pound_id_as_fall_back:
+            pk = "#id"
+            ns.features[pk] = schema_lib.FeatureSchema(format=schema_lib.FeatureFormat.BYTES)
         if pk is None:
             raise ValueError(f"No primary feature found in the schema of {name!r} (i.e. semantic=PRIMARY_ID) and no "
                              f"feature look like a primary key ({_PRIMARY_CANDIDATES!r}). The available features are: "
                              f"{ns.features.keys()!r}. Solution: Specify the primary key in the schema.")
         ns.features[pk].semantic = schema_lib.FeatureSemantic.PRIMARY_ID
     for name, es in schema.edge_sets.items():
+        fix_formats(es.features)
         fix_shapes(es.features)
         if primary_feature_or_none(name, es) is not None:
             continue

@@ -57,10 +57,23 @@ class _Ragged:
         self.n = n
 
 
+def _require_integer_times(name: str, column) -> None:
+    """Timestamp series are searched as int64: a float series would be
+    truncated (an entry at t = 1.5 would pass a cutoff of 1), so it is
+    rejected instead."""
+    col = np.asarray(column)
+    kinds = {col.dtype.kind} if col.dtype != object else {np.asarray(r).dtype.kind for r in col if np.size(r)}
+    if kinds - set("iub"):
+        raise ValueError(f"Timestamp feature `{name}` must hold integer timestamps, got dtype kinds {sorted(kinds)}.")
+
+
 class TimeseriesSlicer:
     """The timestamped timeseries groups of one feature set, in HBM."""
 
     def __init__(self, features: Dict[str, np.ndarray], specs: List[temporal_util.TimeseriesGroupSpec], device=None):
+        for g in specs:
+            if g.timestamp_feature_name is not None:
+                _require_integer_times(g.timestamp_feature_name, features[g.timestamp_feature_name])
         torch = _native.require_cuda()
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.groups = []
@@ -81,6 +94,10 @@ class TimeseriesSlicer:
         """{feature: object array [len(rows)] of each row's causal window}."""
         torch = _native.require_cuda()
         lib = _native.lib()
+        if max_len is not None and max_len < 0:
+            # numpy's times[max(0, end - max_len):end] is empty for a negative
+            # length, exactly as a cap of 0 is.
+            max_len = 0
         rows = np.ascontiguousarray(np.asarray(rows, np.int64))
         cutoffs = np.ascontiguousarray(np.asarray(cutoffs, np.int64))
         n = len(rows)

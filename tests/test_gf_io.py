@@ -356,3 +356,29 @@ def test_fix_schema_suspicious_shapes():
     with pytest.raises(ValueError, match="no feature look like a primary key"):
         gim.fix_schema(S.GraphSchema(node_sets={"m": S.NodeSchema({"y": F(S.FeatureFormat.INTEGER_64)})},
                                      edge_sets={}))
+
+
+def test_fix_schema_pound_id_fallback_and_tf_example():
+    """dgf/src/analyse/schema.py:168-265: the '#id' fallback key and the TF
+    Example format fix (int32 / bool -> int64, float64 -> float32)."""
+    from distributed_graph_flow_b200.data import schema as S
+    from distributed_graph_flow_b200.io import graph_in_memory as gim
+
+    F = S.FeatureSchema
+    s = S.GraphSchema(node_sets={"m": S.NodeSchema({"y": F(S.FeatureFormat.INTEGER_32),
+                                                   "b": F(S.FeatureFormat.BOOL)})},
+                      edge_sets={"e": S.EdgeSchema(source="m", target="m",
+                                                   features={"w": F(S.FeatureFormat.FLOAT_64),
+                                                             "z": F(S.FeatureFormat.BYTES)})})
+    gim.fix_schema(s, create_pound_id_as_fall_back=True, tf_example=True)
+    nf = s.node_sets["m"].features
+    assert nf["#id"].format == S.FeatureFormat.BYTES and nf["#id"].semantic == S.FeatureSemantic.PRIMARY_ID
+    assert nf["y"].format == S.FeatureFormat.INTEGER_64 and nf["b"].format == S.FeatureFormat.INTEGER_64
+    ef = s.edge_sets["e"].features
+    assert ef["w"].format == S.FeatureFormat.FLOAT_32 and ef["z"].format == S.FeatureFormat.BYTES
+    # Without tf_example the formats stay; a key-like feature wins over the fallback.
+    s2 = S.GraphSchema(node_sets={"m": S.NodeSchema({"#id": F(S.FeatureFormat.BYTES),
+                                                    "y": F(S.FeatureFormat.INTEGER_32)})}, edge_sets={})
+    gim.fix_schema(s2, create_pound_id_as_fall_back=True)
+    assert s2.node_sets["m"].features["y"].format == S.FeatureFormat.INTEGER_32
+    assert s2.node_sets["m"].features["#id"].semantic == S.FeatureSemantic.PRIMARY_ID

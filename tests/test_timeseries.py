@@ -134,13 +134,13 @@ def test_gpu_sampler_causal_slicing(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("max_len", [None, 0, 2, 1000])
+@pytest.mark.parametrize("max_len", [None, -1, 0, 2, 1000])
 def test_gpu_slicer_matches_oracle(cuda, max_len):
     from distributed_graph_flow_b200.sampling import temporal
     from distributed_graph_flow_b200.util import temporal as T
     from oracle import oracle as O
 
-    rng = np.random.default_rng(0 if max_len is None else max_len)
+    rng = np.random.default_rng(0 if max_len is None else abs(max_len))
     n = 300
     lens = rng.integers(0, 40, n)
     times = [np.sort(rng.integers(0, 100, k)) for k in lens]
@@ -159,3 +159,14 @@ def test_gpu_slicer_matches_oracle(cuda, max_len):
     for k in groups[0][1]:
         _assert_cols(got[k], exp[k], k)
         assert all(np.asarray(g).dtype == np.asarray(e).dtype for g, e in zip(got[k], exp[k])), k
+
+
+def test_float_timestamps_rejected():
+    """A fractional timestamp series is refused before any device work (an
+    int64 search would let t = 1.5 pass a cutoff of 1)."""
+    from distributed_graph_flow_b200.sampling import temporal
+    from distributed_graph_flow_b200.util import temporal as T
+
+    feats = {"t": _obj([np.array([0.5, 1.5]), np.array([2.0])]), "v": _obj([np.ones(2), np.ones(1)])}
+    with pytest.raises(ValueError, match="integer timestamps"):
+        temporal.TimeseriesSlicer(feats, [T.TimeseriesGroupSpec("t", ["t", "v"])])
