@@ -93,7 +93,9 @@ __global__ void spmm_count_kernel(const int64_t* __restrict__ rowptr, int64_t ro
   }
 }
 
-__global__ void spmm_fill_kernel(const int64_t* __restrict__ task_off, int64_t rows, int32_t* __restrict__ task_row) {
+__global__ void spmm_fill_kernel(const int64_t* __restrict__ task_off, int64_t rows, int32_t* __restrict__ task_row,
+                                 unsigned long long* __restrict__ next_task = nullptr) {
+  if (next_task != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *next_task = 0;
   for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < rows;
        r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     for (int64_t t = task_off[r]; t < task_off[r + 1]; ++t) task_row[t] = static_cast<int32_t>(r);
@@ -524,6 +526,127 @@ __global__ void __launch_bounds__(256, (VPL == 1 && sizeof(MT) == 2) ? 5 : 1) se
   }
 }
 
+// Sorted items (no permutation), heads dividing 32, at most one 16-byte slice
+// per lane (H x D <= 32 slices). A chunk's logits are rows lo..hi of [E, H],
+// contiguous, so the warp first reads them coalesced and reduces the chunk's
+// maximum per head (lane i holds head i % H); the weighted sum then needs no
+// running rescale: per row one exponential, one add and EPV FMAs. The next
+// four message rows are loaded while the current four are consumed, and the
+// first four are in flight during the maximum. Chunk states have the layout
+// of segment_softmax_kernel's, so the same fix-up merges split segments.
+template <class OT, int EPV>
+__device__ __forceinline__ void store_slice(OT* o, const float* acc, float scale);
+template <>
+__device__ __forceinline__ void store_slice<float, 4>(float* o, const float* a, float sc) {
+  *reinterpret_cast<float4*>(o) = make_float4(a[0] * sc, a[1] * sc, a[2] * sc, a[3] * sc);
+}
+template <>
+__device__ __forceinline__ void store_slice<float, 8>(float* o, const float* a, float sc) {
+  reinterpret_cast<float4*>(o)[0] = make_float4(a[0] * sc, a[1] * sc, a[2] * sc, a[3] * sc);
+  reinterpret_cast<float4*>(o)[1] = make_float4(a[4] * sc, a[5] * sc, a[6] * sc, a[7] * sc);
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ void store_slice<__nv_bfloat16, 4>(__nv_bfloat16* o, const float* a, float sc) {
+  *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(a[0] * sc, a[1] * sc), pack_bf16x2(a[2] * sc, a[3] * sc));
+}
+template <>
+__device__ __forceinline__ void store_slice<__nv_bfloat16, 8>(__nv_bfloat16* o, const float* a, float sc) {
+  *reinterpret_cast<uint4*>(o) = make_uint4(pack_bf16x2(a[0] * sc, a[1] * sc), pack_bf16x2(a[2] * sc, a[3] * sc),
+                                            pack_bf16x2(a[4] * sc, a[5] * sc), pack_bf16x2(a[6] * sc, a[7] * sc));
+}
+
+template <int U>
+__device__ __forceinline__ void load_rows(uint4 (&x)[U], float (&l)[U], const uint4* __restrict__ mp,
+                                          const float* __restrict__ lp, int j0, int n, int vpr, int heads,
+                                          bool active) {
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int j = j0 + u;
+    if (active && j < n) {
+      x[u] = __ldg(mp + j * vpr);
+      l[u] = __ldg(lp + j * heads);
+    } else {
+      x[u] = make_uint4(0, 0, 0, 0);
+      l[u] = -INFINITY;
+    }
+  }
+}
+
+template <class MT, class OT>
+__global__ void __launch_bounds__(256, 4) segment_softmax_sorted_kernel(
+    const int64_t* __restrict__ rowptr, const int64_t* __restrict__ task_off, const int64_t* __restrict__ split_off,
+    const int32_t* __restrict__ task_row, const int64_t* __restrict__ num_tasks, const float* __restrict__ logits,
+    int heads, const uint4* __restrict__ msg, int vpr, int head_dim, float* __restrict__ partial,
+    OT* __restrict__ out, unsigned long long* __restrict__ next_task) {
+  constexpr int EPV = 16 / sizeof(MT);
+  constexpr int kU = 4;
+  const int lane = threadIdx.x & 31;
+  const bool active = lane < vpr;
+  const int head = active ? (lane * EPV) / head_dim : 0;
+  const int64_t ntot = *num_tasks;
+  // Tasks are taken from a counter (a persistent grid; chunks hold 1 to
+  // kChunk rows, so a static split leaves warps idle), the next one fetched
+  // while the current one is processed.
+  unsigned long long claim = lane == 0 ? atomicAdd(next_task, 1ull) : 0ull;
+  for (int64_t t = static_cast<int64_t>(__shfl_sync(0xffffffffu, claim, 0)); t < ntot;
+       t = static_cast<int64_t>(__shfl_sync(0xffffffffu, claim, 0))) {
+    claim = lane == 0 ? atomicAdd(next_task, 1ull) : 0ull;
+    const int64_t r = task_row[t];
+    const int64_t c = t - task_off[r];
+    const int64_t ntask = task_off[r + 1] - task_off[r];
+    const int64_t lo = rowptr[r] + c * kChunk;
+    const int n = static_cast<int>(min(rowptr[r + 1], lo + kChunk) - lo);
+    const uint4* mp = msg + lo * vpr + lane;
+    const float* lp = logits + lo * heads + head;
+    uint4 x[kU];
+    float l[kU];
+    load_rows<kU>(x, l, mp, lp, 0, n, vpr, heads, active);
+    // The chunk's maximum per head.
+    const float* lc = logits + lo * heads;
+    const int nl = n * heads;
+    float m = -INFINITY;
+    for (int k = lane; k < nl; k += 32) m = fmaxf(m, __ldg(lc + k));
+    for (int off = heads; off < 32; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    m = __shfl_sync(0xffffffffu, m, head);
+    const float mb = m == -INFINITY ? 0.0f : m;  // a head whose logits are all -inf gets weight 0
+    float s = 0.0f, acc[EPV];
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) acc[k] = 0.0f;
+    for (int j0 = 0; j0 < n; j0 += kU) {
+      uint4 xn[kU];
+      float ln[kU];
+      load_rows<kU>(xn, ln, mp, lp, j0 + kU, n, vpr, heads, active);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const float p = __expf(l[u] - mb);
+        s += p;
+        float f[EPV];
+        unpack16<MT>(x[u], f);
+#pragma unroll
+        for (int k = 0; k < EPV; ++k) acc[k] = fmaf(p, f[k], acc[k]);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        x[u] = xn[u];
+        l[u] = ln[u];
+      }
+    }
+    if (active && ntask == 1) {
+      store_slice<OT, EPV>(out + (r * vpr + lane) * EPV, acc, 1.0f / (s + 1e-9f));
+    } else if (active) {
+      float* p = partial + ((split_off[r] + c) * vpr + lane) * (2 + EPV);
+      p[0] = m;
+      p[1] = s;
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) p[2 + k] = acc[k];
+    }
+  }
+}
+
 // Split segments: merge their chunk states in chunk order (deterministic).
 template <class MT, class OT, int VPL>
 __global__ void __launch_bounds__(256) segment_softmax_fixup_kernel(const int64_t* __restrict__ task_off,
@@ -803,6 +926,7 @@ size_t softmax_ws(int64_t n, int64_t nseg, bool sorted, int64_t vpr, int64_t epv
   a.take<int64_t>(static_cast<size_t>(nseg + 1));                   // split_off
   a.take<int32_t>(static_cast<size_t>(max_tasks(nseg, n)));         // task_row
   a.take<float>(static_cast<size_t>(max_split_tasks(n) * vpr * (2 + epv)));  // chunk states
+  a.take<unsigned long long>(1);                                              // task counter
   return a.used + std::max(scan_workspace_bytes(nseg + 1), sorted ? size_t(0) : radix_sort_workspace_bytes(n)) +
          2048;
 }
@@ -818,13 +942,14 @@ int launch_softmax(const int64_t* rowptr, const uint32_t* perm, int64_t nseg, in
   int64_t* split_off = arena.take<int64_t>(static_cast<size_t>(nseg + 1));
   int32_t* task_row = arena.take<int32_t>(static_cast<size_t>(max_tasks(nseg, n)));
   float* partial = arena.take<float>(static_cast<size_t>(max_split_tasks(n) * vpr * (2 + EPV)));
+  auto* next_task = arena.take<unsigned long long>(1);
   spmm_count_kernel<<<grid_for(nseg, 256), 256, 0, stream>>>(rowptr, nseg, cnt, split_cnt);
   DGFX_CUDA_TRY(cudaGetLastError());
   const size_t mark = arena.used;
   DGFX_TRY(exclusive_scan<int32_t>(cnt, task_off, nseg, true, arena, stream));
   arena.used = mark;
   DGFX_TRY(exclusive_scan<int32_t>(split_cnt, split_off, nseg, true, arena, stream));
-  spmm_fill_kernel<<<grid_for(nseg, 256), 256, 0, stream>>>(task_off, nseg, task_row);
+  spmm_fill_kernel<<<grid_for(nseg, 256), 256, 0, stream>>>(task_off, nseg, task_row, next_task);
   DGFX_CUDA_TRY(cudaGetLastError());
   // Grid sized for the largest possible plan; the kernel reads the exact task
   // count (task_off[nseg]) on the device.
@@ -840,7 +965,17 @@ int launch_softmax(const int64_t* rowptr, const uint32_t* perm, int64_t nseg, in
   DGFX_CUDA_TRY(cudaGetLastError());                                                                           \
   segment_softmax_fixup_kernel<MT, OT, V><<<grid_for(nseg * 32, 256), 256, 0, stream>>>(task_off, split_off,   \
                                                                                         nseg, vpr, partial, o);
-  if (vpl <= 1) {
+  if (perm == nullptr && vpr <= 32 && 32 % heads == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+    // Persistent: four 256-thread CTAs of 64 registers fill an SM.
+    const unsigned pblocks = std::min<unsigned>(blocks, static_cast<unsigned>(sm_count()) * 4);
+    segment_softmax_sorted_kernel<MT, OT><<<pblocks, 256, 0, stream>>>(rowptr, task_off, split_off, task_row,
+                                                                       task_off + nseg, logits, heads, m,
+                                                                       static_cast<int>(vpr), head_dim, partial, o,
+                                                                       next_task);
+    DGFX_CUDA_TRY(cudaGetLastError());
+    segment_softmax_fixup_kernel<MT, OT, 1><<<grid_for(nseg * 32, 256), 256, 0, stream>>>(task_off, split_off, nseg,
+                                                                                          vpr, partial, o);
+  } else if (vpl <= 1) {
     DGFX_SOFTMAX_LAUNCH(1)
   } else if (vpl == 2) {
     DGFX_SOFTMAX_LAUNCH(2)

@@ -159,6 +159,34 @@ def test_segment_softmax(cuda, dtype, sorted_ids, H, D):
     assert float(((got16.double() - ref).abs() / scale).max()) <= (1e-5 if dtype == "float32" else 1e-2)
 
 
+@pytest.mark.parametrize("sorted_ids", [False, True])
+@pytest.mark.parametrize("H,D", [(8, 32), (32, 8), (3, 8)])
+def test_segment_softmax_masked_logits(cuda, sorted_ids, H, D):
+    """Masked attention: about a third of the logits are -inf. Segment heads
+    with a finite logit match the reference sequence; a segment head whose
+    logits are all -inf (NaN in the reference's exp(-inf - -inf)) gives 0."""
+    from distributed_graph_flow_b200 import aggregation
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device="cuda").manual_seed(77 + H)
+    E, nseg = 40_000, 2_000
+    ids = (torch.rand(E, generator=g, device=dev) ** 3 * nseg).long()
+    if sorted_ids:
+        ids = torch.sort(ids).values
+    logits = torch.randn((E, H), generator=g, device=dev) * 3
+    logits[torch.rand((E, H), generator=g, device=dev) < 0.35] = -float("inf")
+    msgs = torch.randn((E, H, D), generator=g, device=dev).to(torch.bfloat16)
+    got = aggregation.segment_softmax(logits, msgs, ids, nseg, indices_are_sorted=sorted_ids, out_dtype=torch.float32)
+    ref = _softmax_reference(logits, msgs.float(), ids, nseg)
+    assert bool(torch.isfinite(got).all())
+    finite = torch.isfinite(ref).all(dim=-1)
+    assert int((~finite).sum()) > 0  # some segment heads are fully masked
+    assert torch.count_nonzero(got[~finite]) == 0
+    err = (got.double() - ref).abs()[finite]
+    scale = ref.abs().amax(dim=-1)[finite].clamp(min=1e-3)
+    assert float((err.amax(dim=-1) / scale).max()) <= 1e-5
+
+
 def test_segment_softmax_deterministic_and_empty(cuda):
     from distributed_graph_flow_b200 import aggregation
 
