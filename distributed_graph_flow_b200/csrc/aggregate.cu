@@ -94,8 +94,10 @@ __global__ void spmm_count_kernel(const int64_t* __restrict__ rowptr, int64_t ro
 }
 
 __global__ void spmm_fill_kernel(const int64_t* __restrict__ task_off, int64_t rows, int32_t* __restrict__ task_row,
-                                 unsigned long long* __restrict__ next_task = nullptr) {
-  if (next_task != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *next_task = 0;
+                                 unsigned long long* __restrict__ next_task = nullptr, int num_counters = 1) {
+  if (next_task != nullptr && blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < num_counters; i += blockDim.x) next_task[i] = 0;  // counters of the launches that follow
+  }
   for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < rows;
        r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     for (int64_t t = task_off[r]; t < task_off[r + 1]; ++t) task_row[t] = static_cast<int32_t>(r);
@@ -130,10 +132,9 @@ spmm_kernel(const int64_t* __restrict__ rowptr, const int32_t* __restrict__ col,
             const XT* __restrict__ X, YT* __restrict__ Y, int64_t feat, int64_t f0, int64_t fw,
             const int64_t* __restrict__ task_off, const int32_t* __restrict__ task_row,
             const int64_t* __restrict__ split_off, float* __restrict__ partial, int64_t rows, int normalize,
-            int64_t num_cols) {
+            int64_t num_cols, unsigned long long* __restrict__ next_task) {
   constexpr int V = Vec<XT>::n;
   const int lane = threadIdx.x & 31;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
   const int64_t ntasks = task_off[rows];
   const int nchunks = static_cast<int>(fw / V);
   auto fetch = [&](int64_t base, int64_t e, int32_t& c, float& w) {
@@ -146,7 +147,13 @@ spmm_kernel(const int64_t* __restrict__ rowptr, const int32_t* __restrict__ col,
       w = 0.f;
     }
   };
-  for (int64_t t = blockIdx.x * static_cast<int64_t>(kWarpsPerBlock) + (threadIdx.x >> 5); t < ntasks; t += warps) {
+  // Tasks (1 to kChunk nonzeros) are taken from a counter, the next index
+  // fetched while the current task runs: a static split of power-law rows
+  // over the persistent grid leaves warps idle.
+  unsigned long long claim = lane == 0 ? atomicAdd(next_task, 1ull) : 0ull;
+  for (int64_t t = static_cast<int64_t>(__shfl_sync(0xffffffffu, claim, 0)); t < ntasks;
+       t = static_cast<int64_t>(__shfl_sync(0xffffffffu, claim, 0))) {
+    claim = lane == 0 ? atomicAdd(next_task, 1ull) : 0ull;
     const int64_t r = task_row[t];
     const int64_t j = t - task_off[r];
     const int64_t rb = rowptr[r], re = rowptr[r + 1];
@@ -701,6 +708,7 @@ struct SpmmBufs {
   int64_t* split_off;
   int32_t* task_row;
   float* partial;
+  unsigned long long* next_task;  // one task counter per feature block
 };
 
 int64_t max_tasks(int64_t rows, int64_t nnz) { return rows + nnz / kChunk + 1; }
@@ -710,6 +718,8 @@ int64_t feat_block(int64_t feat, int dtype) {
   const int64_t cap = dtype == DGFX_BF16 ? 1024 : 512;
   return std::min(feat, cap);
 }
+// Launches per SpMM at most (the smallest feature block is 512 columns).
+int64_t spmm_feature_blocks(int64_t feat) { return ceil_div(std::max<int64_t>(feat, 1), int64_t(512)); }
 
 void carve_spmm(Arena& a, int64_t rows, int64_t nnz, int64_t feat, SpmmBufs* b) {
   b->cnt = a.take<int32_t>(static_cast<size_t>(rows));
@@ -718,6 +728,7 @@ void carve_spmm(Arena& a, int64_t rows, int64_t nnz, int64_t feat, SpmmBufs* b) 
   b->split_off = a.take<int64_t>(static_cast<size_t>(rows + 1));
   b->task_row = a.take<int32_t>(static_cast<size_t>(max_tasks(rows, nnz)));
   b->partial = a.take<float>(static_cast<size_t>(max_split_tasks(nnz) * std::min<int64_t>(feat, 1024)));
+  b->next_task = a.take<unsigned long long>(static_cast<size_t>(spmm_feature_blocks(feat)));
 }
 
 size_t spmm_ws(int64_t rows, int64_t nnz, int64_t feat) {
@@ -734,6 +745,7 @@ int launch_spmm(const int64_t* rowptr, const int32_t* col, const float* val, int
   const int64_t fb = feat_block(feat, xdtype);
   const unsigned grid = static_cast<unsigned>(sm_count() * 3);  // persistent: 3 resident CTAs per SM
   for (int64_t f0 = 0; f0 < feat; f0 += fb) {
+    unsigned long long* next_task = b.next_task + f0 / fb;
     const int64_t fw = std::min(fb, feat - f0);
     const int64_t chunks = fw / V;
     const XT* X = static_cast<const XT*>(x);
@@ -741,15 +753,15 @@ int launch_spmm(const int64_t* rowptr, const int32_t* col, const float* val, int
     if (chunks <= 32) {
       spmm_kernel<XT, YT, 1, 8><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
                                                                            b.task_off, b.task_row, b.split_off,
-                                                                           b.partial, rows, normalize, num_cols);
+                                                                           b.partial, rows, normalize, num_cols, next_task);
     } else if (chunks <= 64) {
       spmm_kernel<XT, YT, 2, 4><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
                                                                            b.task_off, b.task_row, b.split_off,
-                                                                           b.partial, rows, normalize, num_cols);
+                                                                           b.partial, rows, normalize, num_cols, next_task);
     } else {
       spmm_kernel<XT, YT, 4, 2><<<grid, kWarpsPerBlock * 32, 0, stream>>>(rowptr, col, val, X, Y, feat, f0, fw,
                                                                            b.task_off, b.task_row, b.split_off,
-                                                                           b.partial, rows, normalize, num_cols);
+                                                                           b.partial, rows, normalize, num_cols, next_task);
     }
     DGFX_CUDA_TRY(cudaGetLastError());
     spmm_fixup_kernel<YT><<<grid_for(rows * 32, 256), 256, 0, stream>>>(rowptr, b.split_off, b.partial, Y, rows,
@@ -825,7 +837,8 @@ int spmm_impl(const int64_t* rowptr, const int32_t* col, const float* val, int64
   DGFX_TRY(exclusive_scan<int32_t>(b.cnt, b.task_off, rows, true, arena, stream));
   arena.used = mark;
   DGFX_TRY(exclusive_scan<int32_t>(b.split_cnt, b.split_off, rows, true, arena, stream));
-  spmm_fill_kernel<<<grid_for(rows, 256), 256, 0, stream>>>(b.task_off, rows, b.task_row);
+  spmm_fill_kernel<<<grid_for(rows, 256), 256, 0, stream>>>(b.task_off, rows, b.task_row, b.next_task,
+                                                            static_cast<int>(spmm_feature_blocks(feat)));
   DGFX_CUDA_TRY(cudaGetLastError());
   if (xt == DGFX_F32 && yt == DGFX_F32) return launch_spmm<float, float>(rowptr, col, val, rows, num_cols, x, y, feat, normalize, b, stream, xt);
   if (xt == DGFX_F32 && yt == DGFX_BF16) return launch_spmm<float, __nv_bfloat16>(rowptr, col, val, rows, num_cols, x, y, feat, normalize, b, stream, xt);
