@@ -193,6 +193,112 @@ __global__ void id_index_lookup_kernel(KeysDev keys, const unsigned long long* t
   }
 }
 
+// Fixed-width rows of NW 32-bit words on both sides, the same width: two ids
+// are equal exactly when their rows are (both zero padded), so the row stays
+// in registers, its length and hash are computed unrolled (the same values as
+// id_span / hash_span), and a tag match compares the key row word by word.
+constexpr int kMaxRowWords = 8;
+
+template <int NW>
+__device__ __forceinline__ void load_row(const uint32_t* __restrict__ base, int64_t i, uint32_t (&w)[NW]) {
+  const uint32_t* r = base + i * NW;
+#pragma unroll
+  for (int j = 0; j < NW; ++j) w[j] = __ldg(r + j);
+}
+
+template <int NW>
+__device__ __forceinline__ uint64_t hash_row(const uint32_t (&w)[NW]) {
+  int len = 0;  // bytes up to the highest non-zero one (little-endian words)
+#pragma unroll
+  for (int j = 0; j < NW; ++j) {
+    if (w[j] != 0) len = 4 * j + (39 - __clz(w[j])) / 8;
+  }
+  uint64_t h = 0x9E3779B97F4A7C15ull ^ static_cast<uint64_t>(len);
+  const int nw = (len + 3) / 4;
+#pragma unroll
+  for (int j = 0; j < NW; ++j) {
+    if (j < nw) {
+      h = (h ^ w[j]) * 0x9E3779B97F4A7C15ull;
+      h ^= h >> 29;
+    }
+  }
+  return mix64(h);
+}
+
+template <int NW>
+__device__ __forceinline__ bool row_equals(const uint32_t* __restrict__ keys, uint32_t idx, const uint32_t (&w)[NW]) {
+  const uint32_t* k = keys + static_cast<int64_t>(idx) * NW;
+  bool eq = true;
+#pragma unroll
+  for (int j = 0; j < NW; ++j) eq &= __ldg(k + j) == w[j];
+  return eq;
+}
+
+template <int NW>
+__global__ void id_index_build_rows_kernel(const uint32_t* __restrict__ keys, int64_t n, unsigned long long* table,
+                                           uint64_t mask, unsigned long long* full) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    uint32_t w[NW];
+    load_row<NW>(keys, i, w);
+    const uint64_t h = hash_row<NW>(w);
+    const unsigned long long word = (static_cast<unsigned long long>(h >> 32) << 32) | static_cast<uint32_t>(i);
+    uint64_t s = h & mask;
+    bool placed = false;
+    for (uint64_t probe = 0; probe <= mask; ++probe) {
+      unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(&table[s]);
+      if (e == kEmptyWord) {
+        const unsigned long long prev = atomicCAS(&table[s], kEmptyWord, word);
+        if (prev == kEmptyWord) {
+          placed = true;
+          break;
+        }
+        e = prev;
+      }
+      if ((e >> 32) == (word >> 32) && row_equals<NW>(keys, static_cast<uint32_t>(e), w)) {
+        atomicMax(&table[s], word);  // equal ids: the later position wins
+        placed = true;
+        break;
+      }
+      s = (s + 1) & mask;
+    }
+    if (!placed) atomicAdd(full, 1ull);
+  }
+}
+
+template <int NW>
+__global__ void id_index_lookup_rows_kernel(const uint32_t* __restrict__ keys, const unsigned long long* table,
+                                            uint64_t mask, const uint32_t* __restrict__ q, int64_t n, int64_t* out,
+                                            unsigned long long* mismatch) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    uint32_t w[NW];
+    load_row<NW>(q, i, w);
+    const uint64_t h = hash_row<NW>(w);
+    const uint32_t tag = static_cast<uint32_t>(h >> 32);
+    uint64_t s = h & mask;
+    int64_t found = -1;
+    for (uint64_t probe = 0; probe <= mask; ++probe) {
+      const unsigned long long e = table[s];
+      if (e == kEmptyWord) break;
+      if (static_cast<uint32_t>(e >> 32) == tag && row_equals<NW>(keys, static_cast<uint32_t>(e), w)) {
+        found = static_cast<uint32_t>(e);
+        break;
+      }
+      s = (s + 1) & mask;
+    }
+    out[i] = found;
+    if (found < 0) atomicMax(mismatch, static_cast<unsigned long long>(i + 1));
+  }
+}
+
+// Row words of a fixed-width layout read word by word, 0 otherwise.
+int row_words(const KeysDev& k) {
+  if (k.kind != DGFX_IDS_FIXED || !k.words) return 0;
+  const int64_t nw = k.width / 4;
+  return nw >= 1 && nw <= kMaxRowWords ? static_cast<int>(nw) : 0;
+}
+
+#define DGFX_ROW_WORDS_CASES(X) X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8)
+
 __global__ void pair_keep_kernel(const int64_t* src, const int64_t* dst, int64_t n, int32_t* keep) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
     keep[i] = (src[i] >= 0 && dst[i] >= 0) ? 1 : 0;
@@ -299,8 +405,19 @@ extern "C" int dgfx_id_index_create(int32_t kind, const void* d_ids, const int64
   DGFX_CUDA_TRY(cudaMemsetAsync(ix->table, 0xFF, cap * sizeof(unsigned long long), stream));
   DGFX_CUDA_TRY(cudaMemsetAsync(ix->table + cap, 0, 2 * sizeof(unsigned long long), stream));
   if (num_ids > 0) {
-    id_index_build_kernel<<<grid_for(num_ids), kThreads, 0, stream>>>(ix->keys, num_ids, ix->table, ix->mask,
-                                                                      ix->table + cap);
+    const auto* rows = reinterpret_cast<const uint32_t*>(ix->keys.bytes);
+    switch (row_words(ix->keys)) {
+#define DGFX_BUILD_ROWS(NW)                                                                                   \
+  case NW:                                                                                                    \
+    id_index_build_rows_kernel<NW><<<grid_for(num_ids), kThreads, 0, stream>>>(rows, num_ids, ix->table,      \
+                                                                                ix->mask, ix->table + cap); \
+    break;
+      DGFX_ROW_WORDS_CASES(DGFX_BUILD_ROWS)
+#undef DGFX_BUILD_ROWS
+      default:
+        id_index_build_kernel<<<grid_for(num_ids), kThreads, 0, stream>>>(ix->keys, num_ids, ix->table, ix->mask,
+                                                                          ix->table + cap);
+    }
     DGFX_CUDA_TRY(cudaGetLastError());
   }
   unsigned long long full = 0;
@@ -336,8 +453,21 @@ extern "C" int dgfx_id_index_lookup(const dgfx_id_index* ix, int32_t kind, const
   unsigned long long* mm = ix->table + ix->mask + 2;
   DGFX_CUDA_TRY(cudaMemsetAsync(mm, 0, sizeof(unsigned long long), stream));
   if (num_ids > 0) {
-    id_index_lookup_kernel<<<grid_for(num_ids), kThreads, 0, stream>>>(ix->keys, ix->table, ix->mask, q, num_ids,
-                                                                       d_out, mm);
+    const int nw = row_words(q) == row_words(ix->keys) && q.width == ix->keys.width ? row_words(q) : 0;
+    const auto* krows = reinterpret_cast<const uint32_t*>(ix->keys.bytes);
+    const auto* qrows = reinterpret_cast<const uint32_t*>(q.bytes);
+    switch (nw) {
+#define DGFX_LOOKUP_ROWS(NW)                                                                                       \
+  case NW:                                                                                                         \
+    id_index_lookup_rows_kernel<NW><<<grid_for(num_ids), kThreads, 0, stream>>>(krows, ix->table, ix->mask, qrows, \
+                                                                                 num_ids, d_out, mm);              \
+    break;
+      DGFX_ROW_WORDS_CASES(DGFX_LOOKUP_ROWS)
+#undef DGFX_LOOKUP_ROWS
+      default:
+        id_index_lookup_kernel<<<grid_for(num_ids), kThreads, 0, stream>>>(ix->keys, ix->table, ix->mask, q, num_ids,
+                                                                           d_out, mm);
+    }
     DGFX_CUDA_TRY(cudaGetLastError());
   }
   if (mismatch != nullptr) {

@@ -209,6 +209,19 @@ def test_gpu_id_index_matches_oracle(cuda, seed):
     got, m = ids.IdIndex(index_b).lookup(qb)
     np.testing.assert_array_equal(got.cpu().numpy(), exp)
     assert m == me
+    # The same width on both sides (row-compare build and lookup kernels, 1, 3
+    # and 5 words per id), with explicit repeats: the last position wins.
+    index_r = index_b.copy()
+    index_r[rng.integers(0, len(index_r), 2000)] = index_r[rng.integers(0, len(index_r), 2000)]
+    for width in ("S12", "S20", "S4"):
+        ix = index_r.astype(width)  # S4 truncates the ids: more repeats
+        qq = np.concatenate([ix[rng.integers(0, len(ix), 30_000)],
+                             np.array([b"nope%d" % i for i in range(300)], dtype=width)])
+        rng.shuffle(qq)
+        exp, me = O.id_map(ix, qq)
+        got, m = ids.IdIndex(ix).lookup(qq)
+        np.testing.assert_array_equal(got.cpu().numpy(), exp, err_msg=width)
+        assert m == me, width
     # Arrow binary columns (variable length, two chunks, sliced) on both sides.
     arrow_index = pa.chunked_array([pa.array([bytes(x) for x in index_b[:20_000]]),
                                     pa.array([bytes(x) for x in index_b[20_000:]])])
