@@ -815,8 +815,8 @@ def bench_temporal(dev, steps, scale=1.0, streams=8):
                    f"CUDA-graph replay, time per batch)",
            "eager": {"value": round(B / (ms_eager / 1e3), 1), "ms_per_batch": round(ms_eager, 4)},
            "one_batch_per_replay": {"value": round(B / (ms_single / 1e3), 1), "ms_per_batch": round(ms_single, 4),
-                                    "note": "one graph replay per batch issued from Python: bound by the host's "
-                                            "per-replay cost, not the device"},
+                                    "note": "one graph replay per batch issued from Python (one native call: "
+                                            "input copies + graph launch on the caller's stream)"},
            f"{streams}_batches_per_replay": {"value": round(B / (ms_multi / 1e3), 1),
                                              "ms_per_batch": round(ms_multi, 4),
                                              "mode": f"{streams} independent batches forked onto {streams} streams "

@@ -180,55 +180,80 @@ __device__ __forceinline__ uint4 chunk_pack<__nv_bfloat16>(const float* acc, flo
   return r;
 }
 
+// One warp per sample: the sample's (src, dst) edges, sorted by src, are read
+// 32 at a time into lanes and walked in order with shuffle broadcasts; lane
+// ch sums 16-byte chunk ch of the destination rows (four rows loaded ahead),
+// and a node's mean is written when its run of edges ends, zero rows for the
+// nodes without edges in between. No per-node searches: a node's work is
+// its own edges' row loads.
+template <class T>
+__device__ __forceinline__ void batch_mean_flush(uint4* __restrict__ out, int64_t nb, int64_t node_cap, int64_t chunks,
+                                                 int64_t ch, bool on, int64_t cur, int64_t cnt, const float* acc,
+                                                 int64_t* next) {
+  if (cur >= 0) {  // the mean of node cur's run of edges
+    if (on && nb + cur < node_cap) {
+      out[(nb + cur) * chunks + ch] = chunk_pack<T>(acc, 1.0f / static_cast<float>(cnt > 1 ? cnt : 1));
+    }
+    *next = cur + 1;
+  }
+}
+
 template <class T>
 __global__ void batch_mean_kernel(const int64_t* __restrict__ node_off, const int64_t* __restrict__ edge_off,
                                   const int64_t* __restrict__ edge_src, const int64_t* __restrict__ edge_dst,
                                   int64_t B, int64_t node_cap, const uint4* __restrict__ feats, int64_t chunks,
                                   uint4* __restrict__ out) {
   constexpr int V = 16 / sizeof(T);
+  constexpr int kAhead = 4;
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  const int64_t total = node_off[B];
-  for (int64_t v = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; v < total && v < node_cap;
-       v += warps) {
-    int64_t lo = 0, hi = B;  // sample i: node_off[i] <= v < node_off[i + 1]
-    while (hi - lo > 1) {
-      const int64_t mid = (lo + hi) >> 1;
-      if (node_off[mid] <= v) lo = mid;
-      else hi = mid;
-    }
-    const int64_t nb = node_off[lo], l = v - nb;
-    const int64_t eb = edge_off[lo], ne = edge_off[lo + 1] - eb;
-    int64_t a = 0, b = ne;  // first edge with source >= l
-    while (a < b) {
-      const int64_t mid = (a + b) >> 1;
-      if (edge_src[eb + mid] < l) a = mid + 1;
-      else b = mid;
-    }
-    int64_t c = a, d = ne;  // first edge with source > l
-    while (c < d) {
-      const int64_t mid = (c + d) >> 1;
-      if (edge_src[eb + mid] <= l) c = mid + 1;
-      else d = mid;
-    }
-    const int64_t cnt = c - a;
-    const float scale = 1.0f / static_cast<float>(cnt > 1 ? cnt : 1);
-    for (int64_t ch = lane; ch < chunks; ch += 32) {
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; i < B; i += warps) {
+    const int64_t nb = node_off[i], nn = node_off[i + 1] - nb;
+    const int64_t eb = edge_off[i], ne = edge_off[i + 1] - eb;
+    for (int64_t c0 = 0; c0 < chunks; c0 += 32) {
+      const int64_t ch = c0 + lane;
+      const bool on = ch < chunks;
+      int64_t cur = -1, cnt = 0, next = 0;
       float acc[V];
 #pragma unroll
       for (int q = 0; q < V; ++q) acc[q] = 0.0f;
-      for (int64_t k = a; k < c; k += 4) {
-        uint4 r[4];
+      for (int64_t k0 = 0; k0 < ne; k0 += 32) {
+        const int m = static_cast<int>(ne - k0 < 32 ? ne - k0 : 32);
+        const int64_t my_s = lane < m ? edge_src[eb + k0 + lane] : 0;
+        const int64_t my_d = lane < m ? edge_dst[eb + k0 + lane] : 0;
+        for (int j0 = 0; j0 < m; j0 += kAhead) {
+          int64_t src[kAhead];
+          uint4 r[kAhead];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (k + u < c) r[u] = __ldg(feats + (nb + edge_dst[eb + k + u]) * chunks + ch);
-        }
+          for (int u = 0; u < kAhead; ++u) {
+            const int j = (j0 + u) & 31;
+            src[u] = __shfl_sync(0xffffffffu, my_s, j);
+            const int64_t d = __shfl_sync(0xffffffffu, my_d, j);
+            r[u] = (on && j0 + u < m) ? __ldg(feats + (nb + d) * chunks + ch) : make_uint4(0, 0, 0, 0);
+          }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (k + u < c) chunk_add<T>(r[u], acc);
+          for (int u = 0; u < kAhead; ++u) {
+            if (j0 + u >= m) break;  // uniform over the warp
+            if (src[u] != cur) {
+              batch_mean_flush<T>(out, nb, node_cap, chunks, ch, on, cur, cnt, acc, &next);
+              for (int64_t z = next; z < src[u]; ++z) {  // nodes without edges before this run
+                if (on && nb + z < node_cap) out[(nb + z) * chunks + ch] = make_uint4(0, 0, 0, 0);
+              }
+              next = src[u];
+              cur = src[u];
+              cnt = 0;
+#pragma unroll
+              for (int q = 0; q < V; ++q) acc[q] = 0.0f;
+            }
+            chunk_add<T>(r[u], acc);
+            ++cnt;
+          }
         }
       }
-      out[v * chunks + ch] = chunk_pack<T>(acc, scale);
+      batch_mean_flush<T>(out, nb, node_cap, chunks, ch, on, cur, cnt, acc, &next);
+      for (int64_t z = next; z < nn; ++z) {  // trailing nodes without edges
+        if (on && nb + z < node_cap) out[(nb + z) * chunks + ch] = make_uint4(0, 0, 0, 0);
+      }
     }
   }
 }
@@ -255,6 +280,19 @@ extern "C" int dgfx_publish_totals(const int64_t* d_node_total, const int64_t* d
   return DGFX_OK;
 }
 
+extern "C" int dgfx_graph_launch_with_inputs(void* graph_exec, void* dst0, const void* src0, size_t bytes0,
+                                             void* dst1, const void* src1, size_t bytes1, dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (graph_exec == nullptr || (bytes0 > 0 && (dst0 == nullptr || src0 == nullptr)) ||
+      (bytes1 > 0 && (dst1 == nullptr || src1 == nullptr))) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_graph_launch_with_inputs: bad arguments");
+  }
+  if (bytes0 > 0) DGFX_CUDA_TRY(cudaMemcpyAsync(dst0, src0, bytes0, cudaMemcpyDefault, stream));
+  if (bytes1 > 0) DGFX_CUDA_TRY(cudaMemcpyAsync(dst1, src1, bytes1, cudaMemcpyDefault, stream));
+  DGFX_CUDA_TRY(cudaGraphLaunch(reinterpret_cast<cudaGraphExec_t>(graph_exec), stream));
+  return DGFX_OK;
+}
+
 extern "C" int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
                                const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity,
                                const void* d_feats, int dtype, int64_t feat, void* d_out, dgfx_stream stream_) {
@@ -270,7 +308,7 @@ extern "C" int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_e
   }
   if (num_seeds == 0 || node_capacity == 0) return DGFX_OK;
   const int64_t chunks = row_bytes / 16;
-  const unsigned g = grid_for_items(node_capacity * 32, 256);
+  const unsigned g = grid_for_items(num_seeds * 32, 256);  // one warp per sample
   if (dtype == DGFX_F32) {
     batch_mean_kernel<float><<<g, 256, 0, stream>>>(d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst, num_seeds,
                                                     node_capacity, static_cast<const uint4*>(d_feats), chunks,

@@ -601,26 +601,44 @@ class CapturedSampleStep:
                 for k in range(1, K):  # join
                     self.stream.wait_stream(self.branches[k])
         torch.cuda.synchronize(dev)
-
-    def run(self, seeds, seed_ts=None):
-        """Samples ``seeds`` after the caller's current stream."""
-        torch = _torch()
-        self.stream.wait_stream(torch.cuda.current_stream(self.seeds.device))
-        with torch.cuda.stream(self.stream):
-            self.seeds.copy_(seeds.view(self.seeds.shape), non_blocking=True)
-            if self.seed_ts is not None:
-                self.seed_ts.copy_(seed_ts.view(self.seed_ts.shape), non_blocking=True)
-            self.graph.replay()
+        # One foreign call per run: input copies + launch of the graph exec.
+        self._exec = int(self.graph.raw_cuda_graph_exec())
+        self._launch = _native.lib().dgfx_graph_launch_with_inputs
+        self._seed_bytes = self.seeds.numel() * 8
+        self._ts_ptr = None if self.seed_ts is None else int(self.seed_ts.data_ptr())
+        self._seeds_ptr = int(self.seeds.data_ptr())
         if self.aggregates[0] is not None:
             out = list(zip(self.batches, self.features, self.aggregates))
         else:
             out = list(zip(self.batches, self.features))
-        return out[0] if self.single else out
+        self._out = out[0] if self.single else out
+
+    def _input_ptr(self, t, name):
+        torch = _torch()
+        if t.dtype != torch.int64 or t.numel() != self.seeds.numel() or not t.is_contiguous():
+            raise ValueError(f"CapturedSampleStep.run: {name} must be a contiguous int64 tensor of "
+                             f"{self.seeds.numel()} elements")
+        return t.data_ptr()
+
+    def run(self, seeds, seed_ts=None):
+        """Samples ``seeds`` in the caller's current stream order: one native
+        call copies the inputs into the static buffers and launches the
+        captured graph on that stream. The inputs must stay alive until the
+        copies have run (stream order of their own allocation suffices), and
+        consecutive runs must come from one stream, since each run rewrites
+        the static inputs and outputs."""
+        src_ts, ts_bytes = None, 0
+        if self.seed_ts is not None:
+            if seed_ts is None:
+                raise ValueError("CapturedSampleStep.run: seed_ts is required (captured with timestamps)")
+            src_ts, ts_bytes = self._input_ptr(seed_ts, "seed_ts"), self._seed_bytes
+        _native.check(self._launch(self._exec, self._seeds_ptr, self._input_ptr(seeds, "seeds"), self._seed_bytes,
+                                   self._ts_ptr, src_ts, ts_bytes, _native.stream_handle()))
+        return self._out
 
     def wait(self):
-        """Makes the caller's current stream wait for the last run."""
-        torch = _torch()
-        torch.cuda.current_stream(self.seeds.device).wait_stream(self.stream)
+        """Kept for callers of the earlier two-stream form: run() now works in
+        the caller's stream order, so there is nothing to join."""
 
     @property
     def sampler(self):

@@ -674,6 +674,16 @@ int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets
 int dgfx_publish_totals(const int64_t* d_node_total, const int64_t* d_edge_total,
                         int64_t* out2, dgfx_stream stream);
 
+/* Copies up to two inputs into a captured CUDA graph's static buffers
+ * (cudaMemcpyAsync, any direction under unified addressing; a zero size
+ * skips a copy) and launches the graph exec, all in `stream` order: one call
+ * per replay of a captured sampling step, so a caller issuing one batch per
+ * replay pays one foreign call instead of a stream join, two tensor copies
+ * and a replay. graph_exec is a cudaGraphExec_t. No reference counterpart
+ * (the reference samples on the host). */
+int dgfx_graph_launch_with_inputs(void* graph_exec, void* dst0, const void* src0, size_t bytes0, void* dst1,
+                                  const void* src1, size_t bytes1, dgfx_stream stream);
+
 /* ------------------------------------------------------------------------
  * Seeded synthetic inputs (stand-ins for the benchmark datasets, the role of
  * the reference's dgf/src/util/gen_test_graph.py generators at scale).

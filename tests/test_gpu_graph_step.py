@@ -59,6 +59,14 @@ def test_captured_step_matches_eager(cuda):
         np.testing.assert_array_equal(g_edges, e_edges)
         n = int(g_off[-1])
         assert torch.equal(rows[:n], table[batch.node_ids[:n]])
+    # Host inputs go through the same copies; bad inputs are refused.
+    batch, _ = step.run(seeds.cpu(), sts.cpu())
+    torch.cuda.current_stream().synchronize()
+    np.testing.assert_array_equal(ext.batch_to_host(batch)[0], ext.batch_to_host(eager.sample_merged(seeds, sts))[0])
+    with pytest.raises(ValueError, match="contiguous int64"):
+        step.run(seeds.to(torch.int32), sts)
+    with pytest.raises(ValueError, match="seed_ts is required"):
+        step.run(seeds)
     graph_s.check()
 
 

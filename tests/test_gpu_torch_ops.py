@@ -164,3 +164,10 @@ def test_batch_mean_aggregate(cuda):
     agg2 = aggregation.csr_spmm(rp, cl, feats, normalize=True)
     _close(agg2[:n].cpu().numpy(), exp, mag, 1e-5)
     assert torch.count_nonzero(agg2[n:]) == 0
+    # Rows of several 32-chunk groups (200 fp32 = 50 chunks) and bf16 rows.
+    for dim, dt, tol in ((200, torch.float32, 1e-5), (256, torch.bfloat16, 1e-2)):
+        tab = synth.normal_features(0, spec.num_nodes, dim, 10, dt, dev)
+        got = aggregation.batch_mean_aggregate(batch, aggregation.gather_rows(tab, batch.node_ids))
+        th = tab.float().cpu().numpy().astype(np.float64)[nodes]
+        _close(got[:n].float().cpu().numpy(), O.batch_mean_aggregate(off, eoff, edges, th),
+               O.batch_mean_aggregate(off, eoff, edges, np.abs(th)), tol)
