@@ -1234,49 +1234,81 @@ def bench_hetero(dev, steps, scale=1.0):
 
     # Pipelined as the headline step: two samplers over the same index and
     # seed alternate, each call split (warp kernel on the main stream; the
-    # large-tree and padded kernels, scans and compaction on a tail stream),
-    # and the A-feature gather on a high-priority stream, so call i's tail
-    # and gather overlap call i + 1's first kernel. Same batches as serial.
+    # large-tree and padded kernels, scans and compaction on the sampler's
+    # tail stream), and the A-feature gather on a high-priority stream, so
+    # call i's tail and gather overlap call i + 1's. S such steps are captured
+    # in one CUDA graph (random streams from the samplers' device counters),
+    # so the host issues one replay per S steps, as for the headline.
     cc_alt = ext.create_device_sampler(plan, g.nodeset_names, g.num_nodes, g.edgeset_names, g.fwd, g.bwd,
                                        _native.MODE_RANDOM, seed=3, has_temporal=True)
     main = torch.cuda.current_stream(dev)
     gstream = torch.cuda.Stream(device=dev, priority=-1)
-    tstream = torch.cuda.Stream(device=dev)
+    # One tail stream per sampler: the tail (large-tree and padded kernels,
+    # scans, compaction: ~250 us) is this step's critical path, and with a
+    # shared tail stream consecutive tails would serialise.
+    tstreams = [torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)]
     feats2 = [feats, torch.empty_like(feats)]
+    S = max(d for d in range(1, min(steps, 10) + 1) if steps % d == 0)
+    seeds_st = torch.zeros((S, B), dtype=torch.int64, device=dev)
+    sts_st = torch.zeros((S, B), dtype=torch.int64, device=dev)
 
-    def step_pipe(i):
-        c = cc if i % 2 == 0 else cc_alt
-        mm = c.sample_merged(seeds[i], sts[i], None, call_index=i, check=False, tail_stream=tstream)
-        gstream.wait_stream(tstream)
+    def step_pipe(k):
+        c = cc if k % 2 == 0 else cc_alt
+        mm = c.sample_merged(seeds_st[k], sts_st[k], None, call_index=_native.CALL_INDEX_DEVICE, check=False,
+                             tail_stream=tstreams[k % 2])
+        gstream.wait_stream(tstreams[k % 2])
         with torch.cuda.stream(gstream):
             off = mm.node_offsets
             _native.check(_native.lib().dgfx_gather_rows_ranged(
                 _native.ptr(table), n_a, FEAT_DIM * 4, _native.ptr(mm.node_ids), _native.elem_ptr(off, a * B),
-                _native.elem_ptr(off, (a + 1) * B), int(mm.node_ids.numel()), _native.ptr(feats2[i % 2]),
+                _native.elem_ptr(off, (a + 1) * B), int(mm.node_ids.numel()), _native.ptr(feats2[k % 2]),
                 _native.stream_handle()))
-        for t in (mm.node_ids, mm.node_offsets):
-            t.record_stream(gstream)
+        if not torch.cuda.is_current_stream_capturing():
+            for t in (mm.node_ids, mm.node_offsets):
+                t.record_stream(gstream)
+        return mm
 
     def drain():
-        main.wait_stream(tstream)
-        main.wait_stream(gstream)
+        cur = torch.cuda.current_stream(dev)
+        for t in tstreams:
+            cur.wait_stream(t)
+        cur.wait_stream(gstream)
 
-    for i in range(5):
-        step_pipe(i)
+    seeds_st.copy_(seeds[:S])
+    sts_st.copy_(sts[:S])
+    for k in range(S):  # eager pass: streams, workspaces and size caches exist before capture
+        step_pipe(k)
     drain()
     cc.check()
     cc_alt.check()
-    timed(lambda i: step_pipe(8 + i), steps, torch.cuda.synchronize, "hetero_pipelined", finish=drain)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(device=dev)
+    cs.wait_stream(main)
+    with torch.cuda.graph(graph, stream=cs):
+        held = [step_pipe(k) for k in range(S)]  # outputs stay allocated for the replays
+        drain()
+    torch.cuda.synchronize(dev)
+
+    def replay(r):
+        seeds_st.copy_(seeds[8 + r * S:8 + (r + 1) * S], non_blocking=True)
+        sts_st.copy_(sts[8 + r * S:8 + (r + 1) * S], non_blocking=True)
+        graph.replay()
+
+    for _ in range(3):
+        replay(0)
+    R = steps // S
+    timed(replay, R, torch.cuda.synchronize, "hetero_pipelined")
     cc.check()
     cc_alt.check()
-    ms = TIMING["hetero_pipelined"]["mean_ms"]  # whole timed region / K
-    del cc_alt, feats2
+    ms = TIMING["hetero_pipelined"]["mean_ms"] / S  # whole timed region / K
+    del graph, held, cc_alt, feats2
     out = {"workload": "heterogeneous temporal: A 736,389 / B 1,134,649 / C 8,740 / D 59,965 nodes; edges B->A "
                        "7,145,660, A->A 5,416,271, A->D 7,505,078, B->C 1,043,998 (Zipf 2.1); edge ts = "
                        "propagated A creation years; both directions, fanout [15,10]; 4096 A seeds, cutoff = seed "
                        "year; fp32 128-d A features",
            "value": round(B / (ms / 1e3), 1), "unit": "subgraphs/s", "ms_per_step": round(ms, 4),
-           "step_time": "pipelined steps: whole timed region / K",
+           "step_time": "pipelined steps, up to 10 per CUDA-graph replay: whole timed region / K",
            "serial": {"value": round(B / (ms_serial / 1e3), 1), "ms_per_step": round(ms_serial, 4),
                       "note": "one stream, median per-step interval"},
            "nodes_per_step": nodes, "tree_positions": cc.tree_size, "graph_build_s": round(t_build, 2)}
