@@ -299,9 +299,12 @@ int dgfx_segment_sum(const void* d_data, int data_dtype,
  * size <= 2 KB); d_ids int64 [n] (ids outside [0, nseg) are dropped;
  * sorted != 0 promises ascending ids); d_out [nseg, heads, head_dim]
  * (out_dtype), zero rows for empty segments. Segments are split into
- * chunks of 256 items (one warp each, online softmax); chunk states merge in
- * chunk order, so results are deterministic. Segments whose logits are all
- * -inf give zero rows.
+ * chunks of 256 items (one warp each); chunk states merge in chunk order, so
+ * results are deterministic. With sorted ids, heads dividing 32 and rows of
+ * at most 32 16-byte slices, a chunk's per-head maximum is taken from its
+ * contiguous logits first and warps of a persistent grid take chunks from a
+ * counter; otherwise a running (online) softmax over the chunk. Segments
+ * whose logits are all -inf give zero rows.
  * ------------------------------------------------------------------------ */
 int dgfx_segment_softmax_workspace_size(int64_t num_items, int64_t num_segments,
                                         int32_t heads, int64_t head_dim,
