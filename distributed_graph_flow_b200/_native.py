@@ -143,7 +143,6 @@ SIGNATURES = {
     "dgfx_gather_rows_scaled": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "dgfx_batch_csr": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp]),
     "dgfx_batch_mean": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _int, _i64, _vp, _vp]),
-    "dgfx_batch_gather_mean": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _int, _i64, _vp, _vp, _vp]),
     "dgfx_publish_totals": (_int, [_vp, _vp, _vp, _vp]),
     "dgfx_graph_launch_with_inputs": (_int, [_vp, _vp, _vp, _sz, _vp, _vp, _sz, _vp]),
     "dgfx_sampler_kernel_info": (_int, [_vp, _p_i32, _p_i32]),

@@ -320,22 +320,3 @@ def batch_mean_aggregate(batch, features, out=None, stream=None):
         _native.ptr(batch.edge_dst), int(batch.B), cap, _native.ptr(features), _dtype_code(features.dtype), F,
         _native.ptr(out), _native.stream_handle(stream)))
     return out
-
-
-def batch_gather_mean(batch, table, rows_out, out, stream=None):
-    """The feature gather of a merged batch and its mean aggregation in one
-    kernel (dgfx_batch_gather_mean): rows_out[v] = table[batch.node_ids[v]]
-    (zero rows for ids outside the table) and out as batch_mean_aggregate
-    computes it from those rows, one warp per sample. For a batch over one
-    node set; rows past the batch's node count are left as they are."""
-    _native.require_cuda()
-    cap = int(batch.node_ids.numel())
-    F = int(table.shape[1])
-    if rows_out.dtype != table.dtype or out.dtype != table.dtype:
-        raise ValueError("batch_gather_mean: table, rows_out and out must share a dtype")
-    _native.check(_native.lib().dgfx_batch_gather_mean(
-        _native.ptr(batch.node_offsets), _native.ptr(batch.edge_offsets), _native.ptr(batch.edge_src),
-        _native.ptr(batch.edge_dst), _native.ptr(batch.node_ids), int(batch.B), cap, _native.ptr(table),
-        int(table.shape[0]), _dtype_code(table.dtype), F, _native.ptr(rows_out), _native.ptr(out),
-        _native.stream_handle(stream)))
-    return rows_out, out

@@ -198,17 +198,11 @@ __device__ __forceinline__ void batch_mean_flush(uint4* __restrict__ out, int64_
   }
 }
 
-// kGather: the warp first copies its sample's feature rows from `table`
-// (rows node_ids[nb + v]; ids outside the table give zero rows) into `rows`,
-// then averages from them. Each lane reads back only the 16-byte chunks it
-// wrote itself, so no barrier is needed; the reads avoid the read-only path
-// because `rows` is written by the same kernel.
-template <class T, bool kGather>
+template <class T>
 __global__ void batch_mean_kernel(const int64_t* __restrict__ node_off, const int64_t* __restrict__ edge_off,
                                   const int64_t* __restrict__ edge_src, const int64_t* __restrict__ edge_dst,
-                                  int64_t B, int64_t node_cap, uint4* rows, int64_t chunks, uint4* __restrict__ out,
-                                  const int64_t* __restrict__ node_ids, const uint4* __restrict__ table,
-                                  int64_t num_table_rows) {
+                                  int64_t B, int64_t node_cap, const uint4* __restrict__ feats, int64_t chunks,
+                                  uint4* __restrict__ out) {
   constexpr int V = 16 / sizeof(T);
   constexpr int kAhead = 4;
   const int lane = threadIdx.x & 31;
@@ -216,29 +210,6 @@ __global__ void batch_mean_kernel(const int64_t* __restrict__ node_off, const in
   for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; i < B; i += warps) {
     const int64_t nb = node_off[i], nn = node_off[i + 1] - nb;
     const int64_t eb = edge_off[i], ne = edge_off[i + 1] - eb;
-    if (kGather) {
-      for (int64_t v0 = 0; v0 < nn; v0 += 32) {
-        const int mv = static_cast<int>(nn - v0 < 32 ? nn - v0 : 32);
-        const int64_t my_id = lane < mv ? node_ids[nb + v0 + lane] : -1;
-        for (int64_t c0 = 0; c0 < chunks; c0 += 32) {
-          const int64_t ch = c0 + lane;
-          for (int j0 = 0; j0 < mv; j0 += kAhead) {
-            uint4 r[kAhead];
-#pragma unroll
-            for (int u = 0; u < kAhead; ++u) {
-              const int64_t id = __shfl_sync(0xffffffffu, my_id, (j0 + u) & 31);
-              const bool ok = ch < chunks && j0 + u < mv && id >= 0 && id < num_table_rows;
-              r[u] = ok ? __ldg(table + id * chunks + ch) : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int u = 0; u < kAhead; ++u) {
-              const int64_t v = nb + v0 + j0 + u;
-              if (ch < chunks && j0 + u < mv && v < node_cap) rows[v * chunks + ch] = r[u];
-            }
-          }
-        }
-      }
-    }
     for (int64_t c0 = 0; c0 < chunks; c0 += 32) {
       const int64_t ch = c0 + lane;
       const bool on = ch < chunks;
@@ -258,8 +229,7 @@ __global__ void batch_mean_kernel(const int64_t* __restrict__ node_off, const in
             const int j = (j0 + u) & 31;
             src[u] = __shfl_sync(0xffffffffu, my_s, j);
             const int64_t d = __shfl_sync(0xffffffffu, my_d, j);
-            const uint4* src_row = rows + (nb + d) * chunks + ch;
-            r[u] = (on && j0 + u < m) ? (kGather ? *src_row : __ldg(src_row)) : make_uint4(0, 0, 0, 0);
+            r[u] = (on && j0 + u < m) ? __ldg(feats + (nb + d) * chunks + ch) : make_uint4(0, 0, 0, 0);
           }
 #pragma unroll
           for (int u = 0; u < kAhead; ++u) {
@@ -323,62 +293,34 @@ extern "C" int dgfx_graph_launch_with_inputs(void* graph_exec, void* dst0, const
   return DGFX_OK;
 }
 
-namespace {
-int batch_mean_launch(const char* what, const int64_t* d_node_offsets, const int64_t* d_edge_offsets,
-                      const int64_t* d_edge_src, const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity,
-                      void* d_rows, int dtype, int64_t feat, void* d_out, const int64_t* d_node_ids,
-                      const void* d_table, int64_t num_table_rows, cudaStream_t stream) {
-  const bool gather = d_table != nullptr;
+extern "C" int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
+                               const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity,
+                               const void* d_feats, int dtype, int64_t feat, void* d_out, dgfx_stream stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (num_seeds < 0 || node_capacity < 0 || feat <= 0 || d_node_offsets == nullptr || d_edge_offsets == nullptr ||
-      (dtype != DGFX_F32 && dtype != DGFX_BF16) || (gather && (d_node_ids == nullptr || num_table_rows < 0))) {
-    return fail(DGFX_ERR_INVALID_ARGUMENT, std::string(what) + ": bad arguments");
+      (dtype != DGFX_F32 && dtype != DGFX_BF16)) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_batch_mean: bad arguments");
   }
   const int64_t row_bytes = feat * (dtype == DGFX_F32 ? 4 : 2);
-  if (row_bytes % 16 != 0 || reinterpret_cast<uintptr_t>(d_rows) % 16 != 0 ||
-      reinterpret_cast<uintptr_t>(d_out) % 16 != 0 || reinterpret_cast<uintptr_t>(d_table) % 16 != 0) {
-    return fail(DGFX_ERR_INVALID_ARGUMENT, std::string(what) + ": rows must be a multiple of 16 bytes, 16-byte aligned");
+  if (row_bytes % 16 != 0 || reinterpret_cast<uintptr_t>(d_feats) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(d_out) % 16 != 0) {
+    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_batch_mean: rows must be a multiple of 16 bytes, 16-byte aligned");
   }
   if (num_seeds == 0 || node_capacity == 0) return DGFX_OK;
   const int64_t chunks = row_bytes / 16;
   const unsigned g = grid_for_items(num_seeds * 32, 256);  // one warp per sample
-  auto* rows = static_cast<uint4*>(d_rows);
-  auto* out = static_cast<uint4*>(d_out);
-  auto* table = static_cast<const uint4*>(d_table);
-#define DGFX_BATCH_MEAN(T, G)                                                                                        \
-  batch_mean_kernel<T, G><<<g, 256, 0, stream>>>(d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst, num_seeds, \
-                                                 node_capacity, rows, chunks, out, d_node_ids, table, num_table_rows)
   if (dtype == DGFX_F32) {
-    if (gather) DGFX_BATCH_MEAN(float, true);
-    else DGFX_BATCH_MEAN(float, false);
+    batch_mean_kernel<float><<<g, 256, 0, stream>>>(d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst, num_seeds,
+                                                    node_capacity, static_cast<const uint4*>(d_feats), chunks,
+                                                    static_cast<uint4*>(d_out));
   } else {
-    if (gather) DGFX_BATCH_MEAN(__nv_bfloat16, true);
-    else DGFX_BATCH_MEAN(__nv_bfloat16, false);
+    batch_mean_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst,
+                                                            num_seeds, node_capacity,
+                                                            static_cast<const uint4*>(d_feats), chunks,
+                                                            static_cast<uint4*>(d_out));
   }
-#undef DGFX_BATCH_MEAN
   DGFX_CUDA_TRY(cudaGetLastError());
   return DGFX_OK;
-}
-}  // namespace
-
-extern "C" int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
-                               const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity,
-                               const void* d_feats, int dtype, int64_t feat, void* d_out, dgfx_stream stream) {
-  return batch_mean_launch("dgfx_batch_mean", d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst, num_seeds,
-                           node_capacity, const_cast<void*>(d_feats), dtype, feat, d_out, nullptr, nullptr, 0,
-                           reinterpret_cast<cudaStream_t>(stream));
-}
-
-extern "C" int dgfx_batch_gather_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets,
-                                      const int64_t* d_edge_src, const int64_t* d_edge_dst, const int64_t* d_node_ids,
-                                      int64_t num_seeds, int64_t node_capacity, const void* d_table,
-                                      int64_t num_table_rows, int dtype, int64_t feat, void* d_feats_out, void* d_out,
-                                      dgfx_stream stream) {
-  if (d_table == nullptr || d_feats_out == nullptr) {
-    return fail(DGFX_ERR_INVALID_ARGUMENT, "dgfx_batch_gather_mean: null table or rows");
-  }
-  return batch_mean_launch("dgfx_batch_gather_mean", d_node_offsets, d_edge_offsets, d_edge_src, d_edge_dst, num_seeds,
-                           node_capacity, d_feats_out, dtype, feat, d_out, d_node_ids, d_table, num_table_rows,
-                           reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int dgfx_csr_add_diagonal(const int64_t* d_rowptr, const int32_t* d_col, int64_t num_rows, float diag,

@@ -573,15 +573,15 @@ class CapturedSampleStep:
             smp = self.samplers[k]
             batch = smp.sample_merged(self.seeds[k], None if self.seed_ts is None else self.seed_ts[k], None,
                                       call_index=_native.CALL_INDEX_DEVICE, check=False)
-            if table is not None and aggregate:  # gather + mean over each node's sampled neighbours, one kernel
-                aggregation.batch_gather_mean(batch, table, self.features[k], self.aggregates[k])
-            elif table is not None:
+            if table is not None:
                 off = batch.node_offsets
                 _native.check(_native.lib().dgfx_gather_rows_ranged(
                     _native.ptr(table), int(table.shape[0]), int(table.shape[1]) * table.element_size(),
                     _native.ptr(batch.node_ids), _native.elem_ptr(off, ns * self.B),
                     _native.elem_ptr(off, (ns + 1) * self.B), int(batch.node_ids.numel()),
                     _native.ptr(self.features[k]), _native.stream_handle()))
+                if aggregate:  # mean over each node's sampled neighbours
+                    aggregation.batch_mean_aggregate(batch, self.features[k], out=self.aggregates[k])
             return batch
 
         for k in range(K):  # allocates each sampler's workspace outside the capture

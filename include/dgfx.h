@@ -665,17 +665,6 @@ int dgfx_batch_csr(const int64_t* d_node_offsets, const int64_t* d_edge_offsets,
 int dgfx_batch_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets, const int64_t* d_edge_src,
                     const int64_t* d_edge_dst, int64_t num_seeds, int64_t node_capacity, const void* d_feats,
                     int dtype, int64_t feat, void* d_out, dgfx_stream stream);
-/* dgfx_batch_gather_mean: the feature gather of a batch over one node set
- * and its mean aggregation in one kernel. d_feats_out[v] = d_table[
- * d_node_ids[v]] (zero rows for ids outside [0, num_table_rows)), then
- * d_out as dgfx_batch_mean computes it from those rows; one warp per sample
- * does both, so a captured small-batch step has one dependent kernel less.
- * Table, rows and out: dtype rows of feat elements, 16-byte aligned. */
-int dgfx_batch_gather_mean(const int64_t* d_node_offsets, const int64_t* d_edge_offsets,
-                           const int64_t* d_edge_src, const int64_t* d_edge_dst, const int64_t* d_node_ids,
-                           int64_t num_seeds, int64_t node_capacity, const void* d_table,
-                           int64_t num_table_rows, int dtype, int64_t feat, void* d_feats_out, void* d_out,
-                           dgfx_stream stream);
 
 /* Writes *d_node_total and *d_edge_total (for a merged batch: the last words
  * of its node and edge offsets) to out2[0], out2[1] in stream order, from
