@@ -70,6 +70,37 @@ def test_captured_step_matches_eager(cuda):
     graph_s.check()
 
 
+@pytest.mark.parametrize("serial", [False, True])
+def test_captured_step_aggregate_matches_separate_calls(cuda, serial):
+    """CapturedSampleStep(aggregate=True) (gather + mean aggregation inside
+    the graph, two samplers forked or serial) gives the rows and means of
+    eager gather and mean calls on the eager FIRST-mode batches."""
+    from distributed_graph_flow_b200 import _native, aggregation
+    from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
+
+    dev = torch.device("cuda", 0)
+    spec, index, _, _ = _temporal_graph(dev)
+    table = torch.randn((spec.num_nodes, 128), device=dev)
+    eager, _ = _sampler(index, spec.num_nodes, _native.MODE_FIRST)
+    graph_s = [_sampler(index, spec.num_nodes, _native.MODE_FIRST)[0] for _ in range(2)]
+    step = ext.CapturedSampleStep(graph_s, 256, True, table, aggregate=True, serial=serial)
+    rng = np.random.default_rng(3)
+    seeds = torch.from_numpy(rng.integers(0, spec.num_nodes, (2, 256))).to(dev)
+    sts = torch.from_numpy(rng.integers(0, 55, (2, 256))).to(dev)
+    for _ in range(2):
+        outs = step.run(seeds, sts)
+        torch.cuda.current_stream().synchronize()
+        for k, (batch, rows, means) in enumerate(outs):
+            exp = eager.sample_merged(seeds[k], sts[k])
+            n = int(exp.node_offsets[-1])
+            np.testing.assert_array_equal(ext.batch_to_host(batch)[0], ext.batch_to_host(exp)[0])
+            exp_rows = aggregation.gather_rows(table, exp.node_ids)
+            assert torch.equal(rows[:n], exp_rows[:n])
+            assert torch.equal(means[:n], aggregation.batch_mean_aggregate(exp, exp_rows)[:n])
+    for smp in graph_s:
+        smp.check()
+
+
 def test_captured_step_random_stream_advances(cuda):
     from distributed_graph_flow_b200 import _native
     from distributed_graph_flow_b200.sampling import _in_memory_sampler_ext as ext
