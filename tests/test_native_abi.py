@@ -48,3 +48,20 @@ def test_argument_errors_need_no_gpu():
     size = ctypes.c_size_t()
     assert lib.dgfx_csr_build_workspace_size(1000, 10, 10, 1, ctypes.byref(size)) == _native.OK
     assert size.value > 1000 * 24
+
+
+def test_more_argument_errors_need_no_gpu():
+    """Entry points added with the pipelined and captured paths validate
+    their arguments on the host, before any CUDA call."""
+    lib = _native.lib()
+    assert lib.dgfx_graph_launch_with_inputs(None, None, None, 0, None, None, 0, None) == _native.ERR_INVALID_ARGUMENT
+    assert "dgfx_graph_launch_with_inputs" in _native.last_error()
+    # A non-null exec with a copy whose pointers are missing is refused too.
+    assert lib.dgfx_graph_launch_with_inputs(1, None, None, 8, None, None, 0, None) == _native.ERR_INVALID_ARGUMENT
+    assert lib.dgfx_publish_totals(None, None, None, None) == _native.ERR_INVALID_ARGUMENT
+    assert lib.dgfx_batch_mean(None, None, None, None, 1, 1, None, 7, 8, None, None) == _native.ERR_INVALID_ARGUMENT
+    size = ctypes.c_size_t()
+    assert lib.dgfx_segment_softmax_workspace_size(-1, 1, 1, 8, 0, 1, ctypes.byref(size)) == _native.ERR_INVALID_ARGUMENT
+    assert lib.dgfx_segment_softmax_workspace_size(1000, 10, 8, 32, 1, 1, ctypes.byref(size)) == _native.OK
+    assert size.value > 0
+    assert lib.dgfx_spmm_workspace_size(100, 1000, 0, ctypes.byref(size)) == _native.ERR_INVALID_ARGUMENT
